@@ -1,0 +1,385 @@
+"""KV-cache hot-path benchmark (BASELINE.json metric on its Llama-3-8B decode config).
+
+One step = one decode step of one layer for a batch of 64 sequences:
+  1. fused RMSNorm + RoPE + KV append of the 64 new tokens into their pages
+     (kcmm_fused_norm_rope_append_bf16_on_stream), and
+  2. paged decode attention over every sequence's context
+     (kcmm_paged_attn_decode_bf16_on_stream),
+both through the C ABI of libkcmm.so.  Context lengths are uniform in
+[512, 4096] with block tables drawn without replacement from a 40,000-block
+pool.  K/V pages are 1.25 GiB per region, far larger than
+the 126 MB L2, so no flush is needed between steps ("inputs larger than L2").
+
+`value` = whole-job KV-path GB/s (all ranks' attention + append bytes per step
+/ max-over-ranks step time).  `tokens_per_s` = decode tokens/s of a 32-layer
+model's KV path = B_total / (32 * t_step).
+
+Usage:
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+For N > 1 launch with torch.distributed.run (one rank per GPU, weak scaling:
+each rank owns its own 64 sequences and pool; no collective on the data path).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = ("paged decode attn KV GB/s (% of HBM peak) and decode tokens/s at 1/2/4/8 B200")
+CONFIG = {"workload": "llama3-8b decode attention + fused norm/rope/append (BASELINE config 2)",
+          "batch_per_gpu": 64, "num_q_heads": 32, "kv_heads": 8, "head_dim": 128,
+          "block_size": 16, "context": "uniform [512, 4096]", "pool_blocks": 40000,
+          "layers_for_tokens_per_s": 32, "l2": "inputs larger than L2 (2.5 GiB of pages)"}
+LAYERS_FOR_TOKENS = 32
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local}"))
+    return world, rank, local
+
+
+def run_ours(args):
+    import torch
+
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    from lattice_b200.workloads import DecodeWorkload, FusedAppendWorkload
+
+    wl = DecodeWorkload(seed=1000 + rank, device=local).build()
+    # the step's new token of sequence b sits at position L_b - 1 of its table
+    slots = np.array([int(wl.tables[b, (L - 1) // 16]) * 16 + (L - 1) % 16
+                      for b, L in enumerate(wl.seq_lens)], np.int64)
+    fa = FusedAppendWorkload(tokens=wl.batch, pool=wl.pool, seed=2000 + rank,
+                             device=local).build()
+    fa.slots = slots
+    fa.d_slots.copy_(torch.from_numpy(slots))
+    q_step = wl.q  # the rotated q feeds attention
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step():
+        fa.run(stream_ptr=sp, q=q_step)
+        wl.decode(stream_ptr=sp)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+
+    # per-op event pairs for the roofline of the dominant kernel (decode attention)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    t0.record(stream)
+    for i in range(args.steps):
+        a, b, c = ev[i]
+        a.record(stream)
+        fa.run(stream_ptr=sp, q=q_step)
+        b.record(stream)
+        wl.decode(stream_ptr=sp)
+        c.record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    total_ms = t0.elapsed_time(t1)
+    attn_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    app_ms = [e[0].elapsed_time(e[1]) for e in ev]
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([total_ms], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+        dist.barrier()
+    ms_step = total_ms / args.steps
+    attn_bytes = wl.kv_bytes()
+    app_bytes = fa.bytes_per_launch()
+    step_bytes = (attn_bytes + app_bytes) * world
+    value = step_bytes / (ms_step * 1e-3) / 1e9
+    tokens_per_s = wl.batch * world / (LAYERS_FOR_TOKENS * ms_step * 1e-3)
+    attn_avg = statistics.mean(attn_ms)
+    achieved = attn_bytes / (attn_avg * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    from lattice_b200.kcmm import KcmmError  # noqa: F401  (import check)
+
+    splits = int(os.environ.get("KCMM_DECODE_SPLITS", "0"))
+    launches_per_step = 1 + 2  # fused append + decode main + split merge
+    e2e = run_e2e(args, wl, fa, stream) if rank == 0 else None
+    status = wl.pool.kernel_status()
+
+    result = None
+    if rank == 0:
+        cpu = cpu_baseline(wl) if world == 1 else None
+        result = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) bf16 pages/q/x, uniform context lengths)",
+            "config": dict(CONFIG, parallelism=f"replicas x{world} (sequence-sharded, no collective)"),
+            "tokens_per_s": round(tokens_per_s, 1),
+            "kv_gbs_attention_kernel": round(achieved, 1),
+            "hbm_frac_attention": round(achieved / peak, 4),
+            "attn_us_per_launch": round(attn_avg * 1e3, 2),
+            "append_us_per_launch": round(statistics.mean(app_ms) * 1e3, 2),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic_from_profiles(), "peak_kind": peak_kind,
+                         "kernel": "paged decode attention (main + split merge), per launch",
+                         "algorithmic_bytes_per_launch": attn_bytes},
+            "gpu_launches": launches_per_step * args.steps,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+            "device_status": status,
+        }
+        print(json.dumps(result))
+    wl.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def run_e2e(args, wl, fa, stream):
+    """Same step through the public API with host buffers: H2D of the step's inputs from
+    pinned memory, the two ABI calls, D2H of the attention output."""
+    import torch
+
+    ins = [wl.q, fa.x, fa.k, fa.v]
+    host_in = [t.detach().cpu().pin_memory() for t in ins]
+    host_out = torch.empty_like(wl.out, device="cpu").pin_memory()
+    sp = stream.cuda_stream
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = host_out.numel() * host_out.element_size()
+
+    def step():
+        for d, h in zip(ins, host_in):
+            d.copy_(h, non_blocking=True)
+        fa.run(stream_ptr=sp, q=wl.q)
+        wl.decode(stream_ptr=sp)
+        host_out.copy_(wl.out, non_blocking=True)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    byts = wl.kv_bytes() + fa.bytes_per_launch()
+    return {"value": round(byts / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(ms, 5), "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h),
+            "tokens_per_s": round(wl.batch / (LAYERS_FOR_TOKENS * ms * 1e-3), 1)}
+
+
+def traffic_from_profiles():
+    """DRAM bytes per decode launch from the committed ncu summary, if present."""
+    p = ROOT / "profiles" / "decode_attention_llama3_8b.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get("dram_bytes_per_launch")
+        except (ValueError, OSError):
+            return None
+    return None
+
+
+def _ref_attention_sample(wl_like, nseq, workers):
+    """Reference kernel on the host for the first `nseq` sequences; returns (seconds, bytes)."""
+    from oracle import native as N
+
+    q, va_k, va_v, tables, seq, offsets, meta = wl_like
+    t = time.perf_counter()
+    if N.ref_available():
+        N.ref_paged_attn("bf16", q[:nseq], va_k, va_v, tables[:nseq], seq[:nseq], offsets,
+                         workers=workers, **meta)
+        kind = "reference"
+    else:
+        N.paged_attn("bf16", q[:nseq], va_k, va_v, tables[:nseq], seq[:nseq], offsets, **meta)
+        kind = "port"
+    dt = time.perf_counter() - t
+    L = seq[:nseq].astype(np.int64)
+    byts = int((L * meta["hkv"] * meta["d"] * 2 * 2).sum() + 4 * np.ceil(L / 16).sum()
+               + nseq * meta["hq"] * meta["d"] * 4)
+    return dt, byts, kind
+
+
+def cpu_baseline(wl, nseq: int = 16):
+    """The reference's decode attention (its own kernel source compiled for the host,
+    oracle/_ref, bf16 storage) on a bounded sample of this workload, all host threads."""
+    from lattice_b200.workloads import tensor_bits
+
+    workers = os.cpu_count() or 1
+    q = tensor_bits(wl.q).reshape(wl.batch, -1)
+    va_k, va_v = wl.host_region(0, "k"), wl.host_region(0, "v")
+    meta = dict(hq=wl.num_q_heads, hkv=wl.kv_heads, d=wl.head_dim, bs=wl.block_size,
+                max_bps=wl.max_blocks_per_seq, scale=wl.scale)
+    dt, byts, kind = _ref_attention_sample(
+        (q, va_k, va_v, wl.tables, wl.seq_lens, wl.offsets, meta), nseq, workers)
+    return {"value": round(byts / dt / 1e9, 3), "unit": "GB/s", "cores": workers, "kind": kind,
+            "sample": f"decode attention of {nseq} of the {wl.batch} sequences "
+                      f"({int(wl.seq_lens[:nseq].sum())} tokens x 32 q heads), {dt:.2f} s"}
+
+
+def run_reference(args):
+    """Reference arm: the reference's own decode-attention kernel compiled for the host
+    (oracle/_ref; the oracle port when the reference tree was absent at build time),
+    on every host thread, over a bounded sample of the same workload per step."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    from oracle import native as N
+
+    rng = np.random.default_rng(1000)
+    B, hq, hkv, D, bs, pool = 64, 32, 8, 128, 16, 40000
+    seq = rng.integers(512, 4097, B).astype(np.int32)
+    max_bps = 256
+    need = [-(-int(L) // bs) for L in seq]
+    nseq = 4  # sequences per step: a bounded sample (about a second of CPU work)
+    used = sum(need[:nseq])
+    perm = rng.permutation(used).astype(np.int32)
+    tables = np.zeros((B, max_bps), np.int32)
+    pos = 0
+    for b in range(nseq):
+        tables[b, :need[b]] = perm[pos:pos + need[b]]
+        pos += need[b]
+    step_elems = hkv * D
+    offsets = np.arange(used, dtype=np.uint64) * np.uint64(bs * step_elems)
+    va_k = N.f32_to_bf16_bits(rng.standard_normal(used * bs * step_elems).astype(np.float32))
+    va_v = N.f32_to_bf16_bits(rng.standard_normal(used * bs * step_elems).astype(np.float32))
+    q = N.f32_to_bf16_bits(rng.standard_normal((B, hq * D)).astype(np.float32))
+    meta = dict(hq=hq, hkv=hkv, d=D, bs=bs, max_bps=max_bps, scale=D ** -0.5)
+    workers = os.cpu_count() or 1
+    sample = (q, va_k, va_v, tables, seq, offsets, meta)
+    for _ in range(max(1, min(args.warmup, 2))):
+        _ref_attention_sample(sample, nseq, workers)
+    times, byts, kind = [], 0, "reference"
+    for _ in range(args.steps):
+        dt, byts, kind = _ref_attention_sample(sample, nseq, workers)
+        times.append(dt)
+    dt = statistics.mean(times)
+    value = byts / dt / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": dict(CONFIG, parallelism="host cores"),
+        "impl": "reference",
+        "tokens_per_s": round(nseq / (LAYERS_FOR_TOKENS * dt), 2),
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": workers,
+                         "kind": kind if N.ref_available() else "port",
+                         "sample": f"decode attention of {nseq} sequences "
+                                   f"({int(seq[:nseq].sum())} tokens x 32 q heads) per step"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

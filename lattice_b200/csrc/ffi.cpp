@@ -1,0 +1,851 @@
+// extern "C" exports of include/kcmm.h.
+//
+// Argument validation, error strings and return conventions follow
+// ref src/kcmm/ffi.rs (cited per function).  Kernels are compiled offline for
+// sm_100a and linked in; the reference's lazy NVRTC step
+// (ref src/kcmm/ffi.rs:103-171) has no counterpart, so the precompile entry
+// points only force the CUDA module to load.
+#include <cuda_runtime.h>
+
+#include <cctype>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/kcmm.h"
+#include "kcmm_internal.hpp"
+#include "launch.hpp"
+
+using kcmm::Error;
+using kcmm::Pool;
+
+struct kcmm_pool_t {
+  Pool *pool;
+};
+
+namespace {
+
+Pool *P(kcmm_pool_t *h) { return h ? h->pool : nullptr; }
+
+void set_error(kcmm_pool_t *h, const std::string &msg) {
+  if (!h) return;
+  std::lock_guard<std::mutex> g(h->pool->err_mu);
+  h->pool->last_error = msg;
+}
+
+size_t write_c_string(char *buf, size_t max_len, const std::string &s) {
+  if (!buf || max_len == 0) return 0;
+  size_t n = s.size() < max_len - 1 ? s.size() : max_len - 1;
+  std::memcpy(buf, s.data(), n);
+  buf[n] = 0;
+  return n;
+}
+
+// Run `fn`; a thrown error becomes "<op>: <message>" and -1.
+template <typename F>
+int guarded(kcmm_pool_t *h, const char *op, F &&fn) {
+  try {
+    fn();
+    return 0;
+  } catch (const std::exception &e) {
+    set_error(h, std::string(op) + ": " + e.what());
+    return -1;
+  }
+}
+
+cudaStream_t S(uint64_t stream_ptr) { return reinterpret_cast<cudaStream_t>(stream_ptr); }
+
+int check_launch(kcmm_pool_t *h, const char *op, cudaError_t e) {
+  if (e != cudaSuccess) {
+    set_error(h, std::string(op) + ": launch failed: " + cudaGetErrorString(e));
+    return -1;
+  }
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+// ---------------------------------------------------------------------------
+// Lifecycle (ref src/kcmm/ffi.rs:470-590)
+// ---------------------------------------------------------------------------
+
+kcmm_pool_t *kcmm_pool_create(const kcmm_config_t *c) {
+  if (!c) return nullptr;
+  kcmm::PoolConfig cfg;
+  cfg.block_size = c->block_size ? c->block_size : 16;
+  cfg.max_blocks = c->max_blocks ? c->max_blocks : 16384;
+  size_t plen = strnlen(c->cpu_cache_path, sizeof(c->cpu_cache_path));
+  cfg.cpu_cache_path = plen ? std::string(c->cpu_cache_path, plen) : "/dev/shm/kcmm_swap";
+  cfg.tiering = c->tiering != 0;
+  cfg.eviction_policy = c->eviction_policy == 1 ? "lfu" : c->eviction_policy == 2 ? "fifo" : "lru";
+  cfg.prefetch_window = c->prefetch_window ? c->prefetch_window : 4;
+  cfg.max_batch_blocks = c->max_batch_blocks ? c->max_batch_blocks : 64;
+  cfg.device = int(c->device_ordinal);
+  cfg.num_layers = c->num_layers;
+  cfg.kv_heads = c->kv_heads;
+  cfg.head_dim = c->head_dim;
+  cfg.max_batch = c->max_batch;
+  cfg.max_seq_len = c->max_seq_len;
+  cfg.low_watermark = c->low_watermark_threshold > 0.0f ? c->low_watermark_threshold : 0.2f;
+  cfg.evict_interval_ms = c->background_evict_interval_ms ? c->background_evict_interval_ms : 100;
+  cfg.sink_blocks = c->attention_sink_blocks ? c->attention_sink_blocks : 1;
+  cfg.window_blocks = c->recent_window_blocks ? c->recent_window_blocks : 4;
+  try {
+    const char *backend = std::getenv("KCMM_VMM_BACKEND");
+    std::unique_ptr<kcmm::Vmm> vmm = (backend && std::strcmp(backend, "host") == 0)
+                                         ? kcmm::make_host_vmm()
+                                         : kcmm::make_cuda_vmm(cfg.device);
+    auto *h = new kcmm_pool_t;
+    h->pool = new Pool(cfg, std::move(vmm));
+    return h;
+  } catch (const std::exception &e) {
+    if (std::getenv("KCMM_DEBUG")) std::fprintf(stderr, "kcmm_pool_create: %s\n", e.what());
+    return nullptr;
+  }
+}
+
+void kcmm_pool_destroy(kcmm_pool_t *h) {
+  if (!h) return;
+  delete h->pool;
+  delete h;
+}
+
+size_t kcmm_get_last_error(kcmm_pool_t *h, char *buf, size_t max_len) {
+  if (!h || !buf || max_len == 0) return 0;
+  std::lock_guard<std::mutex> g(h->pool->err_mu);
+  if (h->pool->last_error.empty()) return 0;
+  return write_c_string(buf, max_len, h->pool->last_error);
+}
+
+void kcmm_clear_error(kcmm_pool_t *h) {
+  if (!h) return;
+  std::lock_guard<std::mutex> g(h->pool->err_mu);
+  h->pool->last_error.clear();
+}
+
+// ---------------------------------------------------------------------------
+// Allocation and sequences (ref src/kcmm/ffi.rs:605-850)
+// ---------------------------------------------------------------------------
+
+int kcmm_alloc_blocks(kcmm_pool_t *h, uint32_t n, uint32_t *out) {
+  if (!h || !out || n == 0) {
+    set_error(h, "kcmm_alloc_blocks: null output buffer or zero count");
+    return -1;
+  }
+  return guarded(h, "kcmm_alloc_blocks", [&] {
+    for (uint32_t i = 0; i < n; ++i) out[i] = P(h)->alloc_block();
+  });
+}
+
+int kcmm_free_blocks(kcmm_pool_t *h, const uint32_t *blocks, uint32_t n) {
+  if (!h || !blocks || n == 0) return 0;
+  P(h)->free_blocks(blocks, n);
+  return 0;
+}
+
+int kcmm_register_sequence(kcmm_pool_t *h, const uint32_t *table, uint32_t n, uint32_t *out) {
+  if (!h || !table || !out) {
+    set_error(h, "kcmm_register_sequence: null arguments");
+    return -1;
+  }
+  *out = P(h)->register_sequence(std::vector<uint32_t>(table, table + n));
+  return 0;
+}
+
+int kcmm_unregister_sequence(kcmm_pool_t *h, uint32_t seq) {
+  if (!h) return -1;
+  P(h)->unregister_sequence(seq);
+  return 0;
+}
+
+void kcmm_touch(kcmm_pool_t *h, uint32_t seq) {
+  if (!h) return;
+  std::vector<uint32_t> t;
+  if (P(h)->touch(seq) && P(h)->block_table(seq, &t)) {
+    for (uint32_t b : t) P(h)->note_access(b);
+  }
+}
+
+void kcmm_cool(kcmm_pool_t *h, uint32_t seq) {
+  if (h) P(h)->cool(seq);
+}
+
+void kcmm_update_seq_len(kcmm_pool_t *h, uint32_t seq, uint32_t len) {
+  if (h) P(h)->update_seq_len(seq, len);
+}
+
+uint32_t kcmm_get_seq_len(kcmm_pool_t *h, uint32_t seq) {
+  return h ? uint32_t(P(h)->seq_len(seq)) : 0;
+}
+
+int kcmm_append_block_to_sequence(kcmm_pool_t *h, uint32_t seq, uint32_t blk) {
+  if (!h) return -1;
+  if (!P(h)->append_block(seq, blk)) {
+    set_error(h, "kcmm_append_block_to_sequence: seq_idx " + std::to_string(seq) + " out of bounds");
+    return -1;
+  }
+  return 0;
+}
+
+int kcmm_get_block_table(kcmm_pool_t *h, uint32_t seq, uint32_t *out, uint32_t max_blocks,
+                         uint32_t *out_count) {
+  if (!h || !out || !out_count) {
+    set_error(h, "kcmm_get_block_table: null arguments");
+    return -1;
+  }
+  std::vector<uint32_t> t;
+  if (!P(h)->block_table(seq, &t)) {
+    set_error(h, "kcmm_get_block_table: seq_idx " + std::to_string(seq) + " not found");
+    *out_count = 0;
+    return -1;
+  }
+  size_t n = t.size() < max_blocks ? t.size() : max_blocks;
+  std::memcpy(out, t.data(), n * sizeof(uint32_t));
+  *out_count = uint32_t(n);
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Queries (ref src/kcmm/ffi.rs:861-1060, 2143)
+// ---------------------------------------------------------------------------
+
+uint64_t kcmm_get_block_va_offset(kcmm_pool_t *h, uint32_t blk) {
+  uint64_t v = 0;
+  if (h && P(h)->block_va_offset(blk, &v)) return v;
+  return 0;
+}
+
+int kcmm_get_all_block_offsets_f16(kcmm_pool_t *h, uint64_t *out, uint32_t max_blocks,
+                                   uint32_t *out_count) {
+  if (!h || !out || !out_count) {
+    set_error(h, "kcmm_get_all_block_offsets_f16: null arguments");
+    return -1;
+  }
+  auto v = P(h)->all_offsets_f16();
+  size_t n = v.size() < max_blocks ? v.size() : max_blocks;
+  std::memcpy(out, v.data(), n * sizeof(uint64_t));
+  *out_count = uint32_t(n);
+  return 0;
+}
+
+int kcmm_get_all_block_valid(kcmm_pool_t *h, uint8_t *out, uint32_t max_blocks,
+                             uint32_t *out_count) {
+  if (!h || !out || !out_count) {
+    set_error(h, "kcmm_get_all_block_valid: null arguments");
+    return -1;
+  }
+  auto v = P(h)->all_valid();
+  size_t n = v.size() < max_blocks ? v.size() : max_blocks;
+  std::memcpy(out, v.data(), n);
+  *out_count = uint32_t(n);
+  return 0;
+}
+
+int kcmm_get_block_location(kcmm_pool_t *h, uint32_t blk, kcmm_block_location_t *out) {
+  if (!h || !out) return -1;
+  kcmm::Loc loc;
+  if (!P(h)->block_location(blk, &loc)) {
+    set_error(h, "kcmm_get_block_location: block_idx " + std::to_string(blk) + " not found");
+    return -1;
+  }
+  *out = kcmm_block_location_t(int(loc));
+  return 0;
+}
+
+int kcmm_get_block_table_va_offsets(kcmm_pool_t *h, uint32_t seq, uint64_t *out,
+                                    uint32_t max_blocks, uint32_t *out_count) {
+  if (!h || !out || !out_count) {
+    set_error(h, "kcmm_get_block_table_va_offsets: null arguments");
+    return -1;
+  }
+  std::vector<uint64_t> v;
+  if (!P(h)->sequence_va_offsets(seq, &v)) {
+    set_error(h, "kcmm_get_block_table_va_offsets: seq_idx " + std::to_string(seq) + " not found");
+    *out_count = 0;
+    return -1;
+  }
+  size_t n = v.size() < max_blocks ? v.size() : max_blocks;
+  std::memcpy(out, v.data(), n * sizeof(uint64_t));
+  *out_count = uint32_t(n);
+  return 0;
+}
+
+uint64_t kcmm_get_va_k(kcmm_pool_t *h, uint32_t layer) {
+  if (!h || layer >= P(h)->num_layers) return 0;
+  return P(h)->va_k[layer];
+}
+
+uint64_t kcmm_get_va_v(kcmm_pool_t *h, uint32_t layer) {
+  if (!h || layer >= P(h)->num_layers) return 0;
+  return P(h)->va_v[layer];
+}
+
+uint64_t kcmm_block_state_epoch(kcmm_pool_t *h) { return h ? P(h)->epoch() : 0; }
+
+// ---------------------------------------------------------------------------
+// KV append (ref src/kcmm/ffi.rs:1088-1554)
+// ---------------------------------------------------------------------------
+
+static int append_rows(kcmm_pool_t *h, const char *op, uint32_t layer,
+                       const std::vector<int64_t> &dst, uint64_t k_src, uint64_t v_src,
+                       cudaStream_t stream) {
+  Pool *p = P(h);
+  if (dst.empty()) return 0;
+  if (!k_src || !v_src) {
+    set_error(h, std::string(op) + ": null source pointer");
+    return -1;
+  }
+  p->use_device();
+  cudaError_t e = kcmm::dev::copy_rows(
+      reinterpret_cast<const void *>(k_src), reinterpret_cast<const void *>(v_src),
+      reinterpret_cast<void *>(p->va_k[layer]), reinterpret_cast<void *>(p->va_v[layer]),
+      dst.data(), int(dst.size()), int(p->step_elems), stream);
+  return check_launch(h, op, e);
+}
+
+int kcmm_append_kv_step(kcmm_pool_t *h, uint32_t layer, const uint32_t *seqs,
+                        const uint32_t *positions, uint32_t batch, uint64_t k_src,
+                        uint64_t v_src) {
+  const char *op = "kcmm_append_kv_step";
+  if (!h || !seqs || !positions) {
+    set_error(h, std::string(op) + ": null arguments");
+    return -1;
+  }
+  if (layer >= P(h)->num_layers) {
+    set_error(h, std::string(op) + ": layer_idx " + std::to_string(layer) + " out of bounds");
+    return -1;
+  }
+  std::vector<int64_t> dst;
+  if (guarded(h, op, [&] {
+        P(h)->require_device(op);
+        P(h)->step_destinations(seqs, positions, batch, &dst);
+      }))
+    return -1;
+  return append_rows(h, op, layer, dst, k_src, v_src, nullptr);
+}
+
+static int append_slots(kcmm_pool_t *h, uint32_t layer, const int64_t *slots, uint32_t batch,
+                        uint64_t k_src, uint64_t v_src, uint64_t stream) {
+  const char *op = "kcmm_append_kv_slots";
+  if (!h || !slots) {
+    set_error(h, std::string(op) + ": null arguments");
+    return -1;
+  }
+  if (layer >= P(h)->num_layers) {
+    set_error(h, std::string(op) + ": layer_idx " + std::to_string(layer) + " out of bounds");
+    return -1;
+  }
+  std::vector<int64_t> dst;
+  if (guarded(h, op, [&] {
+        P(h)->require_device(op);
+        P(h)->slot_destinations(slots, batch, &dst);
+      }))
+    return -1;
+  return append_rows(h, op, layer, dst, k_src, v_src, S(stream));
+}
+
+int kcmm_append_kv_slots(kcmm_pool_t *h, uint32_t layer, const int64_t *slots, uint32_t batch,
+                         uint64_t k_src, uint64_t v_src) {
+  return append_slots(h, layer, slots, batch, k_src, v_src, 0);
+}
+
+int kcmm_append_kv_slots_on_stream(kcmm_pool_t *h, uint32_t layer, const int64_t *slots,
+                                   uint32_t batch, uint64_t k_src, uint64_t v_src,
+                                   uint64_t stream) {
+  return append_slots(h, layer, slots, batch, k_src, v_src, stream);
+}
+
+int kcmm_append_kv_device_slots_on_stream(kcmm_pool_t *h, uint32_t layer, uint64_t slot_mapping,
+                                          uint64_t offsets, uint64_t valid, uint32_t offsets_len,
+                                          uint32_t batch, uint64_t k_src, uint64_t v_src,
+                                          uint64_t status, uint64_t stream) {
+  const char *op = "kcmm_append_kv_device_slots_on_stream";
+  if (!h || !slot_mapping || !offsets || !k_src || !v_src) {
+    set_error(h, std::string(op) + ": null pointer argument");
+    return -1;
+  }
+  if (batch == 0 || offsets_len == 0) {
+    set_error(h, std::string(op) + ": batch and offset table length must be positive");
+    return -1;
+  }
+  Pool *p = P(h);
+  if (layer >= p->num_layers) {
+    set_error(h, std::string(op) + ": layer_idx " + std::to_string(layer) + " out of bounds");
+    return -1;
+  }
+  if (uint64_t(batch) * p->step_elems > 0x7fffffffull) {
+    set_error(h, std::string(op) + ": total_elements overflow");
+    return -1;
+  }
+  if (guarded(h, op, [&] { p->require_device(op); })) return -1;
+  kcmm::dev::SlotWriteArgs a;
+  a.va_k = reinterpret_cast<void *>(p->va_k[layer]);
+  a.va_v = reinterpret_cast<void *>(p->va_v[layer]);
+  a.slot_mapping = reinterpret_cast<const int64_t *>(slot_mapping);
+  a.block_offsets = reinterpret_cast<const uint64_t *>(offsets);
+  a.valid = reinterpret_cast<const uint8_t *>(valid);
+  a.offsets_len = int(offsets_len);
+  a.batch = int(batch);
+  a.step_elems = int(p->step_elems);
+  a.block_size = int(p->block_size);
+  a.k_src = reinterpret_cast<const void *>(k_src);
+  a.v_src = reinterpret_cast<const void *>(v_src);
+  a.status = reinterpret_cast<int32_t *>(status);
+  a.region_elems = p->region_bytes / 2;
+  p->use_device();
+  return check_launch(h, op, kcmm::dev::device_slot_write(a, S(stream)));
+}
+
+int kcmm_append_kv_device_slots_bf16_on_stream(kcmm_pool_t *h, uint32_t layer,
+                                               uint64_t slot_mapping, uint64_t offsets,
+                                               uint64_t valid, uint32_t offsets_len,
+                                               uint32_t batch, uint64_t k_src, uint64_t v_src,
+                                               uint64_t status, uint64_t stream) {
+  return kcmm_append_kv_device_slots_on_stream(h, layer, slot_mapping, offsets, valid,
+                                               offsets_len, batch, k_src, v_src, status, stream);
+}
+
+int kcmm_precompile_vllm_kv_write_f16(kcmm_pool_t *h) {
+  if (!h) return -1;
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Paged decode attention (ref src/kcmm/ffi.rs:1569-1881)
+// ---------------------------------------------------------------------------
+
+static int decode_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, uint64_t q,
+                       uint64_t out, uint64_t tables, uint64_t seq_lens, uint64_t offsets,
+                       uint32_t batch, uint32_t hq, uint32_t hkv, uint32_t hd, uint32_t bs,
+                       uint32_t max_bps, float scale, uint64_t stream, bool sync,
+                       bool bind) {
+  const char *op = dtype == kcmm::dev::Dtype::F16 ? "kcmm_paged_attn_decode_f16"
+                                                  : "kcmm_paged_attn_decode_bf16";
+  if (!h || !q || !out || !tables || !seq_lens || !offsets) {
+    set_error(h, std::string(op) + ": null pointer argument");
+    return -1;
+  }
+  if (batch == 0 || hq == 0 || hkv == 0 || hd == 0 || bs == 0 || max_bps == 0) {
+    set_error(h, std::string(op) + ": shape arguments must be positive");
+    return -1;
+  }
+  if (hd > 256) {
+    set_error(h, std::string(op) + ": head_dim " + std::to_string(hd) + " exceeds kernel limit 256");
+    return -1;
+  }
+  if (hq > 0xFFFF || hkv > 0xFFFF || bs > 0xFFFF || max_bps > 0xFFFF) {
+    set_error(h, std::string(op) + ": packed shape argument exceeds 65535");
+    return -1;
+  }
+  Pool *p = P(h);
+  if (layer >= p->num_layers) {
+    set_error(h, std::string(op) + ": layer_idx " + std::to_string(layer) + " out of bounds");
+    return -1;
+  }
+  if (uint64_t(batch) * hq > 0x7fffffffull) {
+    set_error(h, std::string(op) + ": total_heads overflow");
+    return -1;
+  }
+  if (guarded(h, op, [&] { p->require_device(op); })) return -1;
+  if (bind) p->use_device();
+  kcmm::dev::DecodeArgs a = {};
+  a.dtype = dtype;
+  a.q = reinterpret_cast<const void *>(q);
+  a.out = reinterpret_cast<void *>(out);
+  a.block_tables = reinterpret_cast<const int32_t *>(tables);
+  a.seq_lens = reinterpret_cast<const int32_t *>(seq_lens);
+  a.block_offsets = reinterpret_cast<const uint64_t *>(offsets);
+  a.va_k = reinterpret_cast<const void *>(p->va_k[layer]);
+  a.va_v = reinterpret_cast<const void *>(p->va_v[layer]);
+  a.region_elems = p->region_bytes / 2;
+  a.batch = int(batch);
+  a.num_q_heads = int(hq);
+  a.kv_heads = int(hkv);
+  a.head_dim = int(hd);
+  a.block_size = int(bs);
+  a.max_blocks_per_seq = int(max_bps);
+  a.scale = scale;
+  a.diag = p->diag_word();
+  if (const char *fs = std::getenv("KCMM_DECODE_SPLITS")) a.force_splits = std::atoi(fs);
+  if (check_launch(h, op, kcmm::dev::decode_attention(a, S(stream)))) return -1;
+  if (sync) {
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+      set_error(h, std::string(op) + ": synchronize failed: " + cudaGetErrorString(e));
+      return -1;
+    }
+  }
+  return 0;
+}
+
+int kcmm_paged_attn_decode_f16(kcmm_pool_t *h, uint32_t layer, uint64_t q, uint64_t out,
+                               uint64_t tables, uint64_t seq_lens, uint64_t offsets,
+                               uint32_t batch, uint32_t hq, uint32_t hkv, uint32_t hd,
+                               uint32_t bs, uint32_t max_bps, float scale) {
+  return decode_impl(h, kcmm::dev::Dtype::F16, layer, q, out, tables, seq_lens, offsets, batch,
+                     hq, hkv, hd, bs, max_bps, scale, 0, true, true);
+}
+
+int kcmm_paged_attn_decode_f16_on_stream(kcmm_pool_t *h, uint32_t layer, uint64_t q,
+                                         uint64_t out, uint64_t tables, uint64_t seq_lens,
+                                         uint64_t offsets, uint32_t batch, uint32_t hq,
+                                         uint32_t hkv, uint32_t hd, uint32_t bs,
+                                         uint32_t max_bps, float scale, uint64_t stream) {
+  return decode_impl(h, kcmm::dev::Dtype::F16, layer, q, out, tables, seq_lens, offsets, batch,
+                     hq, hkv, hd, bs, max_bps, scale, stream, false, true);
+}
+
+int kcmm_paged_attn_decode_f16_on_current_context_stream(
+    kcmm_pool_t *h, uint32_t layer, uint64_t q, uint64_t out, uint64_t tables,
+    uint64_t seq_lens, uint64_t offsets, uint32_t batch, uint32_t hq, uint32_t hkv, uint32_t hd,
+    uint32_t bs, uint32_t max_bps, float scale, uint64_t stream) {
+  return decode_impl(h, kcmm::dev::Dtype::F16, layer, q, out, tables, seq_lens, offsets, batch,
+                     hq, hkv, hd, bs, max_bps, scale, stream, false, false);
+}
+
+int kcmm_paged_attn_decode_bf16_on_stream(kcmm_pool_t *h, uint32_t layer, uint64_t q,
+                                          uint64_t out, uint64_t tables, uint64_t seq_lens,
+                                          uint64_t offsets, uint32_t batch, uint32_t hq,
+                                          uint32_t hkv, uint32_t hd, uint32_t bs,
+                                          uint32_t max_bps, float scale, uint64_t stream) {
+  return decode_impl(h, kcmm::dev::Dtype::BF16, layer, q, out, tables, seq_lens, offsets, batch,
+                     hq, hkv, hd, bs, max_bps, scale, stream, false, true);
+}
+
+int kcmm_precompile_paged_attn_decode_f16(kcmm_pool_t *h) {
+  if (!h) return -1;
+  if (guarded(h, "kcmm_precompile_paged_attn_decode_f16", [&] {
+        P(h)->require_device("kcmm_precompile_paged_attn_decode_f16");
+      }))
+    return -1;
+  P(h)->use_device();
+  return check_launch(h, "kcmm_precompile_paged_attn_decode_f16", kcmm::dev::decode_preload());
+}
+
+// ---------------------------------------------------------------------------
+// Fused RMSNorm + RoPE + append
+// ---------------------------------------------------------------------------
+
+int kcmm_fused_norm_rope_append_bf16_on_stream(
+    kcmm_pool_t *h, uint32_t layer, uint64_t x, uint64_t w, uint64_t normed, uint32_t hidden,
+    float eps, uint64_t q, uint32_t hq, uint64_t k, uint64_t v, uint64_t positions,
+    float theta, uint32_t rope_mode, uint64_t slots, uint64_t offsets, uint64_t valid,
+    uint32_t offsets_len, uint32_t num_tokens, uint64_t status, uint64_t stream) {
+  const char *op = "kcmm_fused_norm_rope_append_bf16_on_stream";
+  if (!h || !x || !w || !normed || !q || !k || !v || !positions || !slots || !offsets) {
+    set_error(h, std::string(op) + ": null pointer argument");
+    return -1;
+  }
+  Pool *p = P(h);
+  if (layer >= p->num_layers) {
+    set_error(h, std::string(op) + ": layer_idx " + std::to_string(layer) + " out of bounds");
+    return -1;
+  }
+  if (num_tokens == 0 || hidden == 0 || hq == 0 || offsets_len == 0) {
+    set_error(h, std::string(op) + ": shape arguments must be positive");
+    return -1;
+  }
+  if (hidden % 8 != 0 || hidden > 65536) {
+    set_error(h, std::string(op) + ": hidden must be a multiple of 8 and at most 65536");
+    return -1;
+  }
+  if (rope_mode > 2) {
+    set_error(h, std::string(op) + ": unknown rope_mode " + std::to_string(rope_mode));
+    return -1;
+  }
+  if (p->cfg_.head_dim % 2 != 0 || (rope_mode == 2 && p->cfg_.head_dim % 4 != 0)) {
+    set_error(h, std::string(op) + ": head_dim must be even (a multiple of 4 for neox)");
+    return -1;
+  }
+  if (hq > 0xFFFF || !(theta > 0.0f)) {
+    set_error(h, std::string(op) + ": invalid num_q_heads or rope_theta");
+    return -1;
+  }
+  if (guarded(h, op, [&] { p->require_device(op); })) return -1;
+  kcmm::dev::FusedAppendArgs a;
+  a.x = reinterpret_cast<const void *>(x);
+  a.norm_weight = reinterpret_cast<const void *>(w);
+  a.normed_out = reinterpret_cast<void *>(normed);
+  a.hidden = int(hidden);
+  a.eps = eps;
+  a.q = reinterpret_cast<void *>(q);
+  a.num_q_heads = int(hq);
+  a.k = reinterpret_cast<const void *>(k);
+  a.v = reinterpret_cast<const void *>(v);
+  a.positions = reinterpret_cast<const int32_t *>(positions);
+  a.rope_theta = theta;
+  a.rope_mode = int(rope_mode);
+  a.slot_mapping = reinterpret_cast<const int64_t *>(slots);
+  a.block_offsets = reinterpret_cast<const uint64_t *>(offsets);
+  a.valid = reinterpret_cast<const uint8_t *>(valid);
+  a.offsets_len = int(offsets_len);
+  a.num_tokens = int(num_tokens);
+  a.kv_heads = int(p->cfg_.kv_heads);
+  a.head_dim = int(p->cfg_.head_dim);
+  a.block_size = int(p->block_size);
+  a.va_k = reinterpret_cast<void *>(p->va_k[layer]);
+  a.va_v = reinterpret_cast<void *>(p->va_v[layer]);
+  a.region_elems = p->region_bytes / 2;
+  a.status = reinterpret_cast<int32_t *>(status);
+  p->use_device();
+  return check_launch(h, op, kcmm::dev::fused_norm_rope_append(a, S(stream)));
+}
+
+// ---------------------------------------------------------------------------
+// Tiering (ref src/kcmm/ffi.rs:1900-2030)
+// ---------------------------------------------------------------------------
+
+uint32_t kcmm_evict_blocks(kcmm_pool_t *h, uint32_t count) {
+  if (!h || count == 0) return 0;
+  uint32_t n = 0;
+  if (guarded(h, "kcmm_evict_blocks", [&] { n = uint32_t(P(h)->evict(count)); })) return 0;
+  return n;
+}
+
+uint64_t kcmm_restore_evicted_block(kcmm_pool_t *h, uint32_t blk) {
+  if (!h) return 0;
+  uint64_t va = 0;
+  if (guarded(h, "kcmm_restore_evicted_block", [&] { va = P(h)->restore_one(blk); })) return 0;
+  return va;
+}
+
+int kcmm_restore_evicted_blocks(kcmm_pool_t *h, const uint32_t *ids, uint32_t count) {
+  if (!h || !ids || count == 0) return 0;
+  return guarded(h, "kcmm_restore_evicted_blocks", [&] { P(h)->restore_many(ids, count); });
+}
+
+int kcmm_is_gpu_resident(kcmm_pool_t *h, uint32_t blk) {
+  kcmm::Loc loc;
+  return (h && P(h)->block_location(blk, &loc) && loc == kcmm::Loc::Gpu) ? 1 : 0;
+}
+
+int kcmm_swap_out_blocks_on_stream(kcmm_pool_t *h, const uint32_t *ids, uint32_t count,
+                                   uint64_t stream) {
+  if (!h) return -1;
+  if (!ids || count == 0) return 0;
+  return guarded(h, "kcmm_swap_out_blocks_on_stream",
+                 [&] { P(h)->swap_out(ids, count, reinterpret_cast<void *>(stream)); });
+}
+
+int kcmm_swap_in_blocks_on_stream(kcmm_pool_t *h, const uint32_t *ids, uint32_t count,
+                                  uint64_t stream) {
+  if (!h) return -1;
+  if (!ids || count == 0) return 0;
+  return guarded(h, "kcmm_swap_in_blocks_on_stream",
+                 [&] { P(h)->swap_in(ids, count, reinterpret_cast<void *>(stream)); });
+}
+
+// ---------------------------------------------------------------------------
+// Metrics and statistics (ref src/kcmm/ffi.rs:2037-2190)
+// ---------------------------------------------------------------------------
+
+int kcmm_get_metrics(kcmm_pool_t *h, kcmm_metrics_t *out) {
+  if (!h || !out) return -1;
+  kcmm_metrics_t m = {};
+  P(h)->collect_metrics(&m.ifr, &m.pme, &m.bu, &m.rfi, &m.gpu_blocks, &m.cpu_blocks);
+  kcmm::Metrics c = P(h)->metrics();
+  m.nvme_blocks = 0;
+  m.eviction_count = c.eviction_count;
+  m.restoration_count = c.restoration_count;
+  *out = m;
+  return 0;
+}
+
+int kcmm_get_pool_stats(kcmm_pool_t *h, kcmm_pool_stats_t *out) {
+  if (!h || !out) return -1;
+  Pool *p = P(h);
+  kcmm_pool_stats_t s = {};
+  s.blocks_in_use = uint32_t(p->blocks_in_use());
+  s.total_blocks = uint32_t(p->total_blocks());
+  s.total_physical_blocks = uint32_t(p->total_physical_blocks());
+  s.free_physical_blocks = uint32_t(p->free_physical_blocks());
+  s.active_sequences = uint32_t(p->active_sequences());
+  s.num_layers = uint32_t(p->num_layers);
+  s.blocks_per_superblock = uint32_t(kcmm::kSuperblockBytes / p->block_bytes);
+  s.superblock_count = uint32_t(p->superblock_count());
+  s.block_size = uint32_t(p->block_size);
+  s.max_blocks_per_seq = uint32_t(p->max_blocks_per_seq);
+  s.block_bytes = uint32_t(p->block_bytes);
+  s.tiering_enabled = p->tiering_enabled() ? 1 : 0;
+  s.sharing_enabled = 1;
+  s.physical_idle_ratio = p->physical_idle_ratio();
+  *out = s;
+  return 0;
+}
+
+uint32_t kcmm_blocks_in_use(kcmm_pool_t *h) { return h ? uint32_t(P(h)->blocks_in_use()) : 0; }
+uint32_t kcmm_total_blocks(kcmm_pool_t *h) { return h ? uint32_t(P(h)->total_blocks()) : 0; }
+uint32_t kcmm_free_physical_blocks(kcmm_pool_t *h) {
+  return h ? uint32_t(P(h)->free_physical_blocks()) : 0;
+}
+int kcmm_has_free_blocks(kcmm_pool_t *h) { return (h && P(h)->free_physical_blocks() > 0) ? 1 : 0; }
+uint32_t kcmm_active_sequences(kcmm_pool_t *h) {
+  return h ? uint32_t(P(h)->active_sequences()) : 0;
+}
+
+// ---------------------------------------------------------------------------
+// Policy, hints, sharing (ref src/kcmm/ffi.rs:2200-2500)
+// ---------------------------------------------------------------------------
+
+int kcmm_set_eviction_policy(kcmm_pool_t *h, const char *policy) {
+  if (!h || !policy) return -1;
+  std::string s(policy);
+  for (char &c : s) c = char(std::tolower(static_cast<unsigned char>(c)));
+  if (!P(h)->tiering_enabled()) {
+    set_error(h, "kcmm_set_eviction_policy: tiering is disabled");
+    return -1;
+  }
+  return guarded(h, "kcmm_set_eviction_policy", [&] { P(h)->set_policy(s); });
+}
+
+uint32_t kcmm_get_eviction_policy(kcmm_pool_t *h, char *out, uint32_t max_len) {
+  if (!h || !out || max_len == 0 || !P(h)->tiering_enabled()) return 0;
+  return uint32_t(write_c_string(out, max_len, P(h)->policy_name()));
+}
+
+int kcmm_is_tiering_enabled(kcmm_pool_t *h) { return (h && P(h)->tiering_enabled()) ? 1 : 0; }
+
+int kcmm_hint(kcmm_pool_t *h, uint32_t seq, kcmm_hint_t hint) {
+  if (!h) return -1;
+  Pool *p = P(h);
+  std::vector<uint32_t> table;
+  if (!p->block_table(seq, &table)) {
+    set_error(h, "kcmm_hint: seq_idx " + std::to_string(seq) + " out of bounds");
+    return -1;
+  }
+  switch (hint) {
+    case KCMM_HINT_MULTI_TURN:
+    case KCMM_HINT_SYSTEM_PROMPT:
+    case KCMM_HINT_ATTENTION_SINK:
+    case KCMM_HINT_HEAVY_HITTER:
+      p->touch(seq);
+      for (uint32_t b : table) p->note_access(b);
+      break;
+    case KCMM_HINT_HIGH_PRIORITY:
+      p->touch(seq);
+      p->set_priority(seq, kcmm::Priority::High);
+      break;
+    case KCMM_HINT_NEAR_END:
+      p->cool(seq);
+      break;
+    case KCMM_HINT_LOW_PRIORITY:
+      p->cool(seq);
+      p->set_priority(seq, kcmm::Priority::Low);
+      break;
+    case KCMM_HINT_EVICTABLE:
+      p->cool(seq);
+      p->set_priority(seq, kcmm::Priority::Evictable);
+      break;
+    default:
+      set_error(h, "kcmm_hint: unknown hint " + std::to_string(int(hint)));
+      return -1;
+  }
+  return 0;
+}
+
+int kcmm_protect(kcmm_pool_t *h, uint32_t, const uint32_t *ids, uint32_t n,
+                 kcmm_protection_t level) {
+  if (!h || !ids || n == 0) return -1;
+  Pool *p = P(h);
+  if (!p->tiering_enabled()) return 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    kcmm::BlockHandle bh;
+    if (!p->block_handle(ids[i], &bh)) {
+      set_error(h, "kcmm_protect: block_idx " + std::to_string(ids[i]) + " not found");
+      return -1;
+    }
+    if (level != KCMM_EVICT_PREFERRED) p->note_access(ids[i]);
+  }
+  return 0;
+}
+
+int kcmm_share_prefix(kcmm_pool_t *h, uint32_t src, uint32_t dst, uint32_t n, uint32_t *out) {
+  if (!h || !out || n == 0) return -1;
+  return guarded(h, "kcmm_share_prefix", [&] {
+    auto v = P(h)->share_prefix(src, dst, n);
+    std::memcpy(out, v.data(), v.size() * sizeof(uint32_t));
+  });
+}
+
+int kcmm_block_incref(kcmm_pool_t *h, uint32_t blk) {
+  if (!h) return -1;
+  return guarded(h, "kcmm_block_incref", [&] { P(h)->incref(blk); });
+}
+
+int kcmm_block_decref(kcmm_pool_t *h, uint32_t blk) {
+  if (!h) return -1;
+  return guarded(h, "kcmm_block_decref", [&] { P(h)->decref(blk); });
+}
+
+uint32_t kcmm_block_refcount(kcmm_pool_t *h, uint32_t blk) { return h ? P(h)->refcount(blk) : 0; }
+
+int kcmm_fork_sequence(kcmm_pool_t *h, uint32_t src, uint32_t *out) {
+  if (!h || !out) {
+    set_error(h, "kcmm_fork_sequence: null arguments");
+    return -1;
+  }
+  return guarded(h, "kcmm_fork_sequence", [&] { *out = P(h)->fork_sequence(src); });
+}
+
+int kcmm_cow_blocks_on_stream(kcmm_pool_t *h, const uint32_t *seqs, const uint32_t *logical,
+                              uint32_t count, uint32_t *out, uint64_t stream) {
+  if (!h) return -1;
+  if (count == 0) return 0;
+  if (!seqs || !logical || !out) {
+    set_error(h, "kcmm_cow_blocks_on_stream: null arguments");
+    return -1;
+  }
+  return guarded(h, "kcmm_cow_blocks_on_stream", [&] {
+    auto v = P(h)->cow_blocks(seqs, logical, count, reinterpret_cast<void *>(stream));
+    std::memcpy(out, v.data(), v.size() * sizeof(uint32_t));
+  });
+}
+
+// ---------------------------------------------------------------------------
+// Utilities and accessors (ref src/kcmm/ffi.rs:2488-2560)
+// ---------------------------------------------------------------------------
+
+int kcmm_below_low_watermark(kcmm_pool_t *h, float threshold) {
+  return (h && P(h)->below_low_watermark(threshold)) ? 1 : 0;
+}
+
+int kcmm_synchronize(kcmm_pool_t *h) {
+  if (!h) return -1;
+  Pool *p = P(h);
+  if (guarded(h, "kcmm_synchronize", [&] { p->require_device("kcmm_synchronize"); })) return -1;
+  p->use_device();
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    set_error(h, std::string("kcmm_synchronize: ") + cudaGetErrorString(e));
+    return -1;
+  }
+  return 0;
+}
+
+uint32_t kcmm_get_block_size(kcmm_pool_t *h) { return h ? uint32_t(P(h)->block_size) : 0; }
+uint32_t kcmm_get_max_blocks_per_seq(kcmm_pool_t *h) {
+  return h ? uint32_t(P(h)->max_blocks_per_seq) : 0;
+}
+uint32_t kcmm_get_block_bytes(kcmm_pool_t *h) { return h ? uint32_t(P(h)->block_bytes) : 0; }
+uint32_t kcmm_get_num_layers(kcmm_pool_t *h) { return h ? uint32_t(P(h)->num_layers) : 0; }
+uint32_t kcmm_get_max_batch(kcmm_pool_t *h) { return h ? uint32_t(P(h)->cfg_.max_batch) : 0; }
+uint32_t kcmm_get_max_seq_len(kcmm_pool_t *h) { return h ? uint32_t(P(h)->cfg_.max_seq_len) : 0; }
+
+int32_t kcmm_get_kernel_status(kcmm_pool_t *h) {
+  if (!h) return -1;
+  Pool *p = P(h);
+  if (guarded(h, "kcmm_get_kernel_status", [&] { p->require_device("kcmm_get_kernel_status"); }))
+    return -1;
+  p->use_device();
+  int32_t v = 0;
+  if (cudaMemcpy(&v, p->diag_word(), sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  if (v) cudaMemset(p->diag_word(), 0, sizeof(v));
+  return v;
+}
+
+const char *kcmm_build_info(void) { return "kcmm-b200 0.1.0 sm_100a"; }
+
+}  // extern "C"

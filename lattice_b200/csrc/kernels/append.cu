@@ -1,0 +1,350 @@
+// KV append kernels for sm_100a: host-addressed row copies, the
+// device-slot write (vLLM reshape_and_cache) and the fused
+// RMSNorm + RoPE + append.
+//
+// All three move 16-bit words without converting them (bf16 and f16 share
+// the kernels) and use 16-byte accesses whenever source, destination and row
+// length allow it; a row that does not qualify falls back to 2-byte accesses
+// instead of faulting.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+
+#include "../launch.hpp"
+#include "ptx.cuh"
+
+namespace kcmm {
+namespace dev {
+namespace {
+
+constexpr int kRowsPerLaunch = 480;  // keeps the parameter block under 4 KB
+
+struct RowCopyParams {
+  const uint16_t *k_src;
+  const uint16_t *v_src;
+  uint16_t *va_k;
+  uint16_t *va_v;
+  int rows;
+  int row_elems;
+  int row_base;  // index of the first row of this launch in k_src/v_src
+  int64_t dst[kRowsPerLaunch];
+};
+
+// One CTA per row; restates the per-row cuMemcpyDtoDAsync pair of
+// ref src/kcmm/ffi.rs:1168-1186 as one launch.
+__global__ void copy_rows_kernel(const RowCopyParams p) {
+  const int r = blockIdx.x;
+  const int64_t dst = p.dst[r];
+  if (dst < 0) return;
+  const int64_t src = int64_t(p.row_base + r) * p.row_elems;
+  const uint16_t *ks = p.k_src + src;
+  const uint16_t *vs = p.v_src + src;
+  uint16_t *kd = p.va_k + dst;
+  uint16_t *vd = p.va_v + dst;
+  const bool vec = ((reinterpret_cast<uintptr_t>(ks) | reinterpret_cast<uintptr_t>(vs) |
+                     reinterpret_cast<uintptr_t>(kd) | reinterpret_cast<uintptr_t>(vd)) &
+                    15) == 0 &&
+                   (p.row_elems & 7) == 0;
+  if (vec) {
+    for (int c = threadIdx.x; c < p.row_elems / 8; c += blockDim.x) {
+      reinterpret_cast<uint4 *>(kd)[c] = reinterpret_cast<const uint4 *>(ks)[c];
+      reinterpret_cast<uint4 *>(vd)[c] = reinterpret_cast<const uint4 *>(vs)[c];
+    }
+  } else {
+    for (int c = threadIdx.x; c < p.row_elems; c += blockDim.x) {
+      kd[c] = ks[c];
+      vd[c] = vs[c];
+    }
+  }
+}
+
+// Device-slot write: one CTA per token row.  Status semantics follow
+// ref src/cuda/kernels/kcmm_vllm_kv_write.cu:37-56 (first error wins):
+// 1 = block id outside the offsets table, 2 = block marked free, and, as an
+// addition, 3 = offset outside the layer region (the reference would fault).
+__global__ void slot_write_kernel(const SlotWriteArgs a) {
+  const int row = blockIdx.x;
+  __shared__ int64_t s_dst;
+  if (threadIdx.x == 0) {
+    int64_t dst = -1;
+    const int64_t slot = a.slot_mapping[row];
+    if (slot >= 0) {
+      const int64_t blk = slot / a.block_size;
+      if (blk >= a.offsets_len) {
+        if (a.status) atomicCAS(a.status, 0, 1);
+      } else if (a.valid && a.valid[blk] == 0) {
+        if (a.status) atomicCAS(a.status, 0, 2);
+      } else {
+        const int64_t d = int64_t(a.block_offsets[blk]) + (slot % a.block_size) * a.step_elems;
+        if (uint64_t(d) + uint64_t(a.step_elems) > a.region_elems) {
+          if (a.status) atomicCAS(a.status, 0, 3);
+        } else {
+          dst = d;
+        }
+      }
+    }
+    s_dst = dst;
+  }
+  __syncthreads();
+  const int64_t dst = s_dst;
+  if (dst < 0) return;
+  const uint16_t *ks = static_cast<const uint16_t *>(a.k_src) + int64_t(row) * a.step_elems;
+  const uint16_t *vs = static_cast<const uint16_t *>(a.v_src) + int64_t(row) * a.step_elems;
+  uint16_t *kd = static_cast<uint16_t *>(a.va_k) + dst;
+  uint16_t *vd = static_cast<uint16_t *>(a.va_v) + dst;
+  const bool vec = ((reinterpret_cast<uintptr_t>(ks) | reinterpret_cast<uintptr_t>(vs) |
+                     reinterpret_cast<uintptr_t>(kd) | reinterpret_cast<uintptr_t>(vd)) &
+                    15) == 0 &&
+                   (a.step_elems & 7) == 0;
+  if (vec) {
+    for (int c = threadIdx.x; c < a.step_elems / 8; c += blockDim.x) {
+      reinterpret_cast<uint4 *>(kd)[c] = reinterpret_cast<const uint4 *>(ks)[c];
+      reinterpret_cast<uint4 *>(vd)[c] = reinterpret_cast<const uint4 *>(vs)[c];
+    }
+  } else {
+    for (int c = threadIdx.x; c < a.step_elems; c += blockDim.x) {
+      kd[c] = ks[c];
+      vd[c] = vs[c];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Fused RMSNorm + RoPE + KV append (bf16), one CTA per token.
+// ---------------------------------------------------------------------------
+
+constexpr int kFusedThreads = 256;
+
+__device__ __forceinline__ float bf(uint16_t v) {
+  return __uint_as_float(uint32_t(v) << 16);
+}
+__device__ __forceinline__ uint16_t to_bf(float v) {
+  __nv_bfloat16 h = __float2bfloat16_rn(v);
+  return *reinterpret_cast<uint16_t *>(&h);
+}
+
+struct Vec8 {
+  uint16_t e[8];
+};
+__device__ __forceinline__ Vec8 load8(const uint16_t *p, bool vec) {
+  Vec8 v;
+  if (vec) {
+    *reinterpret_cast<uint4 *>(v.e) = *reinterpret_cast<const uint4 *>(p);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v.e[i] = p[i];
+  }
+  return v;
+}
+__device__ __forceinline__ void store8(uint16_t *p, const Vec8 &v, bool vec) {
+  if (vec) {
+    *reinterpret_cast<uint4 *>(p) = *reinterpret_cast<const uint4 *>(v.e);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) p[i] = v.e[i];
+  }
+}
+
+// Rotate `heads` rows of head_dim elements at src into dst (dst may equal src).
+// cs/sn hold cos/sin per pair frequency (head_dim/2 entries).
+__device__ __forceinline__ void rope_rows(const uint16_t *src, uint16_t *dst, int heads, int D,
+                                          int mode, const float *cs, const float *sn,
+                                          bool vec) {
+  const int half = D / 2;
+  if (mode != 2) {
+    // interleaved pairs (2i, 2i+1) of each head
+    const int chunks = heads * D / 8;
+    if ((D & 7) == 0) {
+      for (int c = threadIdx.x; c < chunks; c += kFusedThreads) {
+        const int e0 = c * 8, d0 = e0 % D;
+        Vec8 v = load8(src + e0, vec);
+        Vec8 o;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int i = d0 / 2 + j;
+          const float x0 = bf(v.e[2 * j]), x1 = bf(v.e[2 * j + 1]);
+          o.e[2 * j] = to_bf(x0 * cs[i] - x1 * sn[i]);
+          o.e[2 * j + 1] = to_bf(x0 * sn[i] + x1 * cs[i]);
+        }
+        store8(dst + e0, o, vec);
+      }
+    } else {
+      for (int pi = threadIdx.x; pi < heads * half; pi += kFusedThreads) {
+        const int h = pi / half, i = pi % half;
+        const int e = h * D + 2 * i;
+        const float x0 = bf(src[e]), x1 = bf(src[e + 1]);
+        dst[e] = to_bf(x0 * cs[i] - x1 * sn[i]);
+        dst[e + 1] = to_bf(x0 * sn[i] + x1 * cs[i]);
+      }
+    }
+  } else {
+    // half-split pairs (i, i + D/2)
+    if ((half & 7) == 0) {
+      const int per_head = half / 8;
+      for (int c = threadIdx.x; c < heads * per_head; c += kFusedThreads) {
+        const int h = c / per_head, i0 = (c % per_head) * 8;
+        const uint16_t *s = src + h * D;
+        uint16_t *d = dst + h * D;
+        Vec8 a = load8(s + i0, vec), b = load8(s + i0 + half, vec);
+        Vec8 oa, ob;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = i0 + j;
+          const float x0 = bf(a.e[j]), x1 = bf(b.e[j]);
+          oa.e[j] = to_bf(x0 * cs[i] - x1 * sn[i]);
+          ob.e[j] = to_bf(x0 * sn[i] + x1 * cs[i]);
+        }
+        store8(d + i0, oa, vec);
+        store8(d + i0 + half, ob, vec);
+      }
+    } else {
+      for (int pi = threadIdx.x; pi < heads * half; pi += kFusedThreads) {
+        const int h = pi / half, i = pi % half;
+        const int e = h * D + i;
+        const float x0 = bf(src[e]), x1 = bf(src[e + half]);
+        dst[e] = to_bf(x0 * cs[i] - x1 * sn[i]);
+        dst[e + half] = to_bf(x0 * sn[i] + x1 * cs[i]);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kFusedThreads) fused_kernel(const FusedAppendArgs a) {
+  extern __shared__ float fsm[];  // cs[D/2], sn[D/2]
+  __shared__ float red[kFusedThreads / 32];
+  __shared__ int64_t s_dst;
+  const int t = blockIdx.x;
+  const int D = a.head_dim, half = D / 2;
+  float *cs = fsm;
+  float *sn = fsm + half;
+
+  // Slot resolution (thread 0) -- same rules as the device-slot write.
+  if (threadIdx.x == 0) {
+    int64_t dst = -1;
+    const int64_t slot = a.slot_mapping[t];
+    const int step = a.kv_heads * D;
+    if (slot >= 0) {
+      const int64_t blk = slot / a.block_size;
+      if (blk >= a.offsets_len) {
+        if (a.status) atomicCAS(a.status, 0, 1);
+      } else if (a.valid && a.valid[blk] == 0) {
+        if (a.status) atomicCAS(a.status, 0, 2);
+      } else {
+        const int64_t d = int64_t(a.block_offsets[blk]) + (slot % a.block_size) * step;
+        if (uint64_t(d) + uint64_t(step) > a.region_elems) {
+          if (a.status) atomicCAS(a.status, 0, 3);
+        } else {
+          dst = d;
+        }
+      }
+    }
+    s_dst = dst;
+  }
+
+  // Rotary table for this token's position (ref src/cuda/kernels/rope.cu:18,
+  // with the base as a parameter): theta_i = 1 / base^e_i.
+  const float pos = float(a.positions[t]);
+  for (int i = threadIdx.x; i < half; i += kFusedThreads) {
+    const float e = a.rope_mode == 0 ? float(2 * (i / 2)) / float(D) : float(2 * i) / float(D);
+    const float theta = 1.0f / powf(a.rope_theta, e);
+    float s, c;
+    sincosf(pos * theta, &s, &c);
+    cs[i] = c;
+    sn[i] = s;
+  }
+
+  // RMSNorm (ref src/cuda/kernels/rms_norm.cu:14-35): out = ((x * inv_rms) * w)
+  const int H = a.hidden;
+  const uint16_t *x = static_cast<const uint16_t *>(a.x) + int64_t(t) * H;
+  const uint16_t *w = static_cast<const uint16_t *>(a.norm_weight);
+  uint16_t *y = static_cast<uint16_t *>(a.normed_out) + int64_t(t) * H;
+  const bool xvec = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+                      reinterpret_cast<uintptr_t>(y)) &
+                     15) == 0;
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < H / 8; c += kFusedThreads) {
+    Vec8 v = load8(x + c * 8, xvec);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float f = bf(v.e[j]);
+      ss += f * f;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float total = 0.f;
+#pragma unroll
+  for (int i = 0; i < kFusedThreads / 32; ++i) total += red[i];
+  const float inv_rms = 1.0f / sqrtf(total / float(H) + a.eps);
+  for (int c = threadIdx.x; c < H / 8; c += kFusedThreads) {
+    Vec8 v = load8(x + c * 8, xvec), wv = load8(w + c * 8, xvec), o;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o.e[j] = to_bf((bf(v.e[j]) * inv_rms) * bf(wv.e[j]));
+    store8(y + c * 8, o, xvec);
+  }
+
+  // RoPE on q (in place) and k (straight into the page), V copied.
+  const int step = a.kv_heads * D;
+  uint16_t *q = static_cast<uint16_t *>(a.q) + int64_t(t) * a.num_q_heads * D;
+  const bool qvec = (reinterpret_cast<uintptr_t>(q) & 15) == 0;
+  rope_rows(q, q, a.num_q_heads, D, a.rope_mode, cs, sn, qvec);
+  const int64_t dst = s_dst;
+  if (dst >= 0) {
+    const uint16_t *k = static_cast<const uint16_t *>(a.k) + int64_t(t) * step;
+    const uint16_t *v = static_cast<const uint16_t *>(a.v) + int64_t(t) * step;
+    uint16_t *kd = static_cast<uint16_t *>(a.va_k) + dst;
+    uint16_t *vd = static_cast<uint16_t *>(a.va_v) + dst;
+    const bool kvec = ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(kd)) & 15) == 0;
+    rope_rows(k, kd, a.kv_heads, D, a.rope_mode, cs, sn, kvec);
+    const bool vvec = ((reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(vd)) & 15) == 0 &&
+                      (step & 7) == 0;
+    if (vvec) {
+      for (int c = threadIdx.x; c < step / 8; c += kFusedThreads) {
+        reinterpret_cast<uint4 *>(vd)[c] = reinterpret_cast<const uint4 *>(v)[c];
+      }
+    } else {
+      for (int c = threadIdx.x; c < step; c += kFusedThreads) vd[c] = v[c];
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t copy_rows(const void *k_src, const void *v_src, void *va_k, void *va_v,
+                      const int64_t *dst_elems_host, int rows, int row_elems,
+                      cudaStream_t stream) {
+  for (int base = 0; base < rows; base += kRowsPerLaunch) {
+    RowCopyParams p;
+    p.k_src = static_cast<const uint16_t *>(k_src);
+    p.v_src = static_cast<const uint16_t *>(v_src);
+    p.va_k = static_cast<uint16_t *>(va_k);
+    p.va_v = static_cast<uint16_t *>(va_v);
+    p.rows = std::min(kRowsPerLaunch, rows - base);
+    p.row_elems = row_elems;
+    p.row_base = base;
+    for (int r = 0; r < p.rows; ++r) p.dst[r] = dst_elems_host[base + r];
+    const int threads = std::min(256, std::max(32, (row_elems / 8 + 31) / 32 * 32));
+    copy_rows_kernel<<<p.rows, threads, 0, stream>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t device_slot_write(const SlotWriteArgs &a, cudaStream_t stream) {
+  const int threads = std::min(256, std::max(32, (a.step_elems / 8 + 31) / 32 * 32));
+  slot_write_kernel<<<a.batch, threads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t fused_norm_rope_append(const FusedAppendArgs &a, cudaStream_t stream) {
+  const size_t smem = size_t(a.head_dim) * sizeof(float);
+  fused_kernel<<<a.num_tokens, kFusedThreads, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace dev
+}  // namespace kcmm

@@ -1,0 +1,666 @@
+// Paged decode attention for sm_100a.
+//
+// Computes, for every sequence b and query head h (ref
+// src/cuda/kernels/kcmm_vllm_paged_attn.cu:40-101 is the scalar original):
+//   out[b,h,:] = sum_t softmax_t(scale * q[b,h,:] . k_t) v_t,  t < seq_lens[b]
+// with k_t / v_t at va_{k,v} + offsets[table[b][t/bs]] + (t%bs)*Hkv*D + kvh*D
+// and kvh = h*Hkv/Hq.  seq_lens[b] <= 0 leaves out[b] untouched.
+//
+// B200 design (the path is HBM-bound: ~4 FLOP per byte):
+//   * work item = (sequence, kv head, <=16 query heads of its group, split of
+//     the context).  All query heads of a GQA group share one CTA, so each KV
+//     page is read from HBM once per group.
+//   * the context is cut into 16-token units.  One lane per K/V row issues a
+//     `cp.async.bulk` (TMA engine, no tensor map needed for the strided
+//     [bs][Hkv][D] page layout) straight into a padded shared-memory tile;
+//     completion is tracked by an mbarrier per stage.  Each warp runs its own
+//     NS-deep ring, so ~W*NS units (W*NS*8.7 KB at D=128) are in flight per CTA.
+//   * QK^T and PV run on the tensor pipe (m16n8k16, fp32 accumulate) from
+//     ldmatrix'd tiles: this keeps the issue slots per byte far below the HBM
+//     rate; softmax is online, in the log2 domain, with warp shuffles.
+//   * warps of a CTA merge in shared memory; splits of a sequence merge in a
+//     second pass through their log-sum-exp.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "../launch.hpp"
+#include "ptx.cuh"
+
+namespace kcmm {
+namespace dev {
+namespace {
+
+constexpr int kUnit = 16;            // tokens per pipeline unit
+constexpr uint32_t kMaxPolls = 1u << 17;  // bounded mbarrier wait (~2.6 s worst case)
+
+struct DecodeParams {
+  const void *q;
+  void *out;
+  const int32_t *tables;
+  const int32_t *seq_lens;
+  const uint64_t *offsets;
+  const void *va_k;
+  const void *va_v;
+  uint64_t region_elems;
+  int batch, hq, hkv, bs, max_bps;
+  float scale_log2;
+  int units_per_split, num_splits, n_head_tiles;
+  float *part_o;
+  float *part_lse;
+  int32_t *diag;
+};
+
+__device__ __forceinline__ int ceil_div_dev(int a, int b) { return (a + b - 1) / b; }
+
+__device__ __forceinline__ void head_range(int kvh, int ht, int hq, int hkv, int *lo, int *hi) {
+  // query heads h with h*hkv/hq == kvh form [ceil(kvh*hq/hkv), ceil((kvh+1)*hq/hkv))
+  int g_lo = int((int64_t(kvh) * hq + hkv - 1) / hkv);
+  int g_hi = int((int64_t(kvh + 1) * hq + hkv - 1) / hkv);
+  *lo = g_lo + ht * 16;
+  *hi = min(g_hi, *lo + 16);
+}
+
+template <typename T, int D, int W, int NS>
+struct Cfg {
+  static constexpr int RS = D + 8;                  // padded row (elements)
+  static constexpr int STAGE = 2 * kUnit * RS;      // K tile + V tile (elements)
+  static constexpr int Q_ELEMS = 16 * RS;
+  static constexpr size_t SMEM =
+      size_t(Q_ELEMS + W * NS * STAGE) * sizeof(T) + size_t(W * NS) * 8 + 16;
+  static constexpr int KS = D / 16;  // k-steps of QK^T, also 16-wide d slabs of PV
+  static constexpr int ND = D / 8;   // 8-wide output tiles
+};
+
+template <typename T, int D, int W, int NS>
+__global__ void __launch_bounds__(W * 32) decode_kernel(const DecodeParams p) {
+  using C = Cfg<T, D, W, NS>;
+  using MMA = ptx::Mma<T>;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  T *qs = reinterpret_cast<T *>(smem_raw);
+  T *stages = qs + C::Q_ELEMS;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(stages + W * NS * C::STAGE);
+  __shared__ int s_fail;
+
+  const int split = blockIdx.x;
+  const int kvh = blockIdx.y / p.n_head_tiles;
+  const int ht = blockIdx.y % p.n_head_tiles;
+  const int b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  int seq_len = p.seq_lens[b];
+  if (seq_len <= 0) return;
+  seq_len = min(seq_len, p.max_bps * p.bs);
+  const int n_units = ceil_div_dev(seq_len, kUnit);
+  const int u_begin = split * p.units_per_split;
+  if (u_begin >= n_units) return;
+  const int u_end = min(u_begin + p.units_per_split, n_units);
+  int lo, hi;
+  head_range(kvh, ht, p.hq, p.hkv, &lo, &hi);
+  const int G = hi - lo;
+  if (G <= 0) return;
+  const int n_splits_b = ceil_div_dev(n_units, p.units_per_split);
+
+  // ---- stage Q (rows >= G are zero) and init barriers --------------------
+  const T *qg = static_cast<const T *>(p.q) + (int64_t(b) * p.hq + lo) * D;
+  for (int i = threadIdx.x; i < 16 * (D / 8); i += W * 32) {
+    int r = i / (D / 8), c = (i % (D / 8)) * 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < G) {
+      const T *src = qg + int64_t(r) * D + c;
+      if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        v = *reinterpret_cast<const uint4 *>(src);
+      } else {
+        T tmp[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) tmp[e] = src[e];
+        v = *reinterpret_cast<uint4 *>(tmp);
+      }
+    }
+    *reinterpret_cast<uint4 *>(qs + r * C::RS + c) = v;
+  }
+  if (threadIdx.x == 0) s_fail = 0;
+  uint64_t *my_bars = bars + warp * NS;
+  if (lane == 0) {
+    for (int s = 0; s < NS; ++s) ptx::mbar_init(ptx::smem_u32(my_bars + s), 1);
+  }
+  ptx::fence_proxy_async_smem();
+  __syncthreads();
+
+  // ---- Q fragments (A operand, rows = heads) ------------------------------
+  uint32_t qa[C::KS][4];
+  {
+    const int mi = lane >> 3, r = lane & 7;
+    const int row = (mi & 1) * 8 + r;
+#pragma unroll
+    for (int ks = 0; ks < C::KS; ++ks) {
+      int col = ks * 16 + (mi >> 1) * 8;
+      ptx::ldsm_x4(ptx::smem_u32(qs + row * C::RS + col), qa[ks][0], qa[ks][1], qa[ks][2],
+                   qa[ks][3]);
+    }
+  }
+
+  // ---- per-warp unit list and page addresses -----------------------------
+  const int n_w = (u_end - u_begin - warp + W - 1) / W;  // units owned by this warp (<= 32)
+  const int64_t row_stride = int64_t(p.hkv) * D;          // elements between tokens
+  int64_t my_elem = 0;
+  int my_ok = 0;
+  if (lane < n_w) {
+    int u = u_begin + warp + lane * W;
+    int tok0 = u * kUnit;
+    int page = tok0 / p.bs;
+    int blk = p.tables[int64_t(b) * p.max_bps + page];
+    if (blk >= 0) {
+      uint64_t off = p.offsets[blk];
+      int64_t e = int64_t(off) + int64_t(tok0 % p.bs) * row_stride + int64_t(kvh) * D;
+      bool aligned = (off & 7) == 0;
+      bool inside = uint64_t(e + (kUnit - 1) * row_stride + D) <= p.region_elems;
+      my_ok = aligned && inside;
+      my_elem = e;
+    }
+    if (!my_ok) atomicOr(p.diag, int32_t(kDiagBadOffset));
+  }
+
+  const T *vak = static_cast<const T *>(p.va_k);
+  const T *vav = static_cast<const T *>(p.va_v);
+  T *wst = stages + warp * NS * C::STAGE;
+
+  auto issue = [&](int k) {
+    const int st = k % NS;
+    const uint32_t bar = ptx::smem_u32(my_bars + st);
+    const int64_t elem = __shfl_sync(0xffffffffu, my_elem, k);
+    const int ok = __shfl_sync(0xffffffffu, my_ok, k);
+    const int u = u_begin + warp + k * W;
+    const int nvalid = min(kUnit, seq_len - u * kUnit);
+    T *ks_tile = wst + st * C::STAGE;
+    T *vs_tile = ks_tile + kUnit * C::RS;
+    const int r = lane & 15;
+    if (r >= nvalid && lane >= 16) {  // masked V rows must hold zeros, not stale data
+      uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4 *>(vs_tile + r * C::RS + c) = z;
+    }
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      ptx::mbar_arrive_expect_tx(bar, ok ? uint32_t(2 * nvalid * D * sizeof(T)) : 0u);
+    }
+    __syncwarp();
+    if (ok && r < nvalid) {
+      const T *src = (lane < 16 ? vak : vav) + elem + int64_t(r) * row_stride;
+      T *dst = (lane < 16 ? ks_tile : vs_tile) + r * C::RS;
+      ptx::bulk_g2s(ptx::smem_u32(dst), src, uint32_t(D * sizeof(T)), bar);
+    }
+  };
+
+  // ---- main loop -----------------------------------------------------------
+  float o[C::ND][4];
+#pragma unroll
+  for (int i = 0; i < C::ND; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const int g = lane >> 2, t = lane & 3;
+  bool failed = false;
+
+  for (int k = 0; k < NS && k < n_w; ++k) issue(k);
+
+  for (int k = 0; k < n_w; ++k) {
+    const int st = k % NS;
+    const uint32_t bar = ptx::smem_u32(my_bars + st);
+    if (!ptx::mbar_wait_bounded(bar, uint32_t((k / NS) & 1), kMaxPolls)) {
+      failed = true;
+      break;
+    }
+    __syncwarp();
+    const int ok = __shfl_sync(0xffffffffu, my_ok, k);
+    const int u = u_begin + warp + k * W;
+    const int nvalid = min(kUnit, seq_len - u * kUnit);
+    const T *ks_tile = wst + st * C::STAGE;
+    const T *vs_tile = ks_tile + kUnit * C::RS;
+    if (ok) {
+      // S = Q K^T : 16 heads x 16 tokens in two n-tiles
+      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      {
+        const int mi = lane >> 3, r = lane & 7;
+        const int tok = (mi >> 1) * 8 + r;
+#pragma unroll
+        for (int ks = 0; ks < C::KS; ++ks) {
+          uint32_t b0, b1, b2, b3;
+          ptx::ldsm_x4(ptx::smem_u32(ks_tile + tok * C::RS + ks * 16 + (mi & 1) * 8), b0, b1, b2,
+                       b3);
+          MMA::run(s[0], qa[ks], b0, b1);
+          MMA::run(s[1], qa[ks], b2, b3);
+        }
+      }
+      // online softmax (log2 domain)
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          int tok = nt * 8 + 2 * t + (j & 1);
+          float v = tok < nvalid ? s[nt][j] * p.scale_log2 : -INFINITY;
+          s[nt][j] = v;
+        }
+        mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
+        mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
+      }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float a0 = ptx::fast_exp2(m0 - mn0), a1 = ptx::fast_exp2(m1 - mn1);
+      m0 = mn0;
+      m1 = mn1;
+      float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        s[nt][0] = ptx::fast_exp2(s[nt][0] - mn0);
+        s[nt][1] = ptx::fast_exp2(s[nt][1] - mn0);
+        s[nt][2] = ptx::fast_exp2(s[nt][2] - mn1);
+        s[nt][3] = ptx::fast_exp2(s[nt][3] - mn1);
+        ps0 += s[nt][0] + s[nt][1];
+        ps1 += s[nt][2] + s[nt][3];
+      }
+      l0 = l0 * a0 + ps0;
+      l1 = l1 * a1 + ps1;
+#pragma unroll
+      for (int i = 0; i < C::ND; ++i) {
+        o[i][0] *= a0;
+        o[i][1] *= a0;
+        o[i][2] *= a1;
+        o[i][3] *= a1;
+      }
+      uint32_t pa[4];
+      pa[0] = MMA::pack(s[0][0], s[0][1]);
+      pa[1] = MMA::pack(s[0][2], s[0][3]);
+      pa[2] = MMA::pack(s[1][0], s[1][1]);
+      pa[3] = MMA::pack(s[1][2], s[1][3]);
+      // O += P V
+      {
+        const int mi = lane >> 3, r = lane & 7;
+        const int tok = (mi & 1) * 8 + r;
+#pragma unroll
+        for (int j = 0; j < C::KS; ++j) {
+          uint32_t b0, b1, b2, b3;
+          ptx::ldsm_x4_t(ptx::smem_u32(vs_tile + tok * C::RS + j * 16 + (mi >> 1) * 8), b0, b1,
+                         b2, b3);
+          MMA::run(o[2 * j], pa, b0, b1);
+          MMA::run(o[2 * j + 1], pa, b2, b3);
+        }
+      }
+    }
+    __syncwarp();
+    if (k + NS < n_w) issue(k + NS);
+  }
+
+  if (failed) {
+    // Let copies still in flight land before the CTA's shared memory is
+    // released (bounded as well), then report.
+    for (int k = 0; k < NS && k < n_w; ++k) {
+      ptx::mbar_wait_bounded(ptx::smem_u32(my_bars + k), 0, 64);
+      ptx::mbar_wait_bounded(ptx::smem_u32(my_bars + k), 1, 64);
+    }
+    if (lane == 0) {
+      atomicOr(p.diag, int32_t(kDiagWaitTimeout));
+      s_fail = 1;
+    }
+  }
+
+  // ---- merge the warps of this CTA ----------------------------------------
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  __syncthreads();
+  if (s_fail) return;
+  float *cO = reinterpret_cast<float *>(stages);  // [W][16][D]
+  float *cm = cO + W * 16 * D;                     // [W][16]
+  float *cl = cm + W * 16;                         // [W][16]
+  {
+    float *wo = cO + warp * 16 * D;
+#pragma unroll
+    for (int i = 0; i < C::ND; ++i) {
+      int d = i * 8 + 2 * t;
+      if (g < G) *reinterpret_cast<float2 *>(wo + g * D + d) = make_float2(o[i][0], o[i][1]);
+      if (g + 8 < G) *reinterpret_cast<float2 *>(wo + (g + 8) * D + d) = make_float2(o[i][2], o[i][3]);
+    }
+    if (t == 0) {
+      cm[warp * 16 + g] = m0;
+      cl[warp * 16 + g] = l0;
+      cm[warp * 16 + g + 8] = m1;
+      cl[warp * 16 + g + 8] = l1;
+    }
+  }
+  __syncthreads();
+  const int64_t head0 = int64_t(b) * p.hq + lo;
+  for (int i = threadIdx.x; i < G * (D / 2); i += W * 32) {
+    const int h = i / (D / 2), d = (i % (D / 2)) * 2;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < W; ++w) M = fmaxf(M, cm[w * 16 + h]);
+    float L = 0.f, x0 = 0.f, x1 = 0.f;
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      float mw = cm[w * 16 + h];
+      if (mw == -INFINITY) continue;  // warp saw no unit
+      float sc = ptx::fast_exp2(mw - M);
+      L += cl[w * 16 + h] * sc;
+      x0 += cO[(w * 16 + h) * D + d] * sc;
+      x1 += cO[(w * 16 + h) * D + d + 1] * sc;
+    }
+    const float inv = 1.f / L;
+    if (n_splits_b == 1) {
+      T *dst = static_cast<T *>(p.out) + (head0 + h) * D + d;
+      dst[0] = ptx::from_f32<T>(x0 * inv);
+      dst[1] = ptx::from_f32<T>(x1 * inv);
+    } else {
+      const int64_t row = (head0 + h) * p.num_splits + split;
+      *reinterpret_cast<float2 *>(p.part_o + row * D + d) = make_float2(x0 * inv, x1 * inv);
+      if (d == 0) p.part_lse[row] = M + log2f(L);
+    }
+  }
+}
+
+// Second pass: combine the splits of each (sequence, head) through their
+// log-sum-exp.  Sequences that fit one split were written by the first pass.
+template <typename T>
+__global__ void merge_kernel(const DecodeParams p, int D) {
+  const int row = blockIdx.x;  // b * hq + h
+  const int b = row / p.hq;
+  int seq_len = p.seq_lens[b];
+  if (seq_len <= 0) return;
+  seq_len = min(seq_len, p.max_bps * p.bs);
+  const int n_units = ceil_div_dev(seq_len, kUnit);
+  const int ns = ceil_div_dev(n_units, p.units_per_split);
+  if (ns <= 1) return;
+  const float *lse = p.part_lse + int64_t(row) * p.num_splits;
+  float M = -INFINITY;
+  for (int s = 0; s < ns; ++s) M = fmaxf(M, lse[s]);
+  float wsum = 0.f;
+  for (int s = 0; s < ns; ++s) wsum += ptx::fast_exp2(lse[s] - M);
+  const float inv = 1.f / wsum;
+  const float *po = p.part_o + int64_t(row) * p.num_splits * D;
+  T *dst = static_cast<T *>(p.out) + int64_t(row) * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < ns; ++s) acc += po[int64_t(s) * D + d] * ptx::fast_exp2(lse[s] - M);
+    dst[d] = ptx::from_f32<T>(acc * inv);
+  }
+}
+
+// Fallback for shapes outside the tensor-core path (head_dim not a multiple
+// of 16, block_size not a multiple of 16): one warp per (sequence, head),
+// plain loads, same math.
+template <typename T>
+__global__ void decode_generic_kernel(const DecodeParams p, int D) {
+  const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp_global >= p.batch * p.hq) return;
+  const int b = warp_global / p.hq, h = warp_global % p.hq;
+  const int kvh = int(int64_t(h) * p.hkv / p.hq);
+  int seq_len = p.seq_lens[b];
+  if (seq_len <= 0) return;
+  seq_len = min(seq_len, p.max_bps * p.bs);
+  const T *q = static_cast<const T *>(p.q) + (int64_t(b) * p.hq + h) * D;
+  float qv[8], acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int d = lane + 32 * i;
+    qv[i] = d < D ? ptx::to_f32(q[d]) : 0.f;
+    acc[i] = 0.f;
+  }
+  const T *vak = static_cast<const T *>(p.va_k);
+  const T *vav = static_cast<const T *>(p.va_v);
+  float m = -INFINITY, l = 0.f;
+  for (int tok = 0; tok < seq_len; ++tok) {
+    int blk = p.tables[int64_t(b) * p.max_bps + tok / p.bs];
+    int64_t e = blk < 0 ? -1
+                        : int64_t(p.offsets[blk]) + int64_t(tok % p.bs) * p.hkv * D +
+                              int64_t(kvh) * D;
+    if (e < 0 || uint64_t(e + D) > p.region_elems) {
+      if (lane == 0) atomicOr(p.diag, int32_t(kDiagBadOffset));
+      continue;
+    }
+    float part = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      int d = lane + 32 * i;
+      if (d < D) part += qv[i] * ptx::to_f32(vak[e + d]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    float s = part * p.scale_log2;
+    float mn = fmaxf(m, s);
+    float a = ptx::fast_exp2(m - mn), pr = ptx::fast_exp2(s - mn);
+    m = mn;
+    l = l * a + pr;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      int d = lane + 32 * i;
+      if (d < D) acc[i] = acc[i] * a + pr * ptx::to_f32(vav[e + d]);
+    }
+  }
+  if (l == 0.f) return;
+  T *out = static_cast<T *>(p.out) + (int64_t(b) * p.hq + h) * D;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int d = lane + 32 * i;
+    if (d < D) out[d] = ptx::from_f32<T>(acc[i] / l);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+constexpr int kWarps = 4;
+constexpr int kStages = 3;
+
+using KernelFn = void (*)(const DecodeParams);
+
+template <typename T, int D>
+KernelFn fast_kernel() {
+  return decode_kernel<T, D, kWarps, kStages>;
+}
+
+template <typename T>
+bool pick_fast(int D, KernelFn *fn, size_t *smem) {
+  switch (D) {
+#define KCMM_CASE(DD)                                 \
+  case DD:                                            \
+    *fn = fast_kernel<T, DD>();                       \
+    *smem = Cfg<T, DD, kWarps, kStages>::SMEM;        \
+    return true;
+    KCMM_CASE(32)
+    KCMM_CASE(64)
+    KCMM_CASE(80)
+    KCMM_CASE(96)
+    KCMM_CASE(112)
+    KCMM_CASE(128)
+    KCMM_CASE(160)
+    KCMM_CASE(192)
+    KCMM_CASE(256)
+#undef KCMM_CASE
+    default:
+      return false;
+  }
+}
+
+struct Occupancy {
+  std::mutex mu;
+  int sm_count = 0;
+};
+Occupancy &occ() {
+  static Occupancy o;
+  return o;
+}
+
+int sm_count() {
+  Occupancy &o = occ();
+  std::lock_guard<std::mutex> g(o.mu);
+  if (o.sm_count == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&o.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (o.sm_count <= 0) o.sm_count = 148;
+  }
+  return o.sm_count;
+}
+
+struct Plan {
+  bool fast = false;
+  KernelFn fn = nullptr;
+  size_t smem = 0;
+  int n_head_tiles = 1, units_per_split = 1, num_splits = 1;
+  size_t scratch_bytes = 0;
+};
+
+Plan make_plan(const DecodeArgs &a) {
+  Plan pl;
+  const int D = a.head_dim;
+  bool shape_ok = D % 16 == 0 && a.block_size % kUnit == 0;
+  if (shape_ok) {
+    pl.fast = a.dtype == Dtype::BF16 ? pick_fast<__nv_bfloat16>(D, &pl.fn, &pl.smem)
+                                     : pick_fast<__half>(D, &pl.fn, &pl.smem);
+  }
+  if (!pl.fast) return pl;
+  const int g_max = (a.num_q_heads + a.kv_heads - 1) / a.kv_heads;
+  pl.n_head_tiles = (g_max + 15) / 16;
+  const int max_units =
+      int((int64_t(a.max_blocks_per_seq) * a.block_size + kUnit - 1) / kUnit);
+  const int64_t items = int64_t(a.batch) * a.kv_heads * pl.n_head_tiles;
+  // Aim at ~8 waves of 2 resident CTAs per SM over the worst-case context;
+  // at least 16 units per split so each warp's ring fills, at most 32 units
+  // per warp.
+  const int64_t target = int64_t(sm_count()) * 2 * 8;
+  int64_t want_splits = std::max<int64_t>(1, (target + items - 1) / items);
+  int ups = int((max_units + want_splits - 1) / want_splits);
+  ups = std::max(ups, 16);
+  ups = std::min(ups, 32 * kWarps);
+  if (a.force_splits > 0) ups = std::max(1, std::min((max_units + a.force_splits - 1) / a.force_splits, 32 * kWarps));
+  pl.units_per_split = ups;
+  pl.num_splits = (max_units + ups - 1) / ups;
+  if (pl.num_splits > 1) {
+    size_t rows = size_t(a.batch) * a.num_q_heads * pl.num_splits;
+    pl.scratch_bytes = rows * size_t(D) * 4 + rows * 4;
+  }
+  return pl;
+}
+
+cudaMemPool_t scratch_pool(int dev) {
+  static std::mutex mu;
+  static cudaMemPool_t pools[64] = {};
+  std::lock_guard<std::mutex> g(mu);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!pools[dev]) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    if (cudaMemPoolCreate(&pools[dev], &props) != cudaSuccess) return nullptr;
+    uint64_t keep = ~0ull;
+    cudaMemPoolSetAttribute(pools[dev], cudaMemPoolAttrReleaseThreshold, &keep);
+  }
+  return pools[dev];
+}
+
+}  // namespace
+
+size_t decode_scratch_bytes(const DecodeArgs &a) { return make_plan(a).scratch_bytes; }
+
+cudaError_t decode_attention(const DecodeArgs &a, cudaStream_t stream) {
+  DecodeParams p = {};
+  p.q = a.q;
+  p.out = a.out;
+  p.tables = a.block_tables;
+  p.seq_lens = a.seq_lens;
+  p.offsets = a.block_offsets;
+  p.va_k = a.va_k;
+  p.va_v = a.va_v;
+  p.region_elems = a.region_elems;
+  p.batch = a.batch;
+  p.hq = a.num_q_heads;
+  p.hkv = a.kv_heads;
+  p.bs = a.block_size;
+  p.max_bps = a.max_blocks_per_seq;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.diag = a.diag;
+
+  Plan pl = make_plan(a);
+  if (!pl.fast) {
+    const int threads = 256;
+    const int64_t warps = int64_t(a.batch) * a.num_q_heads;
+    const int blocks = int((warps * 32 + threads - 1) / threads);
+    if (a.dtype == Dtype::BF16) {
+      decode_generic_kernel<__nv_bfloat16><<<blocks, threads, 0, stream>>>(p, a.head_dim);
+    } else {
+      decode_generic_kernel<__half><<<blocks, threads, 0, stream>>>(p, a.head_dim);
+    }
+    return cudaGetLastError();
+  }
+  p.units_per_split = pl.units_per_split;
+  p.num_splits = pl.num_splits;
+  p.n_head_tiles = pl.n_head_tiles;
+
+  void *scratch = nullptr;
+  bool owned = false;
+  if (pl.scratch_bytes) {
+    if (a.scratch) {
+      if (a.scratch_bytes < pl.scratch_bytes) return cudaErrorInvalidValue;
+      scratch = a.scratch;
+    } else {
+      int dev = 0;
+      cudaGetDevice(&dev);
+      cudaMemPool_t mp = scratch_pool(dev);
+      if (!mp) return cudaErrorMemoryAllocation;
+      cudaError_t e = cudaMallocFromPoolAsync(&scratch, pl.scratch_bytes, mp, stream);
+      if (e != cudaSuccess) return e;
+      owned = true;
+    }
+    size_t rows = size_t(a.batch) * a.num_q_heads * pl.num_splits;
+    p.part_o = static_cast<float *>(scratch);
+    p.part_lse = p.part_o + rows * size_t(a.head_dim);
+  }
+
+  cudaError_t e = cudaFuncSetAttribute(pl.fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(pl.smem));
+  if (e != cudaSuccess) return e;
+  dim3 grid(pl.num_splits, a.kv_heads * pl.n_head_tiles, a.batch);
+  pl.fn<<<grid, kWarps * 32, pl.smem, stream>>>(p);
+  e = cudaGetLastError();
+  if (e == cudaSuccess && pl.num_splits > 1) {
+    const int rows = a.batch * a.num_q_heads;
+    if (a.dtype == Dtype::BF16) {
+      merge_kernel<__nv_bfloat16><<<rows, 128, 0, stream>>>(p, a.head_dim);
+    } else {
+      merge_kernel<__half><<<rows, 128, 0, stream>>>(p, a.head_dim);
+    }
+    e = cudaGetLastError();
+  }
+  if (owned) {
+    cudaError_t f = cudaFreeAsync(scratch, stream);
+    if (e == cudaSuccess) e = f;
+  }
+  return e;
+}
+
+cudaError_t decode_preload() {
+  cudaFuncAttributes attr;
+  for (int D : {64, 128}) {
+    KernelFn fn;
+    size_t smem;
+    pick_fast<__nv_bfloat16>(D, &fn, &smem);
+    cudaError_t e = cudaFuncGetAttributes(&attr, fn);
+    if (e != cudaSuccess) return e;
+    pick_fast<__half>(D, &fn, &smem);
+    e = cudaFuncGetAttributes(&attr, fn);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace dev
+}  // namespace kcmm

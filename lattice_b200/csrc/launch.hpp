@@ -1,0 +1,113 @@
+// Host-side launchers of the sm_100a kernels (defined in kernels/*.cu).
+// Every launcher validates nothing itself: the ABI layer (ffi.cpp) checks
+// arguments and reports errors; a launcher returns the cudaError_t of the
+// launch (0 on success).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace kcmm {
+namespace dev {
+
+enum class Dtype : int { F16 = 0, BF16 = 1 };
+
+// Sticky bits written into the pool's device diagnostic word.
+enum DiagBits : int32_t {
+  kDiagWaitTimeout = 1 << 0,   // an mbarrier wait gave up (no data arrived)
+  kDiagBadOffset = 1 << 1,     // a block offset was misaligned or past the region
+  kDiagBadLaunch = 1 << 2,
+};
+
+struct DecodeArgs {
+  Dtype dtype;
+  const void *q;
+  void *out;
+  const int32_t *block_tables;
+  const int32_t *seq_lens;
+  const uint64_t *block_offsets;  // 2-byte units
+  const void *va_k;
+  const void *va_v;
+  uint64_t region_elems;  // size of one layer region in 2-byte units
+  int batch, num_q_heads, kv_heads, head_dim, block_size, max_blocks_per_seq;
+  float scale;
+  int32_t *diag;
+  // Optional caller-provided split-K scratch; when null the launcher takes it
+  // from a stream-ordered memory pool (cudaMallocAsync) and frees it after use.
+  float *scratch;
+  size_t scratch_bytes;
+  int force_splits;  // >0 overrides the split heuristic (tests)
+};
+
+// Bytes of split-K scratch decode_attention needs for these arguments
+// (0 when no split is needed).
+size_t decode_scratch_bytes(const DecodeArgs &a);
+cudaError_t decode_attention(const DecodeArgs &a, cudaStream_t stream);
+// Force module load of every decode kernel (precompile entry points).
+cudaError_t decode_preload();
+
+// Copy `rows` K and V rows of `row_elems` 16-bit elements from k_src/v_src
+// (row r at r*row_elems) to va_k/va_v + dst_elems[r]; dst_elems[r] < 0 skips.
+cudaError_t copy_rows(const void *k_src, const void *v_src, void *va_k, void *va_v,
+                      const int64_t *dst_elems_host, int rows, int row_elems,
+                      cudaStream_t stream);
+
+struct SlotWriteArgs {
+  void *va_k;
+  void *va_v;
+  const int64_t *slot_mapping;
+  const uint64_t *block_offsets;
+  const uint8_t *valid;  // may be null
+  int offsets_len;
+  int batch;
+  int step_elems;
+  int block_size;
+  const void *k_src;
+  const void *v_src;
+  int32_t *status;  // may be null
+  uint64_t region_elems;
+};
+cudaError_t device_slot_write(const SlotWriteArgs &a, cudaStream_t stream);
+
+struct FusedAppendArgs {
+  const void *x;
+  const void *norm_weight;
+  void *normed_out;
+  int hidden;
+  float eps;
+  void *q;
+  int num_q_heads;
+  const void *k;
+  const void *v;
+  const int32_t *positions;
+  float rope_theta;
+  int rope_mode;
+  const int64_t *slot_mapping;
+  const uint64_t *block_offsets;
+  const uint8_t *valid;
+  int offsets_len;
+  int num_tokens;
+  int kv_heads;
+  int head_dim;
+  int block_size;
+  void *va_k;
+  void *va_v;
+  uint64_t region_elems;
+  int32_t *status;
+};
+cudaError_t fused_norm_rope_append(const FusedAppendArgs &a, cudaStream_t stream);
+
+// Copy whole blocks: for each pair i and each of the 2*num_layers regions,
+// block_bytes from region + src_off[i] to region + dst_off[i].
+cudaError_t copy_blocks(const uint64_t *d_layer_bases, int num_layers, const uint64_t *src_off,
+                        const uint64_t *dst_off, int count, uint64_t block_bytes,
+                        cudaStream_t stream);
+
+// Swap tier: gather blocks into host-mapped memory (dir=0) or scatter back
+// (dir=1).  Host slot i holds [K0][V0]...[K(L-1)][V(L-1)].
+cudaError_t swap_blocks(const uint64_t *d_layer_bases, int num_layers, const uint64_t *va_off,
+                        const uint64_t *host_off, int count, uint64_t block_bytes,
+                        uint8_t *host_base_dev, int dir, cudaStream_t stream);
+
+}  // namespace dev
+}  // namespace kcmm

@@ -1,0 +1,278 @@
+"""Seeded synthetic workloads of the benchmark configurations.
+
+Builds a KCMM pool on a GPU, draws block tables from it and fills the K/V
+pages, the way the engine would after prefill; shared by bench.py,
+__graft_entry__.smoke() and the GPU tests.  torch provides device buffers and
+streams only; every KV-path operation goes through the C ABI (`kcmm.py`).
+
+The configurations follow BASELINE.json:
+  decode_llama3_8b   Hq 32 / Hkv 8 / D 128, bf16, block 16, batch 64, context
+                     lengths uniform in [512, 4096], tables drawn without
+                     replacement from a 40,000-block pool, scale 1/sqrt(128)
+  fused_append       256 decode tokens, hidden 4096, eps 1e-5, w ~ U(0.5, 1.5),
+                     rope theta 500000 on D 128, positions uniform in [0, 8191],
+                     8 kv heads, seeded distinct slots
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import kcmm
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _cudart():
+    from cuda.bindings import runtime as rt
+
+    return rt
+
+
+def memcpy(dst: int, src: int, nbytes: int, kind: str) -> None:
+    """cudaMemcpy between raw addresses (kind: 'h2d', 'd2h', 'd2d')."""
+    rt = _cudart()
+    k = {"h2d": rt.cudaMemcpyKind.cudaMemcpyHostToDevice,
+         "d2h": rt.cudaMemcpyKind.cudaMemcpyDeviceToHost,
+         "d2d": rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice}[kind]
+    (err,) = rt.cudaMemcpy(dst, src, nbytes, k)
+    if int(err) != 0:
+        raise RuntimeError(f"cudaMemcpy {kind} failed: {err}")
+
+
+def read_device(addr: int, nbytes: int) -> np.ndarray:
+    out = np.empty(nbytes, np.uint8)
+    memcpy(out.ctypes.data, addr, nbytes, "d2h")
+    return out
+
+
+def write_device(addr: int, data: np.ndarray) -> None:
+    data = np.ascontiguousarray(data)
+    memcpy(addr, data.ctypes.data, data.nbytes, "h2d")
+
+
+_LIB = None
+
+
+def library() -> kcmm.KcmmLibrary:
+    global _LIB
+    if _LIB is None:
+        _LIB = kcmm.KcmmLibrary()
+    return _LIB
+
+
+@dataclass
+class DecodeWorkload:
+    """A pool with `batch` sequences of paged KV and one query token each."""
+
+    batch: int = 64
+    num_q_heads: int = 32
+    kv_heads: int = 8
+    head_dim: int = 128
+    block_size: int = 16
+    pool_blocks: int = 40000
+    min_len: int = 512
+    max_len: int = 4096
+    dtype: str = "bf16"
+    seed: int = 0
+    num_layers: int = 1
+    device: int = 0
+    seq_lens_override: list | None = None
+    fill: str = "device"  # "device": torch.randn on the GPU; "host": numpy (readable by the oracle)
+    tiering: bool = False
+    pool: kcmm.KcmmPool | None = field(default=None, repr=False)
+
+    def build(self) -> "DecodeWorkload":
+        torch = _torch()
+        torch.cuda.set_device(self.device)
+        rng = np.random.default_rng(self.seed)
+        bs = self.block_size
+        self.max_blocks_per_seq = -(-self.max_len // bs)
+        # pool capacity: max_batch * ceil(max_seq_len/bs) >= pool_blocks
+        max_batch = max(self.batch, -(-self.pool_blocks // self.max_blocks_per_seq))
+        cfg = kcmm.make_config(num_layers=self.num_layers, kv_heads=self.kv_heads,
+                               head_dim=self.head_dim, max_batch=max_batch,
+                               max_seq_len=self.max_blocks_per_seq * bs, block_size=bs,
+                               tiering=self.tiering, device=self.device,
+                               max_blocks=self.pool_blocks if self.tiering else 0)
+        self.pool = library().create_pool(cfg)
+        self.block_ids = np.array(self.pool.alloc_blocks(self.pool_blocks), np.int64)
+        if self.seq_lens_override is not None:
+            self.seq_lens = np.array(self.seq_lens_override, np.int32)
+        else:
+            self.seq_lens = rng.integers(self.min_len, self.max_len + 1, self.batch).astype(np.int32)
+        need = [max(1, -(-int(L) // bs)) for L in self.seq_lens]
+        picks = rng.choice(len(self.block_ids), size=sum(need), replace=False)
+        self.tables = np.zeros((self.batch, self.max_blocks_per_seq), np.int32)
+        pos = 0
+        self.seq_indices = []
+        for b, n in enumerate(need):
+            ids = self.block_ids[picks[pos:pos + n]]
+            pos += n
+            self.tables[b, :n] = ids
+            self.seq_indices.append(self.pool.register_sequence([int(x) for x in ids]))
+            self.pool.update_seq_len(self.seq_indices[-1], int(self.seq_lens[b]))
+        self.offsets = np.array(self.pool.all_block_offsets_f16(), np.uint64)
+        self.block_bytes = self.pool.stats()["block_bytes"]
+        self.region_used = int(self.offsets.max()) * 2 + self.block_bytes
+        tdt = torch.bfloat16 if self.dtype == "bf16" else torch.float16
+        self.tdtype = tdt
+        dev = f"cuda:{self.device}"
+        gen = torch.Generator(device=dev).manual_seed(self.seed)
+        self.host_regions = {}
+        for layer in range(self.num_layers):
+            for kind in ("k", "v"):
+                base = self.pool.va_k(layer) if kind == "k" else self.pool.va_v(layer)
+                n = self.region_used // 2
+                if self.fill == "host":
+                    vals = rng.standard_normal(n).astype(np.float32)
+                    t = torch.from_numpy(vals).to(dev).to(tdt)
+                    self.host_regions[(layer, kind)] = t.view(torch.int16).cpu().numpy().view(np.uint16)
+                else:
+                    t = torch.randn(n, device=dev, dtype=torch.float32, generator=gen).to(tdt)
+                memcpy(base, t.data_ptr(), self.region_used, "d2d")
+                del t
+        self.q = torch.randn(self.batch, self.num_q_heads, self.head_dim, device=dev,
+                             generator=gen, dtype=torch.float32).to(tdt)
+        self.out = torch.zeros_like(self.q)
+        self.d_tables = torch.from_numpy(self.tables).to(dev)
+        self.d_seq_lens = torch.from_numpy(self.seq_lens).to(dev)
+        self.d_offsets = torch.from_numpy(self.offsets.view(np.int64)).to(dev)
+        self.scale = 1.0 / math.sqrt(self.head_dim)
+        torch.cuda.synchronize()
+        return self
+
+    def decode(self, layer: int = 0, stream_ptr: int | None = None, out=None) -> None:
+        torch = _torch()
+        if stream_ptr is None:
+            stream_ptr = torch.cuda.current_stream().cuda_stream
+        out = self.out if out is None else out
+        self.pool.paged_attn_decode(
+            layer, query_ptr=self.q.data_ptr(), out_ptr=out.data_ptr(),
+            block_tables_ptr=self.d_tables.data_ptr(), seq_lens_ptr=self.d_seq_lens.data_ptr(),
+            block_offsets_f16_ptr=self.d_offsets.data_ptr(), batch=self.batch,
+            num_q_heads=self.num_q_heads, kv_heads=self.kv_heads, head_dim=self.head_dim,
+            block_size=self.block_size, max_blocks_per_seq=self.max_blocks_per_seq,
+            scale=self.scale, dtype=self.dtype, stream_ptr=stream_ptr)
+
+    def kv_bytes(self) -> int:
+        """Algorithmic bytes of one decode pass (K and V rows, tables, q, out)."""
+        e = 2
+        L = self.seq_lens.astype(np.int64)
+        kv = int((L * self.kv_heads * self.head_dim * e * 2).sum())
+        tables = int(4 * np.ceil(L / self.block_size).sum())
+        qo = self.batch * self.num_q_heads * self.head_dim * e * 2
+        return kv + tables + qo + 4 * self.batch
+
+    def host_region(self, layer: int, kind: str) -> np.ndarray:
+        """Current bytes of a region (16-bit words), read back from the device."""
+        base = self.pool.va_k(layer) if kind == "k" else self.pool.va_v(layer)
+        return read_device(base, self.region_used).view(np.uint16)
+
+    def close(self) -> None:
+        if self.pool is not None:
+            self.pool.destroy()
+            self.pool = None
+
+
+@dataclass
+class FusedAppendWorkload:
+    """Inputs of the fused RMSNorm + RoPE + KV append for `tokens` decode tokens."""
+
+    tokens: int = 256
+    hidden: int = 4096
+    num_q_heads: int = 32
+    kv_heads: int = 8
+    head_dim: int = 128
+    block_size: int = 16
+    eps: float = 1e-5
+    theta: float = 500000.0
+    rope_mode: int = kcmm.RopeMode.REFERENCE
+    max_pos: int = 8191
+    seed: int = 0
+    pool: kcmm.KcmmPool | None = None  # reuse a decode pool (same kv shape)
+    layer: int = 0
+    device: int = 0
+
+    def build(self) -> "FusedAppendWorkload":
+        torch = _torch()
+        dev = f"cuda:{self.device}"
+        rng = np.random.default_rng(self.seed + 1)
+        gen = torch.Generator(device=dev).manual_seed(self.seed + 1)
+        self.own_pool = self.pool is None
+        if self.own_pool:
+            cfg = kcmm.make_config(num_layers=1, kv_heads=self.kv_heads, head_dim=self.head_dim,
+                                   max_batch=self.tokens, max_seq_len=self.block_size * 4,
+                                   block_size=self.block_size, device=self.device)
+            self.pool = library().create_pool(cfg)
+            self.pool.alloc_blocks(self.tokens)
+        nblk = self.pool.total_blocks()
+        slots = rng.choice(nblk * self.block_size, size=self.tokens, replace=False)
+        self.slots = slots.astype(np.int64)
+        self.positions = rng.integers(0, self.max_pos + 1, self.tokens).astype(np.int32)
+        bf = torch.bfloat16
+        T, H, D = self.tokens, self.hidden, self.head_dim
+        self.x = torch.randn(T, H, device=dev, generator=gen).to(bf)
+        self.w = (torch.rand(H, device=dev, generator=gen) + 0.5).to(bf)
+        self.q = torch.randn(T, self.num_q_heads, D, device=dev, generator=gen).to(bf)
+        self.k = torch.randn(T, self.kv_heads, D, device=dev, generator=gen).to(bf)
+        self.v = torch.randn(T, self.kv_heads, D, device=dev, generator=gen).to(bf)
+        self.normed = torch.empty_like(self.x)
+        self.d_pos = torch.from_numpy(self.positions).to(dev)
+        self.d_slots = torch.from_numpy(self.slots).to(dev)
+        self.offsets = np.array(self.pool.all_block_offsets_f16(), np.uint64)
+        self.valid = np.array(self.pool.all_block_valid_flags(), np.uint8)
+        self.d_offsets = torch.from_numpy(self.offsets.view(np.int64)).to(dev)
+        self.d_valid = torch.from_numpy(self.valid).to(dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize()
+        return self
+
+    def run(self, stream_ptr: int | None = None, q=None) -> None:
+        torch = _torch()
+        if stream_ptr is None:
+            stream_ptr = torch.cuda.current_stream().cuda_stream
+        q = self.q if q is None else q
+        self.pool.fused_norm_rope_append_bf16(
+            self.layer, x_ptr=self.x.data_ptr(), weight_ptr=self.w.data_ptr(),
+            normed_ptr=self.normed.data_ptr(), hidden=self.hidden, eps=self.eps,
+            q_ptr=q.data_ptr(), num_q_heads=self.num_q_heads, k_ptr=self.k.data_ptr(),
+            v_ptr=self.v.data_ptr(), positions_ptr=self.d_pos.data_ptr(),
+            rope_theta=self.theta, rope_mode=self.rope_mode,
+            slot_mapping_ptr=self.d_slots.data_ptr(),
+            block_offsets_f16_ptr=self.d_offsets.data_ptr(),
+            valid_blocks_ptr=self.d_valid.data_ptr(), block_offsets_f16_len=len(self.offsets),
+            num_tokens=self.tokens, status_ptr=self.status.data_ptr(), stream_ptr=stream_ptr)
+
+    def bytes_per_launch(self) -> int:
+        """Algorithmic bytes: x, q read+write, k, v read, pos, slot, normed/K/V write, w once."""
+        T, H = self.tokens, self.hidden
+        qd = self.num_q_heads * self.head_dim
+        kd = self.kv_heads * self.head_dim
+        per_token = 2 * (H + qd + kd + kd) + 4 + 8 + 2 * (H + qd + kd + kd)
+        return T * per_token + 2 * H
+
+    def close(self) -> None:
+        if self.own_pool and self.pool is not None:
+            self.pool.destroy()
+        self.pool = None
+
+
+def tensor_bits(t) -> np.ndarray:
+    """uint16 bit pattern of a bf16/f16 torch tensor (host copy)."""
+    torch = _torch()
+    return t.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def cuda_stream_ptr() -> int:
+    return _torch().cuda.current_stream().cuda_stream
+
+
+_ = ctypes  # keep ctypes imported for users building raw pointers

@@ -1,0 +1,158 @@
+"""The drop-in boundary: libkcmm.so loads, exports every symbol include/kcmm.h
+declares, and its structs have the reference layout (ref src/kcmm/ffi.rs:2575-2603)."""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "kcmm.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(kcmm_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_reference_surface():
+    names = set(declared_functions())
+    # every reference export (include/kcmm.h + the ffi.rs-only extras) is present
+    reference = {
+        "kcmm_pool_create", "kcmm_pool_destroy", "kcmm_get_last_error", "kcmm_clear_error",
+        "kcmm_alloc_blocks", "kcmm_free_blocks", "kcmm_register_sequence",
+        "kcmm_unregister_sequence", "kcmm_touch", "kcmm_cool", "kcmm_update_seq_len",
+        "kcmm_get_seq_len", "kcmm_append_block_to_sequence", "kcmm_get_block_table",
+        "kcmm_get_block_va_offset", "kcmm_get_all_block_offsets_f16", "kcmm_get_block_location",
+        "kcmm_get_block_table_va_offsets", "kcmm_get_va_k", "kcmm_get_va_v",
+        "kcmm_append_kv_step", "kcmm_append_kv_slots", "kcmm_append_kv_slots_on_stream",
+        "kcmm_paged_attn_decode_f16", "kcmm_paged_attn_decode_f16_on_stream",
+        "kcmm_paged_attn_decode_f16_on_current_context_stream",
+        "kcmm_precompile_paged_attn_decode_f16", "kcmm_evict_blocks",
+        "kcmm_restore_evicted_block", "kcmm_restore_evicted_blocks", "kcmm_is_gpu_resident",
+        "kcmm_get_metrics", "kcmm_get_pool_stats", "kcmm_blocks_in_use", "kcmm_total_blocks",
+        "kcmm_free_physical_blocks", "kcmm_has_free_blocks", "kcmm_active_sequences",
+        "kcmm_set_eviction_policy", "kcmm_get_eviction_policy", "kcmm_is_tiering_enabled",
+        "kcmm_hint", "kcmm_protect", "kcmm_share_prefix", "kcmm_below_low_watermark",
+        "kcmm_synchronize", "kcmm_get_block_size", "kcmm_get_max_blocks_per_seq",
+        "kcmm_get_block_bytes", "kcmm_get_num_layers", "kcmm_get_max_batch",
+        "kcmm_get_max_seq_len",
+        # ffi.rs-only exports
+        "kcmm_precompile_vllm_kv_write_f16", "kcmm_get_all_block_valid",
+        "kcmm_append_kv_device_slots_on_stream", "kcmm_block_state_epoch",
+    }
+    assert reference <= names, reference - names
+
+
+def test_library_exports_every_declared_symbol(kcmm_lib):
+    lib = ctypes.CDLL(str(kcmm_lib.path))
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_alias_library_name(kcmm_lib):
+    alias = kcmm_lib.path.parent / "libbaseline_llm_os.so"
+    assert alias.exists()
+    lib = ctypes.CDLL(str(alias))
+    assert lib.kcmm_pool_create
+
+
+def test_python_binding_covers_header(kcmm_lib):
+    from lattice_b200 import kcmm
+
+    assert set(declared_functions()) == set(kcmm.SIGNATURES)
+
+
+def test_config_layout_python(golden):
+    from lattice_b200 import kcmm
+
+    lay = golden["kats"]["config_layout"]
+    kcmm.assert_layout()
+    assert ctypes.sizeof(kcmm.KcmmConfig) == lay["size"]
+    for f, off in lay["offsets"].items():
+        assert getattr(kcmm.KcmmConfig, f).offset == off
+
+
+def test_config_layout_c(tmp_path, golden):
+    """The C header itself compiles with the reference's static layout checks."""
+    lay = golden["kats"]["config_layout"]
+    checks = "\n".join(
+        f'_Static_assert(offsetof(kcmm_config_t, {f}) == {o}, "{f}");'
+        for f, o in lay["offsets"].items())
+    src = tmp_path / "layout.c"
+    src.write_text(
+        '#include <stddef.h>\n#include "kcmm.h"\n'
+        f'_Static_assert(sizeof(kcmm_config_t) == {lay["size"]}, "size");\n{checks}\n'
+        "_Static_assert(sizeof(kcmm_metrics_t) == 72, \"metrics\");\n"
+        "_Static_assert(sizeof(kcmm_pool_stats_t) == 56, \"stats\");\n"
+        "int main(void) { return 0; }\n")
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", f"-I{ROOT / 'include'}", str(src),
+                    "-o", str(tmp_path / "layout")], check=True)
+
+
+def test_c_program_links_against_library(tmp_path, kcmm_lib, monkeypatch):
+    """A C caller (like ref examples/kcmm_c_integration.c) links and drives the pool."""
+    src = tmp_path / "caller.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include <string.h>
+#include "kcmm.h"
+int main(void) {
+  kcmm_config_t cfg; memset(&cfg, 0, sizeof cfg);
+  cfg.num_layers = 2; cfg.kv_heads = 4; cfg.head_dim = 64; cfg.max_batch = 2;
+  cfg.max_seq_len = 64;
+  kcmm_pool_t *p = kcmm_pool_create(&cfg);
+  if (!p) return 10;
+  uint32_t b[3];
+  if (kcmm_alloc_blocks(p, 3, b) != 0) return 11;
+  uint32_t seq;
+  if (kcmm_register_sequence(p, b, 3, &seq) != 0) return 12;
+  kcmm_pool_stats_t st;
+  if (kcmm_get_pool_stats(p, &st) != 0 || st.blocks_in_use != 3) return 13;
+  if (kcmm_get_block_size(p) != 16 || kcmm_get_block_bytes(p) != 8192) return 14;
+  if (kcmm_get_va_k(p, 2) != 0) return 15;   /* out of range -> 0 */
+  char msg[256];
+  if (kcmm_get_last_error(p, msg, sizeof msg) != 0) return 16;
+  if (kcmm_append_block_to_sequence(p, 99, 0) != -1) return 17;
+  if (kcmm_get_last_error(p, msg, sizeof msg) == 0) return 18;
+  kcmm_clear_error(p);
+  if (kcmm_get_last_error(p, msg, sizeof msg) != 0) return 19;
+  if (kcmm_unregister_sequence(p, seq) != 0 || kcmm_blocks_in_use(p) != 0) return 20;
+  kcmm_pool_destroy(p);
+  kcmm_pool_destroy(NULL);
+  printf("ok\n");
+  return 0;
+}
+''')
+    exe = tmp_path / "caller"
+    subprocess.run(["gcc", "-std=c11", f"-I{ROOT / 'include'}", str(src), "-o", str(exe),
+                    f"-L{kcmm_lib.path.parent}", "-lkcmm", f"-Wl,-rpath,{kcmm_lib.path.parent}"],
+                   check=True)
+    monkeypatch.setenv("KCMM_VMM_BACKEND", "host")
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0, (out.returncode, out.stderr)
+    assert out.stdout.strip() == "ok"
+
+
+def test_null_pool_conventions(kcmm_lib):
+    lib = kcmm_lib.lib
+    assert lib.kcmm_alloc_blocks(None, 1, None) == -1
+    assert lib.kcmm_free_blocks(None, None, 0) == 0
+    assert lib.kcmm_get_va_k(None, 0) == 0
+    assert lib.kcmm_blocks_in_use(None) == 0
+    assert lib.kcmm_pool_create(None) is None
+    assert lib.kcmm_synchronize(None) == -1
+
+
+def test_kernel_entry_points_refuse_host_pool(host_pool_factory):
+    from lattice_b200 import KcmmError
+
+    pool = host_pool_factory(kv_heads=2, head_dim=64, max_batch=1, max_seq_len=32)
+    with pytest.raises(KcmmError, match="no device memory"):
+        pool.paged_attn_decode(0, query_ptr=1, out_ptr=1, block_tables_ptr=1, seq_lens_ptr=1,
+                               block_offsets_f16_ptr=1, batch=1, num_q_heads=2, kv_heads=2,
+                               head_dim=64, block_size=16, max_blocks_per_seq=2, scale=0.1)

@@ -1,0 +1,114 @@
+"""Copy-on-write forks and the host swap tier on the GPU: page contents must be
+bit-exact (north star), checked against the oracle's block-copy semantics."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _torch():
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+def build(tiering=False, layers=2, blocks=64, tmp=None):
+    from lattice_b200.workloads import DecodeWorkload
+
+    _torch()
+    return DecodeWorkload(batch=4, num_q_heads=8, kv_heads=2, head_dim=128, pool_blocks=blocks,
+                          min_len=40, max_len=200, num_layers=layers, tiering=tiering,
+                          seed=11).build()
+
+
+def regions(wl):
+    return {(l, k): wl.host_region(l, k).copy() for l in range(wl.num_layers) for k in "kv"}
+
+
+def test_cow_fork_copies_all_layers():
+    torch = _torch()
+    wl = build()
+    try:
+        pool = wl.pool
+        s = wl.seq_indices[0]
+        table = pool.block_table(s)
+        f = pool.fork_sequence(s)
+        assert all(pool.refcount(b) == 2 for b in table)
+        before = regions(wl)
+        last = len(table) - 1
+        new = pool.cow_blocks([f, s], [last, 0],
+                              stream_ptr=torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert new[0] != table[last] and new[1] == table[0] or pool.refcount(table[0]) == 1
+        assert pool.block_table(f)[last] == new[0]
+        assert pool.refcount(table[last]) == 1 and pool.refcount(new[0]) == 1
+        bb = pool.stats()["block_bytes"] // 2
+        src = pool.block_va_offset(table[last]) // 2
+        dst = pool.block_va_offset(new[0]) // 2
+        after = {(l, k): wl.host_region(l, k) for l in range(wl.num_layers) for k in "kv"}
+        for key in before:
+            assert np.array_equal(after[key][dst:dst + bb], before[key][src:src + bb]), key
+            # every other byte is unchanged
+            mask = np.ones(len(before[key]), bool)
+            mask[dst:dst + bb] = False
+            assert np.array_equal(after[key][mask], before[key][mask])
+    finally:
+        wl.close()
+
+
+def test_swap_out_in_roundtrip_bit_exact(tmp_path):
+    """ref tests/kcmm_bench_tiering.rs:454-472: data survives evict + restore exactly,
+    the block id is kept and its physical slot may move."""
+    torch = _torch()
+    wl = build(tiering=True)
+    try:
+        pool = wl.pool
+        victims = [int(b) for b in wl.tables[0, :3]]
+        before = regions(wl)
+        offs_before = {b: pool.block_va_offset(b) for b in victims}
+        pool.swap_out(victims)
+        assert all(pool.block_location(b) == "cpu" for b in victims)
+        # refill the freed slots with other data so a stale restore would be visible
+        fresh = pool.alloc_blocks(3)
+        assert sorted(pool.block_va_offset(b) for b in fresh) == sorted(offs_before.values())
+        from lattice_b200.workloads import memcpy
+        junk = torch.full((pool.stats()["block_bytes"] // 2,), 3.0, device="cuda").bfloat16()
+        for b in fresh:
+            for l in range(wl.num_layers):
+                memcpy(pool.va_k(l) + pool.block_va_offset(b), junk.data_ptr(), junk.numel() * 2, "d2d")
+        pool.swap_in(victims)
+        bb = pool.stats()["block_bytes"] // 2
+        after = regions(wl)
+        for b in victims:
+            assert pool.block_location(b) == "gpu"
+            src, dst = offs_before[b] // 2, pool.block_va_offset(b) // 2
+            for key in before:
+                assert np.array_equal(after[key][dst:dst + bb], before[key][src:src + bb])
+        m = pool.metrics()
+        assert m["eviction_count"] >= 1 and m["restoration_count"] >= 1
+    finally:
+        wl.close()
+
+
+def test_evict_and_restore_reference_api():
+    wl = build(tiering=True, blocks=32)
+    try:
+        pool = wl.pool
+        assert pool.eviction_policy() == "lru"
+        n = pool.evict_blocks(4)
+        assert n == 4
+        cpu = [b for b in range(pool.total_blocks()) if pool.is_gpu_resident(b) == 0
+               and pool.all_block_valid_flags()[b]]
+        assert len(cpu) == 4
+        va = pool.restore_evicted_block(cpu[0])
+        assert va == pool.block_va_offset(cpu[0]) and pool.is_gpu_resident(cpu[0])
+        pool.restore_evicted_blocks(cpu)
+        assert all(pool.is_gpu_resident(b) for b in cpu)
+        pool.set_eviction_policy("FIFO")
+        assert pool.eviction_policy() == "fifo"
+    finally:
+        wl.close()

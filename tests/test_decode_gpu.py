@@ -1,0 +1,175 @@
+"""Paged decode attention on the GPU through the C ABI, against the CPU oracle.
+
+Tolerance (north star): bf16/f16 outputs within max-abs 2e-3 / max-rel 1e-2 of the
+oracle computed in fp64/fp32, i.e. |out - ref| <= 2e-3 + 1e-2 * |ref| elementwise."""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-3, 1e-2
+
+
+def _torch():
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+def oracle_out(wl):
+    from oracle import native as N
+
+    q = __import__("lattice_b200.workloads", fromlist=["x"]).tensor_bits(wl.q)
+    return N.paged_attn(wl.dtype, q, wl.host_region(0, "k"), wl.host_region(0, "v"), wl.tables,
+                        wl.seq_lens, wl.offsets, hq=wl.num_q_heads, hkv=wl.kv_heads,
+                        d=wl.head_dim, bs=wl.block_size, max_bps=wl.max_blocks_per_seq,
+                        scale=wl.scale)
+
+
+def check(wl, got=None):
+    torch = _torch()
+    ref = oracle_out(wl)
+    got = (wl.out if got is None else got).float().cpu().numpy()
+    live = wl.seq_lens > 0
+    err = np.abs(got[live] - ref[live])
+    bound = ATOL + RTOL * np.abs(ref[live])
+    assert (err <= bound).all(), f"max err {err.max()} (worst excess {(err - bound).max()})"
+    return ref
+
+
+def make(**kw):
+    from lattice_b200.workloads import DecodeWorkload
+
+    _torch()
+    kw.setdefault("pool_blocks", 512)
+    kw.setdefault("min_len", 1)
+    kw.setdefault("max_len", 700)
+    return DecodeWorkload(**kw).build()
+
+
+SHAPES = [
+    # batch, hq, hkv, D, bs
+    (4, 4, 4, 64, 16),      # config-1 shape (MHA, D 64)
+    (6, 32, 8, 128, 16),    # Llama-3-8B heads (GQA 4)
+    (3, 8, 1, 128, 16),     # per-GPU head shard of the 70B config (GQA 8)
+    (2, 64, 2, 128, 16),    # GQA 32: two head tiles per kv head
+    (3, 12, 4, 80, 32),
+    (3, 8, 2, 96, 16),
+    (2, 8, 2, 256, 16),
+    (2, 6, 3, 72, 16),      # head_dim not a multiple of 16: generic kernel
+    (2, 8, 2, 64, 8),       # block_size 8: generic kernel
+    (3, 10, 4, 64, 16),     # query heads not a multiple of kv heads
+]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("shape", SHAPES)
+def test_decode_matches_oracle(shape, dtype):
+    B, hq, hkv, D, bs = shape
+    lens = [1, 15, 16, 17, 255, 700, 333][:B]
+    wl = make(batch=B, num_q_heads=hq, kv_heads=hkv, head_dim=D, block_size=bs, dtype=dtype,
+              seq_lens_override=lens, seed=hash(shape) % 1000)
+    try:
+        wl.decode()
+        _torch().cuda.synchronize()
+        check(wl)
+    finally:
+        wl.close()
+
+
+def test_zero_length_rows_untouched():
+    torch = _torch()
+    wl = make(batch=4, num_q_heads=8, kv_heads=2, head_dim=128, seq_lens_override=[0, 40, -3, 70])
+    try:
+        wl.out.fill_(7.0)
+        wl.decode()
+        torch.cuda.synchronize()
+        o = wl.out.float().cpu().numpy()
+        assert (o[0] == 7.0).all() and (o[2] == 7.0).all()
+        check(wl)
+    finally:
+        wl.close()
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 7])
+def test_split_count_does_not_change_result(splits, monkeypatch):
+    monkeypatch.setenv("KCMM_DECODE_SPLITS", str(splits))
+    wl = make(batch=5, num_q_heads=32, kv_heads=8, head_dim=128, min_len=200, max_len=2000,
+              pool_blocks=1024, seed=splits)
+    try:
+        wl.decode()
+        _torch().cuda.synchronize()
+        check(wl)
+    finally:
+        wl.close()
+
+
+def test_v_row_kat():
+    """ref scripts/kcmm/non_default_stream_ffi_smoke.py:172-179: q = 0, seq_len 1,
+    k = arange+100, v = arange+1000 -> out equals the V row of the mapped kv head."""
+    torch = _torch()
+    from lattice_b200.workloads import memcpy
+
+    wl = make(batch=2, num_q_heads=4, kv_heads=2, head_dim=64, dtype="f16",
+              seq_lens_override=[1, 1], pool_blocks=8)
+    try:
+        n = wl.region_used // 2
+        k = (torch.arange(n, device="cuda") % 512 + 100).half()
+        v = (torch.arange(n, device="cuda") % 512 + 1000).half()
+        memcpy(wl.pool.va_k(0), k.data_ptr(), wl.region_used, "d2d")
+        memcpy(wl.pool.va_v(0), v.data_ptr(), wl.region_used, "d2d")
+        wl.q.zero_()
+        for variant in ("sync", "stream", "current"):
+            wl.out.zero_()
+            kw = dict(query_ptr=wl.q.data_ptr(), out_ptr=wl.out.data_ptr(),
+                      block_tables_ptr=wl.d_tables.data_ptr(),
+                      seq_lens_ptr=wl.d_seq_lens.data_ptr(),
+                      block_offsets_f16_ptr=wl.d_offsets.data_ptr(), batch=2, num_q_heads=4,
+                      kv_heads=2, head_dim=64, block_size=16,
+                      max_blocks_per_seq=wl.max_blocks_per_seq, scale=1.0, dtype="f16")
+            if variant == "sync":
+                wl.pool.paged_attn_decode(0, stream_ptr=None, **kw)
+            else:
+                wl.pool.paged_attn_decode(0, stream_ptr=torch.cuda.current_stream().cuda_stream,
+                                          current_context=variant == "current", **kw)
+            torch.cuda.synchronize()
+            vv = v.cpu().numpy()
+            for b in range(2):
+                for h in range(4):
+                    e = int(wl.offsets[wl.tables[b, 0]]) + (h * 2 // 4) * 64
+                    np.testing.assert_array_equal(wl.out[b, h].cpu().numpy(), vv[e:e + 64])
+    finally:
+        wl.close()
+
+
+def test_llama3_8b_config_full_size():
+    """BASELINE config 2 at full size: 64 sequences, 512..4096 tokens, 40k-block pool."""
+    wl = make(batch=64, num_q_heads=32, kv_heads=8, head_dim=128, min_len=512, max_len=4096,
+              pool_blocks=40000, seed=0)
+    try:
+        wl.decode()
+        _torch().cuda.synchronize()
+        ref = check(wl)
+        # size-independent property: each output is a convex combination of V rows,
+        # so it lies inside the per-dim [min, max] of V (checked loosely via the oracle)
+        assert np.isfinite(ref).all()
+    finally:
+        wl.close()
+
+
+def test_device_diagnostics_clean():
+    """A clean run leaves the pool's device diagnostic word at 0 (no bounded wait gave up,
+    no bad offset); read through the pool's synchronize path."""
+    wl = make(batch=3, num_q_heads=8, kv_heads=2, head_dim=128)
+    try:
+        wl.decode()
+        wl.pool.synchronize()
+        assert wl.pool.kernel_status() == 0
+    finally:
+        wl.close()
