@@ -34,7 +34,8 @@ namespace dev {
 namespace {
 
 constexpr int kUnit = 16;            // tokens per pipeline unit
-constexpr uint32_t kMaxPolls = 1u << 17;  // bounded mbarrier wait (~2.6 s worst case)
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // a KV unit that has not landed in 1 s
+                                                  // is reported, never waited on forever
 
 struct DecodeParams {
   const void *q;
@@ -208,7 +209,8 @@ __global__ void __launch_bounds__(W * 32) decode_kernel(const DecodeParams p) {
   for (int k = 0; k < n_w; ++k) {
     const int st = k % NS;
     const uint32_t bar = ptx::smem_u32(my_bars + st);
-    if (!ptx::mbar_wait_bounded(bar, uint32_t((k / NS) & 1), kMaxPolls)) {
+    const bool landed = ptx::mbar_wait_bounded(bar, uint32_t((k / NS) & 1), kWaitLimitNs);
+    if (!__all_sync(0xffffffffu, landed)) {  // warp-uniform exit
       failed = true;
       break;
     }
@@ -300,8 +302,8 @@ __global__ void __launch_bounds__(W * 32) decode_kernel(const DecodeParams p) {
     // Let copies still in flight land before the CTA's shared memory is
     // released (bounded as well), then report.
     for (int k = 0; k < NS && k < n_w; ++k) {
-      ptx::mbar_wait_bounded(ptx::smem_u32(my_bars + k), 0, 64);
-      ptx::mbar_wait_bounded(ptx::smem_u32(my_bars + k), 1, 64);
+      ptx::mbar_wait_bounded(ptx::smem_u32(my_bars + k), 0, 1000000ull);
+      ptx::mbar_wait_bounded(ptx::smem_u32(my_bars + k), 1, 1000000ull);
     }
     if (lane == 0) {
       atomicOr(p.diag, int32_t(kDiagWaitTimeout));

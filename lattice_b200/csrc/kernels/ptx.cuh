@@ -44,14 +44,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: returns false after `max_polls` unsuccessful polls (each poll
-// may suspend the thread for up to ~20 us), i.e. well under a few seconds.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: gives up (returns false) once `limit_ns` of wall time has
+// passed without the phase completing.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
-                                                  uint32_t max_polls) {
-  for (uint32_t i = 0; i < max_polls; ++i) {
+                                                  uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
-  return false;
 }
 
 // --- bulk copy global -> shared (TMA engine, no tensor map) -----------------
