@@ -125,7 +125,10 @@ def run_ours(args):
     torch.cuda.set_device(local)
     from lattice_b200.workloads import DecodeWorkload, FusedAppendWorkload
 
-    wl = DecodeWorkload(seed=1000 + rank, device=local).build()
+    # --profile: same batch, heads and length distribution with the tables drawn
+    # from a 12k-block pool, so that an ncu capture saves/restores < 1 GB per pass.
+    pool_blocks = 12000 if args.profile else 40000
+    wl = DecodeWorkload(seed=1000 + rank, device=local, pool_blocks=pool_blocks).build()
     # the step's new token of sequence b sits at position L_b - 1 of its table
     slots = np.array([int(wl.tables[b, (L - 1) // 16]) * 16 + (L - 1) % 16
                       for b, L in enumerate(wl.seq_lens)], np.int64)
@@ -189,12 +192,12 @@ def run_ours(args):
 
     splits = int(os.environ.get("KCMM_DECODE_SPLITS", "0"))
     launches_per_step = 1 + 2  # fused append + decode main + split merge
-    e2e = run_e2e(args, wl, fa, stream) if rank == 0 else None
+    e2e = run_e2e(args, wl, fa, stream) if rank == 0 and not args.profile else None
     status = wl.pool.kernel_status()
 
     result = None
     if rank == 0:
-        cpu = cpu_baseline(wl) if world == 1 else None
+        cpu = cpu_baseline(wl) if world == 1 and not args.profile else None
         result = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_step, 5),
@@ -374,6 +377,8 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--profile", action="store_true",
+                    help="profiling case for ncu: 12k-block pool, no CPU baseline / e2e legs")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

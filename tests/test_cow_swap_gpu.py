@@ -40,21 +40,27 @@ def test_cow_fork_copies_all_layers():
         assert all(pool.refcount(b) == 2 for b in table)
         before = regions(wl)
         last = len(table) - 1
+        # both entries are shared (refcount 2): each gets its own fresh copy
         new = pool.cow_blocks([f, s], [last, 0],
                               stream_ptr=torch.cuda.current_stream().cuda_stream)
         torch.cuda.synchronize()
-        assert new[0] != table[last] and new[1] == table[0] or pool.refcount(table[0]) == 1
-        assert pool.block_table(f)[last] == new[0]
-        assert pool.refcount(table[last]) == 1 and pool.refcount(new[0]) == 1
+        assert new[0] not in table and new[1] not in table and new[0] != new[1]
+        assert pool.block_table(f)[last] == new[0] and pool.block_table(s)[0] == new[1]
+        assert pool.block_table(s)[last] == table[last] and pool.block_table(f)[0] == table[0]
+        for b in (table[last], table[0], new[0], new[1]):
+            assert pool.refcount(b) == 1
+        # a block that is no longer shared is left in place
+        assert pool.cow_blocks([f], [last]) == [new[0]]
         bb = pool.stats()["block_bytes"] // 2
-        src = pool.block_va_offset(table[last]) // 2
-        dst = pool.block_va_offset(new[0]) // 2
+        pairs = [(pool.block_va_offset(table[last]) // 2, pool.block_va_offset(new[0]) // 2),
+                 (pool.block_va_offset(table[0]) // 2, pool.block_va_offset(new[1]) // 2)]
         after = {(l, k): wl.host_region(l, k) for l in range(wl.num_layers) for k in "kv"}
         for key in before:
-            assert np.array_equal(after[key][dst:dst + bb], before[key][src:src + bb]), key
-            # every other byte is unchanged
             mask = np.ones(len(before[key]), bool)
-            mask[dst:dst + bb] = False
+            for src, dst in pairs:
+                assert np.array_equal(after[key][dst:dst + bb], before[key][src:src + bb]), key
+                mask[dst:dst + bb] = False
+            # every other byte is unchanged
             assert np.array_equal(after[key][mask], before[key][mask])
     finally:
         wl.close()
