@@ -24,6 +24,8 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "../launch.hpp"
@@ -454,6 +456,16 @@ __global__ void decode_generic_kernel(const DecodeParams p, int D) {
   }
 }
 
+}  // namespace
+}  // namespace dev
+}  // namespace kcmm
+
+#include "decode_streamk.cuh"
+
+namespace kcmm {
+namespace dev {
+namespace {
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -569,9 +581,162 @@ cudaMemPool_t scratch_pool(int dev) {
   return pools[dev];
 }
 
+// --- stream-K plan -------------------------------------------------------------
+
+using SkFn = void (*)(const sk::Params);
+
+struct SkPlan {
+  bool ok = false;
+  SkFn fn = nullptr;
+  void (*merge)(const sk::Params, int) = nullptr;
+  size_t smem = 0;
+  int grid = 0, warps = 4, n_head_tiles = 1, g_max = 16;
+  size_t scratch_bytes = 0;
+  size_t off_lse = 0, off_cum = 0, off_segcum = 0;
+};
+
+template <typename T, int D, int W, int NS>
+void sk_pick(SkPlan *pl, int batch) {
+  constexpr int S = 2;
+  pl->fn = sk::kernel<T, D, W, NS, S>;
+  pl->merge = sk::merge<T, D>;
+  pl->smem = sk::layout<D, W, NS, S>(batch, pl->g_max).total;
+  pl->warps = W;
+}
+
+template <typename T>
+bool sk_select(SkPlan *pl, int D, int batch, int variant) {
+#define KCMM_SK(DD)                                                   \
+  case DD:                                                            \
+    if (variant == 1) sk_pick<T, DD, 4, 3>(pl, batch);                \
+    else if (variant == 2) sk_pick<T, DD, 8, 2>(pl, batch);           \
+    else sk_pick<T, DD, 4, 2>(pl, batch);                             \
+    return true;
+  switch (D) {
+    KCMM_SK(64)
+    KCMM_SK(128)
+    default:
+      break;
+  }
+#undef KCMM_SK
+#define KCMM_SK1(DD)                 \
+  case DD:                           \
+    sk_pick<T, DD, 4, 2>(pl, batch); \
+    return true;
+  switch (D) {
+    KCMM_SK1(32)
+    KCMM_SK1(80)
+    KCMM_SK1(96)
+    KCMM_SK1(112)
+    KCMM_SK1(160)
+    KCMM_SK1(192)
+    KCMM_SK1(256)
+    default:
+      return false;
+  }
+#undef KCMM_SK1
+}
+
+SkPlan make_sk_plan(const DecodeArgs &a) {
+  SkPlan pl;
+  const int D = a.head_dim;
+  if (D % 16 != 0 || a.block_size % 16 != 0 || a.batch > 2048) return pl;
+  if ((reinterpret_cast<uintptr_t>(a.q) & 15) != 0) return pl;
+  const char *impl = std::getenv("KCMM_DECODE_IMPL");
+  if (impl && std::strcmp(impl, "split") == 0) return pl;
+  int variant = 0;
+  if (const char *v = std::getenv("KCMM_SK_VARIANT")) variant = std::atoi(v);
+  const int g_all = (a.num_q_heads + a.kv_heads - 1) / a.kv_heads;
+  pl.n_head_tiles = (g_all + 15) / 16;
+  pl.g_max = std::min(16, g_all);
+  bool found = a.dtype == Dtype::BF16 ? sk_select<__nv_bfloat16>(&pl, D, a.batch, variant)
+                                      : sk_select<__half>(&pl, D, a.batch, variant);
+  if (!found || pl.smem > 227 * 1024) return pl;
+  if (cudaFuncSetAttribute(pl.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pl.smem)) !=
+      cudaSuccess)
+    return pl;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pl.fn, pl.warps * 32, pl.smem) !=
+          cudaSuccess ||
+      per_sm <= 0)
+    return pl;
+  pl.grid = sm_count() * per_sm;
+  if (const char *gs = std::getenv("KCMM_SK_GRID")) pl.grid = std::max(1, std::atoi(gs));
+  const size_t segs = size_t(a.batch) * a.kv_heads * pl.n_head_tiles;
+  const size_t rows = (segs + size_t(pl.grid)) * size_t(pl.g_max);
+  pl.off_lse = rows * size_t(D) * 4;
+  pl.off_cum = (pl.off_lse + rows * 4 + 15) & ~size_t(15);
+  pl.off_segcum = pl.off_cum + (size_t(a.batch) + 1) * 8;
+  pl.scratch_bytes = pl.off_segcum + (size_t(a.batch) + 1) * 4;
+  pl.ok = true;
+  return pl;
+}
+
+cudaError_t scratch_acquire(const DecodeArgs &a, size_t bytes, cudaStream_t stream, void **out,
+                            bool *owned) {
+  *owned = false;
+  if (a.scratch) {
+    if (a.scratch_bytes < bytes) return cudaErrorInvalidValue;
+    *out = a.scratch;
+    return cudaSuccess;
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaMemPool_t mp = scratch_pool(dev);
+  if (!mp) return cudaErrorMemoryAllocation;
+  cudaError_t e = cudaMallocFromPoolAsync(out, bytes, mp, stream);
+  if (e == cudaSuccess) *owned = true;
+  return e;
+}
+
+cudaError_t decode_streamk(const DecodeArgs &a, const SkPlan &pl, cudaStream_t stream) {
+  void *scratch = nullptr;
+  bool owned = false;
+  cudaError_t e = scratch_acquire(a, pl.scratch_bytes, stream, &scratch, &owned);
+  if (e != cudaSuccess) return e;
+  sk::Params p = {};
+  p.q = a.q;
+  p.out = a.out;
+  p.tables = a.block_tables;
+  p.seq_lens = a.seq_lens;
+  p.offsets = a.block_offsets;
+  p.va_k = a.va_k;
+  p.va_v = a.va_v;
+  p.region_elems = a.region_elems;
+  p.batch = a.batch;
+  p.hq = a.num_q_heads;
+  p.hkv = a.kv_heads;
+  p.bs = a.block_size;
+  p.max_bps = a.max_blocks_per_seq;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.n_head_tiles = pl.n_head_tiles;
+  p.g_max = pl.g_max;
+  char *base = static_cast<char *>(scratch);
+  p.part_o = reinterpret_cast<float *>(base);
+  p.part_lse = reinterpret_cast<float *>(base + pl.off_lse);
+  p.cum_out = reinterpret_cast<int64_t *>(base + pl.off_cum);
+  p.segcum_out = reinterpret_cast<int32_t *>(base + pl.off_segcum);
+  p.diag = a.diag;
+  pl.fn<<<pl.grid, pl.warps * 32, pl.smem, stream>>>(p);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) {
+    pl.merge<<<a.batch * a.num_q_heads, 128, 0, stream>>>(p, pl.grid);
+    e = cudaGetLastError();
+  }
+  if (owned) {
+    cudaError_t f = cudaFreeAsync(scratch, stream);
+    if (e == cudaSuccess) e = f;
+  }
+  return e;
+}
+
 }  // namespace
 
-size_t decode_scratch_bytes(const DecodeArgs &a) { return make_plan(a).scratch_bytes; }
+size_t decode_scratch_bytes(const DecodeArgs &a) {
+  SkPlan sp = make_sk_plan(a);
+  if (sp.ok) return sp.scratch_bytes;
+  return make_plan(a).scratch_bytes;
+}
 
 cudaError_t decode_attention(const DecodeArgs &a, cudaStream_t stream) {
   DecodeParams p = {};
@@ -591,6 +756,8 @@ cudaError_t decode_attention(const DecodeArgs &a, cudaStream_t stream) {
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.diag = a.diag;
 
+  SkPlan sp = make_sk_plan(a);
+  if (sp.ok) return decode_streamk(a, sp, stream);
   Plan pl = make_plan(a);
   if (!pl.fast) {
     const int threads = 256;

@@ -1,0 +1,650 @@
+// Persistent "stream-K" paged decode attention for sm_100a (included by decode.cu).
+//
+// Work decomposition.  Every (sequence b, kv head, tile of <=16 query heads)
+// is a *segment* of ceil(L_b/16) 16-token *units*.  The segments of all
+// sequences, laid end to end, form one flat unit space of U units; CTA c of a
+// one-wave persistent grid of P CTAs takes the contiguous slice
+// [c*U/P, (c+1)*U/P).  Every CTA therefore streams the same number of KV bytes
+// (±1 unit) whatever the mix of context lengths, with no atomics and no work
+// queue.  A slice may start or end inside a segment: the CTA then emits a
+// partial result (o, lse) for that *piece*, and a second pass merges the
+// pieces of a segment by log-sum-exp; segments that lie inside one slice are
+// written to `out` directly.
+//
+// Inside a CTA, the W warps take the units of the slice round-robin.  Each
+// warp has its own NS-stage ring of K/V tiles fed by one-row `cp.async.bulk`
+// copies (TMA engine) completing on an mbarrier per stage, and its own
+// look-ahead of page addresses (32 units computed at a time, one batch ahead),
+// so the pipeline never drains at segment boundaries.  Q tiles arrive by bulk
+// copy into S shared-memory slots, one per in-flight piece.  When a warp leaves
+// a piece it deposits (o, m, l) into the piece's merge slot; the last warp to
+// arrive merges the W deposits, frees the slot and starts the Q load of the
+// piece S places ahead.  All waits are bounded in wall time.
+
+namespace kcmm {
+namespace dev {
+namespace sk {
+
+struct Params {
+  const void *q;
+  void *out;
+  const int32_t *tables;
+  const int32_t *seq_lens;
+  const uint64_t *offsets;
+  const void *va_k;
+  const void *va_v;
+  uint64_t region_elems;
+  int batch, hq, hkv, bs, max_bps;
+  float scale_log2;
+  int n_head_tiles;  // ceil(group / 16)
+  int g_max;         // rows of a head tile (<= 16)
+  float *part_o;     // [(segments + P) * g_max * D]
+  float *part_lse;   // [(segments + P) * g_max]
+  int64_t *cum_out;  // [B+1] unit prefix, written by CTA 0 for the merge pass
+  int32_t *segcum_out;  // [B+1] segment prefix
+  int32_t *diag;
+};
+
+constexpr int kUnitTok = 16;
+constexpr uint64_t kLimitNs = 1000000000ull;
+
+struct Layout {
+  size_t rings, qslots, merge_o, merge_ml, bars, cnt, cum, segcum, total;
+};
+
+__host__ __device__ inline size_t al16(size_t x) { return (x + 15) & ~size_t(15); }
+
+template <int D, int W, int NS, int S>
+__host__ __device__ inline Layout layout(int batch, int g_max) {
+  constexpr int RS = D + 8;
+  Layout L;
+  size_t o = 0;
+  L.rings = o;
+  o = al16(o + size_t(W) * NS * 2 * kUnitTok * RS * 2);
+  L.qslots = o;
+  o = al16(o + size_t(S) * 16 * RS * 2);
+  L.merge_o = o;
+  o = al16(o + size_t(S) * W * g_max * D * 4);
+  L.merge_ml = o;
+  o = al16(o + size_t(S) * W * g_max * 2 * 4);
+  L.bars = o;
+  o = al16(o + size_t(W * NS + S) * 8);
+  L.cnt = o;
+  o = al16(o + size_t(2 * S) * 4);
+  L.cum = o;
+  o = al16(o + size_t(batch + 1) * 8);
+  L.segcum = o;
+  o = al16(o + size_t(batch + 1) * 4);
+  L.total = o;
+  return L;
+}
+
+// Largest c in [0, P) with floor(c*U/P) <= u.
+__device__ __forceinline__ int cta_of(int64_t u, int64_t U, int P) {
+  int c = int((u * P) / U);
+  if (c >= P) c = P - 1;
+  while (c + 1 < P && ((int64_t(c) + 1) * U) / P <= u) ++c;
+  while (c > 0 && (int64_t(c) * U) / P > u) --c;
+  return c;
+}
+
+struct Loc {
+  int b, segl, unit, nunits;
+  int64_t seg_start;  // first unit of the segment in the flat space
+  int sc;             // compact segment index
+};
+
+__device__ __forceinline__ Loc locate(int64_t u, const int64_t *cum, const int32_t *segcum,
+                                      int B, int segs_per_seq) {
+  int lo = 0, hi = B - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (cum[mid] <= u) lo = mid; else hi = mid - 1;
+  }
+  Loc r;
+  r.b = lo;
+  r.nunits = int((cum[lo + 1] - cum[lo]) / segs_per_seq);
+  const int64_t rem = u - cum[lo];
+  r.segl = int(rem / r.nunits);
+  r.unit = int(rem - int64_t(r.segl) * r.nunits);
+  r.seg_start = cum[lo] + int64_t(r.segl) * r.nunits;
+  r.sc = segcum[lo] + r.segl;
+  return r;
+}
+
+// Sequence holding compact segment sc.
+__device__ __forceinline__ int seq_of_segment(int sc, const int32_t *segcum, int B) {
+  int lo = 0, hi = B - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (segcum[mid] <= sc) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ void heads_of(int segl, int nht, int hq, int hkv, int *lo, int *G) {
+  const int kvh = segl / nht, ht = segl % nht;
+  const int g_lo = int((int64_t(kvh) * hq + hkv - 1) / hkv);
+  const int g_hi = int((int64_t(kvh + 1) * hq + hkv - 1) / hkv);
+  *lo = g_lo + ht * 16;
+  *G = max(0, min(g_hi, *lo + 16) - *lo);
+}
+
+template <typename T, int D, int W, int NS, int S>
+__global__ void __launch_bounds__(W * 32) kernel(const Params p) {
+  using MMA = ptx::Mma<T>;
+  constexpr int RS = D + 8;
+  constexpr int STAGE = 2 * kUnitTok * RS;
+  constexpr int KS = D / 16, ND = D / 8;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const Layout Lo = layout<D, W, NS, S>(p.batch, p.g_max);
+  T *rings = reinterpret_cast<T *>(smem + Lo.rings);
+  T *qslots = reinterpret_cast<T *>(smem + Lo.qslots);
+  float *merge_o = reinterpret_cast<float *>(smem + Lo.merge_o);
+  float *merge_ml = reinterpret_cast<float *>(smem + Lo.merge_ml);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Lo.bars);
+  uint64_t *qbars = bars + W * NS;
+  int *slot_cnt = reinterpret_cast<int *>(smem + Lo.cnt);
+  int *slot_gen = slot_cnt + S;
+  int64_t *cum = reinterpret_cast<int64_t *>(smem + Lo.cum);
+  int32_t *segcum = reinterpret_cast<int32_t *>(smem + Lo.segcum);
+  __shared__ int s_fail;
+
+  const int c = blockIdx.x, P = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int B = p.batch;
+  const int nht = p.n_head_tiles;
+  const int segs_per_seq = p.hkv * nht;
+  const int max_len = p.max_bps * p.bs;
+  const int g_max = p.g_max;
+
+  // ---- prefix sums over sequences (warp 0) ---------------------------------
+  if (warp == 0) {
+    const int per = (B + 31) / 32, b0 = lane * per;
+    int64_t su = 0;
+    int ss = 0;
+    for (int i = 0; i < per; ++i) {
+      const int b = b0 + i;
+      if (b < B) {
+        int L = p.seq_lens[b];
+        L = L > 0 ? min(L, max_len) : 0;
+        const int nu = (L + kUnitTok - 1) / kUnitTok;
+        su += int64_t(nu) * segs_per_seq;
+        ss += nu > 0 ? segs_per_seq : 0;
+      }
+    }
+    int64_t iu = su;
+    int is = ss;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t vu = __shfl_up_sync(0xffffffffu, iu, o);
+      const int vs = __shfl_up_sync(0xffffffffu, is, o);
+      if (lane >= o) {
+        iu += vu;
+        is += vs;
+      }
+    }
+    int64_t ru = iu - su;
+    int rs = is - ss;
+    for (int i = 0; i < per; ++i) {
+      const int b = b0 + i;
+      if (b < B) {
+        cum[b] = ru;
+        segcum[b] = rs;
+        int L = p.seq_lens[b];
+        L = L > 0 ? min(L, max_len) : 0;
+        const int nu = (L + kUnitTok - 1) / kUnitTok;
+        ru += int64_t(nu) * segs_per_seq;
+        rs += nu > 0 ? segs_per_seq : 0;
+      }
+    }
+    if (lane == 31) {
+      cum[B] = iu;
+      segcum[B] = is;
+    }
+  }
+  if (lane == 0) {
+    for (int s = 0; s < NS; ++s) ptx::mbar_init(ptx::smem_u32(bars + warp * NS + s), 1);
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      ptx::mbar_init(ptx::smem_u32(qbars + s), 1);
+      slot_cnt[s] = 0;
+      slot_gen[s] = 0;
+    }
+    s_fail = 0;
+  }
+  ptx::fence_proxy_async_smem();
+  __syncthreads();
+
+  const int64_t U = cum[B];
+  if (c == 0) {
+    for (int b = threadIdx.x; b <= B; b += W * 32) {
+      p.cum_out[b] = cum[b];
+      p.segcum_out[b] = segcum[b];
+    }
+  }
+  const int64_t lo = (int64_t(c) * U) / P, hi = (int64_t(c) + 1) * U / P;
+  if (lo >= hi) return;
+
+  const Loc first = locate(lo, cum, segcum, B, segs_per_seq);
+  const Loc last = locate(hi - 1, cum, segcum, B, segs_per_seq);
+  const int sc0 = first.sc;
+  const int n_pieces = last.sc - sc0 + 1;
+  const int64_t row_stride = int64_t(p.hkv) * D;
+  const T *qg = static_cast<const T *>(p.q);
+
+  // Q tile of piece k -> slot k % S (rows >= G are never read into outputs).
+  auto issue_q = [&](int k) {
+    const int sc = sc0 + k;
+    const int b = seq_of_segment(sc, segcum, B);
+    int hlo, G;
+    heads_of(sc - segcum[b], nht, p.hq, p.hkv, &hlo, &G);
+    const int slot = k % S;
+    const uint32_t bar = ptx::smem_u32(qbars + slot);
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive_expect_tx(bar, uint32_t(G * D * sizeof(T)));
+    __syncwarp();
+    if (lane < G) {
+      ptx::bulk_g2s(ptx::smem_u32(qslots + slot * 16 * RS + lane * RS),
+                    qg + (int64_t(b) * p.hq + hlo + lane) * D, uint32_t(D * sizeof(T)), bar);
+    }
+  };
+  if (warp == 0) {
+    for (int k = 0; k < S && k < n_pieces; ++k) issue_q(k);
+  }
+
+  // ---- per-warp unit stream ---------------------------------------------------
+  const int64_t span = hi - lo;
+  const int n_pos = span > warp ? int((span - warp + W - 1) / W) : 0;
+  int64_t me[2] = {0, 0};  // look-ahead: element offset of unit (batch*32 + lane)
+  int mi[2] = {0, 0};      // (piece << 6) | (nvalid << 1) | ok
+
+  auto meta = [&](int batch_idx) {
+    const int i = batch_idx * 32 + lane;
+    int64_t e = 0;
+    int info = 0;
+    if (i < n_pos) {
+      const int64_t u = lo + warp + int64_t(i) * W;
+      const Loc l = locate(u, cum, segcum, B, segs_per_seq);
+      int L = p.seq_lens[l.b];
+      L = min(L, max_len);
+      const int tok0 = l.unit * kUnitTok;
+      const int nvalid = min(kUnitTok, L - tok0);
+      const int blk = p.tables[int64_t(l.b) * p.max_bps + tok0 / p.bs];
+      const int kvh = l.segl / nht;
+      int ok = 0;
+      if (blk >= 0) {
+        const uint64_t off = p.offsets[blk];
+        e = int64_t(off) + int64_t(tok0 % p.bs) * row_stride + int64_t(kvh) * D;
+        ok = (off & 7) == 0 && uint64_t(e + (kUnitTok - 1) * row_stride + D) <= p.region_elems;
+      }
+      if (!ok) atomicOr(p.diag, int32_t(kDiagBadOffset));
+      info = ((l.sc - sc0) << 6) | (nvalid << 1) | ok;
+    }
+    if (batch_idx & 1) {
+      me[1] = e;
+      mi[1] = info;
+    } else {
+      me[0] = e;
+      mi[0] = info;
+    }
+  };
+
+  const T *vak = static_cast<const T *>(p.va_k);
+  const T *vav = static_cast<const T *>(p.va_v);
+  T *wring = rings + warp * NS * STAGE;
+  uint64_t *wbars = bars + warp * NS;
+
+  auto fetch = [&](int i, int64_t *e, int *info) {
+    const int buf = (i >> 5) & 1;
+    const int64_t e0 = __shfl_sync(0xffffffffu, me[0], i & 31);
+    const int64_t e1 = __shfl_sync(0xffffffffu, me[1], i & 31);
+    const int i0 = __shfl_sync(0xffffffffu, mi[0], i & 31);
+    const int i1 = __shfl_sync(0xffffffffu, mi[1], i & 31);
+    *e = buf ? e1 : e0;
+    *info = buf ? i1 : i0;
+  };
+
+  auto issue = [&](int i) {
+    int64_t elem;
+    int info;
+    fetch(i, &elem, &info);
+    const int ok = info & 1, nvalid = (info >> 1) & 31;
+    const int st = i % NS;
+    const uint32_t bar = ptx::smem_u32(wbars + st);
+    T *kt = wring + st * STAGE;
+    T *vt = kt + kUnitTok * RS;
+    const int r = lane & 15;
+    if (lane >= 16 && r >= nvalid) {  // masked V rows hold zeros, not stale data
+      const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int cc = 0; cc < D; cc += 8) *reinterpret_cast<uint4 *>(vt + r * RS + cc) = z;
+    }
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive_expect_tx(bar, ok ? uint32_t(2 * nvalid * D * sizeof(T)) : 0u);
+    __syncwarp();
+    if (ok && r < nvalid) {
+      const T *src = (lane < 16 ? vak : vav) + elem + int64_t(r) * row_stride;
+      ptx::bulk_g2s(ptx::smem_u32((lane < 16 ? kt : vt) + r * RS), src,
+                    uint32_t(D * sizeof(T)), bar);
+    }
+  };
+
+  // accumulators of the current piece
+  float o[ND][4];
+  float m0, m1, l0, l1;
+  auto reset = [&]() {
+#pragma unroll
+    for (int i = 0; i < ND; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    m0 = m1 = -INFINITY;
+    l0 = l1 = 0.f;
+  };
+  reset();
+  const int g = lane >> 2, t = lane & 3;
+  bool failed = false;
+
+  // Merge the W deposits of piece k (called by the last warp to deposit).
+  auto merge_piece = [&](int k) {
+    const int slot = k % S;
+    const int sc = sc0 + k;
+    const int b = seq_of_segment(sc, segcum, B);
+    const int segl = sc - segcum[b];
+    int hlo, G;
+    heads_of(segl, nht, p.hq, p.hkv, &hlo, &G);
+    const int nunits = int((cum[b + 1] - cum[b]) / segs_per_seq);
+    const int64_t s_start = cum[b] + int64_t(segl) * nunits, s_end = s_start + nunits;
+    const bool whole = s_start >= lo && s_end <= hi;
+    int64_t gidx = 0;
+    if (!whole) {
+      const int cf = cta_of(s_start, U, P);
+      gidx = int64_t(sc) + cf + (c - cf);
+    }
+    const float *mo = merge_o + size_t(slot) * W * g_max * D;
+    const float *mml = merge_ml + size_t(slot) * W * g_max * 2;
+    for (int idx = lane; idx < G * (D / 2); idx += 32) {
+      const int h = idx / (D / 2), d = (idx % (D / 2)) * 2;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < W; ++w) M = fmaxf(M, mml[(w * g_max + h) * 2]);
+      float Ls = 0.f, x0 = 0.f, x1 = 0.f;
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+        const float mw = mml[(w * g_max + h) * 2];
+        if (mw == -INFINITY) continue;
+        const float sc_w = ptx::fast_exp2(mw - M);
+        Ls += mml[(w * g_max + h) * 2 + 1] * sc_w;
+        const float2 v = *reinterpret_cast<const float2 *>(mo + (size_t(w) * g_max + h) * D + d);
+        x0 += v.x * sc_w;
+        x1 += v.y * sc_w;
+      }
+      const float inv = 1.f / Ls;
+      if (whole) {
+        T *dst = static_cast<T *>(p.out) + (int64_t(b) * p.hq + hlo + h) * D + d;
+        dst[0] = ptx::from_f32<T>(x0 * inv);
+        dst[1] = ptx::from_f32<T>(x1 * inv);
+      } else {
+        *reinterpret_cast<float2 *>(p.part_o + (gidx * g_max + h) * D + d) =
+            make_float2(x0 * inv, x1 * inv);
+        if (d == 0) p.part_lse[gidx * g_max + h] = M + log2f(Ls);
+      }
+    }
+  };
+
+  auto finalize = [&](int k) {
+    const int slot = k % S, gen = k / S;
+    if (lane == 0) {  // wait until the slot's previous piece has been merged
+      volatile int *vg = slot_gen + slot;
+      if (*vg != gen) {
+        const uint64_t t0 = ptx::globaltimer_ns();
+        while (*vg != gen) {
+          if (ptx::globaltimer_ns() - t0 > kLimitNs) {
+            atomicOr(p.diag, int32_t(kDiagWaitTimeout));
+            s_fail = 1;
+            break;
+          }
+        }
+      }
+      __threadfence_block();
+    }
+    __syncwarp();
+    float lq0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
+    lq0 += __shfl_xor_sync(0xffffffffu, lq0, 2);
+    float lq1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
+    lq1 += __shfl_xor_sync(0xffffffffu, lq1, 2);
+    float *mo = merge_o + (size_t(slot) * W + warp) * g_max * D;
+    float *mml = merge_ml + (size_t(slot) * W + warp) * g_max * 2;
+#pragma unroll
+    for (int i = 0; i < ND; ++i) {
+      const int d = i * 8 + 2 * t;
+      if (g < g_max) *reinterpret_cast<float2 *>(mo + g * D + d) = make_float2(o[i][0], o[i][1]);
+      if (g + 8 < g_max)
+        *reinterpret_cast<float2 *>(mo + (g + 8) * D + d) = make_float2(o[i][2], o[i][3]);
+    }
+    if (t == 0) {
+      if (g < g_max) {
+        mml[g * 2] = m0;
+        mml[g * 2 + 1] = lq0;
+      }
+      if (g + 8 < g_max) {
+        mml[(g + 8) * 2] = m1;
+        mml[(g + 8) * 2 + 1] = lq1;
+      }
+    }
+    __threadfence_block();
+    __syncwarp();
+    int old = 0;
+    if (lane == 0) old = atomicAdd(slot_cnt + slot, 1);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old == W - 1) {
+      __threadfence_block();
+      merge_piece(k);
+      __syncwarp();
+      if (lane == 0) {
+        slot_cnt[slot] = 0;
+        __threadfence_block();
+        *reinterpret_cast<volatile int *>(slot_gen + slot) = gen + 1;
+      }
+      __syncwarp();
+      if (k + S < n_pieces) issue_q(k + S);
+    }
+  };
+
+  // ---- main loop -----------------------------------------------------------
+  uint32_t qa[KS][4];
+  int cur = 0;          // piece being accumulated
+  bool have_q = false;  // qa holds the Q tile of `cur`
+  meta(0);
+  if (n_pos > 32) meta(1);
+  for (int i = 0; i < NS && i < n_pos; ++i) issue(i);
+
+  for (int i = 0; i < n_pos; ++i) {
+    if ((i & 31) == 0 && i > 0 && i + 32 < n_pos) meta((i >> 5) + 1);  // one batch ahead
+    int64_t elem;
+    int info;
+    fetch(i, &elem, &info);
+    (void)elem;
+    const int k = info >> 6, nvalid = (info >> 1) & 31, ok = info & 1;
+    while (cur < k) {
+      finalize(cur);
+      ++cur;
+      reset();
+      have_q = false;
+    }
+    if (!have_q) {
+      const bool q_in = ptx::mbar_wait_bounded(ptx::smem_u32(qbars + cur % S),
+                                               uint32_t((cur / S) & 1), kLimitNs);
+      if (!__all_sync(0xffffffffu, q_in)) {
+        failed = true;
+        break;
+      }
+      const T *qt = qslots + (cur % S) * 16 * RS;
+      const int mi2 = lane >> 3, r = lane & 7;
+      const int row = (mi2 & 1) * 8 + r;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        ptx::ldsm_x4(ptx::smem_u32(qt + row * RS + ks * 16 + (mi2 >> 1) * 8), qa[ks][0],
+                     qa[ks][1], qa[ks][2], qa[ks][3]);
+      }
+      have_q = true;
+    }
+    const int st = i % NS;
+    const bool landed =
+        ptx::mbar_wait_bounded(ptx::smem_u32(wbars + st), uint32_t((i / NS) & 1), kLimitNs);
+    if (!__all_sync(0xffffffffu, landed)) {
+      failed = true;
+      break;
+    }
+    const T *kt = wring + st * STAGE;
+    const T *vt = kt + kUnitTok * RS;
+    if (ok) {
+      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      {
+        const int mi2 = lane >> 3, r = lane & 7;
+        const int tok = (mi2 >> 1) * 8 + r;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+          uint32_t b0, b1, b2, b3;
+          ptx::ldsm_x4(ptx::smem_u32(kt + tok * RS + ks * 16 + (mi2 & 1) * 8), b0, b1, b2, b3);
+          MMA::run(s[0], qa[ks], b0, b1);
+          MMA::run(s[1], qa[ks], b2, b3);
+        }
+      }
+      float mx0, mx1;
+      if (nvalid == kUnitTok) {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) s[nt][j] *= p.scale_log2;
+      } else {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int tok = nt * 8 + 2 * t + (j & 1);
+            s[nt][j] = tok < nvalid ? s[nt][j] * p.scale_log2 : -INFINITY;
+          }
+      }
+      mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
+      mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float a0 = ptx::fast_exp2(m0 - mn0), a1 = ptx::fast_exp2(m1 - mn1);
+      m0 = mn0;
+      m1 = mn1;
+      float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        s[nt][0] = ptx::fast_exp2(s[nt][0] - mn0);
+        s[nt][1] = ptx::fast_exp2(s[nt][1] - mn0);
+        s[nt][2] = ptx::fast_exp2(s[nt][2] - mn1);
+        s[nt][3] = ptx::fast_exp2(s[nt][3] - mn1);
+        ps0 += s[nt][0] + s[nt][1];
+        ps1 += s[nt][2] + s[nt][3];
+      }
+      l0 = l0 * a0 + ps0;
+      l1 = l1 * a1 + ps1;
+      if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {
+#pragma unroll
+        for (int d = 0; d < ND; ++d) {
+          o[d][0] *= a0;
+          o[d][1] *= a0;
+          o[d][2] *= a1;
+          o[d][3] *= a1;
+        }
+      }
+      uint32_t pa[4];
+      pa[0] = MMA::pack(s[0][0], s[0][1]);
+      pa[1] = MMA::pack(s[0][2], s[0][3]);
+      pa[2] = MMA::pack(s[1][0], s[1][1]);
+      pa[3] = MMA::pack(s[1][2], s[1][3]);
+      {
+        const int mi2 = lane >> 3, r = lane & 7;
+        const int tok = (mi2 & 1) * 8 + r;
+#pragma unroll
+        for (int j = 0; j < KS; ++j) {
+          uint32_t b0, b1, b2, b3;
+          ptx::ldsm_x4_t(ptx::smem_u32(vt + tok * RS + j * 16 + (mi2 >> 1) * 8), b0, b1, b2, b3);
+          MMA::run(o[2 * j], pa, b0, b1);
+          MMA::run(o[2 * j + 1], pa, b2, b3);
+        }
+      }
+    }
+    __syncwarp();
+    if (i + NS < n_pos) issue(i + NS);
+  }
+
+  if (failed) {
+    // let copies still in flight land before the CTA ends, then report
+    for (int s = 0; s < NS; ++s) {
+      ptx::mbar_wait_bounded(ptx::smem_u32(wbars + s), 0, 1000000ull);
+      ptx::mbar_wait_bounded(ptx::smem_u32(wbars + s), 1, 1000000ull);
+    }
+    if (lane == 0) {
+      atomicOr(p.diag, int32_t(kDiagWaitTimeout));
+      s_fail = 1;
+    }
+    return;
+  }
+  // deposit every remaining piece (a warp with no unit in a piece deposits an
+  // empty partial so the merge count completes)
+  while (cur < n_pieces) {
+    if (s_fail) break;
+    finalize(cur);
+    ++cur;
+    reset();
+  }
+}
+
+// Second pass: pieces of segments that straddle CTAs, merged by log-sum-exp.
+template <typename T, int D>
+__global__ void merge(const Params p, int P) {
+  const int row = blockIdx.x;  // b * hq + h
+  const int b = row / p.hq, h = row % p.hq;
+  const int64_t *cum = p.cum_out;
+  const int B = p.batch;
+  const int nht = p.n_head_tiles, segs_per_seq = p.hkv * nht;
+  const int64_t U = cum[B];
+  if (cum[b + 1] == cum[b] || U == 0) return;
+  const int kvh = int(int64_t(h) * p.hkv / p.hq);
+  const int g_lo = int((int64_t(kvh) * p.hq + p.hkv - 1) / p.hkv);
+  const int ht = (h - g_lo) / 16;
+  const int hlo = g_lo + ht * 16;
+  const int segl = kvh * nht + ht;
+  const int nunits = int((cum[b + 1] - cum[b]) / segs_per_seq);
+  const int64_t s_start = cum[b] + int64_t(segl) * nunits;
+  const int cf = cta_of(s_start, U, P), cl = cta_of(s_start + nunits - 1, U, P);
+  if (cf == cl) return;
+  const int sc = p.segcum_out[b] + segl;
+  const int hr = h - hlo;
+  float M = -INFINITY;
+  for (int j = 0; j <= cl - cf; ++j) {
+    const int64_t gi = int64_t(sc) + cf + j;
+    M = fmaxf(M, p.part_lse[gi * p.g_max + hr]);
+  }
+  float wsum = 0.f;
+  for (int j = 0; j <= cl - cf; ++j) {
+    const int64_t gi = int64_t(sc) + cf + j;
+    wsum += ptx::fast_exp2(p.part_lse[gi * p.g_max + hr] - M);
+  }
+  const float inv = 1.f / wsum;
+  T *dst = static_cast<T *>(p.out) + int64_t(row) * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j <= cl - cf; ++j) {
+      const int64_t gi = int64_t(sc) + cf + j;
+      acc += p.part_o[(gi * p.g_max + hr) * D + d] *
+             ptx::fast_exp2(p.part_lse[gi * p.g_max + hr] - M);
+    }
+    dst[d] = ptx::from_f32<T>(acc * inv);
+  }
+}
+
+}  // namespace sk
+}  // namespace dev
+}  // namespace kcmm

@@ -97,11 +97,22 @@ def test_zero_length_rows_untouched():
         wl.close()
 
 
-@pytest.mark.parametrize("splits", [1, 2, 3, 7])
-def test_split_count_does_not_change_result(splits, monkeypatch):
-    monkeypatch.setenv("KCMM_DECODE_SPLITS", str(splits))
+@pytest.mark.parametrize("env", [
+    {"KCMM_SK_GRID": "1"},            # one CTA walks every segment
+    {"KCMM_SK_GRID": "3"},            # slices cut segments into pieces
+    {"KCMM_SK_GRID": "37"},
+    {"KCMM_SK_GRID": "5000"},         # more CTAs than units: empty slices
+    {"KCMM_SK_VARIANT": "1"},         # 4 warps x 3 stages
+    {"KCMM_SK_VARIANT": "2"},         # 8 warps x 2 stages
+    {"KCMM_DECODE_IMPL": "split", "KCMM_DECODE_SPLITS": "1"},  # split-K kernel
+    {"KCMM_DECODE_IMPL": "split", "KCMM_DECODE_SPLITS": "3"},
+    {"KCMM_DECODE_IMPL": "split", "KCMM_DECODE_SPLITS": "7"},
+])
+def test_work_split_does_not_change_result(env, monkeypatch):
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
     wl = make(batch=5, num_q_heads=32, kv_heads=8, head_dim=128, min_len=200, max_len=2000,
-              pool_blocks=1024, seed=splits)
+              pool_blocks=1024, seed=len(env))
     try:
         wl.decode()
         _torch().cuda.synchronize()
@@ -144,6 +155,23 @@ def test_v_row_kat():
                 for h in range(4):
                     e = int(wl.offsets[wl.tables[b, 0]]) + (h * 2 // 4) * 64
                     np.testing.assert_array_equal(wl.out[b, h].cpu().numpy(), vv[e:e + 64])
+    finally:
+        wl.close()
+
+
+@pytest.mark.parametrize("grid", ["2", "11"])
+def test_piece_merging_with_gqa_tiles_and_empty_rows(grid, monkeypatch):
+    """Head tiles (GQA 32), zero-length rows and pieces that straddle slices together."""
+    monkeypatch.setenv("KCMM_SK_GRID", grid)
+    wl = make(batch=6, num_q_heads=64, kv_heads=2, head_dim=128,
+              seq_lens_override=[0, 33, 700, 1, 0, 257], seed=int(grid))
+    try:
+        wl.out.fill_(5.0)
+        wl.decode()
+        _torch().cuda.synchronize()
+        o = wl.out.float().cpu().numpy()
+        assert (o[0] == 5.0).all() and (o[4] == 5.0).all()
+        check(wl)
     finally:
         wl.close()
 
