@@ -357,11 +357,9 @@ __global__ void __launch_bounds__(W * 32) kernel(const Params p) {
     const int nunits = int((cum[b + 1] - cum[b]) / segs_per_seq);
     const int64_t s_start = cum[b] + int64_t(segl) * nunits, s_end = s_start + nunits;
     const bool whole = s_start >= lo && s_end <= hi;
-    int64_t gidx = 0;
-    if (!whole) {
-      const int cf = cta_of(s_start, U, P);
-      gidx = int64_t(sc) + cf + (c - cf);
-    }
+    // pieces of segment sc live at rows sc + c (c = CTA), which never collide:
+    // the CTAs holding pieces of segment sc+1 start at or after those of sc
+    const int64_t gidx = int64_t(sc) + c;
     const float *mo = merge_o + size_t(slot) * W * g_max * D;
     const float *mml = merge_ml + size_t(slot) * W * g_max * 2;
     for (int idx = lane; idx < G * (D / 2); idx += 32) {
@@ -622,22 +620,24 @@ __global__ void merge(const Params p, int P) {
   if (cf == cl) return;
   const int sc = p.segcum_out[b] + segl;
   const int hr = h - hlo;
+  // CTAs cf..cl hold the pieces, except those whose slice is empty (more CTAs
+  // than units): they wrote nothing and are skipped.
+  auto has_piece = [&](int c) { return (int64_t(c) * U) / P != ((int64_t(c) + 1) * U) / P; };
   float M = -INFINITY;
-  for (int j = 0; j <= cl - cf; ++j) {
-    const int64_t gi = int64_t(sc) + cf + j;
-    M = fmaxf(M, p.part_lse[gi * p.g_max + hr]);
+  for (int c = cf; c <= cl; ++c) {
+    if (has_piece(c)) M = fmaxf(M, p.part_lse[(int64_t(sc) + c) * p.g_max + hr]);
   }
   float wsum = 0.f;
-  for (int j = 0; j <= cl - cf; ++j) {
-    const int64_t gi = int64_t(sc) + cf + j;
-    wsum += ptx::fast_exp2(p.part_lse[gi * p.g_max + hr] - M);
+  for (int c = cf; c <= cl; ++c) {
+    if (has_piece(c)) wsum += ptx::fast_exp2(p.part_lse[(int64_t(sc) + c) * p.g_max + hr] - M);
   }
   const float inv = 1.f / wsum;
   T *dst = static_cast<T *>(p.out) + int64_t(row) * D;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float acc = 0.f;
-    for (int j = 0; j <= cl - cf; ++j) {
-      const int64_t gi = int64_t(sc) + cf + j;
+    for (int c = cf; c <= cl; ++c) {
+      if (!has_piece(c)) continue;
+      const int64_t gi = int64_t(sc) + c;
       acc += p.part_o[(gi * p.g_max + hr) * D + d] *
              ptx::fast_exp2(p.part_lse[gi * p.g_max + hr] - M);
     }
