@@ -583,47 +583,67 @@ cudaMemPool_t scratch_pool(int dev) {
 
 // --- stream-K plan -------------------------------------------------------------
 
-using SkFn = void (*)(const sk::Params);
+using SkFn = void (*)(const sk::Params, int);
 
 struct SkPlan {
   bool ok = false;
   SkFn fn = nullptr;
   void (*merge)(const sk::Params, int) = nullptr;
   size_t smem = 0;
-  int grid = 0, warps = 4, n_head_tiles = 1, g_max = 16;
+  int grid = 0, threads = 160, ring = 0, n_head_tiles = 1, g_max = 16;
   size_t scratch_bytes = 0;
   size_t off_lse = 0, off_cum = 0, off_segcum = 0;
 };
 
-template <typename T, int D, int W, int NS>
-void sk_pick(SkPlan *pl, int batch) {
-  constexpr int S = 2;
-  pl->fn = sk::kernel<T, D, W, NS, S>;
+constexpr int kSlots = 2;
+
+// Ring depth that fills the shared memory left for `per_sm` CTAs per SM.
+template <int D, int C>
+int ring_depth(int batch, int g_max, int per_sm) {
+  const size_t budget = size_t(227 * 1024) / size_t(per_sm) - 1024;
+  const size_t fixed = sk::layout<D, C, kSlots>(batch, g_max, 0).total;
+  const size_t stage = size_t(2) * 16 * (D + 8) * 2 + 2 * 8 + 4 + 16;
+  if (fixed >= budget) return 0;
+  int r = int((budget - fixed) / stage);
+  r = std::min(r, 48);
+  r -= r % C;
+  while (r >= C && sk::layout<D, C, kSlots>(batch, g_max, r).total > budget) r -= C;
+  return r;
+}
+
+template <typename T, int D, int C>
+void sk_pick(SkPlan *pl, int batch, int per_sm) {
+  pl->fn = sk::sk_decode_kernel<T, D, C, kSlots>;
   pl->merge = sk::merge<T, D>;
-  pl->smem = sk::layout<D, W, NS, S>(batch, pl->g_max).total;
-  pl->warps = W;
+  pl->threads = (C + 1) * 32;
+  pl->ring = ring_depth<D, C>(batch, pl->g_max, per_sm);
+  if (const char *r = std::getenv("KCMM_SK_RING")) {
+    int want = std::atoi(r);
+    want -= want % C;
+    if (want >= C && want < pl->ring) pl->ring = want;
+  }
+  pl->smem = sk::layout<D, C, kSlots>(batch, pl->g_max, pl->ring).total;
 }
 
 template <typename T>
 bool sk_select(SkPlan *pl, int D, int batch, int variant) {
-#define KCMM_SK(DD)                                                   \
-  case DD:                                                            \
-    if (variant == 1) sk_pick<T, DD, 4, 3>(pl, batch);                \
-    else if (variant == 2) sk_pick<T, DD, 8, 2>(pl, batch);           \
-    else sk_pick<T, DD, 4, 2>(pl, batch);                             \
-    return true;
+  // variant: 0 = 4 consumers, 1 CTA/SM; 1 = 4 consumers, 2 CTAs/SM;
+  //          2 = 8 consumers, 1 CTA/SM; 3 = 2 consumers, 2 CTAs/SM
   switch (D) {
+#define KCMM_SK(DD)                                             \
+  case DD:                                                      \
+    if (variant == 1) sk_pick<T, DD, 4>(pl, batch, 2);          \
+    else if (variant == 2) sk_pick<T, DD, 8>(pl, batch, 1);     \
+    else if (variant == 3) sk_pick<T, DD, 2>(pl, batch, 2);     \
+    else sk_pick<T, DD, 4>(pl, batch, 1);                       \
+    return true;
     KCMM_SK(64)
     KCMM_SK(128)
-    default:
-      break;
-  }
 #undef KCMM_SK
-#define KCMM_SK1(DD)                 \
-  case DD:                           \
-    sk_pick<T, DD, 4, 2>(pl, batch); \
+#define KCMM_SK1(DD)                    \
+  case DD:                              \
+    sk_pick<T, DD, 4>(pl, batch, 1);    \
     return true;
-  switch (D) {
     KCMM_SK1(32)
     KCMM_SK1(80)
     KCMM_SK1(96)
@@ -631,10 +651,10 @@ bool sk_select(SkPlan *pl, int D, int batch, int variant) {
     KCMM_SK1(160)
     KCMM_SK1(192)
     KCMM_SK1(256)
+#undef KCMM_SK1
     default:
       return false;
   }
-#undef KCMM_SK1
 }
 
 SkPlan make_sk_plan(const DecodeArgs &a) {
@@ -651,12 +671,12 @@ SkPlan make_sk_plan(const DecodeArgs &a) {
   pl.g_max = std::min(16, g_all);
   bool found = a.dtype == Dtype::BF16 ? sk_select<__nv_bfloat16>(&pl, D, a.batch, variant)
                                       : sk_select<__half>(&pl, D, a.batch, variant);
-  if (!found || pl.smem > 227 * 1024) return pl;
+  if (!found || pl.ring < 8 || pl.smem > 227 * 1024) return pl;
   if (cudaFuncSetAttribute(pl.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pl.smem)) !=
       cudaSuccess)
     return pl;
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pl.fn, pl.warps * 32, pl.smem) !=
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pl.fn, pl.threads, pl.smem) !=
           cudaSuccess ||
       per_sm <= 0)
     return pl;
@@ -717,7 +737,7 @@ cudaError_t decode_streamk(const DecodeArgs &a, const SkPlan &pl, cudaStream_t s
   p.cum_out = reinterpret_cast<int64_t *>(base + pl.off_cum);
   p.segcum_out = reinterpret_cast<int32_t *>(base + pl.off_segcum);
   p.diag = a.diag;
-  pl.fn<<<pl.grid, pl.warps * 32, pl.smem, stream>>>(p);
+  pl.fn<<<pl.grid, pl.threads, pl.smem, stream>>>(p, pl.ring);
   e = cudaGetLastError();
   if (e == cudaSuccess) {
     pl.merge<<<a.batch * a.num_q_heads, 128, 0, stream>>>(p, pl.grid);

@@ -5,21 +5,24 @@
 // sequences, laid end to end, form one flat unit space of U units; CTA c of a
 // one-wave persistent grid of P CTAs takes the contiguous slice
 // [c*U/P, (c+1)*U/P).  Every CTA therefore streams the same number of KV bytes
-// (±1 unit) whatever the mix of context lengths, with no atomics and no work
+// (+-1 unit) whatever the mix of context lengths, with no atomics and no work
 // queue.  A slice may start or end inside a segment: the CTA then emits a
 // partial result (o, lse) for that *piece*, and a second pass merges the
 // pieces of a segment by log-sum-exp; segments that lie inside one slice are
 // written to `out` directly.
 //
-// Inside a CTA, the W warps take the units of the slice round-robin.  Each
-// warp has its own NS-stage ring of K/V tiles fed by one-row `cp.async.bulk`
-// copies (TMA engine) completing on an mbarrier per stage, and its own
-// look-ahead of page addresses (32 units computed at a time, one batch ahead),
-// so the pipeline never drains at segment boundaries.  Q tiles arrive by bulk
-// copy into S shared-memory slots, one per in-flight piece.  When a warp leaves
-// a piece it deposits (o, m, l) into the piece's merge slot; the last warp to
-// arrive merges the W deposits, frees the slot and starts the Q load of the
-// piece S places ahead.  All waits are bounded in wall time.
+// Inside a CTA the warps are specialised.  One producer warp walks the slice
+// in order and streams every unit's K and V rows into a deep shared-memory
+// ring (R stages, ~20 at head_dim 128, i.e. ~170 KB in flight per SM) with
+// one-row `cp.async.bulk` copies (TMA engine; the [bs][Hkv][D] page layout
+// needs no tensor map), a full/empty mbarrier pair per stage, and page
+// addresses looked up 32 units at a time, one batch ahead.  C consumer warps
+// take the units round-robin and run QK^T and PV on the tensor pipe
+// (m16n8k16, fp32 accumulate) with an online softmax in the log2 domain.  Q
+// tiles arrive by bulk copy into S slots, one per in-flight piece.  When a
+// consumer leaves a piece it deposits (o, m, l) into the piece's merge slot;
+// the last consumer to arrive merges the C deposits, frees the slot and starts
+// the Q load of the piece S places ahead.  Every wait is bounded in wall time.
 
 namespace kcmm {
 namespace dev {
@@ -49,32 +52,36 @@ constexpr int kUnitTok = 16;
 constexpr uint64_t kLimitNs = 1000000000ull;
 
 struct Layout {
-  size_t rings, qslots, merge_o, merge_ml, bars, cnt, cum, segcum, total;
+  size_t rings, qslots, merge_o, merge_ml, bars, info, cum, segcum, lens, total;
 };
 
 __host__ __device__ inline size_t al16(size_t x) { return (x + 15) & ~size_t(15); }
 
-template <int D, int W, int NS, int S>
-__host__ __device__ inline Layout layout(int batch, int g_max) {
+// Shared-memory plan of a CTA with C consumer warps, S piece slots and an
+// R-stage ring (identical on host and device).
+template <int D, int C, int S>
+__host__ __device__ inline Layout layout(int batch, int g_max, int R) {
   constexpr int RS = D + 8;
   Layout L;
   size_t o = 0;
   L.rings = o;
-  o = al16(o + size_t(W) * NS * 2 * kUnitTok * RS * 2);
+  o = al16(o + size_t(R) * 2 * kUnitTok * RS * 2);
   L.qslots = o;
   o = al16(o + size_t(S) * 16 * RS * 2);
   L.merge_o = o;
-  o = al16(o + size_t(S) * W * g_max * D * 4);
+  o = al16(o + size_t(S) * C * g_max * D * 4);
   L.merge_ml = o;
-  o = al16(o + size_t(S) * W * g_max * 2 * 4);
+  o = al16(o + size_t(S) * C * g_max * 2 * 4);
   L.bars = o;
-  o = al16(o + size_t(W * NS + S) * 8);
-  L.cnt = o;
-  o = al16(o + size_t(2 * S) * 4);
+  o = al16(o + size_t(2 * R + S) * 8);
+  L.info = o;
+  o = al16(o + size_t(R + 2 * S) * 4);
   L.cum = o;
   o = al16(o + size_t(batch + 1) * 8);
   L.segcum = o;
   o = al16(o + size_t(batch + 1) * 4);
+  L.lens = o;
+  o = al16(o + size_t(batch) * 4);
   L.total = o;
   return L;
 }
@@ -130,24 +137,27 @@ __device__ __forceinline__ void heads_of(int segl, int nht, int hq, int hkv, int
   *G = max(0, min(g_hi, *lo + 16) - *lo);
 }
 
-template <typename T, int D, int W, int NS, int S>
-__global__ void __launch_bounds__(W * 32) kernel(const Params p) {
+template <typename T, int D, int C, int S>
+__global__ void __launch_bounds__((C + 1) * 32) sk_decode_kernel(const Params p, int R) {
   using MMA = ptx::Mma<T>;
   constexpr int RS = D + 8;
   constexpr int STAGE = 2 * kUnitTok * RS;
   constexpr int KS = D / 16, ND = D / 8;
   extern __shared__ __align__(128) unsigned char smem[];
-  const Layout Lo = layout<D, W, NS, S>(p.batch, p.g_max);
-  T *rings = reinterpret_cast<T *>(smem + Lo.rings);
+  const Layout Lo = layout<D, C, S>(p.batch, p.g_max, R);
+  T *ring = reinterpret_cast<T *>(smem + Lo.rings);
   T *qslots = reinterpret_cast<T *>(smem + Lo.qslots);
   float *merge_o = reinterpret_cast<float *>(smem + Lo.merge_o);
   float *merge_ml = reinterpret_cast<float *>(smem + Lo.merge_ml);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Lo.bars);
-  uint64_t *qbars = bars + W * NS;
-  int *slot_cnt = reinterpret_cast<int *>(smem + Lo.cnt);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + Lo.bars);
+  uint64_t *empty = full + R;
+  uint64_t *qbars = empty + R;
+  int *info = reinterpret_cast<int *>(smem + Lo.info);
+  int *slot_cnt = info + R;
   int *slot_gen = slot_cnt + S;
   int64_t *cum = reinterpret_cast<int64_t *>(smem + Lo.cum);
   int32_t *segcum = reinterpret_cast<int32_t *>(smem + Lo.segcum);
+  int32_t *lens = reinterpret_cast<int32_t *>(smem + Lo.lens);
   __shared__ int s_fail;
 
   const int c = blockIdx.x, P = gridDim.x;
@@ -168,6 +178,7 @@ __global__ void __launch_bounds__(W * 32) kernel(const Params p) {
       if (b < B) {
         int L = p.seq_lens[b];
         L = L > 0 ? min(L, max_len) : 0;
+        lens[b] = L;
         const int nu = (L + kUnitTok - 1) / kUnitTok;
         su += int64_t(nu) * segs_per_seq;
         ss += nu > 0 ? segs_per_seq : 0;
@@ -191,9 +202,7 @@ __global__ void __launch_bounds__(W * 32) kernel(const Params p) {
       if (b < B) {
         cum[b] = ru;
         segcum[b] = rs;
-        int L = p.seq_lens[b];
-        L = L > 0 ? min(L, max_len) : 0;
-        const int nu = (L + kUnitTok - 1) / kUnitTok;
+        const int nu = (lens[b] + kUnitTok - 1) / kUnitTok;
         ru += int64_t(nu) * segs_per_seq;
         rs += nu > 0 ? segs_per_seq : 0;
       }
@@ -203,10 +212,11 @@ __global__ void __launch_bounds__(W * 32) kernel(const Params p) {
       segcum[B] = is;
     }
   }
-  if (lane == 0) {
-    for (int s = 0; s < NS; ++s) ptx::mbar_init(ptx::smem_u32(bars + warp * NS + s), 1);
-  }
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 32) {
+    for (int s = 0; s < R; ++s) {
+      ptx::mbar_init(ptx::smem_u32(full + s), 1);
+      ptx::mbar_init(ptx::smem_u32(empty + s), 1);
+    }
     for (int s = 0; s < S; ++s) {
       ptx::mbar_init(ptx::smem_u32(qbars + s), 1);
       slot_cnt[s] = 0;
@@ -219,14 +229,14 @@ __global__ void __launch_bounds__(W * 32) kernel(const Params p) {
 
   const int64_t U = cum[B];
   if (c == 0) {
-    for (int b = threadIdx.x; b <= B; b += W * 32) {
+    for (int b = threadIdx.x; b <= B; b += (C + 1) * 32) {
       p.cum_out[b] = cum[b];
       p.segcum_out[b] = segcum[b];
     }
   }
   const int64_t lo = (int64_t(c) * U) / P, hi = (int64_t(c) + 1) * U / P;
   if (lo >= hi) return;
-
+  const int n = int(hi - lo);  // units of this slice
   const Loc first = locate(lo, cum, segcum, B, segs_per_seq);
   const Loc last = locate(hi - 1, cum, segcum, B, segs_per_seq);
   const int sc0 = first.sc;
@@ -234,7 +244,7 @@ __global__ void __launch_bounds__(W * 32) kernel(const Params p) {
   const int64_t row_stride = int64_t(p.hkv) * D;
   const T *qg = static_cast<const T *>(p.q);
 
-  // Q tile of piece k -> slot k % S (rows >= G are never read into outputs).
+  // Q tile of piece k -> slot k % S, issued by one whole warp.
   auto issue_q = [&](int k) {
     const int sc = sc0 + k;
     const int b = seq_of_segment(sc, segcum, B);
@@ -251,89 +261,92 @@ __global__ void __launch_bounds__(W * 32) kernel(const Params p) {
                     qg + (int64_t(b) * p.hq + hlo + lane) * D, uint32_t(D * sizeof(T)), bar);
     }
   };
-  if (warp == 0) {
+
+  if (warp == C) {
+    // ======================= producer warp ================================
     for (int k = 0; k < S && k < n_pieces; ++k) issue_q(k);
+    const T *vak = static_cast<const T *>(p.va_k);
+    const T *vav = static_cast<const T *>(p.va_v);
+    int64_t me0 = 0, me1 = 0;
+    int mi0 = 0, mi1 = 0;  // (nvalid << 1) | ok
+    auto meta = [&](int batch_idx, int64_t *e_out, int *i_out) {
+      const int i = batch_idx * 32 + lane;
+      int64_t e = 0;
+      int inf = 0;
+      if (i < n) {
+        const Loc l = locate(lo + i, cum, segcum, B, segs_per_seq);
+        const int tok0 = l.unit * kUnitTok;
+        const int nvalid = min(kUnitTok, lens[l.b] - tok0);
+        const int blk = p.tables[int64_t(l.b) * p.max_bps + tok0 / p.bs];
+        const int kvh = l.segl / nht;
+        int ok = 0;
+        if (blk >= 0) {
+          const uint64_t off = p.offsets[blk];
+          e = int64_t(off) + int64_t(tok0 % p.bs) * row_stride + int64_t(kvh) * D;
+          ok = (off & 7) == 0 && uint64_t(e + (kUnitTok - 1) * row_stride + D) <= p.region_elems;
+        }
+        if (!ok) atomicOr(p.diag, int32_t(kDiagBadOffset));
+        inf = (nvalid << 1) | ok;
+      }
+      *e_out = e;
+      *i_out = inf;
+    };
+    meta(0, &me0, &mi0);
+    if (n > 32) meta(1, &me1, &mi1);
+    for (int i = 0; i < n; ++i) {
+      if ((i & 31) == 0 && i > 0 && i + 32 < n) {  // refill the batch after next
+        if ((i >> 5) & 1) meta((i >> 5) + 1, &me0, &mi0);
+        else meta((i >> 5) + 1, &me1, &mi1);
+      }
+      const int src = i & 31;
+      const bool odd = (i >> 5) & 1;
+      const int64_t ea = __shfl_sync(0xffffffffu, me0, src), eb = __shfl_sync(0xffffffffu, me1, src);
+      const int ia = __shfl_sync(0xffffffffu, mi0, src), ib = __shfl_sync(0xffffffffu, mi1, src);
+      const int64_t elem = odd ? eb : ea;
+      const int inf = odd ? ib : ia;
+      const int ok = inf & 1, nvalid = inf >> 1;
+      const int st = i % R;
+      if (i >= R) {  // wait until the consumer of unit i-R released the stage
+        const bool freed = ptx::mbar_wait_bounded(ptx::smem_u32(empty + st),
+                                                  uint32_t(((i / R) - 1) & 1), kLimitNs);
+        if (!__all_sync(0xffffffffu, freed)) {
+          if (lane == 0) {
+            atomicOr(p.diag, int32_t(kDiagWaitTimeout));
+            s_fail = 1;
+          }
+          break;
+        }
+      }
+      T *kt = ring + size_t(st) * STAGE;
+      T *vt = kt + kUnitTok * RS;
+      const int r = lane & 15;
+      if (lane >= 16 && r >= nvalid) {  // masked V rows hold zeros, not stale data
+        const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int cc = 0; cc < D; cc += 8) *reinterpret_cast<uint4 *>(vt + r * RS + cc) = z;
+      }
+      if (lane == 0) info[st] = ok;
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      const uint32_t bar = ptx::smem_u32(full + st);
+      if (lane == 0) ptx::mbar_arrive_expect_tx(bar, ok ? uint32_t(2 * nvalid * D * sizeof(T)) : 0u);
+      __syncwarp();
+      if (ok && r < nvalid) {
+        const T *srcp = (lane < 16 ? vak : vav) + elem + int64_t(r) * row_stride;
+        ptx::bulk_g2s(ptx::smem_u32((lane < 16 ? kt : vt) + r * RS), srcp,
+                      uint32_t(D * sizeof(T)), bar);
+      }
+    }
+    // drain: the last copies issued must land before this warp leaves (the
+    // consumers normally wait for them too; this covers a consumer that gave up)
+    for (int i = max(0, n - R); i < n; ++i) {
+      ptx::mbar_wait_bounded(ptx::smem_u32(full + (i % R)), uint32_t((i / R) & 1), 2000000ull);
+    }
+    return;
   }
 
-  // ---- per-warp unit stream ---------------------------------------------------
-  const int64_t span = hi - lo;
-  const int n_pos = span > warp ? int((span - warp + W - 1) / W) : 0;
-  int64_t me[2] = {0, 0};  // look-ahead: element offset of unit (batch*32 + lane)
-  int mi[2] = {0, 0};      // (piece << 6) | (nvalid << 1) | ok
-
-  auto meta = [&](int batch_idx) {
-    const int i = batch_idx * 32 + lane;
-    int64_t e = 0;
-    int info = 0;
-    if (i < n_pos) {
-      const int64_t u = lo + warp + int64_t(i) * W;
-      const Loc l = locate(u, cum, segcum, B, segs_per_seq);
-      int L = p.seq_lens[l.b];
-      L = min(L, max_len);
-      const int tok0 = l.unit * kUnitTok;
-      const int nvalid = min(kUnitTok, L - tok0);
-      const int blk = p.tables[int64_t(l.b) * p.max_bps + tok0 / p.bs];
-      const int kvh = l.segl / nht;
-      int ok = 0;
-      if (blk >= 0) {
-        const uint64_t off = p.offsets[blk];
-        e = int64_t(off) + int64_t(tok0 % p.bs) * row_stride + int64_t(kvh) * D;
-        ok = (off & 7) == 0 && uint64_t(e + (kUnitTok - 1) * row_stride + D) <= p.region_elems;
-      }
-      if (!ok) atomicOr(p.diag, int32_t(kDiagBadOffset));
-      info = ((l.sc - sc0) << 6) | (nvalid << 1) | ok;
-    }
-    if (batch_idx & 1) {
-      me[1] = e;
-      mi[1] = info;
-    } else {
-      me[0] = e;
-      mi[0] = info;
-    }
-  };
-
-  const T *vak = static_cast<const T *>(p.va_k);
-  const T *vav = static_cast<const T *>(p.va_v);
-  T *wring = rings + warp * NS * STAGE;
-  uint64_t *wbars = bars + warp * NS;
-
-  auto fetch = [&](int i, int64_t *e, int *info) {
-    const int buf = (i >> 5) & 1;
-    const int64_t e0 = __shfl_sync(0xffffffffu, me[0], i & 31);
-    const int64_t e1 = __shfl_sync(0xffffffffu, me[1], i & 31);
-    const int i0 = __shfl_sync(0xffffffffu, mi[0], i & 31);
-    const int i1 = __shfl_sync(0xffffffffu, mi[1], i & 31);
-    *e = buf ? e1 : e0;
-    *info = buf ? i1 : i0;
-  };
-
-  auto issue = [&](int i) {
-    int64_t elem;
-    int info;
-    fetch(i, &elem, &info);
-    const int ok = info & 1, nvalid = (info >> 1) & 31;
-    const int st = i % NS;
-    const uint32_t bar = ptx::smem_u32(wbars + st);
-    T *kt = wring + st * STAGE;
-    T *vt = kt + kUnitTok * RS;
-    const int r = lane & 15;
-    if (lane >= 16 && r >= nvalid) {  // masked V rows hold zeros, not stale data
-      const uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int cc = 0; cc < D; cc += 8) *reinterpret_cast<uint4 *>(vt + r * RS + cc) = z;
-    }
-    ptx::fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) ptx::mbar_arrive_expect_tx(bar, ok ? uint32_t(2 * nvalid * D * sizeof(T)) : 0u);
-    __syncwarp();
-    if (ok && r < nvalid) {
-      const T *src = (lane < 16 ? vak : vav) + elem + int64_t(r) * row_stride;
-      ptx::bulk_g2s(ptx::smem_u32((lane < 16 ? kt : vt) + r * RS), src,
-                    uint32_t(D * sizeof(T)), bar);
-    }
-  };
-
-  // accumulators of the current piece
+  // ======================== consumer warps ================================
+  const int g = lane >> 2, t = lane & 3;
   float o[ND][4];
   float m0, m1, l0, l1;
   auto reset = [&]() {
@@ -343,10 +356,7 @@ __global__ void __launch_bounds__(W * 32) kernel(const Params p) {
     l0 = l1 = 0.f;
   };
   reset();
-  const int g = lane >> 2, t = lane & 3;
-  bool failed = false;
 
-  // Merge the W deposits of piece k (called by the last warp to deposit).
   auto merge_piece = [&](int k) {
     const int slot = k % S;
     const int sc = sc0 + k;
@@ -360,16 +370,16 @@ __global__ void __launch_bounds__(W * 32) kernel(const Params p) {
     // pieces of segment sc live at rows sc + c (c = CTA), which never collide:
     // the CTAs holding pieces of segment sc+1 start at or after those of sc
     const int64_t gidx = int64_t(sc) + c;
-    const float *mo = merge_o + size_t(slot) * W * g_max * D;
-    const float *mml = merge_ml + size_t(slot) * W * g_max * 2;
+    const float *mo = merge_o + size_t(slot) * C * g_max * D;
+    const float *mml = merge_ml + size_t(slot) * C * g_max * 2;
     for (int idx = lane; idx < G * (D / 2); idx += 32) {
       const int h = idx / (D / 2), d = (idx % (D / 2)) * 2;
       float M = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < W; ++w) M = fmaxf(M, mml[(w * g_max + h) * 2]);
+      for (int w = 0; w < C; ++w) M = fmaxf(M, mml[(w * g_max + h) * 2]);
       float Ls = 0.f, x0 = 0.f, x1 = 0.f;
 #pragma unroll
-      for (int w = 0; w < W; ++w) {
+      for (int w = 0; w < C; ++w) {
         const float mw = mml[(w * g_max + h) * 2];
         if (mw == -INFINITY) continue;
         const float sc_w = ptx::fast_exp2(mw - M);
@@ -412,8 +422,8 @@ __global__ void __launch_bounds__(W * 32) kernel(const Params p) {
     lq0 += __shfl_xor_sync(0xffffffffu, lq0, 2);
     float lq1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
     lq1 += __shfl_xor_sync(0xffffffffu, lq1, 2);
-    float *mo = merge_o + (size_t(slot) * W + warp) * g_max * D;
-    float *mml = merge_ml + (size_t(slot) * W + warp) * g_max * 2;
+    float *mo = merge_o + (size_t(slot) * C + warp) * g_max * D;
+    float *mml = merge_ml + (size_t(slot) * C + warp) * g_max * 2;
 #pragma unroll
     for (int i = 0; i < ND; ++i) {
       const int d = i * 8 + 2 * t;
@@ -436,7 +446,7 @@ __global__ void __launch_bounds__(W * 32) kernel(const Params p) {
     int old = 0;
     if (lane == 0) old = atomicAdd(slot_cnt + slot, 1);
     old = __shfl_sync(0xffffffffu, old, 0);
-    if (old == W - 1) {
+    if (old == C - 1) {
       __threadfence_block();
       merge_piece(k);
       __syncwarp();
@@ -450,21 +460,14 @@ __global__ void __launch_bounds__(W * 32) kernel(const Params p) {
     }
   };
 
-  // ---- main loop -----------------------------------------------------------
   uint32_t qa[KS][4];
-  int cur = 0;          // piece being accumulated
-  bool have_q = false;  // qa holds the Q tile of `cur`
-  meta(0);
-  if (n_pos > 32) meta(1);
-  for (int i = 0; i < NS && i < n_pos; ++i) issue(i);
-
-  for (int i = 0; i < n_pos; ++i) {
-    if ((i & 31) == 0 && i > 0 && i + 32 < n_pos) meta((i >> 5) + 1);  // one batch ahead
-    int64_t elem;
-    int info;
-    fetch(i, &elem, &info);
-    (void)elem;
-    const int k = info >> 6, nvalid = (info >> 1) & 31, ok = info & 1;
+  int cur = 0;
+  bool have_q = false;
+  bool failed = false;
+  for (int i = warp; i < n; i += C) {
+    const Loc l = locate(lo + i, cum, segcum, B, segs_per_seq);
+    const int k = l.sc - sc0;
+    const int nvalid = min(kUnitTok, lens[l.b] - l.unit * kUnitTok);
     while (cur < k) {
       finalize(cur);
       ++cur;
@@ -488,16 +491,16 @@ __global__ void __launch_bounds__(W * 32) kernel(const Params p) {
       }
       have_q = true;
     }
-    const int st = i % NS;
+    const int st = i % R;
     const bool landed =
-        ptx::mbar_wait_bounded(ptx::smem_u32(wbars + st), uint32_t((i / NS) & 1), kLimitNs);
+        ptx::mbar_wait_bounded(ptx::smem_u32(full + st), uint32_t((i / R) & 1), kLimitNs);
     if (!__all_sync(0xffffffffu, landed)) {
       failed = true;
       break;
     }
-    const T *kt = wring + st * STAGE;
+    const T *kt = ring + size_t(st) * STAGE;
     const T *vt = kt + kUnitTok * RS;
-    if (ok) {
+    if (info[st]) {
       float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
       {
         const int mi2 = lane >> 3, r = lane & 7;
@@ -510,7 +513,6 @@ __global__ void __launch_bounds__(W * 32) kernel(const Params p) {
           MMA::run(s[1], qa[ks], b2, b3);
         }
       }
-      float mx0, mx1;
       if (nvalid == kUnitTok) {
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
@@ -525,8 +527,8 @@ __global__ void __launch_bounds__(W * 32) kernel(const Params p) {
             s[nt][j] = tok < nvalid ? s[nt][j] * p.scale_log2 : -INFINITY;
           }
       }
-      mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
-      mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
+      float mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
+      float mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
@@ -574,23 +576,17 @@ __global__ void __launch_bounds__(W * 32) kernel(const Params p) {
       }
     }
     __syncwarp();
-    if (i + NS < n_pos) issue(i + NS);
+    if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(empty + st));  // release the stage
   }
-
   if (failed) {
-    // let copies still in flight land before the CTA ends, then report
-    for (int s = 0; s < NS; ++s) {
-      ptx::mbar_wait_bounded(ptx::smem_u32(wbars + s), 0, 1000000ull);
-      ptx::mbar_wait_bounded(ptx::smem_u32(wbars + s), 1, 1000000ull);
-    }
     if (lane == 0) {
       atomicOr(p.diag, int32_t(kDiagWaitTimeout));
       s_fail = 1;
     }
     return;
   }
-  // deposit every remaining piece (a warp with no unit in a piece deposits an
-  // empty partial so the merge count completes)
+  // deposit every remaining piece (a consumer with no unit in a piece deposits
+  // an empty partial so that the merge count completes)
   while (cur < n_pieces) {
     if (s_fail) break;
     finalize(cur);
