@@ -180,12 +180,15 @@ __global__ void __launch_bounds__(W * 32) decode_kernel(const DecodeParams p) {
     T *ks_tile = wst + st * C::STAGE;
     T *vs_tile = ks_tile + kUnit * C::RS;
     const int r = lane & 15;
-    if (r >= nvalid && lane >= 16) {  // masked V rows must hold zeros, not stale data
-      uint4 z = make_uint4(0, 0, 0, 0);
+    if (nvalid < kUnit) {
+      if (r >= nvalid && lane >= 16) {  // masked V rows must hold zeros, not stale data
+        uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
-      for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4 *>(vs_tile + r * C::RS + c) = z;
+        for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4 *>(vs_tile + r * C::RS + c) = z;
+      }
+      // order these generic writes before later TMA writes into the same stage
+      ptx::fence_proxy_async_smem();
     }
-    ptx::fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
       ptx::mbar_arrive_expect_tx(bar, ok ? uint32_t(2 * nvalid * D * sizeof(T)) : 0u);

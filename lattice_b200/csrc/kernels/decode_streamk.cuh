@@ -320,13 +320,16 @@ __global__ void __launch_bounds__((C + 1) * 32) sk_decode_kernel(const Params p,
       T *kt = ring + size_t(st) * STAGE;
       T *vt = kt + kUnitTok * RS;
       const int r = lane & 15;
-      if (lane >= 16 && r >= nvalid) {  // masked V rows hold zeros, not stale data
-        const uint4 z = make_uint4(0, 0, 0, 0);
+      if (nvalid < kUnitTok) {
+        if (lane >= 16 && r >= nvalid) {  // masked V rows hold zeros, not stale data
+          const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
-        for (int cc = 0; cc < D; cc += 8) *reinterpret_cast<uint4 *>(vt + r * RS + cc) = z;
+          for (int cc = 0; cc < D; cc += 8) *reinterpret_cast<uint4 *>(vt + r * RS + cc) = z;
+        }
+        // order these generic writes before later TMA writes into the same stage
+        ptx::fence_proxy_async_smem();
       }
       if (lane == 0) info[st] = ok;
-      ptx::fence_proxy_async_smem();
       __syncwarp();
       const uint32_t bar = ptx::smem_u32(full + st);
       if (lane == 0) ptx::mbar_arrive_expect_tx(bar, ok ? uint32_t(2 * nvalid * D * sizeof(T)) : 0u);
