@@ -40,10 +40,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(20000u)
+      : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
 }
@@ -55,14 +55,15 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 // Bounded wait: gives up (returns false) once `limit_ns` of wall time has
-// passed without the phase completing.
+// passed without the phase completing.  try_wait blocks for a short,
+// hardware-chosen time per call; the timer is read every 64 polls.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
                                                   uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  for (;;) {
+  for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > limit_ns) return false;
+    if ((n & 63) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 
