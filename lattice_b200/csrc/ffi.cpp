@@ -470,6 +470,8 @@ static int decode_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, u
   a.scale = scale;
   a.diag = p->diag_word();
   if (const char *fs = std::getenv("KCMM_DECODE_SPLITS")) a.force_splits = std::atoi(fs);
+  a.tensor_maps = p->tensor_maps(layer, int(hkv), int(hd));
+  a.region_tokens = p->region_bytes / (uint64_t(hkv) * hd * 2);
   if (check_launch(h, op, kcmm::dev::decode_attention(a, S(stream)))) return -1;
   if (sync) {
     cudaError_t e = cudaDeviceSynchronize();

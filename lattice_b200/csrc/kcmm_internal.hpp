@@ -57,6 +57,9 @@ std::unique_ptr<Vmm> make_cuda_vmm(int device);
 // on such a pool.  KCMM_HOST_VMM_FAIL_AFTER=n makes the (n+1)-th
 // create_and_map fail, to exercise the out-of-memory paths.
 std::unique_ptr<Vmm> make_host_vmm();
+// Encode a 128-byte CUtensorMap for TMA loads of 16-token x 64-dim tiles of
+// one kv head from the region at `base` (see vmm.cpp).  False if unsupported.
+bool encode_kv_tensor_map(void *out, uint64_t base, uint64_t tokens, int kv_heads, int head_dim);
 
 // ---------------------------------------------------------------------------
 // Allocator
@@ -209,6 +212,9 @@ class Pool {
   void step_destinations(const uint32_t *seqs, const uint32_t *positions, size_t batch,
                          std::vector<int64_t> *dst_elems);
   void slot_destinations(const int64_t *slots, size_t batch, std::vector<int64_t> *dst_elems);
+  // Cached TMA descriptors of a layer's K and V regions for a (kv_heads,
+  // head_dim) view; nullptr when the shape has no TMA path.
+  const void *tensor_maps(size_t layer, int kv_heads, int head_dim);
   void use_device() const;  // make the pool's device current
   void require_device(const char *what) const;
   int32_t *diag_word() const { return diag_; }  // device int32, sticky error bits
@@ -241,6 +247,13 @@ class Pool {
   SwapTier &tier_locked();
 
   std::unique_ptr<Vmm> vmm_;
+  std::mutex tmap_mu_;
+  struct TmapEntry {
+    size_t layer;
+    int kv_heads, head_dim;
+    alignas(64) unsigned char maps[2][128];
+  };
+  std::vector<std::unique_ptr<TmapEntry>> tmaps_;
   std::mutex mu_;  // guards everything below
   BlockAllocator alloc_;
   std::vector<BlockInfo> blocks_;

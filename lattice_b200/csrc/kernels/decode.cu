@@ -20,6 +20,7 @@
 //     rate; softmax is online, in the log2 domain, with warp shuffles.
 //   * warps of a CTA merge in shared memory; splits of a sequence merge in a
 //     second pass through their log-sum-exp.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -605,7 +606,7 @@ template <int D, int C>
 int ring_depth(int batch, int g_max, int per_sm) {
   const size_t budget = size_t(227 * 1024) / size_t(per_sm) - 1024;
   const size_t fixed = sk::layout<D, C, kSlots>(batch, g_max, 0).total;
-  const size_t stage = size_t(2) * 16 * (D + 8) * 2 + 2 * 8 + 4 + 16;
+  const size_t stage = size_t(2) * 16 * D * 2 + 2 * 8 + 4 + 16;
   if (fixed >= budget) return 0;
   int r = int((budget - fixed) / stage);
   r = std::min(r, 48);
@@ -647,11 +648,6 @@ bool sk_select(SkPlan *pl, int D, int batch, int variant) {
   case DD:                              \
     sk_pick<T, DD, 4>(pl, batch, 1);    \
     return true;
-    KCMM_SK1(32)
-    KCMM_SK1(80)
-    KCMM_SK1(96)
-    KCMM_SK1(112)
-    KCMM_SK1(160)
     KCMM_SK1(192)
     KCMM_SK1(256)
 #undef KCMM_SK1
@@ -663,7 +659,7 @@ bool sk_select(SkPlan *pl, int D, int batch, int variant) {
 SkPlan make_sk_plan(const DecodeArgs &a) {
   SkPlan pl;
   const int D = a.head_dim;
-  if (D % 16 != 0 || a.block_size % 16 != 0 || a.batch > 2048) return pl;
+  if (D % 64 != 0 || a.block_size % 16 != 0 || a.batch > 2048 || !a.tensor_maps) return pl;
   if ((reinterpret_cast<uintptr_t>(a.q) & 15) != 0) return pl;
   const char *impl = std::getenv("KCMM_DECODE_IMPL");
   if (impl && std::strcmp(impl, "split") == 0) return pl;
@@ -717,7 +713,11 @@ cudaError_t decode_streamk(const DecodeArgs &a, const SkPlan &pl, cudaStream_t s
   bool owned = false;
   cudaError_t e = scratch_acquire(a, pl.scratch_bytes, stream, &scratch, &owned);
   if (e != cudaSuccess) return e;
-  sk::Params p = {};
+  sk::Params p;
+  std::memset(static_cast<void *>(&p), 0, sizeof(p));
+  std::memcpy(&p.tmk, a.tensor_maps, sizeof(CUtensorMap));
+  std::memcpy(&p.tmv, static_cast<const char *>(a.tensor_maps) + 128, sizeof(CUtensorMap));
+  p.region_tokens = a.region_tokens;
   p.q = a.q;
   p.out = a.out;
   p.tables = a.block_tables;

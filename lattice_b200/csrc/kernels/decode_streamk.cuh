@@ -28,7 +28,10 @@ namespace kcmm {
 namespace dev {
 namespace sk {
 
-struct Params {
+struct alignas(64) Params {
+  CUtensorMap tmk;  // K region of the layer: {D, Hkv, tokens}, box {64, 1, 16}, 128B swizzle
+  CUtensorMap tmv;  // V region, same view
+  uint64_t region_tokens;
   const void *q;
   void *out;
   const int32_t *tables;
@@ -64,8 +67,8 @@ __host__ __device__ inline Layout layout(int batch, int g_max, int R) {
   constexpr int RS = D + 8;
   Layout L;
   size_t o = 0;
-  L.rings = o;
-  o = al16(o + size_t(R) * 2 * kUnitTok * RS * 2);
+  L.rings = o;  // 1024-aligned at run time; stage = K + V tiles of 16 x D, 128B-swizzled
+  o = al16(o + size_t(R) * 2 * kUnitTok * D * 2);
   L.qslots = o;
   o = al16(o + size_t(S) * 16 * RS * 2);
   L.merge_o = o;
@@ -82,7 +85,7 @@ __host__ __device__ inline Layout layout(int batch, int g_max, int R) {
   o = al16(o + size_t(batch + 1) * 4);
   L.lens = o;
   o = al16(o + size_t(batch) * 4);
-  L.total = o;
+  L.total = o + 1024;  // slack for aligning the base to 1024 bytes
   return L;
 }
 
@@ -138,14 +141,18 @@ __device__ __forceinline__ void heads_of(int segl, int nht, int hq, int hkv, int
 }
 
 template <typename T, int D, int C, int S>
-__global__ void __launch_bounds__((C + 1) * 32) sk_decode_kernel(const Params p, int R) {
+__global__ void __launch_bounds__((C + 1) * 32)
+    sk_decode_kernel(const __grid_constant__ Params p, int R) {
   using MMA = ptx::Mma<T>;
   constexpr int RS = D + 8;
-  constexpr int STAGE = 2 * kUnitTok * RS;
+  constexpr int HALVES = D / 64;                 // 64-dim half-tiles per K or V tile
+  constexpr int TILE_B = HALVES * kUnitTok * 128;  // bytes of one K (or V) tile
   constexpr int KS = D / 16, ND = D / 8;
-  extern __shared__ __align__(128) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const Layout Lo = layout<D, C, S>(p.batch, p.g_max, R);
-  T *ring = reinterpret_cast<T *>(smem + Lo.rings);
+  unsigned char *ring = smem + Lo.rings;
   T *qslots = reinterpret_cast<T *>(smem + Lo.qslots);
   float *merge_o = reinterpret_cast<float *>(smem + Lo.merge_o);
   float *merge_ml = reinterpret_cast<float *>(smem + Lo.merge_ml);
@@ -265,13 +272,11 @@ __global__ void __launch_bounds__((C + 1) * 32) sk_decode_kernel(const Params p,
   if (warp == C) {
     // ======================= producer warp ================================
     for (int k = 0; k < S && k < n_pieces; ++k) issue_q(k);
-    const T *vak = static_cast<const T *>(p.va_k);
-    const T *vav = static_cast<const T *>(p.va_v);
-    int64_t me0 = 0, me1 = 0;
-    int mi0 = 0, mi1 = 0;  // (nvalid << 1) | ok
-    auto meta = [&](int batch_idx, int64_t *e_out, int *i_out) {
+    int64_t me0 = 0, me1 = 0;  // token coordinate of unit (batch*32 + lane)
+    int mi0 = 0, mi1 = 0;      // (kvh << 6) | (nvalid << 1) | ok
+    auto meta = [&](int batch_idx, int64_t *z_out, int *i_out) {
       const int i = batch_idx * 32 + lane;
-      int64_t e = 0;
+      int64_t z = 0;
       int inf = 0;
       if (i < n) {
         const Loc l = locate(lo + i, cum, segcum, B, segs_per_seq);
@@ -282,13 +287,13 @@ __global__ void __launch_bounds__((C + 1) * 32) sk_decode_kernel(const Params p,
         int ok = 0;
         if (blk >= 0) {
           const uint64_t off = p.offsets[blk];
-          e = int64_t(off) + int64_t(tok0 % p.bs) * row_stride + int64_t(kvh) * D;
-          ok = (off & 7) == 0 && uint64_t(e + (kUnitTok - 1) * row_stride + D) <= p.region_elems;
+          z = int64_t(off / uint64_t(row_stride)) + tok0 % p.bs;
+          ok = off % uint64_t(row_stride) == 0 && uint64_t(z + nvalid) <= p.region_tokens;
         }
         if (!ok) atomicOr(p.diag, int32_t(kDiagBadOffset));
-        inf = (nvalid << 1) | ok;
+        inf = (kvh << 6) | (nvalid << 1) | ok;
       }
-      *e_out = e;
+      *z_out = z;
       *i_out = inf;
     };
     meta(0, &me0, &mi0);
@@ -300,11 +305,11 @@ __global__ void __launch_bounds__((C + 1) * 32) sk_decode_kernel(const Params p,
       }
       const int src = i & 31;
       const bool odd = (i >> 5) & 1;
-      const int64_t ea = __shfl_sync(0xffffffffu, me0, src), eb = __shfl_sync(0xffffffffu, me1, src);
+      const int64_t za = __shfl_sync(0xffffffffu, me0, src), zb = __shfl_sync(0xffffffffu, me1, src);
       const int ia = __shfl_sync(0xffffffffu, mi0, src), ib = __shfl_sync(0xffffffffu, mi1, src);
-      const int64_t elem = odd ? eb : ea;
+      const int64_t z = odd ? zb : za;
       const int inf = odd ? ib : ia;
-      const int ok = inf & 1, nvalid = inf >> 1;
+      const int ok = inf & 1, kvh = inf >> 6;
       const int st = i % R;
       if (i >= R) {  // wait until the consumer of unit i-R released the stage
         const bool freed = ptx::mbar_wait_bounded(ptx::smem_u32(empty + st),
@@ -317,30 +322,22 @@ __global__ void __launch_bounds__((C + 1) * 32) sk_decode_kernel(const Params p,
           break;
         }
       }
-      T *kt = ring + size_t(st) * STAGE;
-      T *vt = kt + kUnitTok * RS;
-      const int r = lane & 15;
-      if (nvalid < kUnitTok) {
-        if (lane >= 16 && r >= nvalid) {  // masked V rows hold zeros, not stale data
-          const uint4 z = make_uint4(0, 0, 0, 0);
+      if (lane == 0) {
+        info[st] = ok;
+        const uint32_t bar = ptx::smem_u32(full + st);
+        ptx::mbar_arrive_expect_tx(bar, ok ? uint32_t(2 * TILE_B) : 0u);
+        if (ok) {
+          const uint32_t kt = ptx::smem_u32(ring + size_t(st) * 2 * TILE_B);
 #pragma unroll
-          for (int cc = 0; cc < D; cc += 8) *reinterpret_cast<uint4 *>(vt + r * RS + cc) = z;
+          for (int h = 0; h < HALVES; ++h) {
+            ptx::tma_load_3d(kt + h * kUnitTok * 128, &p.tmk, h * 64, kvh, int(z), bar);
+            ptx::tma_load_3d(kt + TILE_B + h * kUnitTok * 128, &p.tmv, h * 64, kvh, int(z), bar);
+          }
         }
-        // order these generic writes before later TMA writes into the same stage
-        ptx::fence_proxy_async_smem();
       }
-      if (lane == 0) info[st] = ok;
       __syncwarp();
-      const uint32_t bar = ptx::smem_u32(full + st);
-      if (lane == 0) ptx::mbar_arrive_expect_tx(bar, ok ? uint32_t(2 * nvalid * D * sizeof(T)) : 0u);
-      __syncwarp();
-      if (ok && r < nvalid) {
-        const T *srcp = (lane < 16 ? vak : vav) + elem + int64_t(r) * row_stride;
-        ptx::bulk_g2s(ptx::smem_u32((lane < 16 ? kt : vt) + r * RS), srcp,
-                      uint32_t(D * sizeof(T)), bar);
-      }
     }
-    // drain: the last copies issued must land before this warp leaves (the
+    // drain: the last loads issued must land before this warp leaves (the
     // consumers normally wait for them too; this covers a consumer that gave up)
     for (int i = max(0, n - R); i < n; ++i) {
       ptx::mbar_wait_bounded(ptx::smem_u32(full + (i % R)), uint32_t((i / R) & 1), 2000000ull);
@@ -501,8 +498,24 @@ __global__ void __launch_bounds__((C + 1) * 32) sk_decode_kernel(const Params p,
       failed = true;
       break;
     }
-    const T *kt = ring + size_t(st) * STAGE;
-    const T *vt = kt + kUnitTok * RS;
+    const uint32_t kt = ptx::smem_u32(ring + size_t(st) * 2 * TILE_B);
+    const uint32_t vt = kt + TILE_B;
+    // byte address of 16-byte chunk (token, dim d0..d0+7) in a swizzled tile
+    auto sw = [](uint32_t tile, int tok, int d0) -> uint32_t {
+      return tile + (d0 >> 6) * (kUnitTok * 128) + tok * 128 +
+             ((((d0 & 63) >> 3) ^ (tok & 7)) << 4);
+    };
+    if (info[st] && nvalid < kUnitTok) {
+      // rows past the context hold whatever the page holds: zero V there so
+      // that P = 0 meets 0, not a stale NaN
+      for (int idx = lane; idx < (kUnitTok - nvalid) * (D / 8); idx += 32) {
+        const int tok = nvalid + idx / (D / 8), d0 = (idx % (D / 8)) * 8;
+        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(sw(vt, tok, d0)), "r"(0)
+                     : "memory");
+      }
+      ptx::fence_proxy_async_smem();  // before the stage is refilled by TMA
+      __syncwarp();
+    }
     if (info[st]) {
       float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
       {
@@ -511,7 +524,7 @@ __global__ void __launch_bounds__((C + 1) * 32) sk_decode_kernel(const Params p,
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
           uint32_t b0, b1, b2, b3;
-          ptx::ldsm_x4(ptx::smem_u32(kt + tok * RS + ks * 16 + (mi2 & 1) * 8), b0, b1, b2, b3);
+          ptx::ldsm_x4(sw(kt, tok, ks * 16 + (mi2 & 1) * 8), b0, b1, b2, b3);
           MMA::run(s[0], qa[ks], b0, b1);
           MMA::run(s[1], qa[ks], b2, b3);
         }
@@ -572,7 +585,7 @@ __global__ void __launch_bounds__((C + 1) * 32) sk_decode_kernel(const Params p,
 #pragma unroll
         for (int j = 0; j < KS; ++j) {
           uint32_t b0, b1, b2, b3;
-          ptx::ldsm_x4_t(ptx::smem_u32(vt + tok * RS + j * 16 + (mi2 >> 1) * 8), b0, b1, b2, b3);
+          ptx::ldsm_x4_t(sw(vt, tok, j * 16 + (mi2 >> 1) * 8), b0, b1, b2, b3);
           MMA::run(o[2 * j], pa, b0, b1);
           MMA::run(o[2 * j + 1], pa, b2, b3);
         }

@@ -78,6 +78,18 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
       : "memory");
 }
 
+// --- tensor TMA: 3-D tiled load global -> shared ---------------------------------
+// tmap: generic address of a __grid_constant__ CUtensorMap; (x, y, z) element
+// coordinates (x * 2 bytes must be a multiple of 16).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *tmap, int x, int y, int z,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
 // --- ldmatrix / mma -----------------------------------------------------------
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,

@@ -37,6 +37,10 @@ struct DecodeArgs {
   float *scratch;
   size_t scratch_bytes;
   int force_splits;  // >0 overrides the split heuristic (tests)
+  // Two 128-byte TMA descriptors (K then V region) for this layer and
+  // (kv_heads, head_dim), or null; region_tokens = tokens they span.
+  const void *tensor_maps;
+  uint64_t region_tokens;
 };
 
 // Bytes of split-K scratch decode_attention needs for these arguments

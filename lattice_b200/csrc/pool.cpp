@@ -194,6 +194,27 @@ Pool::~Pool() {
   vmm_->release_all();
 }
 
+const void *Pool::tensor_maps(size_t layer, int kv_heads, int head_dim) {
+  if (!vmm_->is_device() || layer >= num_layers || kv_heads <= 0 || head_dim % 64 != 0) {
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> g(tmap_mu_);
+  for (auto &e : tmaps_) {
+    if (e->layer == layer && e->kv_heads == kv_heads && e->head_dim == head_dim) return e->maps;
+  }
+  auto e = std::make_unique<TmapEntry>();
+  e->layer = layer;
+  e->kv_heads = kv_heads;
+  e->head_dim = head_dim;
+  const uint64_t tokens = region_bytes / (uint64_t(kv_heads) * head_dim * 2);
+  if (!encode_kv_tensor_map(e->maps[0], va_k[layer], tokens, kv_heads, head_dim) ||
+      !encode_kv_tensor_map(e->maps[1], va_v[layer], tokens, kv_heads, head_dim)) {
+    return nullptr;
+  }
+  tmaps_.push_back(std::move(e));
+  return tmaps_.back()->maps;
+}
+
 void Pool::use_device() const {
   if (vmm_->is_device()) cudaSetDevice(cfg_.device);
 }

@@ -21,6 +21,7 @@ namespace kcmm {
 namespace {
 
 struct DriverApi {
+  PFN_cuTensorMapEncodeTiled_v12000 encode_tiled = nullptr;
   PFN_cuMemAddressReserve_v10020 reserve = nullptr;
   PFN_cuMemAddressFree_v10020 address_free = nullptr;
   PFN_cuMemCreate_v10020 create = nullptr;
@@ -47,6 +48,7 @@ const DriverApi &driver() {
   static std::string failure;
   std::call_once(once, [] {
     try {
+      fetch("cuTensorMapEncodeTiled", &api.encode_tiled);
       fetch("cuMemAddressReserve", &api.reserve);
       fetch("cuMemAddressFree", &api.address_free);
       fetch("cuMemCreate", &api.create);
@@ -174,6 +176,28 @@ class HostVmm final : public Vmm {
 }  // namespace
 
 std::unique_ptr<Vmm> make_cuda_vmm(int device) { return std::make_unique<CudaVmm>(device); }
+
+bool encode_kv_tensor_map(void *out, uint64_t base, uint64_t tokens, int kv_heads, int head_dim) {
+  // 3-D view of a layer region: {head_dim, kv_heads, tokens} of 16-bit words;
+  // box {64, 1, 16} = 16 tokens x 64 dims of one head, 128B-swizzled in smem.
+  if (head_dim % 64 != 0 || tokens == 0 || tokens > (uint64_t(1) << 32)) return false;
+  cuuint64_t dims[3] = {cuuint64_t(head_dim), cuuint64_t(kv_heads), cuuint64_t(tokens)};
+  cuuint64_t strides[2] = {cuuint64_t(head_dim) * 2, cuuint64_t(head_dim) * 2 * kv_heads};
+  cuuint32_t box[3] = {64, 1, 16};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const DriverApi *api = nullptr;
+  try {
+    api = &driver();
+  } catch (const Error &) {
+    return false;
+  }
+  CUresult r = api->encode_tiled(
+      static_cast<CUtensorMap *>(out), CU_TENSOR_MAP_DATA_TYPE_UINT16, 3,
+      reinterpret_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
 std::unique_ptr<Vmm> make_host_vmm() { return std::make_unique<HostVmm>(); }
 
 }  // namespace kcmm
