@@ -113,10 +113,10 @@ __device__ __forceinline__ Loc locate(int64_t u, const int64_t *cum, const int32
   }
   Loc r;
   r.b = lo;
-  r.nunits = int((cum[lo + 1] - cum[lo]) / segs_per_seq);
-  const int64_t rem = u - cum[lo];
-  r.segl = int(rem / r.nunits);
-  r.unit = int(rem - int64_t(r.segl) * r.nunits);
+  r.nunits = int(cum[lo + 1] - cum[lo]) / segs_per_seq;  // one sequence: fits 32 bits
+  const int rem = int(u - cum[lo]);
+  r.segl = rem / r.nunits;
+  r.unit = rem - r.segl * r.nunits;
   r.seg_start = cum[lo] + int64_t(r.segl) * r.nunits;
   r.sc = segcum[lo] + r.segl;
   return r;
@@ -272,43 +272,69 @@ __global__ void __launch_bounds__((C + 1) * 32)
   if (warp == C) {
     // ======================= producer warp ================================
     for (int k = 0; k < S && k < n_pieces; ++k) issue_q(k);
-    int64_t me0 = 0, me1 = 0;  // token coordinate of unit (batch*32 + lane)
-    int mi0 = 0, mi1 = 0;      // (kvh << 6) | (nvalid << 1) | ok
-    auto meta = [&](int batch_idx, int64_t *z_out, int *i_out) {
-      const int i = batch_idx * 32 + lane;
-      int64_t z = 0;
-      int inf = 0;
+    // Page lookups run as a 3-stage register pipeline over batches of 32
+    // consecutive units (lane j holds unit 32*batch + j): at the start of
+    // batch t the table entries of batch t+2 and the offsets of batch t+1 are
+    // requested, and the coordinates of batch t are finished from values that
+    // arrived one batch earlier -- no instruction waits on a fresh load.
+    int a_blk = -1, a_inf = 0;   // stage A: block id (+ unit facts) of batch t+2
+    uint64_t b_off = 0;          // stage B: page offset of batch t+1
+    int b_blk = -1, b_inf = 0;
+    int64_t c_z = 0;             // stage C: TMA token coordinate of batch t
+    int c_inf = 0;               // (kvh << 6) | (nvalid << 1) | ok
+    // unit facts packed as (kvh << 16) | ((tok0 % bs) << 5 ... ) would overflow for
+    // large block sizes, so keep them in two registers per stage
+    int a_tok = 0, b_tok = 0;
+    auto stage_a = [&](int batch) {  // locate + table entry of `batch`
+      const int i = batch * 32 + lane;
+      a_blk = -1;
+      a_inf = 0;
+      a_tok = 0;
       if (i < n) {
         const Loc l = locate(lo + i, cum, segcum, B, segs_per_seq);
         const int tok0 = l.unit * kUnitTok;
         const int nvalid = min(kUnitTok, lens[l.b] - tok0);
-        const int blk = p.tables[int64_t(l.b) * p.max_bps + tok0 / p.bs];
-        const int kvh = l.segl / nht;
-        int ok = 0;
-        if (blk >= 0) {
-          const uint64_t off = p.offsets[blk];
-          z = int64_t(off / uint64_t(row_stride)) + tok0 % p.bs;
-          ok = off % uint64_t(row_stride) == 0 && uint64_t(z + nvalid) <= p.region_tokens;
+        a_blk = p.tables[int64_t(l.b) * p.max_bps + tok0 / p.bs];
+        a_inf = ((l.segl / nht) << 6) | (nvalid << 1) | 1;
+        a_tok = tok0 % p.bs;
+      }
+    };
+    auto stage_b = [&]() {  // request the offsets of the block ids from stage A
+      b_blk = a_blk;
+      b_inf = a_inf;
+      b_tok = a_tok;
+      b_off = (b_inf & 1) && b_blk >= 0 ? p.offsets[b_blk] : 0;
+    };
+    auto stage_c = [&]() {  // finish coordinates from stage B
+      int ok = 0;
+      int64_t z = 0;
+      if (b_inf & 1) {
+        if (b_blk >= 0) {
+          z = int64_t(b_off / uint64_t(row_stride)) + b_tok;
+          const int nvalid = (b_inf >> 1) & 31;
+          ok = b_off % uint64_t(row_stride) == 0 && uint64_t(z + nvalid) <= p.region_tokens;
         }
         if (!ok) atomicOr(p.diag, int32_t(kDiagBadOffset));
-        inf = (kvh << 6) | (nvalid << 1) | ok;
       }
-      *z_out = z;
-      *i_out = inf;
+      c_z = z;
+      c_inf = (b_inf & ~1) | ok;
     };
-    meta(0, &me0, &mi0);
-    if (n > 32) meta(1, &me1, &mi1);
+    // prologue: batch 0 -> C, batch 1 -> B, batch 2 -> A
+    stage_a(0);
+    stage_b();
+    stage_c();
+    stage_a(1);
+    stage_b();
+    stage_a(2);
     for (int i = 0; i < n; ++i) {
-      if ((i & 31) == 0 && i > 0 && i + 32 < n) {  // refill the batch after next
-        if ((i >> 5) & 1) meta((i >> 5) + 1, &me0, &mi0);
-        else meta((i >> 5) + 1, &me1, &mi1);
-      }
       const int src = i & 31;
-      const bool odd = (i >> 5) & 1;
-      const int64_t za = __shfl_sync(0xffffffffu, me0, src), zb = __shfl_sync(0xffffffffu, me1, src);
-      const int ia = __shfl_sync(0xffffffffu, mi0, src), ib = __shfl_sync(0xffffffffu, mi1, src);
-      const int64_t z = odd ? zb : za;
-      const int inf = odd ? ib : ia;
+      if (src == 0 && i > 0) {  // rotate: B -> C, A -> B, new A
+        stage_c();
+        stage_b();
+        stage_a((i >> 5) + 2);
+      }
+      const int64_t z = __shfl_sync(0xffffffffu, c_z, src);
+      const int inf = __shfl_sync(0xffffffffu, c_inf, src);
       const int ok = inf & 1, kvh = inf >> 6;
       const int st = i % R;
       if (i >= R) {  // wait until the consumer of unit i-R released the stage
@@ -322,20 +348,20 @@ __global__ void __launch_bounds__((C + 1) * 32)
           break;
         }
       }
+      const uint32_t bar = ptx::smem_u32(full + st);
       if (lane == 0) {
         info[st] = ok;
-        const uint32_t bar = ptx::smem_u32(full + st);
         ptx::mbar_arrive_expect_tx(bar, ok ? uint32_t(2 * TILE_B) : 0u);
-        if (ok) {
-          const uint32_t kt = ptx::smem_u32(ring + size_t(st) * 2 * TILE_B);
-#pragma unroll
-          for (int h = 0; h < HALVES; ++h) {
-            ptx::tma_load_3d(kt + h * kUnitTok * 128, &p.tmk, h * 64, kvh, int(z), bar);
-            ptx::tma_load_3d(kt + TILE_B + h * kUnitTok * 128, &p.tmv, h * 64, kvh, int(z), bar);
-          }
-        }
       }
       __syncwarp();
+      if (ok && lane < 2 * HALVES) {  // one lane per 16 x 64 half-tile
+        const int h = lane % HALVES;
+        const bool v = lane >= HALVES;
+        const uint32_t dst = ptx::smem_u32(ring + size_t(st) * 2 * TILE_B) + (v ? TILE_B : 0) +
+                             h * kUnitTok * 128;
+        ptx::tma_load_3d(dst, v ? static_cast<const void *>(&p.tmv) : &p.tmk, h * 64, kvh,
+                         int(z), bar);
+      }
     }
     // drain: the last loads issued must land before this warp leaves (the
     // consumers normally wait for them too; this covers a consumer that gave up)
@@ -464,10 +490,35 @@ __global__ void __launch_bounds__((C + 1) * 32)
   int cur = 0;
   bool have_q = false;
   bool failed = false;
+  // segment cursor: advanced incrementally (units only move forward)
+  int cb = 0, csegl = 0, cnu = 1, csc = 0;
+  int64_t cstart = 0, cend = 0;
+  if (warp < n) {
+    const Loc l0 = locate(lo + warp, cum, segcum, B, segs_per_seq);
+    cb = l0.b;
+    csegl = l0.segl;
+    cnu = l0.nunits;
+    csc = l0.sc;
+    cstart = l0.seg_start;
+    cend = cstart + cnu;
+  }
   for (int i = warp; i < n; i += C) {
-    const Loc l = locate(lo + i, cum, segcum, B, segs_per_seq);
-    const int k = l.sc - sc0;
-    const int nvalid = min(kUnitTok, lens[l.b] - l.unit * kUnitTok);
+    const int64_t u = lo + i;
+    while (u >= cend) {  // next segment (sequences without units hold none)
+      if (++csegl == segs_per_seq) {
+        csegl = 0;
+        do {
+          ++cb;
+        } while (cum[cb + 1] == cum[cb]);
+        cnu = int(cum[cb + 1] - cum[cb]) / segs_per_seq;
+      }
+      ++csc;
+      cstart = cend;
+      cend = cstart + cnu;
+    }
+    const int unit = int(u - cstart);
+    const int k = csc - sc0;
+    const int nvalid = min(kUnitTok, lens[cb] - unit * kUnitTok);
     while (cur < k) {
       finalize(cur);
       ++cur;
