@@ -326,42 +326,53 @@ __global__ void __launch_bounds__((C + 1) * 32)
     stage_a(1);
     stage_b();
     stage_a(2);
-    for (int i = 0; i < n; ++i) {
-      const int src = i & 31;
-      if (src == 0 && i > 0) {  // rotate: B -> C, A -> B, new A
+    // Units are issued four at a time: lane group g (8 lanes) serves unit
+    // i + g, so the four empty-waits, expect_tx arrivals and TMA issues of a
+    // quad overlap instead of forming one long dependent chain.
+    constexpr int kQuad = 4;
+    const int grp = lane >> 3, gl = lane & 7;
+    const unsigned gmask = 0xffu << (grp * 8);
+    bool stop = false;
+    for (int i0 = 0; i0 < n && !stop; i0 += kQuad) {
+      if ((i0 & 31) == 0 && i0 > 0) {  // rotate: B -> C, A -> B, new A
         stage_c();
         stage_b();
-        stage_a((i >> 5) + 2);
+        stage_a((i0 >> 5) + 2);
       }
-      const int64_t z = __shfl_sync(0xffffffffu, c_z, src);
-      const int inf = __shfl_sync(0xffffffffu, c_inf, src);
-      const int ok = inf & 1, kvh = inf >> 6;
+      const int i = i0 + grp;
+      const int64_t z = __shfl_sync(0xffffffffu, c_z, i & 31);
+      const int inf = __shfl_sync(0xffffffffu, c_inf, i & 31);
+      const bool live = i < n;
+      const int ok = live && (inf & 1), kvh = inf >> 6;
       const int st = i % R;
-      if (i >= R) {  // wait until the consumer of unit i-R released the stage
-        const bool freed = ptx::mbar_wait_bounded(ptx::smem_u32(empty + st),
-                                                  uint32_t(((i / R) - 1) & 1), kLimitNs);
-        if (!__all_sync(0xffffffffu, freed)) {
-          if (lane == 0) {
-            atomicOr(p.diag, int32_t(kDiagWaitTimeout));
-            s_fail = 1;
-          }
-          break;
+      bool freed = true;
+      if (live && i >= R) {  // wait until the consumer of unit i-R released the stage
+        freed = ptx::mbar_wait_bounded(ptx::smem_u32(empty + st),
+                                       uint32_t(((i / R) - 1) & 1), kLimitNs);
+      }
+      if (!__all_sync(0xffffffffu, freed)) {
+        if (lane == 0) {
+          atomicOr(p.diag, int32_t(kDiagWaitTimeout));
+          s_fail = 1;
         }
+        stop = true;
+        break;
       }
       const uint32_t bar = ptx::smem_u32(full + st);
-      if (lane == 0) {
+      if (live && gl == 0) {
         info[st] = ok;
         ptx::mbar_arrive_expect_tx(bar, ok ? uint32_t(2 * TILE_B) : 0u);
       }
-      __syncwarp();
-      if (ok && lane < 2 * HALVES) {  // one lane per 16 x 64 half-tile
-        const int h = lane % HALVES;
-        const bool v = lane >= HALVES;
+      __syncwarp(gmask);
+      if (ok && gl < 2 * HALVES) {  // one lane per 16 x 64 half-tile
+        const int h = gl % HALVES;
+        const bool v = gl >= HALVES;
         const uint32_t dst = ptx::smem_u32(ring + size_t(st) * 2 * TILE_B) + (v ? TILE_B : 0) +
                              h * kUnitTok * 128;
         ptx::tma_load_3d(dst, v ? static_cast<const void *>(&p.tmv) : &p.tmk, h * 64, kvh,
                          int(z), bar);
       }
+      __syncwarp();
     }
     // drain: the last loads issued must land before this warp leaves (the
     // consumers normally wait for them too; this covers a consumer that gave up)
