@@ -615,11 +615,11 @@ int ring_depth(int batch, int g_max, int per_sm) {
   return r;
 }
 
-template <typename T, int D, int C>
+template <typename T, int D, int C, int NP>
 void sk_pick(SkPlan *pl, int batch, int per_sm) {
-  pl->fn = sk::sk_decode_kernel<T, D, C, kSlots>;
+  pl->fn = sk::sk_decode_kernel<T, D, C, NP, kSlots>;
   pl->merge = sk::merge<T, D>;
-  pl->threads = (C + 1) * 32;
+  pl->threads = (C + NP) * 32;
   pl->ring = ring_depth<D, C>(batch, pl->g_max, per_sm);
   if (const char *r = std::getenv("KCMM_SK_RING")) {
     int want = std::atoi(r);
@@ -631,22 +631,22 @@ void sk_pick(SkPlan *pl, int batch, int per_sm) {
 
 template <typename T>
 bool sk_select(SkPlan *pl, int D, int batch, int variant) {
-  // variant: 0 = 4 consumers, 1 CTA/SM; 1 = 4 consumers, 2 CTAs/SM;
-  //          2 = 8 consumers, 1 CTA/SM; 3 = 2 consumers, 2 CTAs/SM
+  // variant: 0 = 4 consumers + 2 producers, 1 CTA/SM;  1 = 4 + 1, 2 CTAs/SM;
+  //          2 = 6 consumers + 2 producers, 1 CTA/SM;  3 = 4 + 3, 1 CTA/SM
   switch (D) {
 #define KCMM_SK(DD)                                             \
   case DD:                                                      \
-    if (variant == 1) sk_pick<T, DD, 4>(pl, batch, 2);          \
-    else if (variant == 2) sk_pick<T, DD, 8>(pl, batch, 1);     \
-    else if (variant == 3) sk_pick<T, DD, 2>(pl, batch, 2);     \
-    else sk_pick<T, DD, 4>(pl, batch, 1);                       \
+    if (variant == 1) sk_pick<T, DD, 4, 1>(pl, batch, 2);       \
+    else if (variant == 2) sk_pick<T, DD, 6, 2>(pl, batch, 1);  \
+    else if (variant == 3) sk_pick<T, DD, 4, 3>(pl, batch, 1);  \
+    else sk_pick<T, DD, 4, 2>(pl, batch, 1);                    \
     return true;
     KCMM_SK(64)
     KCMM_SK(128)
 #undef KCMM_SK
-#define KCMM_SK1(DD)                    \
-  case DD:                              \
-    sk_pick<T, DD, 4>(pl, batch, 1);    \
+#define KCMM_SK1(DD)                     \
+  case DD:                               \
+    sk_pick<T, DD, 4, 2>(pl, batch, 1);  \
     return true;
     KCMM_SK1(192)
     KCMM_SK1(256)

@@ -140,8 +140,8 @@ __device__ __forceinline__ void heads_of(int segl, int nht, int hq, int hkv, int
   *G = max(0, min(g_hi, *lo + 16) - *lo);
 }
 
-template <typename T, int D, int C, int S>
-__global__ void __launch_bounds__((C + 1) * 32)
+template <typename T, int D, int C, int NP, int S>
+__global__ void __launch_bounds__((C + NP) * 32)
     sk_decode_kernel(const __grid_constant__ Params p, int R) {
   using MMA = ptx::Mma<T>;
   constexpr int RS = D + 8;
@@ -236,7 +236,7 @@ __global__ void __launch_bounds__((C + 1) * 32)
 
   const int64_t U = cum[B];
   if (c == 0) {
-    for (int b = threadIdx.x; b <= B; b += (C + 1) * 32) {
+    for (int b = threadIdx.x; b <= B; b += (C + NP) * 32) {
       p.cum_out[b] = cum[b];
       p.segcum_out[b] = segcum[b];
     }
@@ -269,24 +269,34 @@ __global__ void __launch_bounds__((C + 1) * 32)
     }
   };
 
-  if (warp == C) {
-    // ======================= producer warp ================================
-    for (int k = 0; k < S && k < n_pieces; ++k) issue_q(k);
-    // Page lookups run as a 3-stage register pipeline over batches of 32
-    // consecutive units (lane j holds unit 32*batch + j): at the start of
-    // batch t the table entries of batch t+2 and the offsets of batch t+1 are
-    // requested, and the coordinates of batch t are finished from values that
-    // arrived one batch earlier -- no instruction waits on a fresh load.
-    int a_blk = -1, a_inf = 0;   // stage A: block id (+ unit facts) of batch t+2
-    uint64_t b_off = 0;          // stage B: page offset of batch t+1
-    int b_blk = -1, b_inf = 0;
-    int64_t c_z = 0;             // stage C: TMA token coordinate of batch t
-    int c_inf = 0;               // (kvh << 6) | (nvalid << 1) | ok
-    // unit facts packed as (kvh << 16) | ((tok0 % bs) << 5 ... ) would overflow for
-    // large block sizes, so keep them in two registers per stage
-    int a_tok = 0, b_tok = 0;
-    auto stage_a = [&](int batch) {  // locate + table entry of `batch`
-      const int i = batch * 32 + lane;
+  if (warp >= C) {
+    // ======================= producer warps ===============================
+    // NP producer warps share the ring: producer pw issues the quads of units
+    // q*4 .. q*4+3 with q % NP == pw (a warp issues its TMA loads one after
+    // another, so several warps are needed to keep the ring full).
+    const int pw = warp - C;
+    if (pw == 0) {
+      for (int k = 0; k < S && k < n_pieces; ++k) issue_q(k);
+    }
+    if (lane == 0) {
+      ptx::prefetch_tensormap(&p.tmk);
+      ptx::prefetch_tensormap(&p.tmv);
+    }
+    constexpr int kQuad = 4;
+    // lane l of batch t stands for unit 4 * (pw + NP * (8t + l/4)) + l%4
+    auto unit_of = [&](int batch, int l) { return kQuad * (pw + NP * (8 * batch + (l >> 2))) + (l & 3); };
+    // Page lookups run as a 3-stage register pipeline over these batches: at
+    // the start of batch t the table entries of batch t+2 and the offsets of
+    // batch t+1 are requested, and the coordinates of batch t are finished
+    // from values that arrived one batch earlier -- no instruction waits on a
+    // fresh load.
+    int a_blk = -1, a_inf = 0, a_tok = 0;  // stage A: block id + unit facts of batch t+2
+    uint64_t b_off = 0;                    // stage B: page offset of batch t+1
+    int b_blk = -1, b_inf = 0, b_tok = 0;
+    int64_t c_z = 0;                       // stage C: TMA token coordinate of batch t
+    int c_inf = 0;                         // (kvh << 6) | (nvalid << 1) | ok
+    auto stage_a = [&](int batch) {
+      const int i = unit_of(batch, lane);
       a_blk = -1;
       a_inf = 0;
       a_tok = 0;
@@ -299,13 +309,13 @@ __global__ void __launch_bounds__((C + 1) * 32)
         a_tok = tok0 % p.bs;
       }
     };
-    auto stage_b = [&]() {  // request the offsets of the block ids from stage A
+    auto stage_b = [&]() {
       b_blk = a_blk;
       b_inf = a_inf;
       b_tok = a_tok;
       b_off = (b_inf & 1) && b_blk >= 0 ? p.offsets[b_blk] : 0;
     };
-    auto stage_c = [&]() {  // finish coordinates from stage B
+    auto stage_c = [&]() {
       int ok = 0;
       int64_t z = 0;
       if (b_inf & 1) {
@@ -319,29 +329,27 @@ __global__ void __launch_bounds__((C + 1) * 32)
       c_z = z;
       c_inf = (b_inf & ~1) | ok;
     };
-    // prologue: batch 0 -> C, batch 1 -> B, batch 2 -> A
     stage_a(0);
     stage_b();
     stage_c();
     stage_a(1);
     stage_b();
     stage_a(2);
-    // Units are issued four at a time: lane group g (8 lanes) serves unit
-    // i + g, so the four empty-waits, expect_tx arrivals and TMA issues of a
-    // quad overlap instead of forming one long dependent chain.
-    constexpr int kQuad = 4;
     const int grp = lane >> 3, gl = lane & 7;
     const unsigned gmask = 0xffu << (grp * 8);
     bool stop = false;
-    for (int i0 = 0; i0 < n && !stop; i0 += kQuad) {
-      if ((i0 & 31) == 0 && i0 > 0) {  // rotate: B -> C, A -> B, new A
+    for (int qi = 0; !stop; ++qi) {  // qi-th quad of this producer
+      const int i0 = kQuad * (pw + NP * qi);
+      if (i0 >= n) break;
+      if ((qi & 7) == 0 && qi > 0) {  // rotate: B -> C, A -> B, new A
         stage_c();
         stage_b();
-        stage_a((i0 >> 5) + 2);
+        stage_a((qi >> 3) + 2);
       }
       const int i = i0 + grp;
-      const int64_t z = __shfl_sync(0xffffffffu, c_z, i & 31);
-      const int inf = __shfl_sync(0xffffffffu, c_inf, i & 31);
+      const int src = ((qi & 7) << 2) | grp;
+      const int64_t z = __shfl_sync(0xffffffffu, c_z, src);
+      const int inf = __shfl_sync(0xffffffffu, c_inf, src);
       const bool live = i < n;
       const int ok = live && (inf & 1), kvh = inf >> 6;
       const int st = i % R;
@@ -374,10 +382,15 @@ __global__ void __launch_bounds__((C + 1) * 32)
       }
       __syncwarp();
     }
-    // drain: the last loads issued must land before this warp leaves (the
+    // drain: the last loads this warp issued must land before it leaves (the
     // consumers normally wait for them too; this covers a consumer that gave up)
-    for (int i = max(0, n - R); i < n; ++i) {
-      ptx::mbar_wait_bounded(ptx::smem_u32(full + (i % R)), uint32_t((i / R) & 1), 2000000ull);
+    for (int qi = 0;; ++qi) {
+      const int i0 = kQuad * (pw + NP * qi);
+      if (i0 >= n) break;
+      if (lane < kQuad && i0 + lane < n && i0 + lane >= n - R) {
+        const int i = i0 + lane;
+        ptx::mbar_wait_bounded(ptx::smem_u32(full + (i % R)), uint32_t((i / R) & 1), 2000000ull);
+      }
     }
     return;
   }

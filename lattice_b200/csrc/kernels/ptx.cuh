@@ -90,6 +90,11 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *tmap, int 
       : "memory");
 }
 
+// Warm the TMA descriptor cache for a tensor map held in kernel parameters.
+__device__ __forceinline__ void prefetch_tensormap(const void *tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
 // --- ldmatrix / mma -----------------------------------------------------------
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
