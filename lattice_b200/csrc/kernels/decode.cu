@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(W * 32) decode_kernel(const DecodeParams p) {
   if (threadIdx.x == 0) s_fail = 0;
   uint64_t *my_bars = bars + warp * NS;
   if (lane == 0) {
-    for (int s = 0; s < NS; ++s) ptx::mbar_init(ptx::smem_u32(my_bars + s), 1);
+    for (int s = 0; s < NS; ++s) ptx::mbar_init(ptx::smem_u32(my_bars + s), 32);
   }
   ptx::fence_proxy_async_smem();
   __syncthreads();
@@ -171,35 +171,29 @@ __global__ void __launch_bounds__(W * 32) decode_kernel(const DecodeParams p) {
   const T *vav = static_cast<const T *>(p.va_v);
   T *wst = stages + warp * NS * C::STAGE;
 
+  // One unit = 16 K rows + 16 V rows of D elements, moved as 16-byte cp.async
+  // chunks spread over the 32 lanes (rows past the context are zero-filled);
+  // each lane then arrives on the stage's mbarrier once its copies land.
   auto issue = [&](int k) {
     const int st = k % NS;
     const uint32_t bar = ptx::smem_u32(my_bars + st);
     const int64_t elem = __shfl_sync(0xffffffffu, my_elem, k);
     const int ok = __shfl_sync(0xffffffffu, my_ok, k);
     const int u = u_begin + warp + k * W;
-    const int nvalid = min(kUnit, seq_len - u * kUnit);
-    T *ks_tile = wst + st * C::STAGE;
-    T *vs_tile = ks_tile + kUnit * C::RS;
-    const int r = lane & 15;
-    if (nvalid < kUnit) {
-      if (r >= nvalid && lane >= 16) {  // masked V rows must hold zeros, not stale data
-        uint4 z = make_uint4(0, 0, 0, 0);
+    const int nvalid = ok ? min(kUnit, seq_len - u * kUnit) : 0;
+    const uint32_t ks_tile = ptx::smem_u32(wst + st * C::STAGE);
+    const uint32_t vs_tile = ks_tile + kUnit * C::RS * sizeof(T);
+    constexpr int CPR = D / 8;  // 16-byte chunks per row
 #pragma unroll
-        for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4 *>(vs_tile + r * C::RS + c) = z;
-      }
-      // order these generic writes before later TMA writes into the same stage
-      ptx::fence_proxy_async_smem();
+    for (int j = lane; j < kUnit * CPR; j += 32) {
+      const int r = j / CPR, c = j % CPR;
+      const int64_t off = elem + int64_t(r) * row_stride + c * 8;
+      const uint32_t n = r < nvalid ? 16u : 0u;
+      const uint32_t so = uint32_t((r * C::RS + c * 8) * sizeof(T));
+      ptx::cp_async16(ks_tile + so, vak + (n ? off : 0), n);
+      ptx::cp_async16(vs_tile + so, vav + (n ? off : 0), n);
     }
-    __syncwarp();
-    if (lane == 0) {
-      ptx::mbar_arrive_expect_tx(bar, ok ? uint32_t(2 * nvalid * D * sizeof(T)) : 0u);
-    }
-    __syncwarp();
-    if (ok && r < nvalid) {
-      const T *src = (lane < 16 ? vak : vav) + elem + int64_t(r) * row_stride;
-      T *dst = (lane < 16 ? ks_tile : vs_tile) + r * C::RS;
-      ptx::bulk_g2s(ptx::smem_u32(dst), src, uint32_t(D * sizeof(T)), bar);
-    }
+    ptx::cp_async_mbar_arrive(bar);
   };
 
   // ---- main loop -----------------------------------------------------------

@@ -78,6 +78,19 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
       : "memory");
 }
 
+// --- cp.async (LDGSTS): 16-byte global -> shared, zero-filled when src_bytes is 0 ---
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+
+// The mbarrier receives one arrival from this thread once all of the thread's
+// earlier cp.async copies have landed (its expected count must include it).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 // --- tensor TMA: 3-D tiled load global -> shared ---------------------------------
 // tmap: generic address of a __grid_constant__ CUtensorMap; (x, y, z) element
 // coordinates (x * 2 bytes must be a multiple of 16).
