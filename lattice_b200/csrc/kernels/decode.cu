@@ -650,21 +650,85 @@ bool sk_select(SkPlan *pl, int D, int batch, int variant) {
   }
 }
 
+// --- stream-K with per-warp cp.async rings (default) -----------------------------
+
+template <int D, int W>
+int ld_stages(int batch, int g_max) {
+  for (int ns = 4; ns >= 2; --ns) {
+    if (sk::layout_ld<D, W, kSlots>(batch, g_max, ns).total <= size_t(227 * 1024 - 1024)) return ns;
+  }
+  return 0;
+}
+
+template <typename T, int D, int W>
+void ld_pick(SkPlan *pl, int batch) {
+  pl->fn = sk::sk_ld_kernel<T, D, W, kSlots>;
+  pl->merge = sk::merge<T, D>;
+  pl->threads = W * 32;
+  pl->ring = ld_stages<D, W>(batch, pl->g_max);
+  if (const char *r = std::getenv("KCMM_SK_RING")) {
+    const int want = std::atoi(r);
+    if (want >= 2 && want < pl->ring) pl->ring = want;
+  }
+  pl->smem = sk::layout_ld<D, W, kSlots>(batch, pl->g_max, pl->ring).total;
+}
+
+template <typename T>
+bool ld_select(SkPlan *pl, int D, int batch, int variant) {
+  // variant: 0 = 8 warps, 1 = 6 warps, 2 = 4 warps, 3 = 12 warps (1 CTA per SM)
+  switch (D) {
+#define KCMM_LD(DD)                                         \
+  case DD:                                                  \
+    if (variant == 1) ld_pick<T, DD, 6>(pl, batch);         \
+    else if (variant == 2) ld_pick<T, DD, 4>(pl, batch);    \
+    else if (variant == 3) ld_pick<T, DD, 12>(pl, batch);   \
+    else ld_pick<T, DD, 8>(pl, batch);                      \
+    return true;
+    KCMM_LD(64)
+    KCMM_LD(128)
+#undef KCMM_LD
+#define KCMM_LD1(DD)                 \
+  case DD:                           \
+    ld_pick<T, DD, 8>(pl, batch);    \
+    return true;
+    KCMM_LD1(32)
+    KCMM_LD1(80)
+    KCMM_LD1(96)
+    KCMM_LD1(112)
+    KCMM_LD1(160)
+    KCMM_LD1(192)
+    KCMM_LD1(256)
+#undef KCMM_LD1
+    default:
+      return false;
+  }
+}
+
 SkPlan make_sk_plan(const DecodeArgs &a) {
   SkPlan pl;
   const int D = a.head_dim;
-  if (D % 64 != 0 || a.block_size % 16 != 0 || a.batch > 2048 || !a.tensor_maps) return pl;
+  if (D % 16 != 0 || a.block_size % 16 != 0 || a.batch > 2048) return pl;
   if ((reinterpret_cast<uintptr_t>(a.q) & 15) != 0) return pl;
   const char *impl = std::getenv("KCMM_DECODE_IMPL");
   if (impl && std::strcmp(impl, "split") == 0) return pl;
+  const bool tma = impl && std::strcmp(impl, "tma") == 0;
+  if (tma && (D % 64 != 0 || !a.tensor_maps)) return pl;
   int variant = 0;
   if (const char *v = std::getenv("KCMM_SK_VARIANT")) variant = std::atoi(v);
   const int g_all = (a.num_q_heads + a.kv_heads - 1) / a.kv_heads;
   pl.n_head_tiles = (g_all + 15) / 16;
   pl.g_max = std::min(16, g_all);
-  bool found = a.dtype == Dtype::BF16 ? sk_select<__nv_bfloat16>(&pl, D, a.batch, variant)
-                                      : sk_select<__half>(&pl, D, a.batch, variant);
-  if (!found || pl.ring < 8 || pl.smem > 227 * 1024) return pl;
+  bool found;
+  if (tma) {
+    found = a.dtype == Dtype::BF16 ? sk_select<__nv_bfloat16>(&pl, D, a.batch, variant)
+                                   : sk_select<__half>(&pl, D, a.batch, variant);
+    if (pl.ring < 8) found = false;
+  } else {
+    found = a.dtype == Dtype::BF16 ? ld_select<__nv_bfloat16>(&pl, D, a.batch, variant)
+                                   : ld_select<__half>(&pl, D, a.batch, variant);
+    if (pl.ring < 2) found = false;
+  }
+  if (!found || pl.smem > 227 * 1024) return pl;
   if (cudaFuncSetAttribute(pl.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pl.smem)) !=
       cudaSuccess)
     return pl;

@@ -102,8 +102,12 @@ def test_zero_length_rows_untouched():
     {"KCMM_SK_GRID": "3"},            # slices cut segments into pieces
     {"KCMM_SK_GRID": "37"},
     {"KCMM_SK_GRID": "5000"},         # more CTAs than units: empty slices
-    {"KCMM_SK_VARIANT": "1"},         # 4 warps x 3 stages
-    {"KCMM_SK_VARIANT": "2"},         # 8 warps x 2 stages
+    {"KCMM_SK_VARIANT": "1"},         # 6 warps
+    {"KCMM_SK_VARIANT": "2"},         # 4 warps
+    {"KCMM_SK_VARIANT": "3"},         # 12 warps
+    {"KCMM_SK_RING": "2"},            # shallow rings
+    {"KCMM_DECODE_IMPL": "tma"},      # TMA producer-warp variant
+    {"KCMM_DECODE_IMPL": "tma", "KCMM_SK_GRID": "3"},
     {"KCMM_DECODE_IMPL": "split", "KCMM_DECODE_SPLITS": "1"},  # split-K kernel
     {"KCMM_DECODE_IMPL": "split", "KCMM_DECODE_SPLITS": "3"},
     {"KCMM_DECODE_IMPL": "split", "KCMM_DECODE_SPLITS": "7"},
