@@ -773,8 +773,10 @@ cudaError_t decode_streamk(const DecodeArgs &a, const SkPlan &pl, cudaStream_t s
   if (e != cudaSuccess) return e;
   sk::Params p;
   std::memset(static_cast<void *>(&p), 0, sizeof(p));
-  std::memcpy(&p.tmk, a.tensor_maps, sizeof(CUtensorMap));
-  std::memcpy(&p.tmv, static_cast<const char *>(a.tensor_maps) + 128, sizeof(CUtensorMap));
+  if (a.tensor_maps) {  // only the TMA variant reads them
+    std::memcpy(&p.tmk, a.tensor_maps, sizeof(CUtensorMap));
+    std::memcpy(&p.tmv, static_cast<const char *>(a.tensor_maps) + 128, sizeof(CUtensorMap));
+  }
   p.region_tokens = a.region_tokens;
   p.q = a.q;
   p.out = a.out;
