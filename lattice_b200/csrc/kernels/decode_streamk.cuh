@@ -918,7 +918,8 @@ __global__ void __launch_bounds__(W * 32) sk_ld_kernel(const Params p, int NS) {
       const int r = q / CPR, ch = q % CPR;
       const uint32_t nb = r < nvalid ? 16u : 0u;
       const int64_t off = nb ? e + int64_t(r) * row_stride + ch * 8 : 0;
-      const uint32_t so = uint32_t(r * (D * 2) + ((ch ^ (r & 7)) << 4));
+      const int pc = ch < (CPR & ~7) ? (ch ^ (r & 7)) : ch;  // swizzle full 8-chunk groups only
+      const uint32_t so = uint32_t(r * (D * 2) + (pc << 4));
       ptx::cp_async16(kt + so, vak + off, nb);
       ptx::cp_async16(vt + so, vav + off, nb);
     }
@@ -1124,7 +1125,9 @@ __global__ void __launch_bounds__(W * 32) sk_ld_kernel(const Params p, int NS) {
     const uint32_t kt = ptx::smem_u32(wring + size_t(st) * 2 * TILE_B);
     const uint32_t vt = kt + TILE_B;
     auto sw = [](uint32_t tile, int tok, int d0) -> uint32_t {
-      return tile + tok * (D * 2) + ((((d0 >> 3)) ^ (tok & 7)) << 4);
+      const int ch = d0 >> 3;
+      const int pc = ch < (CPR & ~7) ? (ch ^ (tok & 7)) : ch;  // same rule as the stores
+      return tile + tok * (D * 2) + (pc << 4);
     };
     if (inf & 1) {
       const int nvalid = inf >> 1;
