@@ -675,14 +675,14 @@ void ld_pick(SkPlan *pl, int batch) {
 
 template <typename T>
 bool ld_select(SkPlan *pl, int D, int batch, int variant) {
-  // variant: 0 = 8 warps, 1 = 6 warps, 2 = 4 warps, 3 = 12 warps (1 CTA per SM)
+  // variant: 0 = 12 warps, 1 = 10 warps, 2 = 8 warps, 3 = 6 warps (1 CTA per SM)
   switch (D) {
 #define KCMM_LD(DD)                                         \
   case DD:                                                  \
-    if (variant == 1) ld_pick<T, DD, 6>(pl, batch);         \
-    else if (variant == 2) ld_pick<T, DD, 4>(pl, batch);    \
-    else if (variant == 3) ld_pick<T, DD, 12>(pl, batch);   \
-    else ld_pick<T, DD, 8>(pl, batch);                      \
+    if (variant == 1) ld_pick<T, DD, 10>(pl, batch);        \
+    else if (variant == 2) ld_pick<T, DD, 8>(pl, batch);    \
+    else if (variant == 3) ld_pick<T, DD, 6>(pl, batch);    \
+    else ld_pick<T, DD, 12>(pl, batch);                     \
     return true;
     KCMM_LD(64)
     KCMM_LD(128)

@@ -905,7 +905,10 @@ __global__ void __launch_bounds__(W * 32) sk_ld_kernel(const Params p, int NS) {
   uint64_t *wbars = bars + warp * NS;
 
   // Issue position j into stage j % NS.  Must be called by the whole warp with
-  // j's batch current in stage C.
+  // j's batch current in stage C.  Chunk q = lane + 32m of a tile is row
+  // q / CPR, 16-byte column q % CPR (32-bit offsets from the unit's first row).
+  constexpr int M = kUnitTok * CPR / 32;
+  const int rs32 = int(row_stride);
   auto issue = [&](int j) {
     const int64_t e = __shfl_sync(0xffffffffu, c_e, j & 31);
     const int inf = __shfl_sync(0xffffffffu, c_inf, j & 31);
@@ -913,15 +916,17 @@ __global__ void __launch_bounds__(W * 32) sk_ld_kernel(const Params p, int NS) {
     const int st = j % NS;
     const uint32_t kt = ptx::smem_u32(wring + size_t(st) * 2 * TILE_B);
     const uint32_t vt = kt + TILE_B;
+    const T *kb = vak + e, *vb = vav + e;
 #pragma unroll
-    for (int q = lane; q < kUnitTok * CPR; q += 32) {
-      const int r = q / CPR, ch = q % CPR;
-      const uint32_t nb = r < nvalid ? 16u : 0u;
-      const int64_t off = nb ? e + int64_t(r) * row_stride + ch * 8 : 0;
+    for (int m = 0; m < M; ++m) {
+      const int q = lane + 32 * m, r = q / CPR, ch = q % CPR;
       const int pc = ch < (CPR & ~7) ? (ch ^ (r & 7)) : ch;  // swizzle full 8-chunk groups only
       const uint32_t so = uint32_t(r * (D * 2) + (pc << 4));
-      ptx::cp_async16(kt + so, vak + off, nb);
-      ptx::cp_async16(vt + so, vav + off, nb);
+      const bool live = r < nvalid;
+      const int go = live ? r * rs32 + ch * 8 : 0;
+      const uint32_t nb = live ? 16u : 0u;
+      ptx::cp_async16(kt + so, kb + go, nb);
+      ptx::cp_async16(vt + so, vb + go, nb);
     }
     ptx::cp_async_mbar_arrive(ptx::smem_u32(wbars + st));
     return inf;
@@ -1131,7 +1136,9 @@ __global__ void __launch_bounds__(W * 32) sk_ld_kernel(const Params p, int NS) {
     };
     if (inf & 1) {
       const int nvalid = inf >> 1;
+      // S = Q K^T with two independent accumulation chains (even / odd k-steps)
       float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      float s2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
       {
         const int mi2 = lane >> 3, r = lane & 7;
         const int tok = (mi2 >> 1) * 8 + r;
@@ -1139,41 +1146,44 @@ __global__ void __launch_bounds__(W * 32) sk_ld_kernel(const Params p, int NS) {
         for (int ks = 0; ks < KS; ++ks) {
           uint32_t b0, b1, b2, b3;
           ptx::ldsm_x4(sw(kt, tok, ks * 16 + (mi2 & 1) * 8), b0, b1, b2, b3);
-          MMA::run(s[0], qa[ks], b0, b1);
-          MMA::run(s[1], qa[ks], b2, b3);
+          float(*acc)[4] = (ks & 1) ? s2 : s;
+          MMA::run(acc[0], qa[ks], b0, b1);
+          MMA::run(acc[1], qa[ks], b2, b3);
         }
-      }
-      if (nvalid == kUnitTok) {
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) s[nt][jj] *= p.scale_log2;
-      } else {
+          for (int jj = 0; jj < 4; ++jj) s[nt][jj] += s2[nt][jj];
+      }
+      if (nvalid < kUnitTok) {
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
             const int tok = nt * 8 + 2 * t + (jj & 1);
-            s[nt][jj] = tok < nvalid ? s[nt][jj] * p.scale_log2 : -INFINITY;
+            s[nt][jj] = tok < nvalid ? s[nt][jj] : -INFINITY;
           }
       }
+      // online softmax in the log2 domain; the scale (> 0) is folded into the
+      // exponent, so the running max is kept on scaled values
+      const float sc = p.scale_log2;
       float mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
       float mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float mn0 = fmaxf(m0, mx0 * sc), mn1 = fmaxf(m1, mx1 * sc);
       const float a0 = ptx::fast_exp2(m0 - mn0), a1 = ptx::fast_exp2(m1 - mn1);
       m0 = mn0;
       m1 = mn1;
       float ps0 = 0.f, ps1 = 0.f;
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        s[nt][0] = ptx::fast_exp2(s[nt][0] - mn0);
-        s[nt][1] = ptx::fast_exp2(s[nt][1] - mn0);
-        s[nt][2] = ptx::fast_exp2(s[nt][2] - mn1);
-        s[nt][3] = ptx::fast_exp2(s[nt][3] - mn1);
+        s[nt][0] = ptx::fast_exp2(fmaf(s[nt][0], sc, -mn0));
+        s[nt][1] = ptx::fast_exp2(fmaf(s[nt][1], sc, -mn0));
+        s[nt][2] = ptx::fast_exp2(fmaf(s[nt][2], sc, -mn1));
+        s[nt][3] = ptx::fast_exp2(fmaf(s[nt][3], sc, -mn1));
         ps0 += s[nt][0] + s[nt][1];
         ps1 += s[nt][2] + s[nt][3];
       }
