@@ -585,6 +585,7 @@ using SkFn = void (*)(const sk::Params, int);
 
 struct SkPlan {
   bool ok = false;
+  bool forced = false;  // requested through KCMM_DECODE_IMPL: no silent fallback
   SkFn fn = nullptr;
   void (*merge)(const sk::Params, int) = nullptr;
   size_t smem = 0;
@@ -674,21 +675,24 @@ void ld_pick(SkPlan *pl, int batch) {
 }
 
 template <typename T>
-bool ld_select(SkPlan *pl, int D, int batch, int variant) {
-  // variant: 0 = 12 warps, 1 = 10 warps, 2 = 8 warps, 3 = 6 warps (1 CTA per SM)
+bool ld_select(SkPlan *pl, int D, int batch, int warps) {
+  // warps per CTA (1 CTA per SM): 6, 8 (default), 10 or 12; a ring of at least
+  // two stages per warp must fit next to the merge slots.
   switch (D) {
 #define KCMM_LD(DD)                                         \
   case DD:                                                  \
-    if (variant == 1) ld_pick<T, DD, 10>(pl, batch);        \
-    else if (variant == 2) ld_pick<T, DD, 8>(pl, batch);    \
-    else if (variant == 3) ld_pick<T, DD, 6>(pl, batch);    \
-    else ld_pick<T, DD, 12>(pl, batch);                     \
+    if (warps == 6) ld_pick<T, DD, 6>(pl, batch);           \
+    else if (warps == 10) ld_pick<T, DD, 10>(pl, batch);    \
+    else if (warps == 12) ld_pick<T, DD, 12>(pl, batch);    \
+    else if (warps == 8) ld_pick<T, DD, 8>(pl, batch);      \
+    else return false;                                      \
     return true;
     KCMM_LD(64)
     KCMM_LD(128)
 #undef KCMM_LD
 #define KCMM_LD1(DD)                 \
   case DD:                           \
+    if (warps != 8) return false;    \
     ld_pick<T, DD, 8>(pl, batch);    \
     return true;
     KCMM_LD1(32)
@@ -704,17 +708,27 @@ bool ld_select(SkPlan *pl, int D, int batch, int variant) {
   }
 }
 
+// The split-K kernel is the default: on the Llama-3-8B decode shape it runs at
+// the same speed as the best stream-K configuration that fits in shared memory
+// or faster.  KCMM_DECODE_IMPL=streamk (per-warp cp.async rings, warps from
+// KCMM_SK_WARPS) or =tma (TMA producer warps, KCMM_SK_VARIANT) selects a
+// persistent stream-K kernel instead; when the shapes rule the requested
+// kernel out the call fails rather than running another kernel.
 SkPlan make_sk_plan(const DecodeArgs &a) {
   SkPlan pl;
+  const char *impl = std::getenv("KCMM_DECODE_IMPL");
+  const bool tma = impl && std::strcmp(impl, "tma") == 0;
+  const bool streamk = impl && std::strcmp(impl, "streamk") == 0;
+  if (!tma && !streamk) return pl;
+  pl.forced = true;
   const int D = a.head_dim;
   if (D % 16 != 0 || a.block_size % 16 != 0 || a.batch > 2048) return pl;
   if ((reinterpret_cast<uintptr_t>(a.q) & 15) != 0) return pl;
-  const char *impl = std::getenv("KCMM_DECODE_IMPL");
-  if (impl && std::strcmp(impl, "split") == 0) return pl;
-  const bool tma = impl && std::strcmp(impl, "tma") == 0;
   if (tma && (D % 64 != 0 || !a.tensor_maps)) return pl;
   int variant = 0;
   if (const char *v = std::getenv("KCMM_SK_VARIANT")) variant = std::atoi(v);
+  int warps = 8;
+  if (const char *w = std::getenv("KCMM_SK_WARPS")) warps = std::atoi(w);
   const int g_all = (a.num_q_heads + a.kv_heads - 1) / a.kv_heads;
   pl.n_head_tiles = (g_all + 15) / 16;
   pl.g_max = std::min(16, g_all);
@@ -724,8 +738,8 @@ SkPlan make_sk_plan(const DecodeArgs &a) {
                                    : sk_select<__half>(&pl, D, a.batch, variant);
     if (pl.ring < 8) found = false;
   } else {
-    found = a.dtype == Dtype::BF16 ? ld_select<__nv_bfloat16>(&pl, D, a.batch, variant)
-                                   : ld_select<__half>(&pl, D, a.batch, variant);
+    found = a.dtype == Dtype::BF16 ? ld_select<__nv_bfloat16>(&pl, D, a.batch, warps)
+                                   : ld_select<__half>(&pl, D, a.batch, warps);
     if (pl.ring < 2) found = false;
   }
   if (!found || pl.smem > 227 * 1024) return pl;
@@ -818,6 +832,7 @@ cudaError_t decode_streamk(const DecodeArgs &a, const SkPlan &pl, cudaStream_t s
 size_t decode_scratch_bytes(const DecodeArgs &a) {
   SkPlan sp = make_sk_plan(a);
   if (sp.ok) return sp.scratch_bytes;
+  if (sp.forced) return 0;  // the launch fails with cudaErrorNotSupported
   return make_plan(a).scratch_bytes;
 }
 
@@ -841,6 +856,7 @@ cudaError_t decode_attention(const DecodeArgs &a, cudaStream_t stream) {
 
   SkPlan sp = make_sk_plan(a);
   if (sp.ok) return decode_streamk(a, sp, stream);
+  if (sp.forced) return cudaErrorNotSupported;
   Plan pl = make_plan(a);
   if (!pl.fast) {
     const int threads = 256;

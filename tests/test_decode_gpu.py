@@ -97,20 +97,24 @@ def test_zero_length_rows_untouched():
         wl.close()
 
 
+SK = {"KCMM_DECODE_IMPL": "streamk"}   # persistent stream-K, per-warp cp.async rings
+
+
 @pytest.mark.parametrize("env", [
-    {"KCMM_SK_GRID": "1"},            # one CTA walks every segment
-    {"KCMM_SK_GRID": "3"},            # slices cut segments into pieces
-    {"KCMM_SK_GRID": "37"},
-    {"KCMM_SK_GRID": "5000"},         # more CTAs than units: empty slices
-    {"KCMM_SK_VARIANT": "1"},         # 6 warps
-    {"KCMM_SK_VARIANT": "2"},         # 4 warps
-    {"KCMM_SK_VARIANT": "3"},         # 12 warps
-    {"KCMM_SK_RING": "2"},            # shallow rings
-    {"KCMM_DECODE_IMPL": "tma"},      # TMA producer-warp variant
+    {**SK},                               # 8 warps
+    {**SK, "KCMM_SK_GRID": "1"},          # one CTA walks every segment
+    {**SK, "KCMM_SK_GRID": "3"},          # slices cut segments into pieces
+    {**SK, "KCMM_SK_GRID": "37"},
+    {**SK, "KCMM_SK_GRID": "5000"},       # more CTAs than units: empty slices
+    {**SK, "KCMM_SK_WARPS": "6"},
+    {**SK, "KCMM_SK_WARPS": "10"},
+    {**SK, "KCMM_SK_RING": "2"},          # shallow rings
+    {"KCMM_DECODE_IMPL": "tma"},          # TMA producer-warp variant
     {"KCMM_DECODE_IMPL": "tma", "KCMM_SK_GRID": "3"},
-    {"KCMM_DECODE_IMPL": "split", "KCMM_DECODE_SPLITS": "1"},  # split-K kernel
-    {"KCMM_DECODE_IMPL": "split", "KCMM_DECODE_SPLITS": "3"},
-    {"KCMM_DECODE_IMPL": "split", "KCMM_DECODE_SPLITS": "7"},
+    {"KCMM_DECODE_IMPL": "tma", "KCMM_SK_VARIANT": "2"},
+    {"KCMM_DECODE_SPLITS": "1"},          # split-K kernel (the default)
+    {"KCMM_DECODE_SPLITS": "3"},
+    {"KCMM_DECODE_SPLITS": "7"},
 ])
 def test_work_split_does_not_change_result(env, monkeypatch):
     for k, v in env.items():
@@ -163,9 +167,25 @@ def test_v_row_kat():
         wl.close()
 
 
+def test_requested_streamk_that_does_not_fit_fails(monkeypatch):
+    """12 warps x 2 ring stages of 16x128 K/V tiles plus the merge slots exceed shared
+    memory at head_dim 128: the call reports an error instead of running split-K."""
+    from lattice_b200.kcmm import KcmmError
+
+    wl = make(batch=2, num_q_heads=32, kv_heads=8, head_dim=128, seq_lens_override=[5, 9])
+    try:
+        monkeypatch.setenv("KCMM_DECODE_IMPL", "streamk")
+        monkeypatch.setenv("KCMM_SK_WARPS", "12")
+        with pytest.raises(KcmmError, match="not supported"):
+            wl.decode()
+    finally:
+        wl.close()
+
+
 @pytest.mark.parametrize("grid", ["2", "11"])
 def test_piece_merging_with_gqa_tiles_and_empty_rows(grid, monkeypatch):
     """Head tiles (GQA 32), zero-length rows and pieces that straddle slices together."""
+    monkeypatch.setenv("KCMM_DECODE_IMPL", "streamk")
     monkeypatch.setenv("KCMM_SK_GRID", grid)
     wl = make(batch=6, num_q_heads=64, kv_heads=2, head_dim=128,
               seq_lens_override=[0, 33, 700, 1, 0, 257], seed=int(grid))
