@@ -186,6 +186,7 @@ def test_requested_streamk_that_does_not_fit_fails(monkeypatch):
 def test_piece_merging_with_gqa_tiles_and_empty_rows(grid, monkeypatch):
     """Head tiles (GQA 32), zero-length rows and pieces that straddle slices together."""
     monkeypatch.setenv("KCMM_DECODE_IMPL", "streamk")
+    monkeypatch.setenv("KCMM_SK_WARPS", "6")  # 16-head merge slots: 8 warps do not fit
     monkeypatch.setenv("KCMM_SK_GRID", grid)
     wl = make(batch=6, num_q_heads=64, kv_heads=2, head_dim=128,
               seq_lens_override=[0, 33, 700, 1, 0, 257], seed=int(grid))
