@@ -53,53 +53,113 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples during the timed region."""
+    """SM clock and clock-event reasons sampled every ~2 ms by an NVML thread while
+    the timed region runs (read-only NVML queries; nothing is set).  Falls back to
+    an `nvidia-smi -lms 100` subprocess when NVML is unavailable."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown", 0x8),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap", 0x4),
+               ("hw_power_brake", "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80))
+    SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device: int):
         self.device = device
-        self.proc = None
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self.source = None
+        self._thread = None
+        self._stop = None
+        self._proc = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.device).uuid)
+        h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid) if not uuid.startswith("GPU-") else uuid)
+        return pynvml, h
 
     def start(self):
+        import threading
+
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+            nv, h = self._nvml_handle()
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        except Exception:  # noqa: BLE001 - no NVML: use nvidia-smi
+            self._start_smi()
+            return
+        self.source = "nvml"
+        self._stop = threading.Event()
+
+        def loop():
+            while not self._stop.is_set():
+                try:
+                    mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((float(mhz), int(rs)))
+                except Exception:  # noqa: BLE001
+                    pass
+                self._stop.wait(0.002)
+
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
+        time.sleep(0.01)
+
+    def _start_smi(self):
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.SMI_FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.source = "nvidia-smi"
         except (FileNotFoundError, OSError):
-            self.proc = None
+            self._proc = None
 
     def stop(self):
-        if not self.proc:
-            return None
-        time.sleep(0.25)
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
+            import pynvml
+
+            reasons = set()
+            for _, rs in self.samples:
+                for name, const, bit in self.REASONS:
+                    if rs & int(getattr(pynvml, const, bit)):
+                        reasons.add(name)
+            sm = [m for m, _ in self.samples]
+        elif self._proc is not None:
+            time.sleep(0.25)
+            self._proc.terminate()
             try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
+                out, _ = self._proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+                out, _ = self._proc.communicate()
+            sm, reasons = [], set()
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for line in out.strip().splitlines():
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm.append(float(f[1]))
+                    self.max_mhz = float(f[2])
+                except ValueError:
+                    continue
+                for n, v in zip(names, f[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        else:
+            return None
         if not sm:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(sm), "source": self.source}
 
 
 def dist_setup(args):
@@ -157,7 +217,6 @@ def run_ours(args):
         torch.distributed.barrier()
     torch.cuda.synchronize()
     clocks.start()
-    time.sleep(0.3)
     t0.record(stream)
     for i in range(args.steps):
         a, b, c = ev[i]
@@ -329,12 +388,12 @@ def run_reference(args):
     seq = rng.integers(512, 4097, B).astype(np.int32)
     max_bps = 256
     need = [-(-int(L) // bs) for L in seq]
-    nseq = 4  # sequences per step: a bounded sample (about a second of CPU work)
-    used = sum(need[:nseq])
+    nmax = 4  # at most 4 sequences per step, fewer when K steps would run past ~2 minutes
+    used = sum(need[:nmax])
     perm = rng.permutation(used).astype(np.int32)
     tables = np.zeros((B, max_bps), np.int32)
     pos = 0
-    for b in range(nseq):
+    for b in range(nmax):
         tables[b, :need[b]] = perm[pos:pos + need[b]]
         pos += need[b]
     step_elems = hkv * D
@@ -345,8 +404,9 @@ def run_reference(args):
     meta = dict(hq=hq, hkv=hkv, d=D, bs=bs, max_bps=max_bps, scale=D ** -0.5)
     workers = os.cpu_count() or 1
     sample = (q, va_k, va_v, tables, seq, offsets, meta)
-    for _ in range(max(1, min(args.warmup, 2))):
-        _ref_attention_sample(sample, nseq, workers)
+    t_one = min(_ref_attention_sample(sample, 1, workers)[0]
+                for _ in range(max(1, min(args.warmup, 2))))
+    nseq = max(1, min(nmax, int(120.0 / (max(args.steps, 1) * max(t_one, 1e-6)))))
     times, byts, kind = [], 0, "reference"
     for _ in range(args.steps):
         dt, byts, kind = _ref_attention_sample(sample, nseq, workers)
@@ -374,7 +434,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--profile", action="store_true",
