@@ -336,6 +336,31 @@ int kcmm_paged_attn_decode_bf16_on_stream(
     uint32_t kv_heads, uint32_t head_dim, uint32_t block_size,
     uint32_t max_blocks_per_seq, float scale, uint64_t stream_ptr);
 
+/**
+ * kcmm_paged_attn_decode_bf16_on_stream without any device allocation.  This
+ * entry point has no reference counterpart.
+ *
+ * The regular entry point takes its split/merge scratch from a stream-ordered
+ * memory pool.  This one uses a static 32 MiB per-device array instead.  It is
+ * for callers that cannot allocate on the decode step: a KV pool sized to fill
+ * HBM leaves the memory pool nothing to grow into, and a host with its own
+ * allocator has no scratch buffer to pass.
+ *
+ * Launches needing more than 32 MiB of scratch return -1 with an error
+ * message and launch nothing.  With Llama-3-8B heads that is above about 1000
+ * sequences of up to 4096 tokens, or 500 of up to 8192.  The first
+ * call on each device resolves the array's address and may load its module,
+ * so make that call before any stream capture.  Calls on one device share the
+ * array: overlapping calls (other streams or threads, unordered) race on it.
+ * Same arguments and results as kcmm_paged_attn_decode_bf16_on_stream.
+ */
+int kcmm_paged_attn_decode_bf16_noalloc_on_stream(
+    kcmm_pool_t *pool, uint32_t layer_idx, uint64_t query_ptr, uint64_t out_ptr,
+    uint64_t block_tables_ptr, uint64_t seq_lens_ptr,
+    uint64_t block_offsets_f16_ptr, uint32_t batch, uint32_t num_q_heads,
+    uint32_t kv_heads, uint32_t head_dim, uint32_t block_size,
+    uint32_t max_blocks_per_seq, float scale, uint64_t stream_ptr);
+
 /** bf16 name for the device-slot write (the write copies 16-bit words, so it is the f16 kernel). */
 int kcmm_append_kv_device_slots_bf16_on_stream(
     kcmm_pool_t *pool, uint32_t layer_idx, uint64_t slot_mapping_ptr,

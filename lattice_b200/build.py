@@ -27,7 +27,8 @@ LIB = PKG / "libkcmm.so"
 ALIAS = PKG / "libbaseline_llm_os.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CU_SOURCES = ["kernels/decode.cu", "kernels/append.cu", "kernels/copy.cu"]
+CU_SOURCES = ["kernels/decode.cu", "kernels/decode_noalloc.cu", "kernels/append.cu",
+              "kernels/copy.cu"]
 CPP_SOURCES = ["pool.cpp", "vmm.cpp", "ffi.cpp"]
 HEADERS = ["kcmm_internal.hpp", "launch.hpp", "kernels/ptx.cuh", "kernels/decode_streamk.cuh"]
 

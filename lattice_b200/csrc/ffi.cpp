@@ -421,9 +421,10 @@ static int decode_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, u
                        uint64_t out, uint64_t tables, uint64_t seq_lens, uint64_t offsets,
                        uint32_t batch, uint32_t hq, uint32_t hkv, uint32_t hd, uint32_t bs,
                        uint32_t max_bps, float scale, uint64_t stream, bool sync,
-                       bool bind) {
-  const char *op = dtype == kcmm::dev::Dtype::F16 ? "kcmm_paged_attn_decode_f16"
-                                                  : "kcmm_paged_attn_decode_bf16";
+                       bool bind, bool noalloc = false) {
+  const char *op = noalloc ? "kcmm_paged_attn_decode_bf16_noalloc_on_stream"
+                   : dtype == kcmm::dev::Dtype::F16 ? "kcmm_paged_attn_decode_f16"
+                                                    : "kcmm_paged_attn_decode_bf16";
   if (!h || !q || !out || !tables || !seq_lens || !offsets) {
     set_error(h, std::string(op) + ": null pointer argument");
     return -1;
@@ -470,8 +471,22 @@ static int decode_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, u
   a.scale = scale;
   a.diag = p->diag_word();
   if (const char *fs = std::getenv("KCMM_DECODE_SPLITS")) a.force_splits = std::atoi(fs);
-  a.tensor_maps = p->tensor_maps(layer, int(hkv), int(hd));
   a.region_tokens = p->region_bytes / (uint64_t(hkv) * hd * 2);
+  if (noalloc) {
+    // No tensor maps: encoding them fills a host-side cache, and only the
+    // TMA-producer kernel (opt-in) reads them.
+    const size_t need = kcmm::dev::decode_scratch_bytes(a);
+    const size_t limit = kcmm::dev::decode_noalloc_scratch_limit();
+    if (need > limit) {
+      set_error(h, std::string(op) + ": needs " + std::to_string(need) +
+                       " bytes of scratch, above the static limit of " + std::to_string(limit) +
+                       " bytes; use kcmm_paged_attn_decode_bf16_on_stream or a smaller batch");
+      return -1;
+    }
+    if (check_launch(h, op, kcmm::dev::decode_attention_noalloc(a, S(stream)))) return -1;
+    return 0;
+  }
+  a.tensor_maps = p->tensor_maps(layer, int(hkv), int(hd));
   if (check_launch(h, op, kcmm::dev::decode_attention(a, S(stream)))) return -1;
   if (sync) {
     cudaError_t e = cudaDeviceSynchronize();
@@ -515,6 +530,14 @@ int kcmm_paged_attn_decode_bf16_on_stream(kcmm_pool_t *h, uint32_t layer, uint64
                                           uint32_t max_bps, float scale, uint64_t stream) {
   return decode_impl(h, kcmm::dev::Dtype::BF16, layer, q, out, tables, seq_lens, offsets, batch,
                      hq, hkv, hd, bs, max_bps, scale, stream, false, true);
+}
+
+int kcmm_paged_attn_decode_bf16_noalloc_on_stream(
+    kcmm_pool_t *h, uint32_t layer, uint64_t q, uint64_t out, uint64_t tables,
+    uint64_t seq_lens, uint64_t offsets, uint32_t batch, uint32_t hq, uint32_t hkv, uint32_t hd,
+    uint32_t bs, uint32_t max_bps, float scale, uint64_t stream) {
+  return decode_impl(h, kcmm::dev::Dtype::BF16, layer, q, out, tables, seq_lens, offsets, batch,
+                     hq, hkv, hd, bs, max_bps, scale, stream, false, true, true);
 }
 
 int kcmm_precompile_paged_attn_decode_f16(kcmm_pool_t *h) {

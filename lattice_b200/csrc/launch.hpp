@@ -47,6 +47,12 @@ struct DecodeArgs {
 // (0 when no split is needed).
 size_t decode_scratch_bytes(const DecodeArgs &a);
 cudaError_t decode_attention(const DecodeArgs &a, cudaStream_t stream);
+// decode_attention with its scratch in a static per-device array instead of a
+// stream-ordered allocation (kernels/decode_noalloc.cu).  Returns
+// cudaErrorInvalidValue when the launch needs more than
+// decode_noalloc_scratch_limit() bytes; a.scratch is ignored.
+size_t decode_noalloc_scratch_limit();
+cudaError_t decode_attention_noalloc(const DecodeArgs &a, cudaStream_t stream);
 // Force module load of every decode kernel (precompile entry points).
 cudaError_t decode_preload();
 

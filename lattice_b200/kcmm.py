@@ -202,6 +202,8 @@ SIGNATURES: dict[str, tuple] = {
     # --- B200 additions ---
     "kcmm_paged_attn_decode_bf16_on_stream":
         (i32, [P, u32, u64, u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, f32, u64]),
+    "kcmm_paged_attn_decode_bf16_noalloc_on_stream":
+        (i32, [P, u32, u64, u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, f32, u64]),
     "kcmm_append_kv_device_slots_bf16_on_stream":
         (i32, [P, u32, u64, u64, u64, u32, u32, u64, u64, u64, u64]),
     "kcmm_fused_norm_rope_append_bf16_on_stream":
@@ -480,11 +482,19 @@ class KcmmPool:
                           block_offsets_f16_ptr: int, batch: int, num_q_heads: int,
                           kv_heads: int, head_dim: int, block_size: int,
                           max_blocks_per_seq: int, scale: float, dtype: str = "bf16",
-                          stream_ptr: int | None = 0, current_context: bool = False) -> None:
+                          stream_ptr: int | None = 0, current_context: bool = False,
+                          noalloc: bool = False) -> None:
+        """`noalloc=True` (bf16 only) calls the entry point whose scratch is a static
+        per-device array instead of a stream-ordered allocation."""
         args = (self.handle, layer, query_ptr, out_ptr, block_tables_ptr, seq_lens_ptr,
                 block_offsets_f16_ptr, batch, num_q_heads, kv_heads, head_dim, block_size,
                 max_blocks_per_seq, scale)
-        if dtype == "bf16":
+        if noalloc:
+            if dtype != "bf16":
+                raise ValueError("the no-allocation decode entry point is bf16 only")
+            rc = self.lib.kcmm_paged_attn_decode_bf16_noalloc_on_stream(*args, stream_ptr or 0)
+            op = "kcmm_paged_attn_decode_bf16_noalloc_on_stream"
+        elif dtype == "bf16":
             rc = self.lib.kcmm_paged_attn_decode_bf16_on_stream(*args, stream_ptr or 0)
             op = "kcmm_paged_attn_decode_bf16_on_stream"
         elif stream_ptr is None:

@@ -149,7 +149,8 @@ class DecodeWorkload:
         torch.cuda.synchronize()
         return self
 
-    def decode(self, layer: int = 0, stream_ptr: int | None = None, out=None) -> None:
+    def decode(self, layer: int = 0, stream_ptr: int | None = None, out=None,
+               noalloc: bool = False) -> None:
         torch = _torch()
         if stream_ptr is None:
             stream_ptr = torch.cuda.current_stream().cuda_stream
@@ -160,7 +161,7 @@ class DecodeWorkload:
             block_offsets_f16_ptr=self.d_offsets.data_ptr(), batch=self.batch,
             num_q_heads=self.num_q_heads, kv_heads=self.kv_heads, head_dim=self.head_dim,
             block_size=self.block_size, max_blocks_per_seq=self.max_blocks_per_seq,
-            scale=self.scale, dtype=self.dtype, stream_ptr=stream_ptr)
+            scale=self.scale, dtype=self.dtype, stream_ptr=stream_ptr, noalloc=noalloc)
 
     def kv_bytes(self) -> int:
         """Algorithmic bytes of one decode pass (K and V rows, tables, q, out)."""
