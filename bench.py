@@ -173,9 +173,34 @@ def dist_setup(args):
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device(f"cuda:{local}"))
     return world, rank, local
+
+
+def max_over_ranks(ms: float) -> float:
+    """Max of a per-rank duration over all ranks (identity without a process group)."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return ms
+    dev = (f"cuda:{torch.cuda.current_device()}" if dist.get_backend() == "nccl" else "cpu")
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier() -> None:
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.barrier()
+
+
+def whole_job_gbps(bytes_per_rank_step: int, world: int, ms_step: float) -> float:
+    """Weak scaling: every rank processes its own bytes; the job takes the slowest rank."""
+    return bytes_per_rank_step * world / (ms_step * 1e-3) / 1e9
 
 
 def run_ours(args):
@@ -228,21 +253,14 @@ def run_ours(args):
     t1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
-    total_ms = t0.elapsed_time(t1)
+    total_ms = max_over_ranks(t0.elapsed_time(t1))
     attn_ms = [e[1].elapsed_time(e[2]) for e in ev]
     app_ms = [e[0].elapsed_time(e[1]) for e in ev]
-    if world > 1:
-        import torch.distributed as dist
-
-        t = torch.tensor([total_ms], device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
-        dist.barrier()
+    barrier()
     ms_step = total_ms / args.steps
     attn_bytes = wl.kv_bytes()
     app_bytes = fa.bytes_per_launch()
-    step_bytes = (attn_bytes + app_bytes) * world
-    value = step_bytes / (ms_step * 1e-3) / 1e9
+    value = whole_job_gbps(attn_bytes + app_bytes, world, ms_step)
     tokens_per_s = wl.batch * world / (LAYERS_FOR_TOKENS * ms_step * 1e-3)
     attn_avg = statistics.mean(attn_ms)
     achieved = attn_bytes / (attn_avg * 1e-3) / 1e9
@@ -251,7 +269,7 @@ def run_ours(args):
 
     splits = int(os.environ.get("KCMM_DECODE_SPLITS", "0"))
     launches_per_step = 1 + 2  # fused append + decode main + split merge
-    e2e = run_e2e(args, wl, fa, stream) if rank == 0 and not args.profile else None
+    e2e = run_e2e(args, wl, fa, stream, world) if not args.profile else None
     status = wl.pool.kernel_status()
 
     result = None
@@ -284,14 +302,15 @@ def run_ours(args):
     if world > 1:
         import torch.distributed as dist
 
-        dist.barrier()
+        barrier()
         dist.destroy_process_group()
     return result
 
 
-def run_e2e(args, wl, fa, stream):
+def run_e2e(args, wl, fa, stream, world):
     """Same step through the public API with host buffers: H2D of the step's inputs from
-    pinned memory, the two ABI calls, D2H of the attention output."""
+    pinned memory, the two ABI calls, D2H of the attention output.  Every rank runs it;
+    the time is the max over ranks."""
     import torch
 
     ins = [wl.q, fa.x, fa.k, fa.v]
@@ -311,18 +330,19 @@ def run_e2e(args, wl, fa, stream):
     for _ in range(3):
         step()
     torch.cuda.synchronize()
+    barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     for _ in range(args.steps):
         step()
     t1.record(stream)
     torch.cuda.synchronize()
-    ms = t0.elapsed_time(t1) / args.steps
+    ms = max_over_ranks(t0.elapsed_time(t1)) / args.steps
     byts = wl.kv_bytes() + fa.bytes_per_launch()
-    return {"value": round(byts / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-            "ms_per_step": round(ms, 5), "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(d2h),
-            "tokens_per_s": round(wl.batch / (LAYERS_FOR_TOKENS * ms * 1e-3), 1)}
+    return {"value": round(whole_job_gbps(byts, world, ms), 2), "unit": "GB/s",
+            "ms_per_step": round(ms, 5), "h2d_bytes_per_step": int(h2d) * world,
+            "d2h_bytes_per_step": int(d2h) * world,
+            "tokens_per_s": round(wl.batch * world / (LAYERS_FOR_TOKENS * ms * 1e-3), 1)}
 
 
 def traffic_from_profiles():
@@ -431,6 +451,295 @@ def run_reference(args):
     return line
 
 
+# --- secondary legs (one JSON line each; `--workload` selects one) -----------------
+
+
+def _gate(torch):
+    """Hold the stream for ~1 ms so that the host-side work of the next ABI call
+    (allocator bookkeeping, launch) overlaps it and the following event pair times
+    only the device work."""
+    torch.cuda._sleep(2_000_000)
+
+
+def _line(metric, value, unit, config, roofline, extra=None):
+    out = {"metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": 1,
+           "higher_is_better": True, "dtype": "bf16", "data": "synthetic", "config": config,
+           "roofline": roofline}
+    out.update(extra or {})
+    print(json.dumps(out))
+    return out
+
+
+def run_append_leg(args):
+    """Fused RMSNorm + RoPE + KV append for a 256-token decode batch:
+    (i) one launch, L2 flushed between launches; (ii) 32 layers, one launch per layer
+    over per-layer buffers (336 MB > L2), replayed as one CUDA graph."""
+    import torch
+
+    from lattice_b200 import kcmm
+    from lattice_b200.workloads import FusedAppendWorkload, library
+
+    torch.cuda.set_device(0)
+    peak, kind = peaks()
+    one = FusedAppendWorkload(tokens=256, seed=3).build()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    sp = torch.cuda.current_stream().cuda_stream
+    for _ in range(max(args.warmup, 3)):
+        one.run(stream_ptr=sp)
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        one.run(stream_ptr=sp)
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    t1 = statistics.median(times)
+    st1 = int(one.status.item())
+    b1 = one.bytes_per_launch()
+    one.close()
+
+    layers = 32
+    cfg = kcmm.make_config(num_layers=layers, kv_heads=8, head_dim=128, max_batch=256,
+                           max_seq_len=64, block_size=16)
+    pool = library().create_pool(cfg)
+    pool.alloc_blocks(256)
+    legs = [FusedAppendWorkload(tokens=256, seed=100 + l, pool=pool, layer=l).build()
+            for l in range(layers)]
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = None
+    with torch.cuda.stream(side):
+        for fa in legs:  # warm-up outside capture
+            fa.run(stream_ptr=side.cuda_stream)
+    torch.cuda.synchronize()
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            cs = torch.cuda.current_stream().cuda_stream
+            for fa in legs:
+                fa.run(stream_ptr=cs)
+        replay = graph.replay
+        how = "CUDA graph of 32 launches"
+    except Exception as e:  # noqa: BLE001 - report and time the plain launches instead
+        graph = None
+        how = f"32 plain launches (graph capture failed: {type(e).__name__})"
+
+        def replay():
+            for fa in legs:
+                fa.run(stream_ptr=torch.cuda.current_stream().cuda_stream)
+    for _ in range(3):
+        replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        replay()
+    b.record()
+    torch.cuda.synchronize()
+    t32 = a.elapsed_time(b) / args.steps
+    b32 = sum(fa.bytes_per_launch() for fa in legs)
+    st32 = max(int(fa.status.item()) for fa in legs)
+    del graph
+    for fa in legs:
+        fa.close()
+    pool.destroy()
+    g1 = b1 / (t1 * 1e-3) / 1e9
+    g32 = b32 / (t32 * 1e-3) / 1e9
+    return _line(
+        "fused RMSNorm+RoPE+KV append GB/s (32 layers)", g32, "GB/s",
+        {"workload": "BASELINE config 3: 256 tokens, hidden 4096, Hq 32, Hkv 8, D 128, bs 16, "
+                     "theta 500000, reference rope mode", "layers": layers, "timing": how},
+        {"bound": "hbm", "achieved": round(g32, 1), "peak": peak, "unit": "GB/s",
+         "frac": round(g32 / peak, 4), "traffic": None, "peak_kind": kind,
+         "algorithmic_bytes_per_launch": b32},
+        {"us_32_layers": round(t32 * 1e3, 2),
+         "single_launch": {"us": round(t1 * 1e3, 2), "gbs": round(g1, 1),
+                           "frac": round(g1 / peak, 4), "bytes": b1, "l2": "flushed"},
+         "status": max(st1, st32)})
+
+
+def run_cow_leg(args):
+    """Beam-search CoW (BASELINE config 4 shapes, 32 layers): 16 requests x 4 beams share a
+    2048-token prefix plus a partly filled tail block; a step forks the 4 beams from their
+    request and copies each beam's shared tail (64 whole-block copies across all 64
+    regions), then runs decode attention of the 64 beams over the shared pages."""
+    import torch
+
+    from lattice_b200 import kcmm
+    from lattice_b200.workloads import library, memcpy
+
+    torch.cuda.set_device(0)
+    peak, kind = peaks()
+    layers, reqs, beams, prefix_blocks = 32, 16, 4, 128
+    cfg = kcmm.make_config(num_layers=layers, kv_heads=8, head_dim=128, max_batch=128,
+                           max_seq_len=2048 + 256, block_size=16)
+    pool = library().create_pool(cfg)
+    parents = []
+    for _ in range(reqs):
+        blocks = pool.alloc_blocks(prefix_blocks + 1)
+        s = pool.register_sequence(blocks)
+        pool.update_seq_len(s, 2048 + 8)
+        parents.append(s)
+    bb = pool.stats()["block_bytes"]
+    used = max(pool.block_va_offset(b) for p in parents for b in pool.block_table(p)) + bb
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    for l in range(layers):
+        for base in (pool.va_k(l), pool.va_v(l)):
+            t = torch.randn(used // 2, device="cuda", generator=gen).to(torch.bfloat16)
+            memcpy(base, t.data_ptr(), used, "d2d")
+    del t
+    sp = torch.cuda.current_stream().cuda_stream
+    copy_ms, attn_ms = [], []
+    q = torch.randn(reqs * beams, 32, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    copies = 0
+    for it in range(max(args.warmup, 3) + args.steps):
+        forks = [pool.fork_sequence(p) for p in parents for _ in range(beams)]
+        tails = [prefix_blocks] * len(forks)
+        shared = [pool.block_table(f)[prefix_blocks] for f in forks]
+        _gate(torch)
+        a, b, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        a.record()
+        new = pool.cow_blocks(forks, tails, stream_ptr=sp)
+        b.record()
+        tables = np.array([pool.block_table(f) for f in forks], np.int32)
+        d_tables = torch.from_numpy(tables).cuda()
+        d_lens = torch.full((len(forks),), 2048 + 8, dtype=torch.int32, device="cuda")
+        d_offs = torch.from_numpy(np.array(pool.all_block_offsets_f16(), np.uint64)
+                                  .view(np.int64)).cuda()
+        _gate(torch)
+        b2 = torch.cuda.Event(enable_timing=True)
+        b2.record()
+        pool.paged_attn_decode(0, query_ptr=q.data_ptr(), out_ptr=out.data_ptr(),
+                               block_tables_ptr=d_tables.data_ptr(),
+                               seq_lens_ptr=d_lens.data_ptr(),
+                               block_offsets_f16_ptr=d_offs.data_ptr(), batch=len(forks),
+                               num_q_heads=32, kv_heads=8, head_dim=128, block_size=16,
+                               max_blocks_per_seq=tables.shape[1], scale=128 ** -0.5,
+                               stream_ptr=sp)
+        c.record()
+        torch.cuda.synchronize()
+        if it >= max(args.warmup, 3):
+            copy_ms.append(a.elapsed_time(b))
+            attn_ms.append(b2.elapsed_time(c))
+        copies = sum(1 for n, o in zip(new, shared) if n != o)
+        for f in forks:
+            pool.unregister_sequence(f)
+    status = pool.kernel_status()
+    pool.destroy()
+    tc = statistics.median(copy_ms)
+    ta = statistics.median(attn_ms)
+    cow_bytes = copies * 2 * layers * bb * 2
+    g = cow_bytes / (tc * 1e-3) / 1e9
+    ctx = 2048 + 8
+    logical = reqs * beams * ctx * 8 * 128 * 2 * 2
+    unique = reqs * 2048 * 8 * 128 * 2 * 2 + reqs * beams * 8 * 8 * 128 * 2 * 2
+    return _line(
+        "CoW block copy GB/s (64 beam tails x 32 layers)", g, "GB/s",
+        {"workload": "BASELINE config 4: 16 requests x 4 beams, 2048-token shared prefix, "
+                     "Hkv 8, D 128, bs 16, bf16", "layers": layers,
+         "timing": "device time of kcmm_cow_blocks_on_stream (host bookkeeping overlapped)"},
+        {"bound": "hbm", "achieved": round(g, 1), "peak": peak, "unit": "GB/s",
+         "frac": round(g / peak, 4), "traffic": None, "peak_kind": kind,
+         "algorithmic_bytes_per_launch": cow_bytes},
+        {"copies_per_step": copies, "cow_us": round(tc * 1e3, 2),
+         "beam_attention": {"us": round(ta * 1e3, 2), "logical_bytes": logical,
+                            "unique_bytes": unique,
+                            "logical_gbs": round(logical / (ta * 1e-3) / 1e9, 1),
+                            "unique_gbs": round(unique / (ta * 1e-3) / 1e9, 1)},
+         "status": status})
+
+
+def run_swap_leg(args):
+    """Tiering swap (per GPU: 1 kv head, 8 layers -> 64 KiB per block):
+    20% of 16,384 blocks swapped to the pinned host tier and back, one launch series each
+    way, against the measured pinned host-link copy bandwidth."""
+    import torch
+
+    from lattice_b200 import kcmm
+    from lattice_b200.workloads import library, memcpy
+
+    torch.cuda.set_device(0)
+    layers, seqs, ctx = 8, 8, 32768
+    cfg = kcmm.make_config(num_layers=layers, kv_heads=1, head_dim=128, max_batch=seqs,
+                           max_seq_len=ctx, block_size=16, tiering=True,
+                           max_blocks=seqs * ctx // 16)
+    pool = library().create_pool(cfg)
+    nblk = seqs * ctx // 16
+    blocks = pool.alloc_blocks(nblk)
+    for s in range(seqs):
+        q = pool.register_sequence(blocks[s * (nblk // seqs):(s + 1) * (nblk // seqs)])
+        pool.update_seq_len(q, ctx)
+    bb = pool.stats()["block_bytes"]
+    used = nblk * bb
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    for l in range(layers):
+        for base in (pool.va_k(l), pool.va_v(l)):
+            t = torch.randint(-32768, 32767, (used // 2,), device="cuda", generator=gen,
+                              dtype=torch.int16)
+            memcpy(base, t.data_ptr(), used, "d2d")
+    del t
+    rng = np.random.default_rng(5)
+    sp = torch.cuda.current_stream().cuda_stream
+    nv = nblk // 5
+    out_ms, in_ms = [], []
+    for it in range(max(2, min(args.warmup, 3)) + min(args.steps, 10)):
+        victims = [int(b) for b in rng.choice(blocks, nv, replace=False)]
+        _gate(torch)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        pool.swap_out(victims, stream_ptr=sp)
+        b.record()
+        _gate(torch)
+        c, d = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c.record()
+        pool.swap_in(victims, stream_ptr=sp)
+        d.record()
+        torch.cuda.synchronize()
+        if it >= max(2, min(args.warmup, 3)):
+            out_ms.append(a.elapsed_time(b))
+            in_ms.append(c.elapsed_time(d))
+    status = pool.kernel_status()
+    pool.destroy()
+    # pinned host-link reference: one 256 MiB cudaMemcpyAsync each way
+    n = 256 << 20
+    host = torch.empty(n, dtype=torch.uint8).pin_memory()
+    dev = torch.empty(n, dtype=torch.uint8, device="cuda")
+    link = {}
+    for name, fn in (("h2d", lambda: dev.copy_(host, non_blocking=True)),
+                     ("d2h", lambda: host.copy_(dev, non_blocking=True))):
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        link[name] = n * 5 / (e0.elapsed_time(e1) * 1e-3) / 1e9
+    moved = nv * layers * 2 * bb
+    go = moved / (statistics.median(out_ms) * 1e-3) / 1e9
+    gi = moved / (statistics.median(in_ms) * 1e-3) / 1e9
+    return _line(
+        "swap out+in GB/s (20% of blocks, 64 KiB per block)", 2 * moved /
+        ((statistics.median(out_ms) + statistics.median(in_ms)) * 1e-3) / 1e9, "GB/s",
+        {"workload": "BASELINE config 5 tiering leg per GPU: 8 x 32768 tokens, Hkv 1, D 128, "
+                     "bs 16, 8 layers (64 KiB per block across 16 regions), 20% of blocks",
+         "timing": "device time of kcmm_swap_{out,in}_blocks_on_stream"},
+        {"bound": "host link", "achieved": round(min(go, gi), 2),
+         "peak": round(min(link["d2h"], link["h2d"]), 2), "unit": "GB/s",
+         "frac": round(min(go / link["d2h"], gi / link["h2d"]), 4), "traffic": None,
+         "peak_kind": "measured pinned cudaMemcpyAsync, 256 MiB"},
+        {"blocks_per_step": nv, "bytes_each_way": moved,
+         "swap_out": {"ms": round(statistics.median(out_ms), 3), "gbs": round(go, 2),
+                      "frac_of_d2h": round(go / link["d2h"], 4)},
+         "swap_in": {"ms": round(statistics.median(in_ms), 3), "gbs": round(gi, 2),
+                     "frac_of_h2d": round(gi / link["h2d"], 4)},
+         "pinned_link_gbs": {k: round(v, 2) for k, v in link.items()}, "status": status})
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -439,9 +748,18 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--profile", action="store_true",
                     help="profiling case for ncu: 12k-block pool, no CPU baseline / e2e legs")
+    ap.add_argument("--workload", choices=["step", "append", "cow", "swap"], default="step",
+                    help="step = the headline (default); the others print one line for a "
+                         "secondary BASELINE config")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "append":
+        run_append_leg(args)
+    elif args.workload == "cow":
+        run_cow_leg(args)
+    elif args.workload == "swap":
+        run_swap_leg(args)
     else:
         run_ours(args)
 
