@@ -631,7 +631,12 @@ def run_cow_leg(args):
     pool.destroy()
     tc = statistics.median(copy_ms)
     ta = statistics.median(attn_ms)
-    cow_bytes = copies * 2 * layers * bb * 2
+    # unique bytes: each request's 4 beams copy the same parent tail, so a step reads 16
+    # distinct source blocks and writes 64 new ones (per region); the 3 repeat reads of a
+    # source come from L2 and are not counted as HBM work
+    src_unique = min(copies, reqs) * 2 * layers * bb
+    cow_bytes = src_unique + copies * 2 * layers * bb
+    logical_cow = copies * 2 * layers * bb * 2
     g = cow_bytes / (tc * 1e-3) / 1e9
     ctx = 2048 + 8
     logical = reqs * beams * ctx * 8 * 128 * 2 * 2
@@ -645,6 +650,8 @@ def run_cow_leg(args):
          "frac": round(g / peak, 4), "traffic": None, "peak_kind": kind,
          "algorithmic_bytes_per_launch": cow_bytes},
         {"copies_per_step": copies, "cow_us": round(tc * 1e3, 2),
+         "cow_logical_bytes": logical_cow,
+         "cow_logical_gbs": round(logical_cow / (tc * 1e-3) / 1e9, 1),
          "beam_attention": {"us": round(ta * 1e3, 2), "logical_bytes": logical,
                             "unique_bytes": unique,
                             "logical_gbs": round(logical / (ta * 1e-3) / 1e9, 1),
