@@ -361,6 +361,41 @@ int kcmm_paged_attn_decode_bf16_noalloc_on_stream(
     uint32_t kv_heads, uint32_t head_dim, uint32_t block_size,
     uint32_t max_blocks_per_seq, float scale, uint64_t stream_ptr);
 
+/**
+ * Causal chunked-prefill attention over the paged cache, on the tcgen05 tensor
+ * cores.  The reference has no prefill kernel; its prefill loops decode steps
+ * (ref src/model/transformer.rs:50-65).
+ *
+ * Sequence b contributes the query rows [qs[b], qs[b+1]) of query_ptr
+ * ([total_tokens][num_q_heads][head_dim], 16-bit, 16-byte aligned), where
+ * qs = query_start_loc_ptr (int32 [batch+1], device).  context_lens_ptr[b]
+ * (int32, device) is the number of keys in the sequence's pages after the
+ * chunk: the chunk's own K/V rows must already be written (append or fused
+ * append).  Query row i of the chunk sits at position context_lens[b] - chunk
+ * length + i and attends to keys [0, that position].  Block tables, offsets
+ * and page layout are those of kcmm_paged_attn_decode_f16.  out_ptr has the
+ * shape of query_ptr.
+ *
+ * Limits: head_dim 128, and num_q_heads / kv_heads must divide 128.
+ * max_query_len bounds every chunk length.  Enqueues on stream_ptr and
+ * returns; device-side problems (bad offsets, a context shorter than its
+ * chunk) set kcmm_get_kernel_status bits.
+ */
+int kcmm_paged_prefill_bf16_on_stream(
+    kcmm_pool_t *pool, uint32_t layer_idx, uint64_t query_ptr, uint64_t out_ptr,
+    uint64_t block_tables_ptr, uint64_t query_start_loc_ptr, uint64_t context_lens_ptr,
+    uint64_t block_offsets_f16_ptr, uint32_t batch, uint32_t max_query_len,
+    uint32_t num_q_heads, uint32_t kv_heads, uint32_t head_dim, uint32_t block_size,
+    uint32_t max_blocks_per_seq, float scale, uint64_t stream_ptr);
+
+/** f16 twin of kcmm_paged_prefill_bf16_on_stream. */
+int kcmm_paged_prefill_f16_on_stream(
+    kcmm_pool_t *pool, uint32_t layer_idx, uint64_t query_ptr, uint64_t out_ptr,
+    uint64_t block_tables_ptr, uint64_t query_start_loc_ptr, uint64_t context_lens_ptr,
+    uint64_t block_offsets_f16_ptr, uint32_t batch, uint32_t max_query_len,
+    uint32_t num_q_heads, uint32_t kv_heads, uint32_t head_dim, uint32_t block_size,
+    uint32_t max_blocks_per_seq, float scale, uint64_t stream_ptr);
+
 /** bf16 name for the device-slot write (the write copies 16-bit words, so it is the f16 kernel). */
 int kcmm_append_kv_device_slots_bf16_on_stream(
     kcmm_pool_t *pool, uint32_t layer_idx, uint64_t slot_mapping_ptr,

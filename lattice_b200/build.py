@@ -28,9 +28,10 @@ ALIAS = PKG / "libbaseline_llm_os.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CU_SOURCES = ["kernels/decode.cu", "kernels/decode_noalloc.cu", "kernels/append.cu",
-              "kernels/copy.cu"]
+              "kernels/copy.cu", "kernels/prefill.cu"]
 CPP_SOURCES = ["pool.cpp", "vmm.cpp", "ffi.cpp"]
-HEADERS = ["kcmm_internal.hpp", "launch.hpp", "kernels/ptx.cuh", "kernels/decode_streamk.cuh"]
+HEADERS = ["kcmm_internal.hpp", "launch.hpp", "kernels/ptx.cuh", "kernels/decode_streamk.cuh",
+           "kernels/tcgen05.cuh"]
 
 
 def _nvcc() -> str:

@@ -540,6 +540,91 @@ int kcmm_paged_attn_decode_bf16_noalloc_on_stream(
                      hq, hkv, hd, bs, max_bps, scale, stream, false, true, true);
 }
 
+// ---------------------------------------------------------------------------
+// Chunked prefill (tcgen05)
+// ---------------------------------------------------------------------------
+
+static int prefill_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, uint64_t q,
+                        uint64_t out, uint64_t tables, uint64_t q_start, uint64_t ctx_lens,
+                        uint64_t offsets, uint32_t batch, uint32_t max_q_len, uint32_t hq,
+                        uint32_t hkv, uint32_t hd, uint32_t bs, uint32_t max_bps, float scale,
+                        uint64_t stream) {
+  const char *op = dtype == kcmm::dev::Dtype::F16 ? "kcmm_paged_prefill_f16_on_stream"
+                                                  : "kcmm_paged_prefill_bf16_on_stream";
+  if (!h || !q || !out || !tables || !q_start || !ctx_lens || !offsets) {
+    set_error(h, std::string(op) + ": null pointer argument");
+    return -1;
+  }
+  if (batch == 0 || max_q_len == 0 || hq == 0 || hkv == 0 || hd == 0 || bs == 0 ||
+      max_bps == 0) {
+    set_error(h, std::string(op) + ": shape arguments must be positive");
+    return -1;
+  }
+  if (hd != 128) {
+    set_error(h, std::string(op) + ": head_dim " + std::to_string(hd) +
+                     " unsupported (the tensor-core prefill kernel is built for 128)");
+    return -1;
+  }
+  if (hq % hkv != 0 || 128 % (hq / hkv) != 0) {
+    set_error(h, std::string(op) + ": num_q_heads / kv_heads must be an integer dividing 128");
+    return -1;
+  }
+  if (hq > 0xFFFF || hkv > 0xFFFF || bs > 0xFFFF || max_bps > 0xFFFF || batch > 0xFFFF) {
+    set_error(h, std::string(op) + ": packed shape argument exceeds 65535");
+    return -1;
+  }
+  if (((q | out) & 15) != 0) {
+    set_error(h, std::string(op) + ": query and output must be 16-byte aligned");
+    return -1;
+  }
+  Pool *p = P(h);
+  if (layer >= p->num_layers) {
+    set_error(h, std::string(op) + ": layer_idx " + std::to_string(layer) + " out of bounds");
+    return -1;
+  }
+  if (guarded(h, op, [&] { p->require_device(op); })) return -1;
+  p->use_device();
+  kcmm::dev::PrefillArgs a = {};
+  a.dtype = dtype;
+  a.q = reinterpret_cast<const void *>(q);
+  a.out = reinterpret_cast<void *>(out);
+  a.block_tables = reinterpret_cast<const int32_t *>(tables);
+  a.query_start = reinterpret_cast<const int32_t *>(q_start);
+  a.context_lens = reinterpret_cast<const int32_t *>(ctx_lens);
+  a.block_offsets = reinterpret_cast<const uint64_t *>(offsets);
+  a.va_k = reinterpret_cast<const void *>(p->va_k[layer]);
+  a.va_v = reinterpret_cast<const void *>(p->va_v[layer]);
+  a.region_elems = p->region_bytes / 2;
+  a.batch = int(batch);
+  a.max_q_len = int(max_q_len);
+  a.num_q_heads = int(hq);
+  a.kv_heads = int(hkv);
+  a.head_dim = int(hd);
+  a.block_size = int(bs);
+  a.max_blocks_per_seq = int(max_bps);
+  a.scale = scale;
+  a.diag = p->diag_word();
+  return check_launch(h, op, kcmm::dev::paged_prefill(a, S(stream)));
+}
+
+int kcmm_paged_prefill_bf16_on_stream(kcmm_pool_t *h, uint32_t layer, uint64_t q, uint64_t out,
+                                      uint64_t tables, uint64_t q_start, uint64_t ctx_lens,
+                                      uint64_t offsets, uint32_t batch, uint32_t max_q_len,
+                                      uint32_t hq, uint32_t hkv, uint32_t hd, uint32_t bs,
+                                      uint32_t max_bps, float scale, uint64_t stream) {
+  return prefill_impl(h, kcmm::dev::Dtype::BF16, layer, q, out, tables, q_start, ctx_lens,
+                      offsets, batch, max_q_len, hq, hkv, hd, bs, max_bps, scale, stream);
+}
+
+int kcmm_paged_prefill_f16_on_stream(kcmm_pool_t *h, uint32_t layer, uint64_t q, uint64_t out,
+                                     uint64_t tables, uint64_t q_start, uint64_t ctx_lens,
+                                     uint64_t offsets, uint32_t batch, uint32_t max_q_len,
+                                     uint32_t hq, uint32_t hkv, uint32_t hd, uint32_t bs,
+                                     uint32_t max_bps, float scale, uint64_t stream) {
+  return prefill_impl(h, kcmm::dev::Dtype::F16, layer, q, out, tables, q_start, ctx_lens,
+                      offsets, batch, max_q_len, hq, hkv, hd, bs, max_bps, scale, stream);
+}
+
 int kcmm_precompile_paged_attn_decode_f16(kcmm_pool_t *h) {
   if (!h) return -1;
   if (guarded(h, "kcmm_precompile_paged_attn_decode_f16", [&] {

@@ -1,0 +1,389 @@
+// Chunked prefill attention over paged KV on the sm_100a tensor cores (tcgen05).
+//
+// A chunk of q_len new tokens of sequence b sits at absolute positions
+// [ctx_len - q_len, ctx_len); its K/V rows are already in the pages.  Query
+// token t attends causally to keys [0, ctx_len - q_len + t].  The reference
+// has no prefill kernel (its prefill is a token-by-token decode loop,
+// ref src/model/transformer.rs:50-65); the arithmetic is the decode kernel's
+// softmax(scale * q.k) v (ref src/cuda/kernels/kcmm_vllm_paged_attn.cu:40-101)
+// with a causal limit per query row.
+//
+// CTA = 128 query rows x one kv head: TT = 128 / G tokens x the G query heads
+// of the GQA group (row r = token r / G, head r % G), so every K/V tile feeds
+// all heads of the group.  4 warps; thread r owns row r (TMEM lane r).
+//   per KV tile of 128 tokens (pages gathered by cp.async into 128-byte-swizzled
+//   shared memory, double buffered):
+//     S  = Q K^T      tcgen05.mma M128 N128 K16 x 8, fp32 in TMEM columns [0,128)
+//     softmax         tcgen05.ld S row -> causal mask, online max/sum in the
+//                     log2 domain, P -> swizzled shared memory as two 16-bit
+//                     tiles, P_hi = round(P) and P_lo = round(P - P_hi)
+//     O += P_hi V + P_lo V   tcgen05.mma M128 N128 K16 x 16 (V as an MN-major
+//                     operand), fp32 in TMEM columns [128,256)
+//   The P.V operands must share V's 16-bit type; a single rounded P leaves a
+//   relative error of 2^-9 per weight, which rows over a few keys with
+//   cancelling values do not average out.  The hi/lo pair carries P to ~2^-17.
+//   The running max is only raised when a tile's max exceeds it by more than
+//   2^8 (the rescale of O in TMEM is skipped otherwise); P stays <= 2^8.
+// Every mbarrier wait is bounded; a wait that runs out sets the pool's
+// diagnostic bit, the CTA drains its copies, frees its TMEM and returns.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "../launch.hpp"
+#include "ptx.cuh"
+#include "tcgen05.cuh"
+
+namespace kcmm {
+namespace dev {
+namespace {
+
+constexpr int kRows = 128;   // query rows per CTA (MMA M)
+constexpr int kKvTile = 128;  // keys per tile (MMA N of S, K of P.V)
+constexpr int kHd = 128;      // head_dim
+constexpr uint32_t kTile = 128 * 128 * 2;  // one 128 x 128 16-bit tile: 32 KB
+constexpr uint32_t kHalf = 128 * 128;      // one 64-column half (128 rows x 128 B)
+constexpr uint32_t kOffQ = 0;
+constexpr uint32_t kOffK = kOffQ + kTile;        // 2 stages
+constexpr uint32_t kOffV = kOffK + 2 * kTile;    // 2 stages
+constexpr uint32_t kOffP = kOffV + 2 * kTile;    // P_hi, then P_lo
+constexpr uint32_t kOffBar = kOffP + 2 * kTile;  // 2 mbarriers + TMEM slot
+constexpr size_t kSmem = kOffBar + 64 + 1024;    // + alignment slack
+constexpr uint32_t kTmemCols = 256;
+constexpr uint64_t kLimitNs = 1000000000ull;     // an MMA that has not finished in 1 s
+
+struct PrefillParams {
+  const uint16_t *q;
+  uint16_t *out;
+  const int32_t *tables;
+  const int32_t *q_start;   // [batch + 1]
+  const int32_t *ctx_lens;  // [batch]
+  const uint64_t *offsets;  // 2-byte units
+  const uint16_t *va_k;
+  const uint16_t *va_v;
+  uint64_t region_elems;
+  int hq, hkv, G, bs, max_bps, tt;
+  float scale_log2;
+  uint32_t idesc_qk, idesc_pv;
+  int32_t *diag;
+};
+
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  // byte offset of 16-byte chunk `chunk` (0..15) of a 256-byte row inside a
+  // [2 halves][128 rows][128 B] tile with the 128-byte swizzle
+  return uint32_t((chunk >> 3) * kHalf + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t v);
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t v) {
+  return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162 *>(&v));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t v) {
+  return __half22float2(*reinterpret_cast<__half2 *>(&v));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw = ptx::smem_u32(smem_raw);
+  const uint32_t sb = (raw + 1023u) & ~1023u;  // 1024-aligned base (swizzle atoms)
+  unsigned char *smem = smem_raw + (sb - raw);
+  __shared__ int s_fail;
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int q0 = p.q_start[b];
+  const int qlen = p.q_start[b + 1] - q0;
+  const int ctx = p.ctx_lens[b];
+  if (qt * p.tt >= qlen) return;  // no rows for this CTA
+  if (ctx < qlen || ctx > p.max_bps * p.bs) {
+    if (tid == 0) atomicOr(p.diag, int32_t(kDiagBadLaunch));
+    return;
+  }
+  const int base_pos = ctx - qlen;
+  const int ti_hi = min((qt + 1) * p.tt, qlen);
+  const int kv_hi = base_pos + ti_hi;  // keys [0, kv_hi) reach some row of this CTA
+  const int nt = (kv_hi + kKvTile - 1) / kKvTile;
+
+  const int row = tid;
+  const int ti = qt * p.tt + row / p.G;
+  const bool row_ok = ti < qlen;
+  const int qpos = row_ok ? base_pos + ti : kv_hi - 1;
+
+  const uint32_t bar_s = sb + kOffBar, bar_o = sb + kOffBar + 8, slot = sb + kOffBar + 16;
+  if (warp == 0) {
+    tc::tmem_alloc(slot, kTmemCols);
+    tc::tmem_relinquish();
+    tc::fence_before_sync();
+  }
+  if (tid == 0) {
+    ptx::mbar_init(bar_s, 1);
+    ptx::mbar_init(bar_o, 1);
+    ptx::fence_mbarrier_init();
+    s_fail = 0;
+  }
+
+  // --- Q tile: row r = (token, head) pair, zero rows past the chunk -----------------
+  {
+#pragma unroll 4
+    for (int it = 0; it < 16; ++it) {
+      const int idx = it * 128 + tid, r = idx >> 4, c = idx & 15;
+      const int t_r = qt * p.tt + r / p.G, h_r = h * p.G + r % p.G;
+      const bool ok = t_r < qlen;
+      const uint16_t *src =
+          ok ? p.q + (size_t(q0 + t_r) * p.hq + h_r) * kHd + c * 8 : p.q;
+      ptx::cp_async16(sb + kOffQ + swz(r, c), src, ok ? 16u : 0u);
+    }
+    ptx::cp_async_commit();
+  }
+
+  const size_t tok_stride = size_t(p.hkv) * kHd;
+  const int32_t *table = p.tables + size_t(b) * p.max_bps;
+  bool bad = false;
+  auto load_kv = [&](int j, int st) {
+    const uint32_t kb = sb + kOffK + st * kTile, vb = sb + kOffV + st * kTile;
+#pragma unroll 4
+    for (int it = 0; it < 16; ++it) {
+      const int idx = it * 128 + tid, n = idx >> 4, c = idx & 15;
+      const int kv = j * kKvTile + n;
+      int64_t e = -1;
+      if (kv < kv_hi) {
+        const int blk = table[kv / p.bs];
+        const uint64_t off = p.offsets[blk];
+        const uint64_t elem = off + uint64_t(kv % p.bs) * tok_stride + uint64_t(h) * kHd + c * 8;
+        if ((off & 7) == 0 && elem + 8 <= p.region_elems) {
+          e = int64_t(elem);
+        } else {
+          bad = true;
+        }
+      }
+      const uint32_t so = swz(n, c);
+      ptx::cp_async16(kb + so, e >= 0 ? p.va_k + e : p.va_k, e >= 0 ? 16u : 0u);
+      ptx::cp_async16(vb + so, e >= 0 ? p.va_v + e : p.va_v, e >= 0 ? 16u : 0u);
+    }
+    ptx::cp_async_commit();
+  };
+
+  load_kv(0, 0);
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + kOffBar + 16);
+  const uint32_t lane_base = uint32_t(warp * 32) << 16;
+  const uint32_t tS = tmem, tO = tmem + 128;
+
+  float m_run = -INFINITY, l_run = 0.f;
+  bool failed = false;
+  for (int j = 0; j < nt; ++j) {
+    const int st = j & 1;
+    if (j > 0) {  // P.V of tile j-1 done: its V stage, P and O are free
+      if (!ptx::mbar_wait_bounded(bar_o, uint32_t((j - 1) & 1), kLimitNs)) s_fail = 1;
+      tc::fence_after_sync();
+    }
+    if (j + 1 < nt) {
+      load_kv(j + 1, st ^ 1);
+      ptx::cp_async_wait<1>();
+    } else {
+      ptx::cp_async_wait<0>();
+    }
+    ptx::fence_proxy_async_smem();
+    __syncthreads();
+    if (s_fail) {
+      failed = true;
+      break;
+    }
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t qa = sb + kOffQ, ka = sb + kOffK + st * kTile;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t o = uint32_t((k >> 2) * kHalf + (k & 3) * 32);
+        tc::mma_ss(tS, tc::sw128_desc(qa + o, 16, 1024), tc::sw128_desc(ka + o, 16, 1024),
+                   p.idesc_qk, k > 0);
+      }
+      tc::commit(bar_s);
+    }
+    if (!ptx::mbar_wait_bounded(bar_s, uint32_t(j & 1), kLimitNs)) s_fail = 1;
+    tc::fence_after_sync();
+
+    float s[128];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) tc::ld32(tS + lane_base + c * 32, s + c * 32);
+    tc::wait_ld();
+
+    // causal mask (only the tiles that reach past some row's position) and tile max
+    const int k0 = j * kKvTile;
+    float mx = -INFINITY;
+    if (k0 + kKvTile - 1 > base_pos + qt * p.tt) {
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        if (k0 + c > qpos) s[c] = -INFINITY;
+        mx = fmaxf(mx, s[c]);
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, s[c]);
+    }
+    mx *= p.scale_log2;
+    float m_new = m_run;
+    if (mx > m_run + 8.f) m_new = mx;  // first tile: m_run = -inf
+    const float alpha = ptx::fast_exp2(m_run - m_new);  // 0 on the first tile, else <= 1
+    const bool rescale = j > 0 && m_new != m_run;
+    m_run = m_new;
+
+    // P = exp2(s * scale_log2 - m) -> swizzled shared tile (row-major over keys)
+    float sum = 0.f;
+    const uint32_t pa = sb + kOffP, pl = pa + kTile;
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      uint32_t w[4], r[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float a = ptx::fast_exp2(fmaf(s[c * 8 + 2 * e], p.scale_log2, -m_run));
+        const float bb = ptx::fast_exp2(fmaf(s[c * 8 + 2 * e + 1], p.scale_log2, -m_run));
+        sum += a + bb;
+        w[e] = pack2<T>(a, bb);
+        const float2 hv = unpack2<T>(w[e]);
+        r[e] = pack2<T>(a - hv.x, bb - hv.y);
+      }
+      const uint32_t so = swz(row, c);
+      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(pa + so), "r"(w[0]), "r"(w[1]),
+                   "r"(w[2]), "r"(w[3])
+                   : "memory");
+      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(pl + so), "r"(r[0]), "r"(r[1]),
+                   "r"(r[2]), "r"(r[3])
+                   : "memory");
+    }
+    l_run = l_run * alpha + sum;
+
+    if (__any_sync(0xffffffffu, rescale)) {  // O *= alpha (rows of this warp)
+      const float f = rescale ? alpha : 1.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float o[32];
+        tc::ld32(tO + lane_base + c * 32, o);
+        tc::wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] *= f;
+        tc::st32(tO + lane_base + c * 32, o);
+      }
+      tc::wait_st();
+    }
+    ptx::fence_proxy_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (s_fail) {
+      failed = true;
+      break;
+    }
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t va = sb + kOffV + st * kTile;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t ao = uint32_t((k >> 2) * kHalf + (k & 3) * 32);
+        // V: rows = keys (K), 64-element halves of head_dim (N) kHalf apart
+        const uint64_t vd = tc::sw128_desc(va + uint32_t(k) * 2048, kHalf, 1024);
+        tc::mma_ss(tO, tc::sw128_desc(pa + ao, 16, 1024), vd, p.idesc_pv,
+                   (j > 0 || k > 0) ? 1u : 0u);
+        tc::mma_ss(tO, tc::sw128_desc(pl + ao, 16, 1024), vd, p.idesc_pv, 1u);
+      }
+      tc::commit(bar_o);
+    }
+  }
+
+  if (!failed) {
+    if (!ptx::mbar_wait_bounded(bar_o, uint32_t((nt - 1) & 1), kLimitNs)) s_fail = 1;
+    tc::fence_after_sync();
+  }
+  __syncthreads();
+  failed = failed || s_fail;
+  if (!failed) {
+    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+    uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + row % p.G) * kHd;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float o[32];
+      tc::ld32(tO + lane_base + c * 32, o);
+      tc::wait_ld();
+      if (row_ok) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 v;
+          v.x = pack2<T>(o[q * 8 + 0] * inv, o[q * 8 + 1] * inv);
+          v.y = pack2<T>(o[q * 8 + 2] * inv, o[q * 8 + 3] * inv);
+          v.z = pack2<T>(o[q * 8 + 4] * inv, o[q * 8 + 5] * inv);
+          v.w = pack2<T>(o[q * 8 + 6] * inv, o[q * 8 + 7] * inv);
+          *reinterpret_cast<uint4 *>(dst + c * 32 + q * 8) = v;
+        }
+      }
+    }
+  } else {
+    ptx::cp_async_wait<0>();
+    if (tid == 0) atomicOr(p.diag, int32_t(kDiagWaitTimeout));
+  }
+  if (bad) atomicOr(p.diag, int32_t(kDiagBadOffset));
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace
+
+cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
+  if (a.head_dim != kHd || a.kv_heads <= 0 || a.num_q_heads % a.kv_heads != 0)
+    return cudaErrorInvalidValue;
+  const int G = a.num_q_heads / a.kv_heads;
+  if (G > kRows || kRows % G != 0) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.out)) & 15)
+    return cudaErrorInvalidValue;
+  if (a.batch <= 0 || a.max_q_len <= 0) return cudaSuccess;
+  PrefillParams p;
+  p.q = static_cast<const uint16_t *>(a.q);
+  p.out = static_cast<uint16_t *>(a.out);
+  p.tables = a.block_tables;
+  p.q_start = a.query_start;
+  p.ctx_lens = a.context_lens;
+  p.offsets = a.block_offsets;
+  p.va_k = static_cast<const uint16_t *>(a.va_k);
+  p.va_v = static_cast<const uint16_t *>(a.va_v);
+  p.region_elems = a.region_elems;
+  p.hq = a.num_q_heads;
+  p.hkv = a.kv_heads;
+  p.G = G;
+  p.bs = a.block_size;
+  p.max_bps = a.max_blocks_per_seq;
+  p.tt = kRows / G;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  const bool bf16 = a.dtype == Dtype::BF16;
+  p.idesc_qk = tc::idesc_f16(bf16, 128, 128, false, false);
+  p.idesc_pv = tc::idesc_f16(bf16, 128, 128, false, true);
+  p.diag = a.diag;
+  auto fn = bf16 ? prefill_kernel<__nv_bfloat16> : prefill_kernel<__half>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem));
+  if (e != cudaSuccess) return e;
+  dim3 grid((a.max_q_len + p.tt - 1) / p.tt, a.kv_heads, a.batch);
+  fn<<<grid, 128, kSmem, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace dev
+}  // namespace kcmm

@@ -85,6 +85,21 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32
                : "memory");
 }
 
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Wait until at most N of this thread's committed cp.async groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Make mbarrier initialisation visible to the other proxies (tensor-core commits).
+__device__ __forceinline__ void fence_mbarrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
 // The mbarrier receives one arrival from this thread once all of the thread's
 // earlier cp.async copies have landed (its expected count must include it).
 __device__ __forceinline__ void cp_async_mbar_arrive(uint32_t bar) {

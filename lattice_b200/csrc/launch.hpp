@@ -56,6 +56,25 @@ cudaError_t decode_attention_noalloc(const DecodeArgs &a, cudaStream_t stream);
 // Force module load of every decode kernel (precompile entry points).
 cudaError_t decode_preload();
 
+struct PrefillArgs {
+  Dtype dtype;
+  const void *q;      // [total_q_tokens, num_q_heads, head_dim]
+  void *out;          // same shape
+  const int32_t *block_tables;  // [batch, max_blocks_per_seq]
+  const int32_t *query_start;   // [batch + 1] prefix sum of chunk lengths
+  const int32_t *context_lens;  // [batch] keys after the chunk (chunk included)
+  const uint64_t *block_offsets;
+  const void *va_k;
+  const void *va_v;
+  uint64_t region_elems;
+  int batch, max_q_len, num_q_heads, kv_heads, head_dim, block_size, max_blocks_per_seq;
+  float scale;
+  int32_t *diag;
+};
+// Causal chunked-prefill attention on the tcgen05 tensor cores
+// (kernels/prefill.cu).  head_dim 128; num_q_heads / kv_heads must divide 128.
+cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream);
+
 // Copy `rows` K and V rows of `row_elems` 16-bit elements from k_src/v_src
 // (row r at r*row_elems) to va_k/va_v + dst_elems[r]; dst_elems[r] < 0 skips.
 cudaError_t copy_rows(const void *k_src, const void *v_src, void *va_k, void *va_v,

@@ -204,6 +204,12 @@ SIGNATURES: dict[str, tuple] = {
         (i32, [P, u32, u64, u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, f32, u64]),
     "kcmm_paged_attn_decode_bf16_noalloc_on_stream":
         (i32, [P, u32, u64, u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, f32, u64]),
+    "kcmm_paged_prefill_bf16_on_stream":
+        (i32, [P, u32, u64, u64, u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, u32, f32,
+               u64]),
+    "kcmm_paged_prefill_f16_on_stream":
+        (i32, [P, u32, u64, u64, u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, u32, f32,
+               u64]),
     "kcmm_append_kv_device_slots_bf16_on_stream":
         (i32, [P, u32, u64, u64, u64, u32, u32, u64, u64, u64, u64]),
     "kcmm_fused_norm_rope_append_bf16_on_stream":
@@ -507,6 +513,19 @@ class KcmmPool:
             rc = self.lib.kcmm_paged_attn_decode_f16_on_stream(*args, stream_ptr)
             op = "kcmm_paged_attn_decode_f16_on_stream"
         self._check(rc, op)
+
+    def paged_prefill(self, layer: int, *, query_ptr: int, out_ptr: int, block_tables_ptr: int,
+                      query_start_loc_ptr: int, context_lens_ptr: int,
+                      block_offsets_f16_ptr: int, batch: int, max_query_len: int,
+                      num_q_heads: int, kv_heads: int, head_dim: int, block_size: int,
+                      max_blocks_per_seq: int, scale: float, dtype: str = "bf16",
+                      stream_ptr: int = 0) -> None:
+        op = f"kcmm_paged_prefill_{dtype}_on_stream"
+        fn = getattr(self.lib, op)
+        self._check(fn(self.handle, layer, query_ptr, out_ptr, block_tables_ptr,
+                       query_start_loc_ptr, context_lens_ptr, block_offsets_f16_ptr, batch,
+                       max_query_len, num_q_heads, kv_heads, head_dim, block_size,
+                       max_blocks_per_seq, scale, stream_ptr), op)
 
     def precompile_paged_attn_decode_f16(self) -> None:
         self._check(self.lib.kcmm_precompile_paged_attn_decode_f16(self.handle),

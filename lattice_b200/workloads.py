@@ -266,6 +266,78 @@ class FusedAppendWorkload:
         self.pool = None
 
 
+@dataclass
+class PrefillWorkload:
+    """A chunk of new tokens per sequence over paged KV (pages from a DecodeWorkload whose
+    seq_lens are the context lengths after the chunk)."""
+
+    ctx_lens: list
+    chunk_lens: list
+    num_q_heads: int = 8
+    kv_heads: int = 1
+    head_dim: int = 128
+    block_size: int = 16
+    pool_blocks: int = 0
+    dtype: str = "bf16"
+    seed: int = 0
+    fill: str = "host"
+    device: int = 0
+
+    def build(self) -> "PrefillWorkload":
+        torch = _torch()
+        assert all(0 <= c <= L for c, L in zip(self.chunk_lens, self.ctx_lens))
+        bs = self.block_size
+        need = sum(max(1, -(-int(L) // bs)) for L in self.ctx_lens)
+        self.kv = DecodeWorkload(
+            batch=len(self.ctx_lens), num_q_heads=self.num_q_heads, kv_heads=self.kv_heads,
+            head_dim=self.head_dim, block_size=bs, pool_blocks=max(self.pool_blocks, need),
+            max_len=max(self.ctx_lens), dtype=self.dtype, seed=self.seed,
+            seq_lens_override=list(self.ctx_lens), fill=self.fill, device=self.device).build()
+        dev = f"cuda:{self.device}"
+        self.q_start = np.concatenate([[0], np.cumsum(self.chunk_lens)]).astype(np.int32)
+        total = int(self.q_start[-1])
+        gen = torch.Generator(device=dev).manual_seed(self.seed + 7)
+        self.q = torch.randn(max(total, 1), self.num_q_heads, self.head_dim, device=dev,
+                             generator=gen).to(self.kv.tdtype)
+        self.out = torch.zeros_like(self.q)
+        self.d_q_start = torch.from_numpy(self.q_start).to(dev)
+        self.d_ctx = torch.from_numpy(np.asarray(self.ctx_lens, np.int32)).to(dev)
+        self.scale = 1.0 / math.sqrt(self.head_dim)
+        self.max_q_len = max(1, max(self.chunk_lens))
+        torch.cuda.synchronize()
+        return self
+
+    @property
+    def pool(self):
+        return self.kv.pool
+
+    def run(self, stream_ptr: int | None = None, out=None) -> None:
+        torch = _torch()
+        if stream_ptr is None:
+            stream_ptr = torch.cuda.current_stream().cuda_stream
+        out = self.out if out is None else out
+        kv = self.kv
+        self.pool.paged_prefill(
+            0, query_ptr=self.q.data_ptr(), out_ptr=out.data_ptr(),
+            block_tables_ptr=kv.d_tables.data_ptr(), query_start_loc_ptr=self.d_q_start.data_ptr(),
+            context_lens_ptr=self.d_ctx.data_ptr(), block_offsets_f16_ptr=kv.d_offsets.data_ptr(),
+            batch=len(self.ctx_lens), max_query_len=self.max_q_len, num_q_heads=self.num_q_heads,
+            kv_heads=self.kv_heads, head_dim=self.head_dim, block_size=self.block_size,
+            max_blocks_per_seq=kv.max_blocks_per_seq, scale=self.scale, dtype=self.dtype,
+            stream_ptr=stream_ptr)
+
+    def flops(self) -> int:
+        """Causal attention FLOPs: 4 * d per (query row, key) pair with key <= position."""
+        total = 0
+        for L, c in zip(self.ctx_lens, self.chunk_lens):
+            base = L - c
+            total += c * base + c * (c + 1) // 2
+        return 4 * self.head_dim * self.num_q_heads * total
+
+    def close(self) -> None:
+        self.kv.close()
+
+
 def tensor_bits(t) -> np.ndarray:
     """uint16 bit pattern of a bf16/f16 torch tensor (host copy)."""
     torch = _torch()

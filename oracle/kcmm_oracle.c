@@ -131,6 +131,65 @@ void oracle_paged_attn(int dt, const void *q, void *out, float *out_f32, const v
   }
 }
 
+/* --- chunked prefill: causal paged attention for a chunk of new tokens ---------
+ * The reference has no prefill kernel (ref src/model/transformer.rs:50-65 runs
+ * prefill as decode steps); each query row is the decode computation above
+ * (ref kcmm_vllm_paged_attn.cu:40-101, GQA map h*hkv/hq) over keys
+ * [0, position], position = ctx_lens[b] - chunk length + i.  q/out rows are
+ * [total_tokens][hq][d]; rows whose token has mask[token] == 0 are skipped
+ * (mask may be NULL). */
+void oracle_paged_prefill(int dt, const void *q, float *out_f32, const void *va_k,
+                          const void *va_v, const int32_t *tables, const int32_t *q_start,
+                          const int32_t *ctx_lens, const uint64_t *offsets, const uint8_t *mask,
+                          int batch, int hq, int hkv, int d, int bs, int max_bps, float scale) {
+  const int esize = dt == DT_F32 ? 4 : 2;
+  const int64_t total = q_start[batch];
+  #pragma omp parallel for schedule(dynamic, 4)
+  for (int64_t th = 0; th < total * hq; ++th) {
+    const int64_t tok = th / hq;
+    const int h = (int)(th % hq);
+    if (mask && !mask[tok]) continue;
+    int b = 0;
+    while (b + 1 < batch && q_start[b + 1] <= tok) ++b;
+    const int qlen = q_start[b + 1] - q_start[b];
+    const int i = (int)(tok - q_start[b]);
+    const int L = ctx_lens[b] - qlen + i + 1;  /* keys [0, position] */
+    const int kvh = (int)((int64_t)h * hkv / hq);
+    if (L <= 0) continue;
+    double *logits = (double *)malloc(sizeof(double) * (size_t)L);
+    double *acc = (double *)calloc((size_t)d, sizeof(double));
+    double *qv = (double *)malloc(sizeof(double) * (size_t)d);
+    for (int e = 0; e < d; ++e) qv[e] = load_elem(dt, q, th * d + e);
+    double mx = -INFINITY;
+    for (int t = 0; t < L; ++t) {
+      const int blk = tables[(int64_t)b * max_bps + t / bs];
+      const uint8_t *kb = (const uint8_t *)va_k + offsets[blk] * 2 +
+                          ((int64_t)(t % bs) * hkv * d + (int64_t)kvh * d) * esize;
+      double sc = 0.0;
+      for (int e = 0; e < d; ++e) sc += qv[e] * load_elem(dt, kb, e);
+      sc *= (double)scale;
+      logits[t] = sc;
+      if (sc > mx) mx = sc;
+    }
+    double den = 0.0;
+    for (int t = 0; t < L; ++t) {
+      logits[t] = exp(logits[t] - mx);
+      den += logits[t];
+    }
+    for (int t = 0; t < L; ++t) {
+      const int blk = tables[(int64_t)b * max_bps + t / bs];
+      const uint8_t *vb = (const uint8_t *)va_v + offsets[blk] * 2 +
+                          ((int64_t)(t % bs) * hkv * d + (int64_t)kvh * d) * esize;
+      const double pr = logits[t] / den;
+      for (int e = 0; e < d; ++e) acc[e] += pr * load_elem(dt, vb, e);
+    }
+    for (int e = 0; e < d; ++e) out_f32[th * d + e] = (float)acc[e];
+    free(logits);
+    free(acc);
+    free(qv);
+  }
+}
+
 /* --- RMSNorm (ref rms_norm.cu:14-35): y = ((x * (1/sqrt(mean(x^2)+eps))) * w) -- */
 void oracle_rms_norm(int dt, const void *x, const void *w, void *y, int rows, int cols,
                      float eps) {

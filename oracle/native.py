@@ -114,6 +114,24 @@ def paged_attn(dtype: str, q, va_k, va_v, tables, seq_lens, offsets, *, hq, hkv,
     return out_f32
 
 
+def paged_prefill(dtype: str, q, va_k, va_v, tables, q_start, ctx_lens, offsets, *, hq, hkv,
+                  d, bs, max_bps, scale, token_mask=None):
+    """Causal chunked-prefill attention; q bits [total_tokens, hq*d].  Returns fp32
+    [total_tokens, hq, d]; tokens with token_mask == 0 are left at zero."""
+    q_start = np.ascontiguousarray(q_start, np.int32)
+    total = int(q_start[-1])
+    out_f32 = np.zeros((total, hq, d), np.float32)
+    mask = None if token_mask is None else np.ascontiguousarray(token_mask, np.uint8)
+    oracle_lib().oracle_paged_prefill(
+        ctypes.c_int(DT[dtype]), _ptr(q), _ptr(out_f32), _ptr(va_k), _ptr(va_v),
+        _ptr(np.ascontiguousarray(tables, np.int32)), _ptr(q_start),
+        _ptr(np.ascontiguousarray(ctx_lens, np.int32)),
+        _ptr(np.ascontiguousarray(offsets, np.uint64)), _ptr(mask) if mask is not None else None,
+        ctypes.c_int(len(q_start) - 1), ctypes.c_int(hq), ctypes.c_int(hkv), ctypes.c_int(d),
+        ctypes.c_int(bs), ctypes.c_int(max_bps), ctypes.c_float(scale))
+    return out_f32
+
+
 def rms_norm(dtype: str, x, w, eps: float):
     rows, cols = x.shape
     y = np.zeros_like(x)

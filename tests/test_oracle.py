@@ -147,3 +147,31 @@ def test_rope_modes_and_theta():
         else:
             want[..., : D // 2], want[..., D // 2:] = y0, y1
         np.testing.assert_allclose(got, want, atol=2e-3, rtol=1e-2)
+
+
+def test_prefill_oracle_rows_are_decode_steps():
+    """Pins the prefill restatement to the decode one (itself pinned to the reference
+    kernel): chunk row i equals decode over the first ctx - chunk + i + 1 keys."""
+    from oracle import native as N
+
+    rng = np.random.default_rng(3)
+    hq, hkv, d, bs = 8, 2, 64, 16
+    ctx, chunk = np.array([70, 45], np.int32), np.array([9, 45], np.int32)
+    nblk = 8
+    tables = np.stack([rng.permutation(nblk)[:5], rng.permutation(nblk)[:5]]).astype(np.int32)
+    step = hkv * d
+    offsets = np.arange(nblk, dtype=np.uint64) * np.uint64(bs * step)
+    va_k = N.f32_to_bf16_bits(rng.standard_normal(nblk * bs * step).astype(np.float32))
+    va_v = N.f32_to_bf16_bits(rng.standard_normal(nblk * bs * step).astype(np.float32))
+    qs = np.array([0, 9, 54], np.int32)
+    q = N.f32_to_bf16_bits(rng.standard_normal((54, hq * d)).astype(np.float32))
+    got = N.paged_prefill("bf16", q, va_k, va_v, tables, qs, ctx, offsets, hq=hq, hkv=hkv, d=d,
+                          bs=bs, max_bps=5, scale=0.125)
+    for b in range(2):
+        for i in range(int(chunk[b])):
+            tok = qs[b] + i
+            L = int(ctx[b] - chunk[b] + i + 1)
+            ref = N.paged_attn("bf16", q[tok:tok + 1], va_k, va_v, tables[b:b + 1],
+                               np.array([L], np.int32), offsets, hq=hq, hkv=hkv, d=d, bs=bs,
+                               max_bps=5, scale=0.125)
+            np.testing.assert_allclose(got[tok], ref[0], rtol=1e-6, atol=1e-6)

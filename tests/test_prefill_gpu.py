@@ -1,0 +1,132 @@
+"""Chunked prefill on the tcgen05 tensor cores, through the C ABI, against the CPU oracle.
+
+Tolerance (north star, fp32 reference): |out - ref| <= 2e-3 + 1e-2 * |ref| elementwise."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-3, 1e-2
+
+
+def _torch():
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+def make(**kw):
+    from lattice_b200.workloads import PrefillWorkload
+
+    _torch()
+    return PrefillWorkload(**kw).build()
+
+
+def oracle(wl, token_mask=None):
+    from lattice_b200.workloads import tensor_bits
+    from oracle import native as N
+
+    kv = wl.kv
+    q = tensor_bits(wl.q).reshape(wl.q.shape[0], -1)
+    return N.paged_prefill(wl.dtype, q, kv.host_region(0, "k"), kv.host_region(0, "v"),
+                           kv.tables, wl.q_start, wl.ctx_lens, kv.offsets, hq=wl.num_q_heads,
+                           hkv=wl.kv_heads, d=wl.head_dim, bs=wl.block_size,
+                           max_bps=kv.max_blocks_per_seq, scale=wl.scale, token_mask=token_mask)
+
+
+def check(wl, rows=None):
+    ref = oracle(wl)
+    got = wl.out.float().cpu().numpy()
+    total = int(wl.q_start[-1])
+    sel = slice(0, total) if rows is None else rows
+    err = np.abs(got[sel] - ref[sel])
+    bound = ATOL + RTOL * np.abs(ref[sel])
+    assert (err <= bound).all(), f"max err {err.max()} (worst excess {(err - bound).max()})"
+
+
+CASES = [
+    # ctx lens, chunk lens, hq, hkv
+    ([300, 1000, 777], [100, 256, 777], 8, 1),      # 70B per-GPU shard (GQA 8): full prefill too
+    ([129, 513, 64], [1, 200, 64], 32, 8),          # Llama-3-8B heads (GQA 4)
+    ([400, 333], [130, 333], 4, 4),                 # MHA: 128 tokens per CTA
+    ([600, 90], [77, 90], 32, 2),                   # GQA 16: 8 tokens per CTA
+    ([250, 700, 31], [0, 129, 31], 16, 8),          # an empty chunk; GQA 2
+]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("case", CASES, ids=[f"g{c[2] // c[3]}_{i}" for i, c in enumerate(CASES)])
+def test_prefill_matches_oracle(case, dtype):
+    ctx, chunks, hq, hkv = case
+    wl = make(ctx_lens=ctx, chunk_lens=chunks, num_q_heads=hq, kv_heads=hkv, dtype=dtype,
+              seed=sum(ctx) % 97)
+    try:
+        wl.run()
+        _torch().cuda.synchronize()
+        check(wl)
+        assert wl.pool.kernel_status() == 0
+    finally:
+        wl.close()
+
+
+def test_prefill_last_row_equals_decode():
+    """The last row of a chunk is a decode step over the whole context: both kernels agree."""
+    torch = _torch()
+    wl = make(ctx_lens=[900, 1500], chunk_lens=[300, 64], num_q_heads=32, kv_heads=8, seed=5)
+    try:
+        wl.run()
+        kv = wl.kv
+        last = torch.stack([wl.q[int(wl.q_start[b + 1]) - 1] for b in range(2)])
+        kv.q.copy_(last)
+        kv.decode()
+        torch.cuda.synchronize()
+        got = torch.stack([wl.out[int(wl.q_start[b + 1]) - 1] for b in range(2)]).float()
+        ref = kv.out.float()
+        assert torch.allclose(got, ref, atol=ATOL, rtol=RTOL)
+    finally:
+        wl.close()
+
+
+def test_prefill_70b_chunk_full_context():
+    """Config-5 shape at full context per GPU: a 2048-token chunk at the end of a 32768-token
+    sequence (8 q heads on 1 kv head).  Checked on a sample of rows against the oracle."""
+    torch = _torch()
+    wl = make(ctx_lens=[32768], chunk_lens=[2048], num_q_heads=8, kv_heads=1, seed=11)
+    try:
+        wl.run()
+        torch.cuda.synchronize()
+        rng = np.random.default_rng(0)
+        toks = np.unique(np.concatenate([[0, 1, 127, 128, 2047], rng.integers(0, 2048, 11)]))
+        mask = np.zeros(2048, np.uint8)
+        mask[toks] = 1
+        ref = oracle(wl, token_mask=mask)
+        got = wl.out.float().cpu().numpy()
+        err = np.abs(got[toks] - ref[toks])
+        assert (err <= ATOL + RTOL * np.abs(ref[toks])).all(), err.max()
+        assert wl.pool.kernel_status() == 0
+    finally:
+        wl.close()
+
+
+def test_prefill_rejects_unsupported_shapes():
+    from lattice_b200.kcmm import KcmmError
+
+    wl = make(ctx_lens=[40], chunk_lens=[8], num_q_heads=8, kv_heads=1, seed=1)
+    try:
+        kv = wl.kv
+        base = dict(query_ptr=wl.q.data_ptr(), out_ptr=wl.out.data_ptr(),
+                    block_tables_ptr=kv.d_tables.data_ptr(),
+                    query_start_loc_ptr=wl.d_q_start.data_ptr(),
+                    context_lens_ptr=wl.d_ctx.data_ptr(),
+                    block_offsets_f16_ptr=kv.d_offsets.data_ptr(), batch=1, max_query_len=8,
+                    block_size=16, max_blocks_per_seq=kv.max_blocks_per_seq, scale=0.1)
+        with pytest.raises(KcmmError, match="head_dim 64 unsupported"):
+            wl.pool.paged_prefill(0, num_q_heads=8, kv_heads=1, head_dim=64, **base)
+        with pytest.raises(KcmmError, match="dividing 128"):
+            wl.pool.paged_prefill(0, num_q_heads=6, kv_heads=2, head_dim=128, **base)
+    finally:
+        wl.close()
