@@ -747,6 +747,76 @@ def run_swap_leg(args):
          "pinned_link_gbs": {k: round(v, 2) for k, v in link.items()}, "status": status})
 
 
+def run_prefill_leg(args):
+    """Chunked prefill (per GPU: 8 q heads on 1 kv head, D 128, bf16):
+    8 sequences of 32,768 tokens prefilled in 16 chunks of 2048 tokens, one launch per
+    chunk for all 8 sequences (one layer).  Tensor-bound: causal FLOPs / time against
+    the measured bf16 dense peak."""
+    import torch
+
+    from lattice_b200.workloads import PrefillWorkload
+
+    torch.cuda.set_device(0)
+    seqs, ctx, chunk, hq, hkv = 8, 32768, 2048, 8, 1
+    wl = PrefillWorkload(ctx_lens=[ctx] * seqs, chunk_lens=[chunk] * seqs, num_q_heads=hq,
+                         kv_heads=hkv, seed=5, fill="device").build()
+    ctx_by_chunk = [torch.full((seqs,), (c + 1) * chunk, dtype=torch.int32, device="cuda")
+                    for c in range(ctx // chunk)]
+    sp = torch.cuda.current_stream().cuda_stream
+
+    def chunk_call(c):
+        wl.d_ctx = ctx_by_chunk[c]
+        wl.run(stream_ptr=sp)
+
+    def flops(c):
+        base = c * chunk
+        return 4 * 128 * hq * seqs * (chunk * base + chunk * (chunk + 1) // 2)
+
+    for _ in range(max(args.warmup, 3)):
+        chunk_call(ctx // chunk - 1)
+    torch.cuda.synchronize()
+    steps = max(1, min(args.steps, 5))
+    nchunks = ctx // chunk
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(nchunks)] for _ in range(steps)]
+    clocks = ClockSampler(0)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for s_ in range(steps):
+        for c in range(nchunks):
+            ev[s_][c][0].record()
+            chunk_call(c)
+            ev[s_][c][1].record()
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / steps
+    total = sum(flops(c) for c in range(nchunks))
+    per_chunk = [statistics.median(ev[s_][c][0].elapsed_time(ev[s_][c][1]) for s_ in range(steps))
+                 for c in range(nchunks)]
+    last_tf = flops(nchunks - 1) / (per_chunk[-1] * 1e-3) / 1e12
+    tf = total / (ms * 1e-3) / 1e12
+    status = wl.pool.kernel_status()
+    wl.close()
+    d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(d.get("bf16_tflops", 1590.0))
+    kind = "measured (burst)" if d else "fallback"
+    return _line(
+        "chunked prefill TFLOP/s (causal, 32k context in 2048-token chunks)", tf, "TFLOP/s",
+        {"workload": "BASELINE config 5 per GPU: 8 seqs x 32768 tokens, 2048-token chunks, "
+                     "8 q heads / 1 kv head, D 128, bf16, one layer", "launches": nchunks},
+        {"bound": "tensor", "achieved": round(last_tf, 1), "peak": peak, "unit": "TFLOP/s",
+         "frac": round(last_tf / peak, 4), "traffic": None, "peak_kind": kind,
+         "kernel": "prefill_kernel, last chunk (2048 queries x 32768 keys x 8 seqs)",
+         "algorithmic_flops_per_launch": flops(nchunks - 1)},
+        {"ms_per_layer": round(ms, 3), "total_flops": total,
+         "frac_of_peak_all_chunks": round(tf / peak, 4),
+         "sustained_peak": d.get("bf16_tflops_sustained"),
+         "us_per_chunk": [round(t * 1e3, 1) for t in per_chunk], "clocks": clk,
+         "status": status})
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -755,7 +825,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--profile", action="store_true",
                     help="profiling case for ncu: 12k-block pool, no CPU baseline / e2e legs")
-    ap.add_argument("--workload", choices=["step", "append", "cow", "swap"], default="step",
+    ap.add_argument("--workload", choices=["step", "append", "cow", "swap", "prefill"],
+                    default="step",
                     help="step = the headline (default); the others print one line for a "
                          "secondary BASELINE config")
     args = ap.parse_args()
@@ -767,6 +838,8 @@ def main():
         run_cow_leg(args)
     elif args.workload == "swap":
         run_swap_leg(args)
+    elif args.workload == "prefill":
+        run_prefill_leg(args)
     else:
         run_ours(args)
 

@@ -28,7 +28,11 @@
 // diagnostic bit, the CTA drains its copies, frees its TMEM and returns.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda.h>
 #include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <cstring>
 
 #include "../launch.hpp"
 #include "ptx.cuh"
@@ -87,6 +91,40 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t *>(&v);
 }
 
+// Online-softmax step for one row over one key tile, in place: s[c] becomes
+// P = exp2(s * scale_log2 - m) with keys past `qpos` masked out (when the tile
+// reaches past the CTA's first row).  The running max m is only raised when the
+// tile's max exceeds it by more than 8 (log2 units).  Returns the row sum of P;
+// alpha = exp2(m_old - m_new) rescales the earlier sum and O.
+__device__ __forceinline__ float exp_tile(float (&s)[128], int k0, int qpos, bool need_mask,
+                                          float scale_log2, bool has_prev, float &m_run,
+                                          float &alpha, bool &rescale) {
+  float mx = -INFINITY;
+  if (need_mask) {
+#pragma unroll
+    for (int c = 0; c < 128; ++c) {
+      if (k0 + c > qpos) s[c] = -INFINITY;
+      mx = fmaxf(mx, s[c]);
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 128; ++c) mx = fmaxf(mx, s[c]);
+  }
+  mx *= scale_log2;
+  float m_new = m_run;
+  if (mx > m_run + 8.f) m_new = mx;  // first tile: m_run = -inf
+  alpha = ptx::fast_exp2(m_run - m_new);  // 0 on the first tile, else <= 1
+  rescale = has_prev && m_new != m_run;
+  m_run = m_new;
+  float sum = 0.f;
+#pragma unroll
+  for (int c = 0; c < 128; ++c) {
+    s[c] = ptx::fast_exp2(fmaf(s[c], scale_log2, -m_new));
+    sum += s[c];
+  }
+  return sum;
+}
+
 template <typename T>
 __device__ __forceinline__ float2 unpack2(uint32_t v);
 template <>
@@ -96,6 +134,65 @@ __device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t v) {
 template <>
 __device__ __forceinline__ float2 unpack2<__half>(uint32_t v) {
   return __half22float2(*reinterpret_cast<__half2 *>(&v));
+}
+
+// P row -> the P_hi and P_lo tiles (128-byte swizzle, keys along the row).
+template <typename T>
+__device__ __forceinline__ void store_p(const float (&s)[128], uint32_t pa, uint32_t pl, int row) {
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    uint32_t w[4], r[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float a = s[c * 8 + 2 * e], bb = s[c * 8 + 2 * e + 1];
+      w[e] = pack2<T>(a, bb);
+      const float2 hv = unpack2<T>(w[e]);
+      r[e] = pack2<T>(a - hv.x, bb - hv.y);
+    }
+    const uint32_t so = swz(row, c);
+    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(pa + so), "r"(w[0]), "r"(w[1]),
+                 "r"(w[2]), "r"(w[3])
+                 : "memory");
+    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(pl + so), "r"(r[0]), "r"(r[1]),
+                 "r"(r[2]), "r"(r[3])
+                 : "memory");
+  }
+}
+
+// Store one row of O (fp32 in TMEM, 128 columns) / l to global memory.
+template <typename T>
+__device__ __forceinline__ void store_o_row(uint32_t t_row, float inv, uint16_t *dst, bool ok) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float o[32];
+    tc::ld32(t_row + c * 32, o);
+    tc::wait_ld();
+    if (ok) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 v;
+        v.x = pack2<T>(o[q * 8 + 0] * inv, o[q * 8 + 1] * inv);
+        v.y = pack2<T>(o[q * 8 + 2] * inv, o[q * 8 + 3] * inv);
+        v.z = pack2<T>(o[q * 8 + 4] * inv, o[q * 8 + 5] * inv);
+        v.w = pack2<T>(o[q * 8 + 6] * inv, o[q * 8 + 7] * inv);
+        *reinterpret_cast<uint4 *>(dst + c * 32 + q * 8) = v;
+      }
+    }
+  }
+}
+
+// O row *= f (all lanes of the warp execute this; f = 1 for rows that keep their max).
+__device__ __forceinline__ void scale_o_row(uint32_t t_row, float f) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float o[32];
+    tc::ld32(t_row + c * 32, o);
+    tc::wait_ld();
+#pragma unroll
+    for (int e = 0; e < 32; ++e) o[e] *= f;
+    tc::st32(t_row + c * 32, o);
+  }
+  tc::wait_st();
 }
 
 template <typename T>
@@ -226,64 +323,15 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
     for (int c = 0; c < 4; ++c) tc::ld32(tS + lane_base + c * 32, s + c * 32);
     tc::wait_ld();
 
-    // causal mask (only the tiles that reach past some row's position) and tile max
-    const int k0 = j * kKvTile;
-    float mx = -INFINITY;
-    if (k0 + kKvTile - 1 > base_pos + qt * p.tt) {
-#pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        if (k0 + c > qpos) s[c] = -INFINITY;
-        mx = fmaxf(mx, s[c]);
-      }
-    } else {
-#pragma unroll
-      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, s[c]);
-    }
-    mx *= p.scale_log2;
-    float m_new = m_run;
-    if (mx > m_run + 8.f) m_new = mx;  // first tile: m_run = -inf
-    const float alpha = ptx::fast_exp2(m_run - m_new);  // 0 on the first tile, else <= 1
-    const bool rescale = j > 0 && m_new != m_run;
-    m_run = m_new;
-
-    // P = exp2(s * scale_log2 - m) -> swizzled shared tile (row-major over keys)
-    float sum = 0.f;
     const uint32_t pa = sb + kOffP, pl = pa + kTile;
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      uint32_t w[4], r[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float a = ptx::fast_exp2(fmaf(s[c * 8 + 2 * e], p.scale_log2, -m_run));
-        const float bb = ptx::fast_exp2(fmaf(s[c * 8 + 2 * e + 1], p.scale_log2, -m_run));
-        sum += a + bb;
-        w[e] = pack2<T>(a, bb);
-        const float2 hv = unpack2<T>(w[e]);
-        r[e] = pack2<T>(a - hv.x, bb - hv.y);
-      }
-      const uint32_t so = swz(row, c);
-      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(pa + so), "r"(w[0]), "r"(w[1]),
-                   "r"(w[2]), "r"(w[3])
-                   : "memory");
-      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(pl + so), "r"(r[0]), "r"(r[1]),
-                   "r"(r[2]), "r"(r[3])
-                   : "memory");
-    }
+    float alpha;
+    bool rescale;
+    const float sum = exp_tile(s, j * kKvTile, qpos, j * kKvTile + kKvTile - 1 > base_pos + qt * p.tt,
+                               p.scale_log2, j > 0, m_run, alpha, rescale);
+    store_p<T>(s, pa, pl, row);
     l_run = l_run * alpha + sum;
 
-    if (__any_sync(0xffffffffu, rescale)) {  // O *= alpha (rows of this warp)
-      const float f = rescale ? alpha : 1.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float o[32];
-        tc::ld32(tO + lane_base + c * 32, o);
-        tc::wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] *= f;
-        tc::st32(tO + lane_base + c * 32, o);
-      }
-      tc::wait_st();
-    }
+    if (__any_sync(0xffffffffu, rescale)) scale_o_row(tO + lane_base, rescale ? alpha : 1.f);
     ptx::fence_proxy_async_smem();
     tc::fence_before_sync();
     __syncthreads();
@@ -316,23 +364,7 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
   if (!failed) {
     const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
     uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + row % p.G) * kHd;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float o[32];
-      tc::ld32(tO + lane_base + c * 32, o);
-      tc::wait_ld();
-      if (row_ok) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 v;
-          v.x = pack2<T>(o[q * 8 + 0] * inv, o[q * 8 + 1] * inv);
-          v.y = pack2<T>(o[q * 8 + 2] * inv, o[q * 8 + 3] * inv);
-          v.z = pack2<T>(o[q * 8 + 4] * inv, o[q * 8 + 5] * inv);
-          v.w = pack2<T>(o[q * 8 + 6] * inv, o[q * 8 + 7] * inv);
-          *reinterpret_cast<uint4 *>(dst + c * 32 + q * 8) = v;
-        }
-      }
-    }
+    store_o_row<T>(tO + lane_base, inv, dst, row_ok);
   } else {
     ptx::cp_async_wait<0>();
     if (tid == 0) atomicOr(p.diag, int32_t(kDiagWaitTimeout));
@@ -343,6 +375,279 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
   if (warp == 0) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// --- warp-specialised kernel: TMA producer, MMA issuer, softmax warps -----------------
+//
+// warps 0-3  softmax: row r = thread r; S_j from TMEM -> P_hi/P_lo in shared memory,
+//            O rescale in TMEM, epilogue
+// warp 4     producer: Q (cp.async), K/V page boxes by TMA into 2-stage rings; the last,
+//            partial V tile by zero-filling cp.async so rows past the context are 0
+// warp 5     MMA issuer (lane 0) and TMEM owner: QK of tile j+1 is issued before P.V of
+//            tile j, into the other of two S buffers, so softmax of one tile overlaps the
+//            tensor work of its neighbours
+// TMEM columns: S0 [0,128), S1 [128,256), O [256,384) of a 512-column allocation.
+
+struct alignas(64) PrefillTmaParams {
+  CUtensorMap tmk;  // K region: {D, Hkv, tokens}, box {64, 1, 16}, 128-byte swizzle
+  CUtensorMap tmv;
+  PrefillParams p;
+  uint64_t region_tokens;
+};
+
+constexpr uint32_t kWsTmemCols = 512;
+constexpr size_t kWsSmem = kOffBar + 128 + 1024;
+enum WsBar { kQFull = 0, kKFull = 1, kVFull = 3, kKEmpty = 5, kVEmpty = 7, kSFull = 9, kPFull = 11,
+             kODone = 12, kSlot = 13 };
+
+// Bounded wait that also gives up as soon as another role has failed.
+__device__ __forceinline__ bool ws_wait(uint32_t bar, uint32_t parity, volatile int *fail) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = ptx::globaltimer_ns();
+  for (uint32_t n = 1;; ++n) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if ((n & 63) == 0) {
+      if (*fail) return false;
+      if (ptx::globaltimer_ns() - t0 > kLimitNs) {
+        *fail = 1;
+        return false;
+      }
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(192, 1) prefill_ws_kernel(const __grid_constant__ PrefillTmaParams P) {
+  const PrefillParams &p = P.p;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw = ptx::smem_u32(smem_raw);
+  const uint32_t sb = (raw + 1023u) & ~1023u;
+  unsigned char *smem = smem_raw + (sb - raw);
+  __shared__ int s_fail;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int q0 = p.q_start[b];
+  const int qlen = p.q_start[b + 1] - q0;
+  const int ctx = p.ctx_lens[b];
+  if (qt * p.tt >= qlen) return;
+  if (ctx < qlen || ctx > p.max_bps * p.bs) {
+    if (tid == 0) atomicOr(p.diag, int32_t(kDiagBadLaunch));
+    return;
+  }
+  const int base_pos = ctx - qlen;
+  const int ti_hi = min((qt + 1) * p.tt, qlen);
+  const int kv_hi = base_pos + ti_hi;
+  const int nt = (kv_hi + kKvTile - 1) / kKvTile;
+  auto bar = [&](int i) { return sb + kOffBar + uint32_t(i) * 8; };
+
+  if (tid == 0) {
+    ptx::mbar_init(bar(kQFull), 32);
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(bar(kKFull + i), 1);
+      ptx::mbar_init(bar(kVFull + i), 32);
+      ptx::mbar_init(bar(kKEmpty + i), 1);
+      ptx::mbar_init(bar(kVEmpty + i), 1);
+      ptx::mbar_init(bar(kSFull + i), 1);
+    }
+    ptx::mbar_init(bar(kPFull), 128);
+    ptx::mbar_init(bar(kODone), 1);
+    ptx::fence_mbarrier_init();
+    s_fail = 0;
+  }
+  if (warp == 5) {
+    tc::tmem_alloc(bar(kSlot), kWsTmemCols);
+    tc::tmem_relinquish();
+    tc::fence_before_sync();
+  }
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + kOffBar + kSlot * 8);
+  volatile int *fail = &s_fail;
+  const int32_t *table = p.tables + size_t(b) * p.max_bps;
+  const uint32_t row_stride = uint32_t(p.hkv) * kHd;  // elements per token row
+
+  if (warp == 4) {
+    // ---------------- producer ----------------
+    for (int it = 0; it < 64; ++it) {
+      const int idx = it * 32 + lane, r = idx >> 4, c = idx & 15;
+      const int t_r = qt * p.tt + r / p.G, h_r = h * p.G + r % p.G;
+      const bool ok = t_r < qlen;
+      const uint16_t *src = ok ? p.q + (size_t(q0 + t_r) * p.hq + h_r) * kHd + c * 8 : p.q;
+      ptx::cp_async16(sb + kOffQ + swz(r, c), src, ok ? 16u : 0u);
+    }
+    ptx::cp_async_mbar_arrive(bar(kQFull));
+    if (lane == 0) {
+      ptx::prefetch_tensormap(&P.tmk);
+      ptx::prefetch_tensormap(&P.tmv);
+    }
+    bool bad = false;
+    // Lane l resolves the 16-row box l & 7 of the tile (lanes 8..31 repeat lanes 0..7).
+    auto box_z = [&](int j, int bx, int64_t *z) -> bool {
+      const int key = j * kKvTile + bx * 16;
+      if (key >= kv_hi) return false;
+      const int blk = table[key / p.bs];
+      const uint64_t off = p.offsets[blk];
+      const int64_t zz = int64_t(off / row_stride) + key % p.bs;
+      if (off % row_stride != 0 || uint64_t(zz) + 16 > P.region_tokens) {
+        bad = true;
+        return false;
+      }
+      *z = zz;
+      return true;
+    };
+    for (int j = 0; j < nt; ++j) {
+      const int st = j & 1;
+      const uint32_t kdst = sb + kOffK + st * kTile, vdst = sb + kOffV + st * kTile;
+      int64_t z = 0;
+      const bool live = box_z(j, lane & 7, &z);
+      const uint32_t live_mask = __ballot_sync(0xffffffffu, live && lane < 8);
+      const uint32_t bytes = uint32_t(__popc(live_mask)) * 2u * 2048u;
+      // K tile (QK of tile j-2 must have finished reading this stage)
+      if (j >= 2 && !ws_wait(bar(kKEmpty + st), uint32_t(((j >> 1) - 1) & 1), fail)) break;
+      if (lane == 0) ptx::mbar_arrive_expect_tx(bar(kKFull + st), bytes);
+      __syncwarp();
+      if (lane < 16 && live) {  // lanes 8..15 load the second head_dim half of the same boxes
+        const int bx = lane & 7, half = lane >> 3;
+        ptx::tma_load_3d(kdst + half * kHalf + bx * 2048, &P.tmk, half * 64, h, int(z),
+                         bar(kKFull + st));
+      }
+      // V tile (P.V of tile j-2 must have finished reading this stage)
+      if (j >= 2 && !ws_wait(bar(kVEmpty + st), uint32_t(((j >> 1) - 1) & 1), fail)) break;
+      const bool full = j * kKvTile + kKvTile <= kv_hi;
+      if (full && live_mask == 0xffu) {
+        if (lane == 0) {
+          ptx::mbar_arrive_expect_tx(bar(kVFull + st), bytes);
+        } else {
+          ptx::mbar_arrive(bar(kVFull + st));
+        }
+        __syncwarp();
+        if (lane < 16) {
+          const int bx = lane & 7, half = lane >> 3;
+          ptx::tma_load_3d(vdst + half * kHalf + bx * 2048, &P.tmv, half * 64, h, int(z),
+                           bar(kVFull + st));
+        }
+      } else {
+        // partial tile: rows past the context (or of a bad block) are zero-filled
+        for (int it = 0; it < 64; ++it) {
+          const int idx = it * 32 + lane, n = idx >> 4, c = idx & 15;
+          const int key = j * kKvTile + n;
+          int64_t e = -1;
+          if (key < kv_hi) {
+            const int blk = table[key / p.bs];
+            const uint64_t off = p.offsets[blk];
+            const uint64_t elem = off + uint64_t(key % p.bs) * row_stride + uint64_t(h) * kHd + c * 8;
+            if ((off & 7) == 0 && elem + 8 <= p.region_elems) e = int64_t(elem);
+            else bad = true;
+          }
+          ptx::cp_async16(vdst + swz(n, c), e >= 0 ? p.va_v + e : p.va_v, e >= 0 ? 16u : 0u);
+        }
+        ptx::cp_async_mbar_arrive(bar(kVFull + st));
+      }
+    }
+    ptx::cp_async_wait<0>();
+    if (bad) atomicOr(p.diag, int32_t(kDiagBadOffset));
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    const uint32_t qa = sb + kOffQ;
+    const uint32_t pa = sb + kOffP, pl = pa + kTile;
+    const uint32_t tO = tmem + 256;
+    auto issue_qk = [&](int j) {
+      const uint32_t ka = sb + kOffK + (j & 1) * kTile, tS = tmem + (j & 1) * 128;
+      if (lane == 0) {
+        tc::fence_after_sync();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t o = uint32_t((k >> 2) * kHalf + (k & 3) * 32);
+          tc::mma_ss(tS, tc::sw128_desc(qa + o, 16, 1024), tc::sw128_desc(ka + o, 16, 1024),
+                     p.idesc_qk, k > 0);
+        }
+        tc::commit(bar(kSFull + (j & 1)));
+        tc::commit(bar(kKEmpty + (j & 1)));
+      }
+      __syncwarp();
+    };
+    bool ok = ws_wait(bar(kQFull), 0, fail) && ws_wait(bar(kKFull), 0, fail);
+    if (ok) issue_qk(0);
+    for (int j = 0; ok && j < nt; ++j) {
+      if (j + 1 < nt) {
+        if (!ws_wait(bar(kKFull + ((j + 1) & 1)), uint32_t(((j + 1) >> 1) & 1), fail)) break;
+        issue_qk(j + 1);
+      }
+      if (!ws_wait(bar(kPFull), uint32_t(j & 1), fail)) break;
+      if (!ws_wait(bar(kVFull + (j & 1)), uint32_t((j >> 1) & 1), fail)) break;
+      if (lane == 0) {
+        tc::fence_after_sync();
+        const uint32_t va = sb + kOffV + (j & 1) * kTile;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t ao = uint32_t((k >> 2) * kHalf + (k & 3) * 32);
+          const uint64_t vd = tc::sw128_desc(va + uint32_t(k) * 2048, kHalf, 1024);
+          tc::mma_ss(tO, tc::sw128_desc(pa + ao, 16, 1024), vd, p.idesc_pv,
+                     (j > 0 || k > 0) ? 1u : 0u);
+          tc::mma_ss(tO, tc::sw128_desc(pl + ao, 16, 1024), vd, p.idesc_pv, 1u);
+        }
+        tc::commit(bar(kODone));
+        tc::commit(bar(kVEmpty + (j & 1)));
+      }
+      __syncwarp();
+    }
+  } else {
+    // ---------------- softmax warps ----------------
+    const int row = tid;
+    const int ti = qt * p.tt + row / p.G;
+    const bool row_ok = ti < qlen;
+    const int qpos = row_ok ? base_pos + ti : kv_hi - 1;
+    const uint32_t lane_base = uint32_t(warp * 32) << 16;
+    const uint32_t tO = tmem + 256 + lane_base;
+    const uint32_t pa = sb + kOffP, pl = pa + kTile;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      if (!ws_wait(bar(kSFull + (j & 1)), uint32_t((j >> 1) & 1), fail)) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      float s[128];
+      const uint32_t tS = tmem + (j & 1) * 128 + lane_base;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::ld32(tS + c * 32, s + c * 32);
+      tc::wait_ld();
+      float alpha;
+      bool rescale;
+      const float sum = exp_tile(s, j * kKvTile, qpos,
+                                 j * kKvTile + kKvTile - 1 > base_pos + qt * p.tt, p.scale_log2,
+                                 j > 0, m_run, alpha, rescale);
+      l_run = l_run * alpha + sum;
+      if (j > 0) {  // P.V of tile j-1 done: P tiles free, O stable
+        if (!ws_wait(bar(kODone), uint32_t((j - 1) & 1), fail)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+      }
+      store_p<T>(s, pa, pl, row);
+      if (__any_sync(0xffffffffu, rescale)) scale_o_row(tO, rescale ? alpha : 1.f);
+      ptx::fence_proxy_async_smem();
+      tc::fence_before_sync();
+      ptx::mbar_arrive(bar(kPFull));
+    }
+    if (ok && ws_wait(bar(kODone), uint32_t((nt - 1) & 1), fail)) {
+      tc::fence_after_sync();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + row % p.G) * kHd;
+      store_o_row<T>(tO, inv, dst, row_ok);
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (s_fail && tid == 0) atomicOr(p.diag, int32_t(kDiagWaitTimeout));
+  if (warp == 5) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kWsTmemCols);
   }
 }
 
@@ -377,10 +682,30 @@ cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
   p.idesc_qk = tc::idesc_f16(bf16, 128, 128, false, false);
   p.idesc_pv = tc::idesc_f16(bf16, 128, 128, false, true);
   p.diag = a.diag;
+  dim3 grid((a.max_q_len + p.tt - 1) / p.tt, a.kv_heads, a.batch);
+  // TMA page boxes need 16-token pages that start on whole token rows of the
+  // {D, Hkv, tokens} view: block_size % 16 == 0 and kv_heads * 128 dividing the
+  // 2 MiB superblock (1 Mi elements).  Otherwise the cp.async kernel runs.
+  const bool tma = a.tensor_maps && a.block_size % 16 == 0 &&
+                   (uint64_t(1) << 20) % (uint64_t(a.kv_heads) * kHd) == 0 &&
+                   !(std::getenv("KCMM_PREFILL_IMPL") &&
+                     std::strcmp(std::getenv("KCMM_PREFILL_IMPL"), "cpasync") == 0);
+  if (tma) {
+    PrefillTmaParams tp;
+    std::memcpy(&tp.tmk, a.tensor_maps, sizeof(CUtensorMap));
+    std::memcpy(&tp.tmv, static_cast<const char *>(a.tensor_maps) + 128, sizeof(CUtensorMap));
+    tp.p = p;
+    tp.region_tokens = a.region_tokens;
+    auto fn = bf16 ? prefill_ws_kernel<__nv_bfloat16> : prefill_ws_kernel<__half>;
+    cudaError_t e =
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kWsSmem));
+    if (e != cudaSuccess) return e;
+    fn<<<grid, 192, kWsSmem, stream>>>(tp);
+    return cudaGetLastError();
+  }
   auto fn = bf16 ? prefill_kernel<__nv_bfloat16> : prefill_kernel<__half>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem));
   if (e != cudaSuccess) return e;
-  dim3 grid((a.max_q_len + p.tt - 1) / p.tt, a.kv_heads, a.batch);
   fn<<<grid, 128, kSmem, stream>>>(p);
   return cudaGetLastError();
 }

@@ -73,6 +73,23 @@ def test_prefill_matches_oracle(case, dtype):
         wl.close()
 
 
+@pytest.mark.parametrize("impl,bs", [("cpasync", 16), ("tma", 32), ("tma", 8)])
+def test_prefill_kernel_paths(impl, bs, monkeypatch):
+    """The cp.async kernel (forced, and chosen for 8-token pages) and the TMA kernel with
+    32-token pages (two boxes per page) agree with the oracle."""
+    if impl == "cpasync":
+        monkeypatch.setenv("KCMM_PREFILL_IMPL", "cpasync")
+    wl = make(ctx_lens=[700, 260], chunk_lens=[300, 260], num_q_heads=16, kv_heads=2,
+              block_size=bs, seed=bs)
+    try:
+        wl.run()
+        _torch().cuda.synchronize()
+        check(wl)
+        assert wl.pool.kernel_status() == 0
+    finally:
+        wl.close()
+
+
 def test_prefill_last_row_equals_decode():
     """The last row of a chunk is a decode step over the whole context: both kernels agree."""
     torch = _torch()
