@@ -96,21 +96,28 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
 // reaches past the CTA's first row).  The running max m is only raised when the
 // tile's max exceeds it by more than 8 (log2 units).  Returns the row sum of P;
 // alpha = exp2(m_old - m_new) rescales the earlier sum and O.
-__device__ __forceinline__ float exp_tile(float (&s)[128], int k0, int qpos, bool need_mask,
-                                          float scale_log2, bool has_prev, float &m_run,
-                                          float &alpha, bool &rescale) {
+template <int N>
+__device__ __forceinline__ float masked_max(float (&s)[N], int k0, int qpos, bool need_mask) {
   float mx = -INFINITY;
   if (need_mask) {
 #pragma unroll
-    for (int c = 0; c < 128; ++c) {
+    for (int c = 0; c < N; ++c) {
       if (k0 + c > qpos) s[c] = -INFINITY;
       mx = fmaxf(mx, s[c]);
     }
   } else {
 #pragma unroll
-    for (int c = 0; c < 128; ++c) mx = fmaxf(mx, s[c]);
+    for (int c = 0; c < N; ++c) mx = fmaxf(mx, s[c]);
   }
-  mx *= scale_log2;
+  return mx;
+}
+
+// Given the tile's row max mx (already in log2 units), update the running max and
+// turn s into P in place; returns the sum of this thread's P values.
+template <int N>
+__device__ __forceinline__ float exp_given_max(float (&s)[N], float mx, float scale_log2,
+                                               bool has_prev, float &m_run, float &alpha,
+                                               bool &rescale) {
   float m_new = m_run;
   if (mx > m_run + 8.f) m_new = mx;  // first tile: m_run = -inf
   alpha = ptx::fast_exp2(m_run - m_new);  // 0 on the first tile, else <= 1
@@ -118,11 +125,18 @@ __device__ __forceinline__ float exp_tile(float (&s)[128], int k0, int qpos, boo
   m_run = m_new;
   float sum = 0.f;
 #pragma unroll
-  for (int c = 0; c < 128; ++c) {
+  for (int c = 0; c < N; ++c) {
     s[c] = ptx::fast_exp2(fmaf(s[c], scale_log2, -m_new));
     sum += s[c];
   }
   return sum;
+}
+
+__device__ __forceinline__ float exp_tile(float (&s)[128], int k0, int qpos, bool need_mask,
+                                          float scale_log2, bool has_prev, float &m_run,
+                                          float &alpha, bool &rescale) {
+  const float mx = masked_max<128>(s, k0, qpos, need_mask) * scale_log2;
+  return exp_given_max<128>(s, mx, scale_log2, has_prev, m_run, alpha, rescale);
 }
 
 template <typename T>
@@ -159,11 +173,36 @@ __device__ __forceinline__ void store_p(const float (&s)[128], uint32_t pa, uint
   }
 }
 
-// Store one row of O (fp32 in TMEM, 128 columns) / l to global memory.
-template <typename T>
+// P values of N keys of one row -> TMEM as 16-bit pairs (element 2c in the low half of
+// column c): P_hi at column t_hi, P_lo = round(P - P_hi) at column t_lo.
+template <typename T, int N>
+__device__ __forceinline__ void store_p_tmem(const float (&s)[N], uint32_t t_hi, uint32_t t_lo) {
+#pragma unroll
+  for (int part = 0; part < N / 64; ++part) {
+    uint32_t w[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) w[i] = pack2<T>(s[64 * part + 2 * i], s[64 * part + 2 * i + 1]);
+    tc::st32u(t_hi + 32 * part, w);
+  }
+#pragma unroll
+  for (int part = 0; part < N / 64; ++part) {
+    uint32_t w[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float a = s[64 * part + 2 * i], b = s[64 * part + 2 * i + 1];
+      const float2 hv = unpack2<T>(pack2<T>(a, b));
+      w[i] = pack2<T>(a - hv.x, b - hv.y);
+    }
+    tc::st32u(t_lo + 32 * part, w);
+  }
+  tc::wait_st();
+}
+
+// Store N columns of one row of O (fp32 in TMEM) / l to global memory.
+template <typename T, int N = 128>
 __device__ __forceinline__ void store_o_row(uint32_t t_row, float inv, uint16_t *dst, bool ok) {
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < N / 32; ++c) {
     float o[32];
     tc::ld32(t_row + c * 32, o);
     tc::wait_ld();
@@ -181,10 +220,12 @@ __device__ __forceinline__ void store_o_row(uint32_t t_row, float inv, uint16_t 
   }
 }
 
-// O row *= f (all lanes of the warp execute this; f = 1 for rows that keep their max).
+// N columns of an O row *= f (all lanes of the warp execute this; f = 1 for rows that
+// keep their max).
+template <int N = 128>
 __device__ __forceinline__ void scale_o_row(uint32_t t_row, float f) {
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < N / 32; ++c) {
     float o[32];
     tc::ld32(t_row + c * 32, o);
     tc::wait_ld();
@@ -380,14 +421,20 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
 
 // --- warp-specialised kernel: TMA producer, MMA issuer, softmax warps -----------------
 //
-// warps 0-3  softmax: row r = thread r; S_j from TMEM -> P_hi/P_lo in shared memory,
-//            O rescale in TMEM, epilogue
-// warp 4     producer: Q (cp.async), K/V page boxes by TMA into 2-stage rings; the last,
+// warps 0-7  softmax: warp w owns rows 32*(w%4) .. +31 (its TMEM lane quarter) and key /
+//            head_dim columns [64*(w/4), +64): two warps share each row and trade their
+//            partial row max through shared memory.  S_j from TMEM -> P_hi/P_lo written
+//            back over S_j's own TMEM columns (16-bit pairs: P_hi in the first 64
+//            columns, P_lo in the last 64), O rescale in TMEM, epilogue
+// warp 8     producer: Q (cp.async), K/V page boxes by TMA into 2-stage rings; the last,
 //            partial V tile by zero-filling cp.async so rows past the context are 0
-// warp 5     MMA issuer (lane 0) and TMEM owner: QK of tile j+1 is issued before P.V of
+// warp 9     MMA issuer (lane 0) and TMEM owner: QK of tile j+1 is issued before P.V of
 //            tile j, into the other of two S buffers, so softmax of one tile overlaps the
-//            tensor work of its neighbours
-// TMEM columns: S0 [0,128), S1 [128,256), O [256,384) of a 512-column allocation.
+//            tensor work of its neighbours.  P.V takes P from TMEM (A operand) and V from
+//            shared memory, so only V is read from shared memory.
+// TMEM columns: S0/P0 [0,128), S1/P1 [128,256), O [256,384) of a 512-column allocation.
+// Tensor-core operations of the CTA execute in issue order: QK of tile j+2 (into S_j's
+// columns) runs after P.V of tile j has read P_j from them.
 
 struct alignas(64) PrefillTmaParams {
   CUtensorMap tmk;  // K region: {D, Hkv, tokens}, box {64, 1, 16}, 128-byte swizzle
@@ -397,9 +444,12 @@ struct alignas(64) PrefillTmaParams {
 };
 
 constexpr uint32_t kWsTmemCols = 512;
-constexpr size_t kWsSmem = kOffBar + 128 + 1024;
+constexpr uint32_t kWsOffBar = kOffP;           // no P tiles in shared memory
+constexpr uint32_t kWsOffXch = kWsOffBar + 256;  // row-max exchange [2 parity][2 half][128]
+constexpr size_t kWsSmem = kWsOffXch + 2 * 2 * 128 * 4 + 1024;
+constexpr int kWsThreads = 320;
 enum WsBar { kQFull = 0, kKFull = 1, kVFull = 3, kKEmpty = 5, kVEmpty = 7, kSFull = 9, kPFull = 11,
-             kODone = 12, kSlot = 13 };
+             kODone = 12, kPair = 13, kSlot = 17 };  // kPair: 4 barriers, one per row quarter
 
 // Bounded wait that also gives up as soon as another role has failed.
 __device__ __forceinline__ bool ws_wait(uint32_t bar, uint32_t parity, volatile int *fail) {
@@ -418,7 +468,7 @@ __device__ __forceinline__ bool ws_wait(uint32_t bar, uint32_t parity, volatile 
 }
 
 template <typename T>
-__global__ void __launch_bounds__(192, 1) prefill_ws_kernel(const __grid_constant__ PrefillTmaParams P) {
+__global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_constant__ PrefillTmaParams P) {
   const PrefillParams &p = P.p;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = ptx::smem_u32(smem_raw);
@@ -440,7 +490,7 @@ __global__ void __launch_bounds__(192, 1) prefill_ws_kernel(const __grid_constan
   const int ti_hi = min((qt + 1) * p.tt, qlen);
   const int kv_hi = base_pos + ti_hi;
   const int nt = (kv_hi + kKvTile - 1) / kKvTile;
-  auto bar = [&](int i) { return sb + kOffBar + uint32_t(i) * 8; };
+  auto bar = [&](int i) { return sb + kWsOffBar + uint32_t(i) * 8; };
 
   if (tid == 0) {
     ptx::mbar_init(bar(kQFull), 32);
@@ -451,24 +501,25 @@ __global__ void __launch_bounds__(192, 1) prefill_ws_kernel(const __grid_constan
       ptx::mbar_init(bar(kVEmpty + i), 1);
       ptx::mbar_init(bar(kSFull + i), 1);
     }
-    ptx::mbar_init(bar(kPFull), 128);
+    ptx::mbar_init(bar(kPFull), 256);
     ptx::mbar_init(bar(kODone), 1);
+    for (int i = 0; i < 4; ++i) ptx::mbar_init(bar(kPair + i), 64);
     ptx::fence_mbarrier_init();
     s_fail = 0;
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tc::tmem_alloc(bar(kSlot), kWsTmemCols);
     tc::tmem_relinquish();
     tc::fence_before_sync();
   }
   __syncthreads();
   tc::fence_after_sync();
-  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + kOffBar + kSlot * 8);
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + kWsOffBar + kSlot * 8);
   volatile int *fail = &s_fail;
   const int32_t *table = p.tables + size_t(b) * p.max_bps;
   const uint32_t row_stride = uint32_t(p.hkv) * kHd;  // elements per token row
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------- producer ----------------
     for (int it = 0; it < 64; ++it) {
       const int idx = it * 32 + lane, r = idx >> 4, c = idx & 15;
@@ -548,10 +599,9 @@ __global__ void __launch_bounds__(192, 1) prefill_ws_kernel(const __grid_constan
     }
     ptx::cp_async_wait<0>();
     if (bad) atomicOr(p.diag, int32_t(kDiagBadOffset));
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
     const uint32_t qa = sb + kOffQ;
-    const uint32_t pa = sb + kOffP, pl = pa + kTile;
     const uint32_t tO = tmem + 256;
     auto issue_qk = [&](int j) {
       const uint32_t ka = sb + kOffK + (j & 1) * kTile, tS = tmem + (j & 1) * 128;
@@ -580,13 +630,12 @@ __global__ void __launch_bounds__(192, 1) prefill_ws_kernel(const __grid_constan
       if (lane == 0) {
         tc::fence_after_sync();
         const uint32_t va = sb + kOffV + (j & 1) * kTile;
+        const uint32_t tp = tmem + (j & 1) * 128;  // P_hi columns [0,64), P_lo [64,128)
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const uint32_t ao = uint32_t((k >> 2) * kHalf + (k & 3) * 32);
           const uint64_t vd = tc::sw128_desc(va + uint32_t(k) * 2048, kHalf, 1024);
-          tc::mma_ss(tO, tc::sw128_desc(pa + ao, 16, 1024), vd, p.idesc_pv,
-                     (j > 0 || k > 0) ? 1u : 0u);
-          tc::mma_ss(tO, tc::sw128_desc(pl + ao, 16, 1024), vd, p.idesc_pv, 1u);
+          tc::mma_ts(tO, tp + k * 8, vd, p.idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+          tc::mma_ts(tO, tp + 64 + k * 8, vd, p.idesc_pv, 1u);
         }
         tc::commit(bar(kODone));
         tc::commit(bar(kVEmpty + (j & 1)));
@@ -595,13 +644,15 @@ __global__ void __launch_bounds__(192, 1) prefill_ws_kernel(const __grid_constan
     }
   } else {
     // ---------------- softmax warps ----------------
-    const int row = tid;
+    const int q4 = warp & 3, hf = warp >> 2;
+    const int row = q4 * 32 + lane;
     const int ti = qt * p.tt + row / p.G;
     const bool row_ok = ti < qlen;
     const int qpos = row_ok ? base_pos + ti : kv_hi - 1;
-    const uint32_t lane_base = uint32_t(warp * 32) << 16;
-    const uint32_t tO = tmem + 256 + lane_base;
-    const uint32_t pa = sb + kOffP, pl = pa + kTile;
+    const uint32_t lane_base = uint32_t(q4 * 32) << 16;
+    const uint32_t tO = tmem + 256 + lane_base + hf * 64;
+    float *xch = reinterpret_cast<float *>(smem + kWsOffXch);
+    const uint32_t pbar = bar(kPair + q4);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
@@ -610,42 +661,67 @@ __global__ void __launch_bounds__(192, 1) prefill_ws_kernel(const __grid_constan
         break;
       }
       tc::fence_after_sync();
-      float s[128];
+      float s[64];
       const uint32_t tS = tmem + (j & 1) * 128 + lane_base;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tc::ld32(tS + c * 32, s + c * 32);
+      tc::ld32(tS + hf * 64, s);
+      tc::ld32(tS + hf * 64 + 32, s + 32);
       tc::wait_ld();
+      const bool need_mask = j * kKvTile + kKvTile - 1 > base_pos + qt * p.tt;
+      float mx = masked_max<64>(s, j * kKvTile + hf * 64, qpos, need_mask) * p.scale_log2;
+      // trade the partial row max with the warp holding the other 64 keys of the rows;
+      // this also orders both warps' reads of S_j before either writes P_j over it
+      xch[((j & 1) * 2 + hf) * 128 + row] = mx;
+      tc::fence_before_sync();
+      ptx::mbar_arrive(pbar);
+      if (!ws_wait(pbar, uint32_t(j & 1), fail)) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      mx = fmaxf(mx, xch[((j & 1) * 2 + (hf ^ 1)) * 128 + row]);
       float alpha;
       bool rescale;
-      const float sum = exp_tile(s, j * kKvTile, qpos,
-                                 j * kKvTile + kKvTile - 1 > base_pos + qt * p.tt, p.scale_log2,
-                                 j > 0, m_run, alpha, rescale);
+      const float sum = exp_given_max<64>(s, mx, p.scale_log2, j > 0, m_run, alpha, rescale);
       l_run = l_run * alpha + sum;
-      if (j > 0) {  // P.V of tile j-1 done: P tiles free, O stable
+      store_p_tmem<T, 64>(s, tS + hf * 32, tS + 64 + hf * 32);
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O *= alpha once P.V of tile j-1 is done.  At this point that is the only
+        // P.V that may still run (tile j-2's finished before QK of tile j, whose S
+        // we hold), so the parity wait cannot see a later phase.
         if (!ws_wait(bar(kODone), uint32_t((j - 1) & 1), fail)) {
           ok = false;
           break;
         }
         tc::fence_after_sync();
+        scale_o_row<64>(tO, rescale ? alpha : 1.f);
       }
-      store_p<T>(s, pa, pl, row);
-      if (__any_sync(0xffffffffu, rescale)) scale_o_row(tO, rescale ? alpha : 1.f);
-      ptx::fence_proxy_async_smem();
       tc::fence_before_sync();
       ptx::mbar_arrive(bar(kPFull));
     }
+    // row sum = both halves' partial sums (same running max in both warps)
+    if (ok) {
+      xch[((nt & 1) * 2 + hf) * 128 + row] = l_run;
+      ptx::mbar_arrive(pbar);
+      if (ws_wait(pbar, uint32_t(nt & 1), fail)) {
+        l_run += xch[((nt & 1) * 2 + (hf ^ 1)) * 128 + row];
+      } else {
+        ok = false;
+      }
+    }
+    // P.V of tile nt-2 may still be running: wait its phase, then the last one
+    if (ok && nt >= 2 && !ws_wait(bar(kODone), uint32_t((nt - 2) & 1), fail)) ok = false;
     if (ok && ws_wait(bar(kODone), uint32_t((nt - 1) & 1), fail)) {
       tc::fence_after_sync();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + row % p.G) * kHd;
-      store_o_row<T>(tO, inv, dst, row_ok);
+      uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + row % p.G) * kHd + hf * 64;
+      store_o_row<T, 64>(tO, inv, dst, row_ok);
     }
   }
 
   tc::fence_before_sync();
   __syncthreads();
   if (s_fail && tid == 0) atomicOr(p.diag, int32_t(kDiagWaitTimeout));
-  if (warp == 5) {
+  if (warp == 9) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, kWsTmemCols);
   }
@@ -700,7 +776,7 @@ cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
     cudaError_t e =
         cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kWsSmem));
     if (e != cudaSuccess) return e;
-    fn<<<grid, 192, kWsSmem, stream>>>(tp);
+    fn<<<grid, kWsThreads, kWsSmem, stream>>>(tp);
     return cudaGetLastError();
   }
   auto fn = bf16 ? prefill_kernel<__nv_bfloat16> : prefill_kernel<__half>;
