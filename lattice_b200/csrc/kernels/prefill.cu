@@ -426,8 +426,9 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
 //            partial row max through shared memory.  S_j from TMEM -> P_hi/P_lo written
 //            back over S_j's own TMEM columns (16-bit pairs: P_hi in the first 64
 //            columns, P_lo in the last 64), O rescale in TMEM, epilogue
-// warp 8     producer: Q (cp.async), K/V page boxes by TMA into 2-stage rings; the last,
-//            partial V tile by zero-filling cp.async so rows past the context are 0
+// warp 8     K producer: Q (cp.async), then K page boxes by TMA into a 3-stage ring
+// warp 10    V producer: V page boxes by TMA into a 2-stage ring; the last, partial V
+//            tile by zero-filling cp.async so rows past the context are 0
 // warp 9     MMA issuer (lane 0) and TMEM owner: QK of tile j+1 is issued before P.V of
 //            tile j, into the other of two S buffers, so softmax of one tile overlaps the
 //            tensor work of its neighbours.  P.V takes P from TMEM (A operand) and V from
@@ -444,12 +445,56 @@ struct alignas(64) PrefillTmaParams {
 };
 
 constexpr uint32_t kWsTmemCols = 512;
-constexpr uint32_t kWsOffBar = kOffP;           // no P tiles in shared memory
-constexpr uint32_t kWsOffXch = kWsOffBar + 256;  // row-max exchange [2 parity][2 half][128]
+constexpr int kKStages = 3;                              // K ring depth (V: 2)
+constexpr uint32_t kWsOffK = kOffQ + kTile;
+constexpr uint32_t kWsOffV = kWsOffK + kKStages * kTile;
+constexpr uint32_t kWsOffBar = kWsOffV + 2 * kTile;     // no P tiles in shared memory
+constexpr uint32_t kWsOffXch = kWsOffBar + 256;          // row-max exchange [2 parity][2 half][128]
 constexpr size_t kWsSmem = kWsOffXch + 2 * 2 * 128 * 4 + 1024;
-constexpr int kWsThreads = 320;
-enum WsBar { kQFull = 0, kKFull = 1, kVFull = 3, kKEmpty = 5, kVEmpty = 7, kSFull = 9, kPFull = 11,
-             kODone = 12, kPair = 13, kSlot = 17 };  // kPair: 4 barriers, one per row quarter
+constexpr int kWsThreads = 352;
+enum WsBar { kQFull = 0, kKFull = 1, kKEmpty = 4, kVFull = 7, kVEmpty = 9, kSFull = 11,
+             kPFull = 13, kODone = 14, kPair = 15, kSlot = 19 };  // kPair: one per row quarter
+
+// Page lookups for the 16-token boxes of successive KV tiles, two tiles ahead: the
+// block id of tile j+2 and the block offset of tile j+1 are loaded while tile j is
+// issued, so the dependent table -> offset loads stay off the issue path.
+struct BoxLookup {
+  const int32_t *table;
+  const uint64_t *offsets;
+  int bs, kv_hi, nt, bx, j;
+  int blk1, blk2;     // block ids of the next tile and the one after (-1: none)
+  uint64_t off1;      // offset of the next tile's block
+  __device__ int blk_of(int t) const {
+    const int key = t * kKvTile + bx * 16;
+    return (t < nt && key < kv_hi) ? table[key / bs] : -1;
+  }
+  __device__ BoxLookup(const int32_t *tb, const uint64_t *of, int bs_, int kv_hi_, int nt_, int bx_)
+      : table(tb), offsets(of), bs(bs_), kv_hi(kv_hi_), nt(nt_), bx(bx_), j(0) {
+    const int b0 = blk_of(0);
+    off1 = b0 >= 0 ? offsets[b0] : 0;
+    blk1 = b0;
+    blk2 = blk_of(1);
+  }
+  // Token coordinate of this lane's box in the next tile; false when the box lies past
+  // the keys in use or its block offset is not a whole-row index inside the region.
+  __device__ bool next(uint32_t row_stride, uint64_t region_tokens, int64_t *z, bool *bad) {
+    const int blk = blk1;
+    const uint64_t off = off1;
+    const int key = j * kKvTile + bx * 16;
+    off1 = blk2 >= 0 ? offsets[blk2] : 0;
+    blk1 = blk2;
+    blk2 = blk_of(j + 2);
+    ++j;
+    if (blk < 0) return false;
+    const int64_t zz = int64_t(off / row_stride) + key % bs;
+    if (off % row_stride != 0 || uint64_t(zz) + 16 > region_tokens) {
+      *bad = true;
+      return false;
+    }
+    *z = zz;
+    return true;
+  }
+};
 
 // Bounded wait that also gives up as soon as another role has failed.
 __device__ __forceinline__ bool ws_wait(uint32_t bar, uint32_t parity, volatile int *fail) {
@@ -495,11 +540,13 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
   if (tid == 0) {
     ptx::mbar_init(bar(kQFull), 32);
     for (int i = 0; i < 2; ++i) {
-      ptx::mbar_init(bar(kKFull + i), 1);
       ptx::mbar_init(bar(kVFull + i), 32);
-      ptx::mbar_init(bar(kKEmpty + i), 1);
       ptx::mbar_init(bar(kVEmpty + i), 1);
       ptx::mbar_init(bar(kSFull + i), 1);
+    }
+    for (int i = 0; i < kKStages; ++i) {
+      ptx::mbar_init(bar(kKFull + i), 1);
+      ptx::mbar_init(bar(kKEmpty + i), 1);
     }
     ptx::mbar_init(bar(kPFull), 256);
     ptx::mbar_init(bar(kODone), 1);
@@ -520,7 +567,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
   const uint32_t row_stride = uint32_t(p.hkv) * kHd;  // elements per token row
 
   if (warp == 8) {
-    // ---------------- producer ----------------
+    // ---------------- K producer (and Q) ----------------
     for (int it = 0; it < 64; ++it) {
       const int idx = it * 32 + lane, r = idx >> 4, c = idx & 15;
       const int t_r = qt * p.tt + r / p.G, h_r = h * p.G + r % p.G;
@@ -529,47 +576,47 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
       ptx::cp_async16(sb + kOffQ + swz(r, c), src, ok ? 16u : 0u);
     }
     ptx::cp_async_mbar_arrive(bar(kQFull));
-    if (lane == 0) {
-      ptx::prefetch_tensormap(&P.tmk);
-      ptx::prefetch_tensormap(&P.tmv);
-    }
+    if (lane == 0) ptx::prefetch_tensormap(&P.tmk);
     bool bad = false;
-    // Lane l resolves the 16-row box l & 7 of the tile (lanes 8..31 repeat lanes 0..7).
-    auto box_z = [&](int j, int bx, int64_t *z) -> bool {
-      const int key = j * kKvTile + bx * 16;
-      if (key >= kv_hi) return false;
-      const int blk = table[key / p.bs];
-      const uint64_t off = p.offsets[blk];
-      const int64_t zz = int64_t(off / row_stride) + key % p.bs;
-      if (off % row_stride != 0 || uint64_t(zz) + 16 > P.region_tokens) {
-        bad = true;
-        return false;
-      }
-      *z = zz;
-      return true;
-    };
+    BoxLookup lk(table, p.offsets, p.bs, kv_hi, nt, lane & 7);
     for (int j = 0; j < nt; ++j) {
-      const int st = j & 1;
-      const uint32_t kdst = sb + kOffK + st * kTile, vdst = sb + kOffV + st * kTile;
+      const int st = j % kKStages;
       int64_t z = 0;
-      const bool live = box_z(j, lane & 7, &z);
+      const bool live = lk.next(row_stride, P.region_tokens, &z, &bad);
       const uint32_t live_mask = __ballot_sync(0xffffffffu, live && lane < 8);
-      const uint32_t bytes = uint32_t(__popc(live_mask)) * 2u * 2048u;
-      // K tile (QK of tile j-2 must have finished reading this stage)
-      if (j >= 2 && !ws_wait(bar(kKEmpty + st), uint32_t(((j >> 1) - 1) & 1), fail)) break;
-      if (lane == 0) ptx::mbar_arrive_expect_tx(bar(kKFull + st), bytes);
+      // QK of tile j - kKStages must have finished reading this stage
+      if (j >= kKStages &&
+          !ws_wait(bar(kKEmpty + st), uint32_t((j / kKStages - 1) & 1), fail))
+        break;
+      if (lane == 0) {
+        ptx::mbar_arrive_expect_tx(bar(kKFull + st), uint32_t(__popc(live_mask)) * 2u * 2048u);
+      }
       __syncwarp();
       if (lane < 16 && live) {  // lanes 8..15 load the second head_dim half of the same boxes
         const int bx = lane & 7, half = lane >> 3;
-        ptx::tma_load_3d(kdst + half * kHalf + bx * 2048, &P.tmk, half * 64, h, int(z),
-                         bar(kKFull + st));
+        ptx::tma_load_3d(sb + kWsOffK + st * kTile + half * kHalf + bx * 2048, &P.tmk, half * 64,
+                         h, int(z), bar(kKFull + st));
       }
-      // V tile (P.V of tile j-2 must have finished reading this stage)
+    }
+    ptx::cp_async_wait<0>();
+    if (bad) atomicOr(p.diag, int32_t(kDiagBadOffset));
+  } else if (warp == 10) {
+    // ---------------- V producer ----------------
+    if (lane == 0) ptx::prefetch_tensormap(&P.tmv);
+    bool bad = false;
+    BoxLookup lk(table, p.offsets, p.bs, kv_hi, nt, lane & 7);
+    for (int j = 0; j < nt; ++j) {
+      const int st = j & 1;
+      const uint32_t vdst = sb + kWsOffV + st * kTile;
+      int64_t z = 0;
+      const bool live = lk.next(row_stride, P.region_tokens, &z, &bad);
+      const uint32_t live_mask = __ballot_sync(0xffffffffu, live && lane < 8);
+      // P.V of tile j-2 must have finished reading this stage
       if (j >= 2 && !ws_wait(bar(kVEmpty + st), uint32_t(((j >> 1) - 1) & 1), fail)) break;
       const bool full = j * kKvTile + kKvTile <= kv_hi;
       if (full && live_mask == 0xffu) {
         if (lane == 0) {
-          ptx::mbar_arrive_expect_tx(bar(kVFull + st), bytes);
+          ptx::mbar_arrive_expect_tx(bar(kVFull + st), 16u * 2048u);
         } else {
           ptx::mbar_arrive(bar(kVFull + st));
         }
@@ -604,7 +651,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
     const uint32_t qa = sb + kOffQ;
     const uint32_t tO = tmem + 256;
     auto issue_qk = [&](int j) {
-      const uint32_t ka = sb + kOffK + (j & 1) * kTile, tS = tmem + (j & 1) * 128;
+      const uint32_t ka = sb + kWsOffK + (j % kKStages) * kTile, tS = tmem + (j & 1) * 128;
       if (lane == 0) {
         tc::fence_after_sync();
 #pragma unroll
@@ -614,7 +661,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
                      p.idesc_qk, k > 0);
         }
         tc::commit(bar(kSFull + (j & 1)));
-        tc::commit(bar(kKEmpty + (j & 1)));
+        tc::commit(bar(kKEmpty + j % kKStages));
       }
       __syncwarp();
     };
@@ -622,14 +669,15 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
     if (ok) issue_qk(0);
     for (int j = 0; ok && j < nt; ++j) {
       if (j + 1 < nt) {
-        if (!ws_wait(bar(kKFull + ((j + 1) & 1)), uint32_t(((j + 1) >> 1) & 1), fail)) break;
+        if (!ws_wait(bar(kKFull + (j + 1) % kKStages), uint32_t(((j + 1) / kKStages) & 1), fail))
+          break;
         issue_qk(j + 1);
       }
       if (!ws_wait(bar(kPFull), uint32_t(j & 1), fail)) break;
       if (!ws_wait(bar(kVFull + (j & 1)), uint32_t((j >> 1) & 1), fail)) break;
       if (lane == 0) {
         tc::fence_after_sync();
-        const uint32_t va = sb + kOffV + (j & 1) * kTile;
+        const uint32_t va = sb + kWsOffV + (j & 1) * kTile;
         const uint32_t tp = tmem + (j & 1) * 128;  // P_hi columns [0,64), P_lo [64,128)
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
