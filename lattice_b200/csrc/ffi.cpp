@@ -604,8 +604,6 @@ static int prefill_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, 
   a.max_blocks_per_seq = int(max_bps);
   a.scale = scale;
   a.diag = p->diag_word();
-  a.tensor_maps = p->tensor_maps(layer, int(hkv), int(hd));
-  a.region_tokens = p->region_bytes / (uint64_t(hkv) * hd * 2);
   return check_launch(h, op, kcmm::dev::paged_prefill(a, S(stream)));
 }
 

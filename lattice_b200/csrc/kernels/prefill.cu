@@ -28,7 +28,6 @@
 // diagnostic bit, the CTA drains its copies, frees its TMEM and returns.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
-#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdlib>
@@ -419,16 +418,17 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
   }
 }
 
-// --- warp-specialised kernel: TMA producer, MMA issuer, softmax warps -----------------
+// --- warp-specialised kernel: producer warps, MMA issuer, softmax warps -------------------
 //
 // warps 0-7  softmax: warp w owns rows 32*(w%4) .. +31 (its TMEM lane quarter) and key /
 //            head_dim columns [64*(w/4), +64): two warps share each row and trade their
 //            partial row max through shared memory.  S_j from TMEM -> P_hi/P_lo written
 //            back over S_j's own TMEM columns (16-bit pairs: P_hi in the first 64
 //            columns, P_lo in the last 64), O rescale in TMEM, epilogue
-// warp 8     K producer: Q (cp.async), then K page boxes by TMA into a 3-stage ring
-// warp 10    V producer: V page boxes by TMA into a 2-stage ring; the last, partial V
-//            tile by zero-filling cp.async so rows past the context are 0
+// warp 8     K producer: Q, then K tiles into a 3-stage ring
+// warp 10    V producer: V tiles into a 2-stage ring
+//            (both gather 16-token page boxes with 16-byte cp.async from all lanes,
+//            zero-filling keys past the context; TMA boxes of 2 KB issue too slowly)
 // warp 9     MMA issuer (lane 0) and TMEM owner: QK of tile j+1 is issued before P.V of
 //            tile j, into the other of two S buffers, so softmax of one tile overlaps the
 //            tensor work of its neighbours.  P.V takes P from TMEM (A operand) and V from
@@ -437,12 +437,7 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
 // Tensor-core operations of the CTA execute in issue order: QK of tile j+2 (into S_j's
 // columns) runs after P.V of tile j has read P_j from them.
 
-struct alignas(64) PrefillTmaParams {
-  CUtensorMap tmk;  // K region: {D, Hkv, tokens}, box {64, 1, 16}, 128-byte swizzle
-  CUtensorMap tmv;
-  PrefillParams p;
-  uint64_t region_tokens;
-};
+
 
 constexpr uint32_t kWsTmemCols = 512;
 constexpr int kKStages = 3;                              // K ring depth (V: 2)
@@ -455,44 +450,53 @@ constexpr int kWsThreads = 352;
 enum WsBar { kQFull = 0, kKFull = 1, kKEmpty = 4, kVFull = 7, kVEmpty = 9, kSFull = 11,
              kPFull = 13, kODone = 14, kPair = 15, kSlot = 19 };  // kPair: one per row quarter
 
-// Page lookups for the 16-token boxes of successive KV tiles, two tiles ahead: the
-// block id of tile j+2 and the block offset of tile j+1 are loaded while tile j is
-// issued, so the dependent table -> offset loads stay off the issue path.
+// Page lookups for the 16-token boxes of successive KV tiles, four tiles ahead.  The
+// producer warp's lanes form 4 groups of 8 (lane = 8 * group + box); group g serves
+// tiles g, g+4, g+8, ...  After its tile j is issued the group loads the block ids of
+// tile j+4, and two tiles later their offsets, so each dependent global load has two
+// tiles of time to return.
 struct BoxLookup {
   const int32_t *table;
   const uint64_t *offsets;
-  int bs, kv_hi, nt, bx, j;
-  int blk1, blk2;     // block ids of the next tile and the one after (-1: none)
-  uint64_t off1;      // offset of the next tile's block
+  int bs, kv_hi, nt, bx, grp, j;
+  int tile;       // tile this lane's group is gathering
+  int blk;        // its block id (-1: past the keys in use)
+  uint64_t off;   // its block offset (valid once loaded)
   __device__ int blk_of(int t) const {
     const int key = t * kKvTile + bx * 16;
     return (t < nt && key < kv_hi) ? table[key / bs] : -1;
   }
-  __device__ BoxLookup(const int32_t *tb, const uint64_t *of, int bs_, int kv_hi_, int nt_, int bx_)
-      : table(tb), offsets(of), bs(bs_), kv_hi(kv_hi_), nt(nt_), bx(bx_), j(0) {
-    const int b0 = blk_of(0);
-    off1 = b0 >= 0 ? offsets[b0] : 0;
-    blk1 = b0;
-    blk2 = blk_of(1);
+  __device__ BoxLookup(const int32_t *tb, const uint64_t *of, int bs_, int kv_hi_, int nt_,
+                       int lane)
+      : table(tb), offsets(of), bs(bs_), kv_hi(kv_hi_), nt(nt_), bx(lane & 7), grp(lane >> 3),
+        j(0), tile(lane >> 3) {
+    blk = blk_of(tile);
+    off = blk >= 0 ? offsets[blk] : 0;
   }
-  // Token coordinate of this lane's box in the next tile; false when the box lies past
-  // the keys in use or its block offset is not a whole-row index inside the region.
-  __device__ bool next(uint32_t row_stride, uint64_t region_tokens, int64_t *z, bool *bad) {
-    const int blk = blk1;
-    const uint64_t off = off1;
-    const int key = j * kKvTile + bx * 16;
-    off1 = blk2 >= 0 ? offsets[blk2] : 0;
-    blk1 = blk2;
-    blk2 = blk_of(j + 2);
-    ++j;
-    if (blk < 0) return false;
-    const int64_t zz = int64_t(off / row_stride) + key % bs;
-    if (off % row_stride != 0 || uint64_t(zz) + 16 > region_tokens) {
-      *bad = true;
-      return false;
+  // Element offset (2-byte units) of the first token row of this lane's box (lane & 7)
+  // in the next tile, from the group that holds it; false when the box lies past the
+  // keys in use, or its block offset is misaligned or its 16 rows leave the region.
+  // All 32 lanes must call this together.
+  __device__ bool next(uint32_t row_stride, uint64_t region_elems, int64_t *e0, bool *bad) {
+    const int g = j & 3;
+    int64_t zz = 0;
+    bool live = false;
+    if (grp == g && blk >= 0) {
+      zz = int64_t(off + uint64_t((j * kKvTile + bx * 16) % bs) * row_stride);
+      live = (off & 7) == 0 && uint64_t(zz) + 16ull * row_stride <= region_elems;
+      if (!live) *bad = true;
     }
-    *z = zz;
-    return true;
+    const int src = (g << 3) | bx;
+    zz = __shfl_sync(0xffffffffu, zz, src);
+    live = __shfl_sync(0xffffffffu, int(live), src) != 0;
+    if (grp == g) {  // start gathering tile j + 4
+      tile = j + 4;
+      blk = blk_of(tile);
+    }
+    if (j >= 2 && grp == ((j + 2) & 3)) off = blk >= 0 ? offsets[blk] : 0;  // tile j + 2
+    ++j;
+    *e0 = zz;
+    return live;
   }
 };
 
@@ -512,9 +516,30 @@ __device__ __forceinline__ bool ws_wait(uint32_t bar, uint32_t parity, volatile 
   }
 }
 
+// One warp copies a 128-key tile of one kv head into the swizzled [2 halves][128
+// rows][128 B] layout with 16-byte cp.async: each half-warp moves one 256-byte token
+// row per step.  Box b (keys 16b .. 16b+15) starts at element e0 of lane b; keys past
+// kv_hi and boxes that are not live are zero-filled.
+__device__ __forceinline__ void gather_tile(const uint16_t *va, uint32_t dst, int64_t e0, bool live,
+                                            int j, int kv_hi, uint32_t row_stride, int h,
+                                            int lane) {
+  const int hw = lane >> 4, c = lane & 15;
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    const int64_t eb = __shfl_sync(0xffffffffu, e0, b);
+    const bool lb = __shfl_sync(0xffffffffu, int(live), b) != 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = 2 * i + hw, row = b * 16 + r;
+      const bool ok = lb && j * kKvTile + row < kv_hi;
+      const uint16_t *src = va + eb + int64_t(r) * row_stride + h * kHd + c * 8;
+      ptx::cp_async16(dst + swz(row, c), ok ? src : va, ok ? 16u : 0u);
+    }
+  }
+}
+
 template <typename T>
-__global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_constant__ PrefillTmaParams P) {
-  const PrefillParams &p = P.p;
+__global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const PrefillParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = ptx::smem_u32(smem_raw);
   const uint32_t sb = (raw + 1023u) & ~1023u;
@@ -540,12 +565,12 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
   if (tid == 0) {
     ptx::mbar_init(bar(kQFull), 32);
     for (int i = 0; i < 2; ++i) {
-      ptx::mbar_init(bar(kVFull + i), 32);
+      ptx::mbar_init(bar(kVFull + i), 32);  // 32 cp.async arrivals per tile
       ptx::mbar_init(bar(kVEmpty + i), 1);
       ptx::mbar_init(bar(kSFull + i), 1);
     }
     for (int i = 0; i < kKStages; ++i) {
-      ptx::mbar_init(bar(kKFull + i), 1);
+      ptx::mbar_init(bar(kKFull + i), 32);
       ptx::mbar_init(bar(kKEmpty + i), 1);
     }
     ptx::mbar_init(bar(kPFull), 256);
@@ -576,73 +601,33 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
       ptx::cp_async16(sb + kOffQ + swz(r, c), src, ok ? 16u : 0u);
     }
     ptx::cp_async_mbar_arrive(bar(kQFull));
-    if (lane == 0) ptx::prefetch_tensormap(&P.tmk);
     bool bad = false;
-    BoxLookup lk(table, p.offsets, p.bs, kv_hi, nt, lane & 7);
+    BoxLookup lk(table, p.offsets, p.bs, kv_hi, nt, lane);
     for (int j = 0; j < nt; ++j) {
       const int st = j % kKStages;
-      int64_t z = 0;
-      const bool live = lk.next(row_stride, P.region_tokens, &z, &bad);
-      const uint32_t live_mask = __ballot_sync(0xffffffffu, live && lane < 8);
+      int64_t e0 = 0;
+      const bool live = lk.next(row_stride, p.region_elems, &e0, &bad);
       // QK of tile j - kKStages must have finished reading this stage
       if (j >= kKStages &&
           !ws_wait(bar(kKEmpty + st), uint32_t((j / kKStages - 1) & 1), fail))
         break;
-      if (lane == 0) {
-        ptx::mbar_arrive_expect_tx(bar(kKFull + st), uint32_t(__popc(live_mask)) * 2u * 2048u);
-      }
-      __syncwarp();
-      if (lane < 16 && live) {  // lanes 8..15 load the second head_dim half of the same boxes
-        const int bx = lane & 7, half = lane >> 3;
-        ptx::tma_load_3d(sb + kWsOffK + st * kTile + half * kHalf + bx * 2048, &P.tmk, half * 64,
-                         h, int(z), bar(kKFull + st));
-      }
+      gather_tile(p.va_k, sb + kWsOffK + st * kTile, e0, live, j, kv_hi, row_stride, h, lane);
+      ptx::cp_async_mbar_arrive(bar(kKFull + st));
     }
     ptx::cp_async_wait<0>();
     if (bad) atomicOr(p.diag, int32_t(kDiagBadOffset));
   } else if (warp == 10) {
     // ---------------- V producer ----------------
-    if (lane == 0) ptx::prefetch_tensormap(&P.tmv);
     bool bad = false;
-    BoxLookup lk(table, p.offsets, p.bs, kv_hi, nt, lane & 7);
+    BoxLookup lk(table, p.offsets, p.bs, kv_hi, nt, lane);
     for (int j = 0; j < nt; ++j) {
       const int st = j & 1;
-      const uint32_t vdst = sb + kWsOffV + st * kTile;
-      int64_t z = 0;
-      const bool live = lk.next(row_stride, P.region_tokens, &z, &bad);
-      const uint32_t live_mask = __ballot_sync(0xffffffffu, live && lane < 8);
+      int64_t e0 = 0;
+      const bool live = lk.next(row_stride, p.region_elems, &e0, &bad);
       // P.V of tile j-2 must have finished reading this stage
       if (j >= 2 && !ws_wait(bar(kVEmpty + st), uint32_t(((j >> 1) - 1) & 1), fail)) break;
-      const bool full = j * kKvTile + kKvTile <= kv_hi;
-      if (full && live_mask == 0xffu) {
-        if (lane == 0) {
-          ptx::mbar_arrive_expect_tx(bar(kVFull + st), 16u * 2048u);
-        } else {
-          ptx::mbar_arrive(bar(kVFull + st));
-        }
-        __syncwarp();
-        if (lane < 16) {
-          const int bx = lane & 7, half = lane >> 3;
-          ptx::tma_load_3d(vdst + half * kHalf + bx * 2048, &P.tmv, half * 64, h, int(z),
-                           bar(kVFull + st));
-        }
-      } else {
-        // partial tile: rows past the context (or of a bad block) are zero-filled
-        for (int it = 0; it < 64; ++it) {
-          const int idx = it * 32 + lane, n = idx >> 4, c = idx & 15;
-          const int key = j * kKvTile + n;
-          int64_t e = -1;
-          if (key < kv_hi) {
-            const int blk = table[key / p.bs];
-            const uint64_t off = p.offsets[blk];
-            const uint64_t elem = off + uint64_t(key % p.bs) * row_stride + uint64_t(h) * kHd + c * 8;
-            if ((off & 7) == 0 && elem + 8 <= p.region_elems) e = int64_t(elem);
-            else bad = true;
-          }
-          ptx::cp_async16(vdst + swz(n, c), e >= 0 ? p.va_v + e : p.va_v, e >= 0 ? 16u : 0u);
-        }
-        ptx::cp_async_mbar_arrive(bar(kVFull + st));
-      }
+      gather_tile(p.va_v, sb + kWsOffV + st * kTile, e0, live, j, kv_hi, row_stride, h, lane);
+      ptx::cp_async_mbar_arrive(bar(kVFull + st));
     }
     ptx::cp_async_wait<0>();
     if (bad) atomicOr(p.diag, int32_t(kDiagBadOffset));
@@ -654,6 +639,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
       const uint32_t ka = sb + kWsOffK + (j % kKStages) * kTile, tS = tmem + (j & 1) * 128;
       if (lane == 0) {
         tc::fence_after_sync();
+        ptx::fence_proxy_async_smem();  // cp.async-written K (and Q) -> tensor-core reads
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t o = uint32_t((k >> 2) * kHalf + (k & 3) * 32);
@@ -677,6 +663,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const __grid_
       if (!ws_wait(bar(kVFull + (j & 1)), uint32_t((j >> 1) & 1), fail)) break;
       if (lane == 0) {
         tc::fence_after_sync();
+        ptx::fence_proxy_async_smem();  // cp.async-written V -> tensor-core reads
         const uint32_t va = sb + kWsOffV + (j & 1) * kTile;
         const uint32_t tp = tmem + (j & 1) * 128;  // P_hi columns [0,64), P_lo [64,128)
 #pragma unroll
@@ -807,24 +794,15 @@ cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
   p.idesc_pv = tc::idesc_f16(bf16, 128, 128, false, true);
   p.diag = a.diag;
   dim3 grid((a.max_q_len + p.tt - 1) / p.tt, a.kv_heads, a.batch);
-  // TMA page boxes need 16-token pages that start on whole token rows of the
-  // {D, Hkv, tokens} view: block_size % 16 == 0 and kv_heads * 128 dividing the
-  // 2 MiB superblock (1 Mi elements).  Otherwise the cp.async kernel runs.
-  const bool tma = a.tensor_maps && a.block_size % 16 == 0 &&
-                   (uint64_t(1) << 20) % (uint64_t(a.kv_heads) * kHd) == 0 &&
-                   !(std::getenv("KCMM_PREFILL_IMPL") &&
-                     std::strcmp(std::getenv("KCMM_PREFILL_IMPL"), "cpasync") == 0);
-  if (tma) {
-    PrefillTmaParams tp;
-    std::memcpy(&tp.tmk, a.tensor_maps, sizeof(CUtensorMap));
-    std::memcpy(&tp.tmv, static_cast<const char *>(a.tensor_maps) + 128, sizeof(CUtensorMap));
-    tp.p = p;
-    tp.region_tokens = a.region_tokens;
+  // The warp-specialised kernel gathers 16-token page boxes: block_size % 16 == 0.
+  // Otherwise (or with KCMM_PREFILL_IMPL=cpasync) the single-role kernel runs.
+  const char *impl = std::getenv("KCMM_PREFILL_IMPL");
+  if (a.block_size % 16 == 0 && !(impl && std::strcmp(impl, "cpasync") == 0)) {
     auto fn = bf16 ? prefill_ws_kernel<__nv_bfloat16> : prefill_ws_kernel<__half>;
     cudaError_t e =
         cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kWsSmem));
     if (e != cudaSuccess) return e;
-    fn<<<grid, kWsThreads, kWsSmem, stream>>>(tp);
+    fn<<<grid, kWsThreads, kWsSmem, stream>>>(p);
     return cudaGetLastError();
   }
   auto fn = bf16 ? prefill_kernel<__nv_bfloat16> : prefill_kernel<__half>;

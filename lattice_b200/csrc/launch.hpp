@@ -70,10 +70,6 @@ struct PrefillArgs {
   int batch, max_q_len, num_q_heads, kv_heads, head_dim, block_size, max_blocks_per_seq;
   float scale;
   int32_t *diag;
-  // K and V TMA descriptors of the layer ({D, Hkv, tokens}, box {64, 1, 16}) or null;
-  // region_tokens = tokens they span.  Without them the cp.async kernel runs.
-  const void *tensor_maps;
-  uint64_t region_tokens;
 };
 // Causal chunked-prefill attention on the tcgen05 tensor cores
 // (kernels/prefill.cu).  head_dim 128; num_q_heads / kv_heads must divide 128.

@@ -55,6 +55,7 @@ CASES = [
     ([400, 333], [130, 333], 4, 4),                 # MHA: 128 tokens per CTA
     ([600, 90], [77, 90], 32, 2),                   # GQA 16: 8 tokens per CTA
     ([250, 700, 31], [0, 129, 31], 16, 8),          # an empty chunk; GQA 2
+    ([300, 517], [300, 200], 12, 3),                # 3 kv heads: blocks not token-aligned in 2 MiB
 ]
 
 
@@ -73,10 +74,11 @@ def test_prefill_matches_oracle(case, dtype):
         wl.close()
 
 
-@pytest.mark.parametrize("impl,bs", [("cpasync", 16), ("tma", 32), ("tma", 8)])
+@pytest.mark.parametrize("impl,bs", [("cpasync", 16), ("ws", 32), ("ws", 8)])
 def test_prefill_kernel_paths(impl, bs, monkeypatch):
-    """The cp.async kernel (forced, and chosen for 8-token pages) and the TMA kernel with
-    32-token pages (two boxes per page) agree with the oracle."""
+    """The single-role kernel (forced, and chosen for 8-token pages) and the
+    warp-specialised kernel with 32-token pages (two boxes per page) agree with the
+    oracle."""
     if impl == "cpasync":
         monkeypatch.setenv("KCMM_PREFILL_IMPL", "cpasync")
     wl = make(ctx_lens=[700, 260], chunk_lens=[300, 260], num_q_heads=16, kv_heads=2,
