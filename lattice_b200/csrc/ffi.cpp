@@ -604,6 +604,7 @@ static int prefill_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, 
   a.max_blocks_per_seq = int(max_bps);
   a.scale = scale;
   a.diag = p->diag_word();
+  a.tensor_maps = p->tensor_maps(layer, int(hkv), int(hd));
   return check_launch(h, op, kcmm::dev::paged_prefill(a, S(stream)));
 }
 

@@ -28,6 +28,7 @@
 // diagnostic bit, the CTA drains its copies, frees its TMEM and returns.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdlib>
@@ -427,8 +428,12 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
 //            columns, P_lo in the last 64), O rescale in TMEM, epilogue
 // warp 8     K producer: Q, then K tiles into a 3-stage ring
 // warp 10    V producer: V tiles into a 2-stage ring
-//            (both gather 16-token page boxes with 16-byte cp.async from all lanes,
-//            zero-filling keys past the context; TMA boxes of 2 KB issue too slowly)
+// TMA variant: 16-token page boxes ({64, 1, 16}, 2 KB) by TMA, K boxes 0-3 from warp 8
+//            and 4-7 from warp 11, V boxes from warps 10 and 12 (TMA issue is serial
+//            within a warp, ~90 cycles a box); V tiles that reach past the context
+//            are gathered with zero-filling cp.async instead.
+// Gather variant (layouts the tensor map cannot address): warps 8 and 10 copy whole
+//            tiles with 16-byte cp.async from all lanes.
 // warp 9     MMA issuer (lane 0) and TMEM owner: QK of tile j+1 is issued before P.V of
 //            tile j, into the other of two S buffers, so softmax of one tile overlaps the
 //            tensor work of its neighbours.  P.V takes P from TMEM (A operand) and V from
@@ -446,7 +451,16 @@ constexpr uint32_t kWsOffV = kWsOffK + kKStages * kTile;
 constexpr uint32_t kWsOffBar = kWsOffV + 2 * kTile;     // no P tiles in shared memory
 constexpr uint32_t kWsOffXch = kWsOffBar + 256;          // row-max exchange [2 parity][2 half][128]
 constexpr size_t kWsSmem = kWsOffXch + 2 * 2 * 128 * 4 + 1024;
-constexpr int kWsThreads = 352;
+// Kernel parameters with the layer's K and V tensor maps ({D, Hkv, tokens}, box
+// {64, 1, 16}, 128-byte swizzle) for the TMA variant; row_shift = log2(Hkv * D).
+struct alignas(64) WsParams {
+  CUtensorMap tmk;
+  CUtensorMap tmv;
+  PrefillParams p;
+  uint32_t row_shift;
+};
+template <bool TMA>
+constexpr int ws_threads() { return TMA ? 13 * 32 : 11 * 32; }
 enum WsBar { kQFull = 0, kKFull = 1, kKEmpty = 4, kVFull = 7, kVEmpty = 9, kSFull = 11,
              kPFull = 13, kODone = 14, kPair = 15, kSlot = 19 };  // kPair: one per row quarter
 
@@ -520,12 +534,13 @@ __device__ __forceinline__ bool ws_wait(uint32_t bar, uint32_t parity, volatile 
 // rows][128 B] layout with 16-byte cp.async: each half-warp moves one 256-byte token
 // row per step.  Box b (keys 16b .. 16b+15) starts at element e0 of lane b; keys past
 // kv_hi and boxes that are not live are zero-filled.
+template <int B0 = 0, int NB = 8>
 __device__ __forceinline__ void gather_tile(const uint16_t *va, uint32_t dst, int64_t e0, bool live,
                                             int j, int kv_hi, uint32_t row_stride, int h,
                                             int lane) {
   const int hw = lane >> 4, c = lane & 15;
 #pragma unroll
-  for (int b = 0; b < 8; ++b) {
+  for (int b = B0; b < B0 + NB; ++b) {
     const int64_t eb = __shfl_sync(0xffffffffu, e0, b);
     const bool lb = __shfl_sync(0xffffffffu, int(live), b) != 0;
 #pragma unroll
@@ -538,8 +553,10 @@ __device__ __forceinline__ void gather_tile(const uint16_t *va, uint32_t dst, in
   }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const PrefillParams p) {
+template <typename T, bool TMA>
+__global__ void __launch_bounds__(ws_threads<TMA>(), 1)
+    prefill_ws_kernel(const __grid_constant__ WsParams P) {
+  const PrefillParams &p = P.p;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = ptx::smem_u32(smem_raw);
   const uint32_t sb = (raw + 1023u) & ~1023u;
@@ -565,12 +582,14 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const Prefill
   if (tid == 0) {
     ptx::mbar_init(bar(kQFull), 32);
     for (int i = 0; i < 2; ++i) {
-      ptx::mbar_init(bar(kVFull + i), 32);  // 32 cp.async arrivals per tile
+      // V: 32 arrivals per producer warp (cp.async noinc, or one expect_tx + 31 plain)
+      ptx::mbar_init(bar(kVFull + i), TMA ? 64 : 32);
       ptx::mbar_init(bar(kVEmpty + i), 1);
       ptx::mbar_init(bar(kSFull + i), 1);
     }
     for (int i = 0; i < kKStages; ++i) {
-      ptx::mbar_init(bar(kKFull + i), 32);
+      // K: one expect_tx per TMA producer warp, or 32 cp.async arrivals
+      ptx::mbar_init(bar(kKFull + i), TMA ? 2 : 32);
       ptx::mbar_init(bar(kKEmpty + i), 1);
     }
     ptx::mbar_init(bar(kPFull), 256);
@@ -590,44 +609,99 @@ __global__ void __launch_bounds__(kWsThreads, 1) prefill_ws_kernel(const Prefill
   volatile int *fail = &s_fail;
   const int32_t *table = p.tables + size_t(b) * p.max_bps;
   const uint32_t row_stride = uint32_t(p.hkv) * kHd;  // elements per token row
+  // producer roles: K part 0 (+Q) = warp 8, V part 0 = warp 10; with TMA, K part 1 =
+  // warp 11 and V part 1 = warp 12 (a part = boxes 4*part .. 4*part+3 of each tile)
+  const bool k_prod = warp == 8 || (TMA && warp == 11);
+  const bool v_prod = warp == 10 || (TMA && warp == 12);
 
-  if (warp == 8) {
-    // ---------------- K producer (and Q) ----------------
-    for (int it = 0; it < 64; ++it) {
-      const int idx = it * 32 + lane, r = idx >> 4, c = idx & 15;
-      const int t_r = qt * p.tt + r / p.G, h_r = h * p.G + r % p.G;
-      const bool ok = t_r < qlen;
-      const uint16_t *src = ok ? p.q + (size_t(q0 + t_r) * p.hq + h_r) * kHd + c * 8 : p.q;
-      ptx::cp_async16(sb + kOffQ + swz(r, c), src, ok ? 16u : 0u);
+  if (k_prod) {
+    // ---------------- K producer (warp 8 also loads Q) ----------------
+    if (warp == 8) {
+      for (int it = 0; it < 64; ++it) {
+        const int idx = it * 32 + lane, r = idx >> 4, c = idx & 15;
+        const int t_r = qt * p.tt + r / p.G, h_r = h * p.G + r % p.G;
+        const bool ok = t_r < qlen;
+        const uint16_t *src = ok ? p.q + (size_t(q0 + t_r) * p.hq + h_r) * kHd + c * 8 : p.q;
+        ptx::cp_async16(sb + kOffQ + swz(r, c), src, ok ? 16u : 0u);
+      }
+      ptx::cp_async_mbar_arrive(bar(kQFull));
     }
-    ptx::cp_async_mbar_arrive(bar(kQFull));
+    const int part = warp == 8 ? 0 : 1;
+    if (TMA && lane == 0) ptx::prefetch_tensormap(&P.tmk);
     bool bad = false;
     BoxLookup lk(table, p.offsets, p.bs, kv_hi, nt, lane);
     for (int j = 0; j < nt; ++j) {
       const int st = j % kKStages;
       int64_t e0 = 0;
-      const bool live = lk.next(row_stride, p.region_elems, &e0, &bad);
+      bool live = lk.next(row_stride, p.region_elems, &e0, &bad);
       // QK of tile j - kKStages must have finished reading this stage
       if (j >= kKStages &&
           !ws_wait(bar(kKEmpty + st), uint32_t((j / kKStages - 1) & 1), fail))
         break;
-      gather_tile(p.va_k, sb + kWsOffK + st * kTile, e0, live, j, kv_hi, row_stride, h, lane);
-      ptx::cp_async_mbar_arrive(bar(kKFull + st));
+      const uint32_t dst = sb + kWsOffK + st * kTile;
+      if constexpr (TMA) {
+        if (live && (e0 & (row_stride - 1)) != 0) {  // not a whole token row: no TMA box
+          live = false;
+          bad = true;
+        }
+        const bool mine = ((lane & 7) >> 2) == part;
+        const uint32_t lm = __ballot_sync(0xffffffffu, live && mine && lane < 8);
+        if (lane == 0) ptx::mbar_arrive_expect_tx(bar(kKFull + st), uint32_t(__popc(lm)) * 4096u);
+        __syncwarp();
+        if (lane < 16 && live && mine) {  // lanes 8..15: second head_dim half of the boxes
+          const int bx = lane & 7, half = lane >> 3;
+          ptx::tma_load_3d(dst + half * kHalf + bx * 2048, &P.tmk, half * 64, h,
+                           int(e0 >> P.row_shift), bar(kKFull + st));
+        }
+      } else {
+        gather_tile(p.va_k, dst, e0, live, j, kv_hi, row_stride, h, lane);
+        ptx::cp_async_mbar_arrive(bar(kKFull + st));
+      }
     }
     ptx::cp_async_wait<0>();
     if (bad) atomicOr(p.diag, int32_t(kDiagBadOffset));
-  } else if (warp == 10) {
+  } else if (v_prod) {
     // ---------------- V producer ----------------
+    const int part = warp == 10 ? 0 : 1;
+    if (TMA && lane == 0) ptx::prefetch_tensormap(&P.tmv);
     bool bad = false;
     BoxLookup lk(table, p.offsets, p.bs, kv_hi, nt, lane);
     for (int j = 0; j < nt; ++j) {
       const int st = j & 1;
       int64_t e0 = 0;
-      const bool live = lk.next(row_stride, p.region_elems, &e0, &bad);
+      bool live = lk.next(row_stride, p.region_elems, &e0, &bad);
       // P.V of tile j-2 must have finished reading this stage
       if (j >= 2 && !ws_wait(bar(kVEmpty + st), uint32_t(((j >> 1) - 1) & 1), fail)) break;
-      gather_tile(p.va_v, sb + kWsOffV + st * kTile, e0, live, j, kv_hi, row_stride, h, lane);
-      ptx::cp_async_mbar_arrive(bar(kVFull + st));
+      const uint32_t dst = sb + kWsOffV + st * kTile;
+      if constexpr (TMA) {
+        const bool aligned = (e0 & (row_stride - 1)) == 0;
+        const bool mine = ((lane & 7) >> 2) == part;
+        const uint32_t lm = __ballot_sync(0xffffffffu, live && aligned && mine && lane < 8);
+        // whole tile inside the context and all 4 boxes loadable: TMA, else zero-filling copies
+        if (j * kKvTile + kKvTile <= kv_hi && __popc(lm) == 4) {
+          if (lane == 0) {
+            ptx::mbar_arrive_expect_tx(bar(kVFull + st), 4u * 4096u);
+          } else {
+            ptx::mbar_arrive(bar(kVFull + st));
+          }
+          __syncwarp();
+          if (lane < 16 && mine) {
+            const int bx = lane & 7, half = lane >> 3;
+            ptx::tma_load_3d(dst + half * kHalf + bx * 2048, &P.tmv, half * 64, h,
+                             int(e0 >> P.row_shift), bar(kVFull + st));
+          }
+        } else {
+          if (part == 0) {
+            gather_tile<0, 4>(p.va_v, dst, e0, live, j, kv_hi, row_stride, h, lane);
+          } else {
+            gather_tile<4, 4>(p.va_v, dst, e0, live, j, kv_hi, row_stride, h, lane);
+          }
+          ptx::cp_async_mbar_arrive(bar(kVFull + st));
+        }
+      } else {
+        gather_tile(p.va_v, dst, e0, live, j, kv_hi, row_stride, h, lane);
+        ptx::cp_async_mbar_arrive(bar(kVFull + st));
+      }
     }
     ptx::cp_async_wait<0>();
     if (bad) atomicOr(p.diag, int32_t(kDiagBadOffset));
@@ -797,12 +871,27 @@ cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
   // The warp-specialised kernel gathers 16-token page boxes: block_size % 16 == 0.
   // Otherwise (or with KCMM_PREFILL_IMPL=cpasync) the single-role kernel runs.
   const char *impl = std::getenv("KCMM_PREFILL_IMPL");
-  if (a.block_size % 16 == 0 && !(impl && std::strcmp(impl, "cpasync") == 0)) {
-    auto fn = bf16 ? prefill_ws_kernel<__nv_bfloat16> : prefill_ws_kernel<__half>;
+  const bool single = impl && std::strcmp(impl, "cpasync") == 0;
+  const bool gather = impl && std::strcmp(impl, "gather") == 0;
+  if (a.block_size % 16 == 0 && !single) {
+    // TMA boxes address whole token rows of the {D, Hkv, tokens} view: Hkv * D must be
+    // a power of two dividing the 2 MiB superblock (1 Mi elements).
+    const uint32_t rs = uint32_t(a.kv_heads) * kHd;
+    const bool tma = !gather && a.tensor_maps && (rs & (rs - 1)) == 0 && (1u << 20) % rs == 0;
+    WsParams wp;
+    std::memset(static_cast<void *>(&wp), 0, sizeof(wp));
+    wp.p = p;
+    wp.row_shift = uint32_t(__builtin_ctz(rs));
+    if (tma) {
+      std::memcpy(&wp.tmk, a.tensor_maps, sizeof(CUtensorMap));
+      std::memcpy(&wp.tmv, static_cast<const char *>(a.tensor_maps) + 128, sizeof(CUtensorMap));
+    }
+    auto fn = tma ? (bf16 ? prefill_ws_kernel<__nv_bfloat16, true> : prefill_ws_kernel<__half, true>)
+                  : (bf16 ? prefill_ws_kernel<__nv_bfloat16, false> : prefill_ws_kernel<__half, false>);
     cudaError_t e =
         cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kWsSmem));
     if (e != cudaSuccess) return e;
-    fn<<<grid, kWsThreads, kWsSmem, stream>>>(p);
+    fn<<<grid, tma ? ws_threads<true>() : ws_threads<false>(), kWsSmem, stream>>>(wp);
     return cudaGetLastError();
   }
   auto fn = bf16 ? prefill_kernel<__nv_bfloat16> : prefill_kernel<__half>;

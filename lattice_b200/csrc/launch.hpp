@@ -70,6 +70,8 @@ struct PrefillArgs {
   int batch, max_q_len, num_q_heads, kv_heads, head_dim, block_size, max_blocks_per_seq;
   float scale;
   int32_t *diag;
+  // K and V TMA descriptors of the layer ({D, Hkv, tokens}, box {64, 1, 16}) or null.
+  const void *tensor_maps;
 };
 // Causal chunked-prefill attention on the tcgen05 tensor cores
 // (kernels/prefill.cu).  head_dim 128; num_q_heads / kv_heads must divide 128.
