@@ -98,18 +98,18 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
 // alpha = exp2(m_old - m_new) rescales the earlier sum and O.
 template <int N>
 __device__ __forceinline__ float masked_max(float (&s)[N], int k0, int qpos, bool need_mask) {
-  float mx = -INFINITY;
   if (need_mask) {
 #pragma unroll
-    for (int c = 0; c < N; ++c) {
-      if (k0 + c > qpos) s[c] = -INFINITY;
-      mx = fmaxf(mx, s[c]);
-    }
-  } else {
-#pragma unroll
-    for (int c = 0; c < N; ++c) mx = fmaxf(mx, s[c]);
+    for (int c = 0; c < N; ++c) s[c] = k0 + c > qpos ? -INFINITY : s[c];
   }
-  return mx;
+  // four independent chains of three-input max
+  float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+  for (int c = 0; c < N; c += 8) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m[i] = ptx::max3(m[i], s[c + 2 * i], s[c + 2 * i + 1]);
+  }
+  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
 }
 
 // Given the tile's row max mx (already in log2 units), update the running max and
@@ -123,13 +123,13 @@ __device__ __forceinline__ float exp_given_max(float (&s)[N], float mx, float sc
   alpha = ptx::fast_exp2(m_run - m_new);  // 0 on the first tile, else <= 1
   rescale = has_prev && m_new != m_run;
   m_run = m_new;
-  float sum = 0.f;
+  float sum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int c = 0; c < N; ++c) {
     s[c] = ptx::fast_exp2(fmaf(s[c], scale_log2, -m_new));
-    sum += s[c];
+    sum[c & 3] += s[c];
   }
-  return sum;
+  return (sum[0] + sum[1]) + (sum[2] + sum[3]);
 }
 
 __device__ __forceinline__ float exp_tile(float (&s)[128], int k0, int qpos, bool need_mask,
