@@ -434,13 +434,13 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
 //            are gathered with zero-filling cp.async instead.
 // Gather variant (layouts the tensor map cannot address): warps 8 and 10 copy whole
 //            tiles with 16-byte cp.async from all lanes.
-// warp 9     MMA issuer (lane 0) and TMEM owner: QK of tile j+1 is issued before P.V of
-//            tile j, into the other of two S buffers, so softmax of one tile overlaps the
-//            tensor work of its neighbours.  P.V takes P from TMEM (A operand) and V from
-//            shared memory, so only V is read from shared memory.
-// TMEM columns: S0/P0 [0,128), S1/P1 [128,256), O [256,384) of a 512-column allocation.
-// Tensor-core operations of the CTA execute in issue order: QK of tile j+2 (into S_j's
-// columns) runs after P.V of tile j has read P_j from them.
+// warp 9     MMA issuer (lane 0) and TMEM owner: QK runs two tiles ahead of P.V, so
+//            softmax of one tile overlaps the tensor work of its neighbours.  P.V takes
+//            P from TMEM (A operand) and V from shared memory.
+// TMEM columns: S/P buffers [0,128), [128,256), [256,384) and O [384,512).  QK of tile
+// j+2 is issued before P.V of tile j, into the buffer of tile j-1; tensor-core
+// operations of the CTA execute in issue order, so it runs after P.V of tile j-1 has
+// read P_(j-1) from those columns.
 
 
 
@@ -461,8 +461,12 @@ struct alignas(64) WsParams {
 };
 template <bool TMA>
 constexpr int ws_threads() { return TMA ? 13 * 32 : 11 * 32; }
+constexpr int kSBufs = 3;  // S/P buffers in TMEM: QK of tile j+2 issues before P.V of tile j
+// kSFull/kPFull: one per S buffer; kODone: one per tile parity; kPair: one per row quarter.
+// Each waiter's barrier can complete at most once past the phase it waits on, so the
+// parity waits are unambiguous.
 enum WsBar { kQFull = 0, kKFull = 1, kKEmpty = 4, kVFull = 7, kVEmpty = 9, kSFull = 11,
-             kPFull = 13, kODone = 14, kPair = 15, kSlot = 19 };  // kPair: one per row quarter
+             kPFull = 14, kODone = 17, kPair = 19, kSlot = 23 };
 
 // Page lookups for the 16-token boxes of successive KV tiles, four tiles ahead.  The
 // producer warp's lanes form 4 groups of 8 (lane = 8 * group + box); group g serves
@@ -585,15 +589,17 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
       // V: 32 arrivals per producer warp (cp.async noinc, or one expect_tx + 31 plain)
       ptx::mbar_init(bar(kVFull + i), TMA ? 64 : 32);
       ptx::mbar_init(bar(kVEmpty + i), 1);
+      ptx::mbar_init(bar(kODone + i), 1);
+    }
+    for (int i = 0; i < kSBufs; ++i) {
       ptx::mbar_init(bar(kSFull + i), 1);
+      ptx::mbar_init(bar(kPFull + i), 256);
     }
     for (int i = 0; i < kKStages; ++i) {
       // K: one expect_tx per TMA producer warp, or 32 cp.async arrivals
       ptx::mbar_init(bar(kKFull + i), TMA ? 2 : 32);
       ptx::mbar_init(bar(kKEmpty + i), 1);
     }
-    ptx::mbar_init(bar(kPFull), 256);
-    ptx::mbar_init(bar(kODone), 1);
     for (int i = 0; i < 4; ++i) ptx::mbar_init(bar(kPair + i), 64);
     ptx::fence_mbarrier_init();
     s_fail = 0;
@@ -708,9 +714,9 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
   } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
     const uint32_t qa = sb + kOffQ;
-    const uint32_t tO = tmem + 256;
+    const uint32_t tO = tmem + kSBufs * 128;
     auto issue_qk = [&](int j) {
-      const uint32_t ka = sb + kWsOffK + (j % kKStages) * kTile, tS = tmem + (j & 1) * 128;
+      const uint32_t ka = sb + kWsOffK + (j % kKStages) * kTile, tS = tmem + (j % kSBufs) * 128;
       if (lane == 0) {
         tc::fence_after_sync();
         ptx::fence_proxy_async_smem();  // cp.async-written K (and Q) -> tensor-core reads
@@ -720,33 +726,39 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
           tc::mma_ss(tS, tc::sw128_desc(qa + o, 16, 1024), tc::sw128_desc(ka + o, 16, 1024),
                      p.idesc_qk, k > 0);
         }
-        tc::commit(bar(kSFull + (j & 1)));
+        tc::commit(bar(kSFull + j % kSBufs));
         tc::commit(bar(kKEmpty + j % kKStages));
       }
       __syncwarp();
     };
     bool ok = ws_wait(bar(kQFull), 0, fail) && ws_wait(bar(kKFull), 0, fail);
     if (ok) issue_qk(0);
+    if (ok && nt > 1) {
+      ok = ws_wait(bar(kKFull + 1), 0, fail);
+      if (ok) issue_qk(1);
+    }
     for (int j = 0; ok && j < nt; ++j) {
-      if (j + 1 < nt) {
-        if (!ws_wait(bar(kKFull + (j + 1) % kKStages), uint32_t(((j + 1) / kKStages) & 1), fail))
+      // QK of tile j+2 goes into the buffer of tile j-1, whose P.V was issued last
+      // iteration (tensor-core operations run in issue order)
+      if (j + 2 < nt) {
+        if (!ws_wait(bar(kKFull + (j + 2) % kKStages), uint32_t(((j + 2) / kKStages) & 1), fail))
           break;
-        issue_qk(j + 1);
+        issue_qk(j + 2);
       }
-      if (!ws_wait(bar(kPFull), uint32_t(j & 1), fail)) break;
+      if (!ws_wait(bar(kPFull + j % kSBufs), uint32_t((j / kSBufs) & 1), fail)) break;
       if (!ws_wait(bar(kVFull + (j & 1)), uint32_t((j >> 1) & 1), fail)) break;
       if (lane == 0) {
         tc::fence_after_sync();
         ptx::fence_proxy_async_smem();  // cp.async-written V -> tensor-core reads
         const uint32_t va = sb + kWsOffV + (j & 1) * kTile;
-        const uint32_t tp = tmem + (j & 1) * 128;  // P_hi columns [0,64), P_lo [64,128)
+        const uint32_t tp = tmem + (j % kSBufs) * 128;  // P_hi columns [0,64), P_lo [64,128)
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint64_t vd = tc::sw128_desc(va + uint32_t(k) * 2048, kHalf, 1024);
           tc::mma_ts(tO, tp + k * 8, vd, p.idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
           tc::mma_ts(tO, tp + 64 + k * 8, vd, p.idesc_pv, 1u);
         }
-        tc::commit(bar(kODone));
+        tc::commit(bar(kODone + (j & 1)));
         tc::commit(bar(kVEmpty + (j & 1)));
       }
       __syncwarp();
@@ -759,19 +771,19 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
     const bool row_ok = ti < qlen;
     const int qpos = row_ok ? base_pos + ti : kv_hi - 1;
     const uint32_t lane_base = uint32_t(q4 * 32) << 16;
-    const uint32_t tO = tmem + 256 + lane_base + hf * 64;
+    const uint32_t tO = tmem + kSBufs * 128 + lane_base + hf * 64;
     float *xch = reinterpret_cast<float *>(smem + kWsOffXch);
     const uint32_t pbar = bar(kPair + q4);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
-      if (!ws_wait(bar(kSFull + (j & 1)), uint32_t((j >> 1) & 1), fail)) {
+      if (!ws_wait(bar(kSFull + j % kSBufs), uint32_t((j / kSBufs) & 1), fail)) {
         ok = false;
         break;
       }
       tc::fence_after_sync();
       float s[64];
-      const uint32_t tS = tmem + (j & 1) * 128 + lane_base;
+      const uint32_t tS = tmem + (j % kSBufs) * 128 + lane_base;
       tc::ld32(tS + hf * 64, s);
       tc::ld32(tS + hf * 64 + 32, s + 32);
       tc::wait_ld();
@@ -794,10 +806,9 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
       l_run = l_run * alpha + sum;
       store_p_tmem<T, 64>(s, tS + hf * 32, tS + 64 + hf * 32);
       if (__any_sync(0xffffffffu, rescale)) {
-        // O *= alpha once P.V of tile j-1 is done.  At this point that is the only
-        // P.V that may still run (tile j-2's finished before QK of tile j, whose S
-        // we hold), so the parity wait cannot see a later phase.
-        if (!ws_wait(bar(kODone), uint32_t((j - 1) & 1), fail)) {
+        // O *= alpha once P.V of tile j-1 is done (P.V of tile j waits for this
+        // tile's P, so it cannot have run)
+        if (!ws_wait(bar(kODone + ((j - 1) & 1)), uint32_t(((j - 1) >> 1) & 1), fail)) {
           ok = false;
           break;
         }
@@ -805,7 +816,7 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
         scale_o_row<64>(tO, rescale ? alpha : 1.f);
       }
       tc::fence_before_sync();
-      ptx::mbar_arrive(bar(kPFull));
+      ptx::mbar_arrive(bar(kPFull + j % kSBufs));
     }
     // row sum = both halves' partial sums (same running max in both warps)
     if (ok) {
@@ -817,9 +828,8 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
         ok = false;
       }
     }
-    // P.V of tile nt-2 may still be running: wait its phase, then the last one
-    if (ok && nt >= 2 && !ws_wait(bar(kODone), uint32_t((nt - 2) & 1), fail)) ok = false;
-    if (ok && ws_wait(bar(kODone), uint32_t((nt - 1) & 1), fail)) {
+    // the last P.V done (all earlier ones ran before it)
+    if (ok && ws_wait(bar(kODone + ((nt - 1) & 1)), uint32_t(((nt - 1) >> 1) & 1), fail)) {
       tc::fence_after_sync();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + row % p.G) * kHd + hf * 64;
