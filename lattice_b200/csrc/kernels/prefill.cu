@@ -445,12 +445,13 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
 
 
 constexpr uint32_t kWsTmemCols = 512;
-constexpr int kKStages = 3;                              // K ring depth (V: 2)
+constexpr int kKStages = 3;                              // K ring depth
+constexpr int kVStages = 2;                              // V ring depth
 constexpr uint32_t kWsOffK = kOffQ + kTile;
 constexpr uint32_t kWsOffV = kWsOffK + kKStages * kTile;
-constexpr uint32_t kWsOffBar = kWsOffV + 2 * kTile;     // no P tiles in shared memory
+constexpr uint32_t kWsOffBar = kWsOffV + kVStages * kTile;  // no P tiles in shared memory
 constexpr uint32_t kWsOffXch = kWsOffBar + 256;          // row-max exchange [2 parity][2 half][128]
-constexpr size_t kWsSmem = kWsOffXch + 2 * 2 * 128 * 4 + 1024;
+constexpr size_t kWsSmem = kWsOffXch + 2 * 2 * 128 * 4 + 1024;  // + alignment slack
 // Kernel parameters with the layer's K and V tensor maps ({D, Hkv, tokens}, box
 // {64, 1, 16}, 128-byte swizzle) for the TMA variant; row_shift = log2(Hkv * D).
 struct alignas(64) WsParams {
@@ -465,8 +466,11 @@ constexpr int kSBufs = 3;  // S/P buffers in TMEM: QK of tile j+2 issues before 
 // kSFull/kPFull: one per S buffer; kODone: one per tile parity; kPair: one per row quarter.
 // Each waiter's barrier can complete at most once past the phase it waits on, so the
 // parity waits are unambiguous.
-enum WsBar { kQFull = 0, kKFull = 1, kKEmpty = 4, kVFull = 7, kVEmpty = 9, kSFull = 11,
-             kPFull = 14, kODone = 17, kPair = 19, kSlot = 23 };
+// kOFinal: single use, committed after the last P.V (the epilogue's wait cannot use
+// kODone: softmax may finish its last tile while P.V of tile nt-3, on the same
+// barrier, is still running, and a parity wait would then pass one phase early).
+enum WsBar { kQFull = 0, kKFull = 1, kKEmpty = 4, kVFull = 7, kVEmpty = 10, kSFull = 13,
+             kPFull = 16, kODone = 19, kPair = 21, kOFinal = 25, kSlot = 26 };
 
 // Page lookups for the 16-token boxes of successive KV tiles, four tiles ahead.  The
 // producer warp's lanes form 4 groups of 8 (lane = 8 * group + box); group g serves
@@ -585,12 +589,13 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
 
   if (tid == 0) {
     ptx::mbar_init(bar(kQFull), 32);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kVStages; ++i) {
       // V: 32 arrivals per producer warp (cp.async noinc, or one expect_tx + 31 plain)
       ptx::mbar_init(bar(kVFull + i), TMA ? 64 : 32);
       ptx::mbar_init(bar(kVEmpty + i), 1);
-      ptx::mbar_init(bar(kODone + i), 1);
     }
+    for (int i = 0; i < 2; ++i) ptx::mbar_init(bar(kODone + i), 1);
+    ptx::mbar_init(bar(kOFinal), 1);
     for (int i = 0; i < kSBufs; ++i) {
       ptx::mbar_init(bar(kSFull + i), 1);
       ptx::mbar_init(bar(kPFull + i), 256);
@@ -615,8 +620,9 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
   volatile int *fail = &s_fail;
   const int32_t *table = p.tables + size_t(b) * p.max_bps;
   const uint32_t row_stride = uint32_t(p.hkv) * kHd;  // elements per token row
-  // producer roles: K part 0 (+Q) = warp 8, V part 0 = warp 10; with TMA, K part 1 =
-  // warp 11 and V part 1 = warp 12 (a part = boxes 4*part .. 4*part+3 of each tile)
+  // Roles: warps 0-7 softmax, 8 K producer part 0 (+Q), 9 MMA, 10 V producer part 0;
+  // with TMA, 11 = K part 1 and 12 = V part 1 (a part = boxes 4*part .. 4*part+3 of a
+  // tile).
   const bool k_prod = warp == 8 || (TMA && warp == 11);
   const bool v_prod = warp == 10 || (TMA && warp == 12);
 
@@ -673,11 +679,13 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
     bool bad = false;
     BoxLookup lk(table, p.offsets, p.bs, kv_hi, nt, lane);
     for (int j = 0; j < nt; ++j) {
-      const int st = j & 1;
+      const int st = j % kVStages;
       int64_t e0 = 0;
       bool live = lk.next(row_stride, p.region_elems, &e0, &bad);
-      // P.V of tile j-2 must have finished reading this stage
-      if (j >= 2 && !ws_wait(bar(kVEmpty + st), uint32_t(((j >> 1) - 1) & 1), fail)) break;
+      // P.V of tile j - kVStages must have finished reading this stage
+      if (j >= kVStages &&
+          !ws_wait(bar(kVEmpty + st), uint32_t((j / kVStages - 1) & 1), fail))
+        break;
       const uint32_t dst = sb + kWsOffV + st * kTile;
       if constexpr (TMA) {
         const bool aligned = (e0 & (row_stride - 1)) == 0;
@@ -746,11 +754,11 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
         issue_qk(j + 2);
       }
       if (!ws_wait(bar(kPFull + j % kSBufs), uint32_t((j / kSBufs) & 1), fail)) break;
-      if (!ws_wait(bar(kVFull + (j & 1)), uint32_t((j >> 1) & 1), fail)) break;
+      if (!ws_wait(bar(kVFull + j % kVStages), uint32_t((j / kVStages) & 1), fail)) break;
       if (lane == 0) {
         tc::fence_after_sync();
         ptx::fence_proxy_async_smem();  // cp.async-written V -> tensor-core reads
-        const uint32_t va = sb + kWsOffV + (j & 1) * kTile;
+        const uint32_t va = sb + kWsOffV + (j % kVStages) * kTile;
         const uint32_t tp = tmem + (j % kSBufs) * 128;  // P_hi columns [0,64), P_lo [64,128)
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
@@ -759,11 +767,12 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
           tc::mma_ts(tO, tp + 64 + k * 8, vd, p.idesc_pv, 1u);
         }
         tc::commit(bar(kODone + (j & 1)));
-        tc::commit(bar(kVEmpty + (j & 1)));
+        tc::commit(bar(kVEmpty + j % kVStages));
+        if (j == nt - 1) tc::commit(bar(kOFinal));
       }
       __syncwarp();
     }
-  } else {
+  } else if (warp < 8) {
     // ---------------- softmax warps ----------------
     const int q4 = warp & 3, hf = warp >> 2;
     const int row = q4 * 32 + lane;
@@ -828,8 +837,8 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
         ok = false;
       }
     }
-    // the last P.V done (all earlier ones ran before it)
-    if (ok && ws_wait(bar(kODone + ((nt - 1) & 1)), uint32_t(((nt - 1) >> 1) & 1), fail)) {
+    // every P.V done
+    if (ok && ws_wait(bar(kOFinal), 0, fail)) {
       tc::fence_after_sync();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + row % p.G) * kHd + hf * 64;
