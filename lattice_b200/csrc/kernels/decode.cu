@@ -275,11 +275,11 @@ __global__ void __launch_bounds__(W * 32) decode_kernel(const DecodeParams p) {
         o[i][2] *= a1;
         o[i][3] *= a1;
       }
-      uint32_t pa[4];
-      pa[0] = MMA::pack(s[0][0], s[0][1]);
-      pa[1] = MMA::pack(s[0][2], s[0][3]);
-      pa[2] = MMA::pack(s[1][0], s[1][1]);
-      pa[3] = MMA::pack(s[1][2], s[1][3]);
+      uint32_t pa[4], pl[4];  // P = hi + lo (16-bit each)
+      MMA::split(s[0][0], s[0][1], pa[0], pl[0]);
+      MMA::split(s[0][2], s[0][3], pa[1], pl[1]);
+      MMA::split(s[1][0], s[1][1], pa[2], pl[2]);
+      MMA::split(s[1][2], s[1][3], pa[3], pl[3]);
       // O += P V
       {
         const int mi = lane >> 3, r = lane & 7;
@@ -290,7 +290,9 @@ __global__ void __launch_bounds__(W * 32) decode_kernel(const DecodeParams p) {
           ptx::ldsm_x4_t(ptx::smem_u32(vs_tile + tok * C::RS + j * 16 + (mi >> 1) * 8), b0, b1,
                          b2, b3);
           MMA::run(o[2 * j], pa, b0, b1);
+          MMA::run(o[2 * j], pl, b0, b1);
           MMA::run(o[2 * j + 1], pa, b2, b3);
+          MMA::run(o[2 * j + 1], pl, b2, b3);
         }
       }
     }

@@ -649,11 +649,11 @@ __global__ void __launch_bounds__((C + NP) * 32)
           o[d][3] *= a1;
         }
       }
-      uint32_t pa[4];
-      pa[0] = MMA::pack(s[0][0], s[0][1]);
-      pa[1] = MMA::pack(s[0][2], s[0][3]);
-      pa[2] = MMA::pack(s[1][0], s[1][1]);
-      pa[3] = MMA::pack(s[1][2], s[1][3]);
+      uint32_t pa[4], pl[4];  // P = hi + lo (16-bit each)
+      MMA::split(s[0][0], s[0][1], pa[0], pl[0]);
+      MMA::split(s[0][2], s[0][3], pa[1], pl[1]);
+      MMA::split(s[1][0], s[1][1], pa[2], pl[2]);
+      MMA::split(s[1][2], s[1][3], pa[3], pl[3]);
       {
         const int mi2 = lane >> 3, r = lane & 7;
         const int tok = (mi2 & 1) * 8 + r;
@@ -662,7 +662,9 @@ __global__ void __launch_bounds__((C + NP) * 32)
           uint32_t b0, b1, b2, b3;
           ptx::ldsm_x4_t(sw(vt, tok, j * 16 + (mi2 >> 1) * 8), b0, b1, b2, b3);
           MMA::run(o[2 * j], pa, b0, b1);
+          MMA::run(o[2 * j], pl, b0, b1);
           MMA::run(o[2 * j + 1], pa, b2, b3);
+          MMA::run(o[2 * j + 1], pl, b2, b3);
         }
       }
     }
@@ -1198,11 +1200,11 @@ __global__ void __launch_bounds__(W * 32) sk_ld_kernel(const Params p, int NS) {
           o[d][3] *= a1;
         }
       }
-      uint32_t pa[4];
-      pa[0] = MMA::pack(s[0][0], s[0][1]);
-      pa[1] = MMA::pack(s[0][2], s[0][3]);
-      pa[2] = MMA::pack(s[1][0], s[1][1]);
-      pa[3] = MMA::pack(s[1][2], s[1][3]);
+      uint32_t pa[4], pl[4];  // P = hi + lo (16-bit each)
+      MMA::split(s[0][0], s[0][1], pa[0], pl[0]);
+      MMA::split(s[0][2], s[0][3], pa[1], pl[1]);
+      MMA::split(s[1][0], s[1][1], pa[2], pl[2]);
+      MMA::split(s[1][2], s[1][3], pa[3], pl[3]);
       {
         const int mi2 = lane >> 3, r = lane & 7;
         const int tok = (mi2 & 1) * 8 + r;
@@ -1211,7 +1213,9 @@ __global__ void __launch_bounds__(W * 32) sk_ld_kernel(const Params p, int NS) {
           uint32_t b0, b1, b2, b3;
           ptx::ldsm_x4_t(sw(vt, tok, jj * 16 + (mi2 >> 1) * 8), b0, b1, b2, b3);
           MMA::run(o[2 * jj], pa, b0, b1);
+          MMA::run(o[2 * jj], pl, b0, b1);
           MMA::run(o[2 * jj + 1], pa, b2, b3);
+          MMA::run(o[2 * jj + 1], pl, b2, b3);
         }
       }
     }

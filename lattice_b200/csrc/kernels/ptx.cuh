@@ -163,6 +163,14 @@ struct Mma<__nv_bfloat16> {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&v);
   }
+  // (a, b) = hi + lo with hi the rounded pair and lo the rounded remainder: a P.V
+  // over both halves carries P to ~2^-17 instead of the 2^-9 of one 16-bit copy.
+  __device__ __forceinline__ static void split(float a, float b, uint32_t &hi, uint32_t &lo) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const float2 f = __bfloat1622float2(h);
+    hi = *reinterpret_cast<uint32_t *>(&h);
+    lo = pack(a - f.x, b - f.y);
+  }
 };
 
 template <>
@@ -178,6 +186,12 @@ struct Mma<__half> {
   __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
     __half2 v = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&v);
+  }
+  __device__ __forceinline__ static void split(float a, float b, uint32_t &hi, uint32_t &lo) {
+    __half2 h = __floats2half2_rn(a, b);
+    const float2 f = __half22float2(h);
+    hi = *reinterpret_cast<uint32_t *>(&h);
+    lo = pack(a - f.x, b - f.y);
   }
 };
 

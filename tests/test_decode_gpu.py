@@ -129,6 +129,24 @@ def test_work_split_does_not_change_result(env, monkeypatch):
         wl.close()
 
 
+@pytest.mark.parametrize("seed", [0, 2, 9])
+@pytest.mark.parametrize("impl", ["split", "streamk"])
+def test_short_rows_within_tolerance(seed, impl, monkeypatch):
+    """64 rows of 1..47 keys: few keys dominate each row, so a P rounded once to 16 bits
+    would miss the tolerance; the kernels carry P as a hi + lo pair."""
+    if impl == "streamk":
+        monkeypatch.setenv("KCMM_DECODE_IMPL", "streamk")
+    lens = list(np.random.default_rng(seed).integers(1, 48, 64))
+    wl = make(batch=64, num_q_heads=32, kv_heads=8, head_dim=128, seq_lens_override=lens,
+              max_len=64, pool_blocks=512, seed=seed)
+    try:
+        wl.decode()
+        _torch().cuda.synchronize()
+        check(wl)
+    finally:
+        wl.close()
+
+
 def test_v_row_kat():
     """ref scripts/kcmm/non_default_stream_ffi_smoke.py:172-179: q = 0, seq_len 1,
     k = arange+100, v = arange+1000 -> out equals the V row of the mapped kv head."""
