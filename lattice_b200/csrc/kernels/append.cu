@@ -9,6 +9,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <cmath>
 
 #include "../launch.hpp"
@@ -311,6 +313,197 @@ __global__ void __launch_bounds__(kFusedThreads) fused_kernel(const FusedAppendA
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fused RMSNorm + RoPE + KV append, latency-oriented form (one CTA per token).
+// Every global load of the token is issued at entry -- the slot lookup chain, x,
+// the norm weight, q, k and v -- so their DRAM round trips overlap.  The first
+// head_dim/2 threads then compute the token's rotary factors into shared memory
+// while the loads are in flight; the one barrier of the RMS reduction also
+// publishes the table.  Same arithmetic as fused_kernel: normed =
+// bf16((x * inv_rms) * w), rotation in fp32, one rounding per element.
+// Requirements (checked by the launcher): 16-byte aligned rows, head_dim % 16 ==
+// 0, and the per-thread chunk budgets below.
+// ---------------------------------------------------------------------------
+
+constexpr int kFastX = 4;  // x chunks (8 elements) per thread: hidden <= 8192
+constexpr int kFastQ = 4;  // q chunks per thread: num_q_heads * head_dim <= 8192
+constexpr int kFastK = 2;  // k / v chunks per thread: kv_heads * head_dim <= 4096
+
+// Rotate the 8-element chunk `in` of a head row starting at element d0.
+// Interleaved modes rotate pairs (2i, 2i+1) inside the chunk; for neox the chunk
+// holds the low halves of pairs (i, i + D/2) and `partner` the high halves.
+__device__ __forceinline__ void rot_chunk(uint4 &lo, uint4 *partner, int pair0, const float *cs,
+                                          const float *sn, bool neox) {
+  uint16_t *e = reinterpret_cast<uint16_t *>(&lo);
+  if (!neox) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float c = cs[pair0 + j], s = sn[pair0 + j];
+      const float x0 = bf(e[2 * j]), x1 = bf(e[2 * j + 1]);
+      e[2 * j] = to_bf(x0 * c - x1 * s);
+      e[2 * j + 1] = to_bf(x0 * s + x1 * c);
+    }
+  } else {
+    uint16_t *f = reinterpret_cast<uint16_t *>(partner);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float c = cs[pair0 + j], s = sn[pair0 + j];
+      const float x0 = bf(e[j]), x1 = bf(f[j]);
+      e[j] = to_bf(x0 * c - x1 * s);
+      f[j] = to_bf(x0 * s + x1 * c);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kFusedThreads) fused_fast_kernel(const FusedAppendArgs a) {
+  extern __shared__ float fsm[];  // cs[D/2], sn[D/2]
+  __shared__ float red[kFusedThreads / 32];
+  __shared__ int64_t s_dst;
+  const int t = blockIdx.x, tid = threadIdx.x;
+  const int D = a.head_dim, H = a.hidden, half = D / 2;
+  const int step = a.kv_heads * D;
+  const int qelems = a.num_q_heads * D;
+  const bool neox = a.rope_mode == 2;
+  float *cs = fsm;
+  float *sn = fsm + half;
+
+  int64_t slot = -1;
+  if (tid == 0) slot = a.slot_mapping[t];
+  const float pos = float(a.positions[t]);
+  const uint4 *x = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(a.x) + int64_t(t) * H);
+  const uint4 *w = reinterpret_cast<const uint4 *>(a.norm_weight);
+  uint4 *q = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.q) + int64_t(t) * qelems);
+  const uint4 *k = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(a.k) + int64_t(t) * step);
+  const uint4 *v = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(a.v) + int64_t(t) * step);
+  const int nx = H / 8, nq = qelems / 8, nk = step / 8;
+  const int cph = D / 8;  // chunks per head row
+  uint4 xr[kFastX], wr[kFastX], qr[kFastQ], kr[kFastK], vr[kFastK];
+#pragma unroll
+  for (int i = 0; i < kFastX; ++i) {
+    const int c = tid + i * kFusedThreads;
+    if (c < nx) {
+      xr[i] = x[c];
+      wr[i] = w[c];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kFastQ; ++i) {
+    const int c = tid + i * kFusedThreads;
+    if (c < nq) qr[i] = q[c];
+  }
+#pragma unroll
+  for (int i = 0; i < kFastK; ++i) {
+    const int c = tid + i * kFusedThreads;
+    if (c < nk) {
+      kr[i] = k[c];
+      vr[i] = v[c];
+    }
+  }
+  if (tid == 0) {
+    int64_t dst = -1;
+    if (slot >= 0) {
+      const int64_t blk = slot / a.block_size;
+      if (blk >= a.offsets_len) {
+        if (a.status) atomicCAS(a.status, 0, 1);
+      } else if (a.valid && a.valid[blk] == 0) {
+        if (a.status) atomicCAS(a.status, 0, 2);
+      } else {
+        const int64_t d = int64_t(a.block_offsets[blk]) + (slot % a.block_size) * step;
+        if (uint64_t(d) + uint64_t(step) > a.region_elems) {
+          if (a.status) atomicCAS(a.status, 0, 3);
+        } else {
+          dst = d;
+        }
+      }
+    }
+    s_dst = dst;
+  }
+  // Rotary table for this token (ref src/cuda/kernels/rope.cu:18, base as a parameter)
+  if (tid < half) {
+    const float e = a.rope_mode == 0 ? float(2 * (tid / 2)) / float(D) : float(2 * tid) / float(D);
+    const float theta = 1.0f / powf(a.rope_theta, e);
+    float sv, cv;
+    sincosf(pos * theta, &sv, &cv);
+    cs[tid] = cv;
+    sn[tid] = sv;
+  }
+  // RMSNorm partial sum (ref src/cuda/kernels/rms_norm.cu:14-35)
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kFastX; ++i) {
+    if (tid + i * kFusedThreads < nx) {
+      const uint16_t *e = reinterpret_cast<const uint16_t *>(&xr[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float f = bf(e[j]);
+        ss += f * f;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();  // red[], s_dst and the rotary table
+  float total = 0.f;
+#pragma unroll
+  for (int i = 0; i < kFusedThreads / 32; ++i) total += red[i];
+  const float inv_rms = 1.0f / sqrtf(total / float(H) + a.eps);
+  uint4 *y = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.normed_out) + int64_t(t) * H);
+#pragma unroll
+  for (int i = 0; i < kFastX; ++i) {
+    const int c = tid + i * kFusedThreads;
+    if (c < nx) {
+      const uint16_t *xe = reinterpret_cast<const uint16_t *>(&xr[i]);
+      const uint16_t *we = reinterpret_cast<const uint16_t *>(&wr[i]);
+      uint4 out;
+      uint16_t *oe = reinterpret_cast<uint16_t *>(&out);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) oe[j] = to_bf((bf(xe[j]) * inv_rms) * bf(we[j]));
+      y[c] = out;
+    }
+  }
+  // q: interleaved pairs rotate inside a chunk; neox chunks of the low half of a
+  // head pair with the chunk half/8 further on (read again, it is in L1)
+#pragma unroll
+  for (int i = 0; i < kFastQ; ++i) {
+    const int c = tid + i * kFusedThreads;
+    if (c < nq) {
+      const int d0 = (c % cph) * 8;
+      if (!neox) {
+        rot_chunk(qr[i], nullptr, d0 / 2, cs, sn, false);
+        q[c] = qr[i];
+      } else if (d0 < half) {
+        uint4 hi = q[c + half / 8];
+        rot_chunk(qr[i], &hi, d0, cs, sn, true);
+        q[c] = qr[i];
+        q[c + half / 8] = hi;
+      }
+    }
+  }
+  const int64_t dst = s_dst;
+  if (dst >= 0) {
+    uint4 *kd = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.va_k) + dst);
+    uint4 *vd = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.va_v) + dst);
+#pragma unroll
+    for (int i = 0; i < kFastK; ++i) {
+      const int c = tid + i * kFusedThreads;
+      if (c < nk) {
+        const int d0 = (c % cph) * 8;
+        if (!neox) {
+          rot_chunk(kr[i], nullptr, d0 / 2, cs, sn, false);
+          kd[c] = kr[i];
+        } else if (d0 < half) {
+          uint4 hi = k[c + half / 8];
+          rot_chunk(kr[i], &hi, d0, cs, sn, true);
+          kd[c] = kr[i];
+          kd[c + half / 8] = hi;
+        }
+        vd[c] = vr[i];
+      }
+    }
+  }
+}
+
 }  // namespace
 
 cudaError_t copy_rows(const void *k_src, const void *v_src, void *va_k, void *va_v,
@@ -341,7 +534,22 @@ cudaError_t device_slot_write(const SlotWriteArgs &a, cudaStream_t stream) {
 }
 
 cudaError_t fused_norm_rope_append(const FusedAppendArgs &a, cudaStream_t stream) {
+  const uintptr_t align = reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.norm_weight) |
+                          reinterpret_cast<uintptr_t>(a.normed_out) | reinterpret_cast<uintptr_t>(a.q) |
+                          reinterpret_cast<uintptr_t>(a.k) | reinterpret_cast<uintptr_t>(a.v) |
+                          reinterpret_cast<uintptr_t>(a.va_k) | reinterpret_cast<uintptr_t>(a.va_v);
+  const int step = a.kv_heads * a.head_dim;
+  const bool fast = (align & 15) == 0 && a.head_dim % 16 == 0 && a.hidden % 8 == 0 &&
+                    a.hidden <= 8 * kFusedThreads * kFastX &&
+                    a.num_q_heads * a.head_dim <= 8 * kFusedThreads * kFastQ &&
+                    step <= 8 * kFusedThreads * kFastK &&
+                    !(std::getenv("KCMM_FUSED_IMPL") &&
+                      std::strcmp(std::getenv("KCMM_FUSED_IMPL"), "table") == 0);
   const size_t smem = size_t(a.head_dim) * sizeof(float);
+  if (fast) {
+    fused_fast_kernel<<<a.num_tokens, kFusedThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+  }
   fused_kernel<<<a.num_tokens, kFusedThreads, smem, stream>>>(a);
   return cudaGetLastError();
 }
