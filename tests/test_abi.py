@@ -156,3 +156,37 @@ def test_kernel_entry_points_refuse_host_pool(host_pool_factory):
         pool.paged_attn_decode(0, query_ptr=1, out_ptr=1, block_tables_ptr=1, seq_lens_ptr=1,
                                block_offsets_f16_ptr=1, batch=1, num_q_heads=2, kv_heads=2,
                                head_dim=64, block_size=16, max_blocks_per_seq=2, scale=0.1)
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(head_dim=64), "head_dim 64 unsupported"),
+    (dict(num_q_heads=6, kv_heads=4), "dividing 128"),
+    (dict(num_q_heads=384, kv_heads=1), "dividing 128"),
+    (dict(batch=0), "must be positive"),
+    (dict(query_ptr=24), "16-byte aligned"),
+    (dict(block_tables_ptr=0), "null pointer"),
+])
+def test_prefill_argument_checks(host_pool_factory, kw, msg):
+    """The prefill entry point validates its shapes before it touches the device."""
+    from lattice_b200 import KcmmError
+
+    pool = host_pool_factory(kv_heads=2, head_dim=128, max_batch=1, max_seq_len=32)
+    args = dict(query_ptr=16, out_ptr=16, block_tables_ptr=16, query_start_loc_ptr=16,
+                context_lens_ptr=16, block_offsets_f16_ptr=16, batch=1, max_query_len=4,
+                num_q_heads=8, kv_heads=2, head_dim=128, block_size=16, max_blocks_per_seq=2,
+                scale=0.1)
+    args.update(kw)
+    with pytest.raises(KcmmError, match=msg):
+        pool.paged_prefill(0, **args)
+
+
+def test_prefill_refuses_host_pool(host_pool_factory):
+    from lattice_b200 import KcmmError
+
+    pool = host_pool_factory(kv_heads=2, head_dim=128, max_batch=1, max_seq_len=32)
+    with pytest.raises(KcmmError, match="no device memory"):
+        pool.paged_prefill(0, query_ptr=16, out_ptr=16, block_tables_ptr=16,
+                           query_start_loc_ptr=16, context_lens_ptr=16,
+                           block_offsets_f16_ptr=16, batch=1, max_query_len=4, num_q_heads=8,
+                           kv_heads=2, head_dim=128, block_size=16, max_blocks_per_seq=2,
+                           scale=0.1)
