@@ -849,6 +849,85 @@ def run_prefill_leg(args):
          "status": status})
 
 
+def run_headsplit_leg(args):
+    """Llama-3-70B decode with KV heads sharded across the N ranks:
+    8 sequences of 32,768 tokens, 64 q heads / 8 kv heads, D 128, bf16.  Rank r holds
+    kv heads [r*8/N, (r+1)*8/N) and their query heads for every sequence; a step is the
+    paged decode of the rank's heads followed by an NCCL all-gather of the per-head
+    outputs ([8, 64/N, 128] bf16 per rank) so every rank holds the full [8, 64, 128].
+    Strong scaling: the total work is fixed as N grows."""
+    import torch
+
+    from lattice_b200.workloads import DecodeWorkload
+
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    hq, hkv, seqs, ctx = 64, 8, 8, 32768
+    if hkv % world:
+        raise SystemExit(f"headsplit needs a rank count dividing {hkv}")
+    hkv_l, hq_l = hkv // world, hq // world
+    wl = DecodeWorkload(batch=seqs, num_q_heads=hq_l, kv_heads=hkv_l, head_dim=128,
+                        min_len=ctx, max_len=ctx, pool_blocks=seqs * ctx // 16,
+                        seed=3000 + rank, device=local).build()
+    gathered = torch.empty((world,) + tuple(wl.out.shape), dtype=wl.out.dtype,
+                           device=f"cuda:{local}")
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    import torch.distributed as dist
+
+    def step():
+        wl.decode(stream_ptr=sp)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, wl.out)
+        else:
+            gathered[0].copy_(wl.out)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(t0.elapsed_time(t1)) / args.steps
+    # attention alone, for the split of the step
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(args.steps):
+        wl.decode(stream_ptr=sp)
+    a1.record(stream)
+    torch.cuda.synchronize()
+    attn_ms = max_over_ranks(a0.elapsed_time(a1)) / args.steps
+    kv_total = wl.kv_bytes() * world  # every rank reads its own heads' pages
+    status = wl.pool.kernel_status()
+    wl.close()
+    peak, kind = peaks()
+    line = None
+    if rank == 0:
+        gbs = kv_total / (ms * 1e-3) / 1e9
+        line = _line(
+            "70B decode, KV heads sharded: KV GB/s (whole job) and decode tokens/s", gbs,
+            "GB/s",
+            {"workload": "BASELINE config 5 decode: 8 seqs x 32768 tokens, Hq 64 / Hkv 8, "
+                         "D 128, bf16; kv heads sharded over the ranks, outputs all-gathered "
+                         "(NCCL)", "ranks": world, "scaling": "strong"},
+            {"bound": "hbm", "achieved": round(gbs / world, 1), "peak": peak, "unit": "GB/s",
+             "frac": round(gbs / world / peak, 4), "traffic": None, "peak_kind": kind,
+             "per": "GPU"},
+            {"n_gpus": world, "ms_per_step": round(ms, 4),
+             "attention_ms": round(attn_ms, 4),
+             "allgather_ms": round(max(ms - attn_ms, 0.0), 4),
+             "tokens_per_s_80_layers": round(seqs / (80 * ms * 1e-3), 1),
+             "status": status})
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -857,7 +936,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--profile", action="store_true",
                     help="profiling case for ncu: 12k-block pool, no CPU baseline / e2e legs")
-    ap.add_argument("--workload", choices=["step", "append", "cow", "swap", "prefill"],
+    ap.add_argument("--workload",
+                    choices=["step", "append", "cow", "swap", "prefill", "headsplit"],
                     default="step",
                     help="step = the headline (default); the others print one line for a "
                          "secondary BASELINE config")
@@ -872,6 +952,8 @@ def main():
         run_swap_leg(args)
     elif args.workload == "prefill":
         run_prefill_leg(args)
+    elif args.workload == "headsplit":
+        run_headsplit_leg(args)
     else:
         run_ours(args)
 
