@@ -605,6 +605,7 @@ static int prefill_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, 
   a.scale = scale;
   a.diag = p->diag_word();
   a.tensor_maps = p->tensor_maps(layer, int(hkv), int(hd));
+  a.v_page_map = p->v_page_map(layer, int(hkv), int(hd));
   return check_launch(h, op, kcmm::dev::paged_prefill(a, S(stream)));
 }
 

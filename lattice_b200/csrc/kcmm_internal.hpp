@@ -60,6 +60,11 @@ std::unique_ptr<Vmm> make_host_vmm();
 // Encode a 128-byte CUtensorMap for TMA loads of 16-token x 64-dim tiles of
 // one kv head from the region at `base` (see vmm.cpp).  False if unsupported.
 bool encode_kv_tensor_map(void *out, uint64_t base, uint64_t tokens, int kv_heads, int head_dim);
+// 4-D view {64, tokens, head_dim/64, kv_heads} of a layer region whose box
+// {64, 16, head_dim/64, 1} is 16 token rows of one head, both head_dim halves:
+// it lands in shared memory as [half][16 rows][128 B] (128-byte swizzle).
+bool encode_kv_page_tensor_map(void *out, uint64_t base, uint64_t tokens, int kv_heads,
+                               int head_dim);
 
 // ---------------------------------------------------------------------------
 // Allocator
@@ -215,6 +220,8 @@ class Pool {
   // Cached TMA descriptors of a layer's K and V regions for a (kv_heads,
   // head_dim) view; nullptr when the shape has no TMA path.
   const void *tensor_maps(size_t layer, int kv_heads, int head_dim);
+  // The V page-box map of the layer (third map above), or null when unavailable.
+  const void *v_page_map(size_t layer, int kv_heads, int head_dim);
   void use_device() const;  // make the pool's device current
   void require_device(const char *what) const;
   int32_t *diag_word() const { return diag_; }  // device int32, sticky error bits
@@ -251,7 +258,10 @@ class Pool {
   struct TmapEntry {
     size_t layer;
     int kv_heads, head_dim;
-    alignas(64) unsigned char maps[2][128];
+    // [0] K and [1] V as {D, Hkv, tokens} with box {64, 1, 16}; [2] V as
+    // {64, tokens, D/64, Hkv} with box {64, 16, D/64, 1} (one box = one page of one head)
+    alignas(64) unsigned char maps[3][128];
+    bool page_ok = false;
   };
   std::vector<std::unique_ptr<TmapEntry>> tmaps_;
   std::mutex mu_;  // guards everything below

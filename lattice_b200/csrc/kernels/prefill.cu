@@ -78,6 +78,13 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   return uint32_t((chunk >> 3) * kHalf + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
 }
 
+// The same for the V tiles of the warp-specialised kernel, stored box-major:
+// [8 boxes of 16 keys][2 halves][16 rows][128 B], the layout one 4-D page box lands in.
+__device__ __forceinline__ uint32_t swz_v(int row, int chunk) {
+  return uint32_t((row >> 4) * 4096 + (chunk >> 3) * 2048 + (row & 15) * 128 +
+                  (((chunk & 7) ^ (row & 7)) << 4));
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi);
 template <>
@@ -428,10 +435,11 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
 //            columns, P_lo in the last 64), O rescale in TMEM, epilogue
 // warp 8     K producer: Q, then K tiles into a 3-stage ring
 // warp 10    V producer: V tiles into a 2-stage ring
-// TMA variant: 16-token page boxes ({64, 1, 16}, 2 KB) by TMA, K boxes 0-3 from warp 8
-//            and 4-7 from warp 11, V boxes from warps 10 and 12 (TMA issue is serial
-//            within a warp, ~90 cycles a box); V tiles that reach past the context
-//            are gathered with zero-filling cp.async instead.
+// TMA variant: 16-token page boxes by TMA.  K boxes ({64, 1, 16}: one head_dim half,
+//            2 KB) 0-3 from warp 8 and 4-7 from warp 11; V boxes ({64, 16, 2, 1}: both
+//            halves of a page, 4 KB, landing box-major) from warps 10 and 12.  TMA
+//            issue costs ~90 cycles a box, so V boxes halve V's cost.  V tiles that
+//            reach past the context are gathered with zero-filling cp.async instead.
 // Gather variant (layouts the tensor map cannot address): warps 8 and 10 copy whole
 //            tiles with 16-byte cp.async from all lanes.
 // warp 9     MMA issuer (lane 0) and TMEM owner: QK runs two tiles ahead of P.V, so
@@ -452,8 +460,9 @@ constexpr uint32_t kWsOffV = kWsOffK + kKStages * kTile;
 constexpr uint32_t kWsOffBar = kWsOffV + kVStages * kTile;  // no P tiles in shared memory
 constexpr uint32_t kWsOffXch = kWsOffBar + 256;          // row-max exchange [2 parity][2 half][128]
 constexpr size_t kWsSmem = kWsOffXch + 2 * 2 * 128 * 4 + 1024;  // + alignment slack
-// Kernel parameters with the layer's K and V tensor maps ({D, Hkv, tokens}, box
-// {64, 1, 16}, 128-byte swizzle) for the TMA variant; row_shift = log2(Hkv * D).
+// Kernel parameters with the layer's tensor maps for the TMA variant: K as {D, Hkv,
+// tokens} with box {64, 1, 16}, V as {64, tokens, 2, Hkv} with box {64, 16, 2, 1} (a
+// whole 16-token page of one head per box); row_shift = log2(Hkv * D).
 struct alignas(64) WsParams {
   CUtensorMap tmk;
   CUtensorMap tmv;
@@ -542,7 +551,7 @@ __device__ __forceinline__ bool ws_wait(uint32_t bar, uint32_t parity, volatile 
 // rows][128 B] layout with 16-byte cp.async: each half-warp moves one 256-byte token
 // row per step.  Box b (keys 16b .. 16b+15) starts at element e0 of lane b; keys past
 // kv_hi and boxes that are not live are zero-filled.
-template <int B0 = 0, int NB = 8>
+template <bool BOXV = false, int B0 = 0, int NB = 8>
 __device__ __forceinline__ void gather_tile(const uint16_t *va, uint32_t dst, int64_t e0, bool live,
                                             int j, int kv_hi, uint32_t row_stride, int h,
                                             int lane) {
@@ -556,7 +565,7 @@ __device__ __forceinline__ void gather_tile(const uint16_t *va, uint32_t dst, in
       const int r = 2 * i + hw, row = b * 16 + r;
       const bool ok = lb && j * kKvTile + row < kv_hi;
       const uint16_t *src = va + eb + int64_t(r) * row_stride + h * kHd + c * 8;
-      ptx::cp_async16(dst + swz(row, c), ok ? src : va, ok ? 16u : 0u);
+      ptx::cp_async16(dst + (BOXV ? swz_v(row, c) : swz(row, c)), ok ? src : va, ok ? 16u : 0u);
     }
   }
 }
@@ -699,21 +708,20 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
             ptx::mbar_arrive(bar(kVFull + st));
           }
           __syncwarp();
-          if (lane < 16 && mine) {
-            const int bx = lane & 7, half = lane >> 3;
-            ptx::tma_load_3d(dst + half * kHalf + bx * 2048, &P.tmv, half * 64, h,
-                             int(e0 >> P.row_shift), bar(kVFull + st));
+          if (lane < 8 && mine) {  // one box = 16 token rows x both head_dim halves
+            ptx::tma_load_4d(dst + lane * 4096, &P.tmv, 0, int(e0 >> P.row_shift), 0, h,
+                             bar(kVFull + st));
           }
         } else {
           if (part == 0) {
-            gather_tile<0, 4>(p.va_v, dst, e0, live, j, kv_hi, row_stride, h, lane);
+            gather_tile<true, 0, 4>(p.va_v, dst, e0, live, j, kv_hi, row_stride, h, lane);
           } else {
-            gather_tile<4, 4>(p.va_v, dst, e0, live, j, kv_hi, row_stride, h, lane);
+            gather_tile<true, 4, 4>(p.va_v, dst, e0, live, j, kv_hi, row_stride, h, lane);
           }
           ptx::cp_async_mbar_arrive(bar(kVFull + st));
         }
       } else {
-        gather_tile(p.va_v, dst, e0, live, j, kv_hi, row_stride, h, lane);
+        gather_tile<true>(p.va_v, dst, e0, live, j, kv_hi, row_stride, h, lane);
         ptx::cp_async_mbar_arrive(bar(kVFull + st));
       }
     }
@@ -762,7 +770,8 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
         const uint32_t tp = tmem + (j % kSBufs) * 128;  // P_hi columns [0,64), P_lo [64,128)
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const uint64_t vd = tc::sw128_desc(va + uint32_t(k) * 2048, kHalf, 1024);
+          // V box k: 16 keys (K) x head_dim (N), the two halves 2048 B apart
+          const uint64_t vd = tc::sw128_desc(va + uint32_t(k) * 4096, 2048, 1024);
           tc::mma_ts(tO, tp + k * 8, vd, p.idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
           tc::mma_ts(tO, tp + 64 + k * 8, vd, p.idesc_pv, 1u);
         }
@@ -896,14 +905,15 @@ cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
     // TMA boxes address whole token rows of the {D, Hkv, tokens} view: Hkv * D must be
     // a power of two dividing the 2 MiB superblock (1 Mi elements).
     const uint32_t rs = uint32_t(a.kv_heads) * kHd;
-    const bool tma = !gather && a.tensor_maps && (rs & (rs - 1)) == 0 && (1u << 20) % rs == 0;
+    const bool tma = !gather && a.tensor_maps && a.v_page_map && (rs & (rs - 1)) == 0 &&
+                     (1u << 20) % rs == 0;
     WsParams wp;
     std::memset(static_cast<void *>(&wp), 0, sizeof(wp));
     wp.p = p;
     wp.row_shift = uint32_t(__builtin_ctz(rs));
     if (tma) {
       std::memcpy(&wp.tmk, a.tensor_maps, sizeof(CUtensorMap));
-      std::memcpy(&wp.tmv, static_cast<const char *>(a.tensor_maps) + 128, sizeof(CUtensorMap));
+      std::memcpy(&wp.tmv, a.v_page_map, sizeof(CUtensorMap));
     }
     auto fn = tma ? (bf16 ? prefill_ws_kernel<__nv_bfloat16, true> : prefill_ws_kernel<__half, true>)
                   : (bf16 ? prefill_ws_kernel<__nv_bfloat16, false> : prefill_ws_kernel<__half, false>);

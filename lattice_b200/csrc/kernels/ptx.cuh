@@ -125,6 +125,15 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *tmap, int 
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void *tmap, int x, int y, int z,
+                                            int w, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
+      : "memory");
+}
+
 // Warm the TMA descriptor cache for a tensor map held in kernel parameters.
 __device__ __forceinline__ void prefetch_tensormap(const void *tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");

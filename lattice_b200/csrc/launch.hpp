@@ -70,8 +70,10 @@ struct PrefillArgs {
   int batch, max_q_len, num_q_heads, kv_heads, head_dim, block_size, max_blocks_per_seq;
   float scale;
   int32_t *diag;
-  // K and V TMA descriptors of the layer ({D, Hkv, tokens}, box {64, 1, 16}) or null.
+  // K and V TMA descriptors of the layer ({D, Hkv, tokens}, box {64, 1, 16}) or null,
+  // and the V page-box descriptor ({64, tokens, D/64, Hkv}, box {64, 16, D/64, 1}) or null.
   const void *tensor_maps;
+  const void *v_page_map;
 };
 // Causal chunked-prefill attention on the tcgen05 tensor cores
 // (kernels/prefill.cu).  head_dim 128; num_q_heads / kv_heads must divide 128.

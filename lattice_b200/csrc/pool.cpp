@@ -211,8 +211,20 @@ const void *Pool::tensor_maps(size_t layer, int kv_heads, int head_dim) {
       !encode_kv_tensor_map(e->maps[1], va_v[layer], tokens, kv_heads, head_dim)) {
     return nullptr;
   }
+  e->page_ok = encode_kv_page_tensor_map(e->maps[2], va_v[layer], tokens, kv_heads, head_dim);
   tmaps_.push_back(std::move(e));
   return tmaps_.back()->maps;
+}
+
+const void *Pool::v_page_map(size_t layer, int kv_heads, int head_dim) {
+  if (!tensor_maps(layer, kv_heads, head_dim)) return nullptr;
+  std::lock_guard<std::mutex> g(tmap_mu_);
+  for (auto &e : tmaps_) {
+    if (e->layer == layer && e->kv_heads == kv_heads && e->head_dim == head_dim) {
+      return e->page_ok ? e->maps[2] : nullptr;
+    }
+  }
+  return nullptr;
 }
 
 void Pool::use_device() const {

@@ -198,6 +198,29 @@ bool encode_kv_tensor_map(void *out, uint64_t base, uint64_t tokens, int kv_head
       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
+bool encode_kv_page_tensor_map(void *out, uint64_t base, uint64_t tokens, int kv_heads,
+                               int head_dim) {
+  if (head_dim % 64 != 0 || head_dim / 64 > 8 || tokens == 0 || tokens > (uint64_t(1) << 32))
+    return false;
+  const cuuint64_t row = cuuint64_t(kv_heads) * head_dim * 2;  // bytes per token row
+  cuuint64_t dims[4] = {64, cuuint64_t(tokens), cuuint64_t(head_dim / 64), cuuint64_t(kv_heads)};
+  cuuint64_t strides[3] = {row, 128, cuuint64_t(head_dim) * 2};
+  cuuint32_t box[4] = {64, 16, cuuint32_t(head_dim / 64), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const DriverApi *api = nullptr;
+  try {
+    api = &driver();
+  } catch (const Error &) {
+    return false;
+  }
+  CUresult r = api->encode_tiled(
+      static_cast<CUtensorMap *>(out), CU_TENSOR_MAP_DATA_TYPE_UINT16, 4,
+      reinterpret_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 std::unique_ptr<Vmm> make_host_vmm() { return std::make_unique<HostVmm>(); }
 
 }  // namespace kcmm
