@@ -546,10 +546,11 @@ Plan make_plan(const DecodeArgs &a) {
   const int max_units =
       int((int64_t(a.max_blocks_per_seq) * a.block_size + kUnit - 1) / kUnit);
   const int64_t items = int64_t(a.batch) * a.kv_heads * pl.n_head_tiles;
-  // Aim at ~8 waves of 2 resident CTAs per SM over the worst-case context;
-  // at least 16 units per split so each warp's ring fills, at most 32 units
-  // per warp.
-  const int64_t target = int64_t(sm_count()) * 2 * 8;
+  // Aim at ~6 waves of 2 resident CTAs per SM over the worst-case context (on
+  // the Llama-3-8B decode shape: 4 splits, 113.6 us, against 117.4 us at 8 waves
+  // and 119.4 us at 6 splits); at least 16 units per split so each warp's ring
+  // fills, at most 32 units per warp.
+  const int64_t target = int64_t(sm_count()) * 2 * 6;
   int64_t want_splits = std::max<int64_t>(1, (target + items - 1) / items);
   int ups = int((max_units + want_splits - 1) / want_splits);
   ups = std::max(ups, 16);

@@ -102,12 +102,14 @@ def test_noalloc_leaves_free_memory_unchanged():
         wl.close()
 
 
-def test_noalloc_rejects_oversized_scratch():
-    """64 sequences x 64 query heads on one kv head at head_dim 256 split into 10
-    pieces: 40960 partial rows of 1028 bytes, above the 32 MiB array."""
+def test_noalloc_rejects_oversized_scratch(monkeypatch):
+    """64 sequences x 64 query heads on one kv head at head_dim 256, split into 10
+    pieces (pinned with KCMM_DECODE_SPLITS): 40960 partial rows of 1028 bytes, above
+    the 32 MiB array."""
     from lattice_b200.kcmm import KcmmError
 
     torch = _torch()
+    monkeypatch.setenv("KCMM_DECODE_SPLITS", "10")
     wl = _make(batch=64, num_q_heads=64, kv_heads=1, head_dim=256, pool_blocks=128,
                seq_lens_override=[1] * 64, max_len=4096, seed=7)
     try:
@@ -117,6 +119,7 @@ def test_noalloc_rejects_oversized_scratch():
         torch.cuda.synchronize()
         assert bool((sentinel == 7.0).all()), "a rejected call must launch nothing"
         # the regular entry point still serves the same batch
+        monkeypatch.delenv("KCMM_DECODE_SPLITS")
         wl.decode()
         torch.cuda.synchronize()
         assert wl.pool.kernel_status() == 0
