@@ -244,3 +244,37 @@ def test_device_diagnostics_clean():
         assert wl.pool.kernel_status() == 0
     finally:
         wl.close()
+
+
+def test_calls_on_two_streams_and_in_a_graph(monkeypatch):
+    """Split-K decode (partials in stream-ordered scratch, then the merge launch) run on
+    the current stream, on a side stream, and captured in a CUDA graph and replayed,
+    interleaved; every result against the oracle."""
+    torch = _torch()
+    monkeypatch.setenv("KCMM_DECODE_SPLITS", "4")
+    wl = make(batch=6, num_q_heads=32, kv_heads=8, head_dim=128, min_len=300, max_len=2000,
+              pool_blocks=2048, seed=21)
+    graph = None
+    try:
+        wl.decode()  # loads the modules outside the capture
+        torch.cuda.synchronize()
+        check(wl)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            wl.decode(stream_ptr=side.cuda_stream)
+        for _ in range(2):
+            wl.out.zero_()
+            graph.replay()
+            torch.cuda.synchronize()
+            check(wl)
+            wl.out.zero_()
+            torch.cuda.synchronize()
+            with torch.cuda.stream(side):
+                wl.decode(stream_ptr=side.cuda_stream)
+            torch.cuda.synchronize()
+            check(wl)
+    finally:
+        del graph
+        wl.close()
