@@ -31,7 +31,7 @@ CU_SOURCES = ["kernels/decode.cu", "kernels/decode_noalloc.cu", "kernels/append.
               "kernels/copy.cu", "kernels/prefill.cu"]
 CPP_SOURCES = ["pool.cpp", "vmm.cpp", "ffi.cpp"]
 HEADERS = ["kcmm_internal.hpp", "launch.hpp", "kernels/ptx.cuh", "kernels/decode_streamk.cuh",
-           "kernels/tcgen05.cuh"]
+           "kernels/tcgen05.cuh", "kernels/pdl.cuh"]
 
 
 def _nvcc() -> str:

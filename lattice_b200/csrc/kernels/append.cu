@@ -14,6 +14,7 @@
 #include <cmath>
 
 #include "../launch.hpp"
+#include "pdl.cuh"
 #include "ptx.cuh"
 
 namespace kcmm {
@@ -216,6 +217,8 @@ __global__ void __launch_bounds__(kFusedThreads) fused_kernel(const FusedAppendA
   extern __shared__ float fsm[];  // cs[D/2], sn[D/2]
   __shared__ float red[kFusedThreads / 32];
   __shared__ int64_t s_dst;
+  ptx::grid_dependency_wait();  // a programmatic dependent: see pdl.cuh
+  ptx::launch_dependents();
   const int t = blockIdx.x;
   const int D = a.head_dim, half = D / 2;
   float *cs = fsm;
@@ -359,6 +362,8 @@ __global__ void __launch_bounds__(kFusedThreads) fused_fast_kernel(const FusedAp
   extern __shared__ float fsm[];  // cs[D/2], sn[D/2]
   __shared__ float red[kFusedThreads / 32];
   __shared__ int64_t s_dst;
+  ptx::grid_dependency_wait();  // a programmatic dependent: see pdl.cuh
+  ptx::launch_dependents();
   const int t = blockIdx.x, tid = threadIdx.x;
   const int D = a.head_dim, H = a.hidden, half = D / 2;
   const int step = a.kv_heads * D;
@@ -546,12 +551,9 @@ cudaError_t fused_norm_rope_append(const FusedAppendArgs &a, cudaStream_t stream
                     !(std::getenv("KCMM_FUSED_IMPL") &&
                       std::strcmp(std::getenv("KCMM_FUSED_IMPL"), "table") == 0);
   const size_t smem = size_t(a.head_dim) * sizeof(float);
-  if (fast) {
-    fused_fast_kernel<<<a.num_tokens, kFusedThreads, smem, stream>>>(a);
-    return cudaGetLastError();
-  }
-  fused_kernel<<<a.num_tokens, kFusedThreads, smem, stream>>>(a);
-  return cudaGetLastError();
+  if (fast)
+    return launch_pdl(fused_fast_kernel, dim3(a.num_tokens), dim3(kFusedThreads), smem, stream, a);
+  return launch_pdl(fused_kernel, dim3(a.num_tokens), dim3(kFusedThreads), smem, stream, a);
 }
 
 }  // namespace dev

@@ -27,9 +27,11 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 
 #include "../launch.hpp"
+#include "pdl.cuh"
 #include "ptx.cuh"
 
 namespace kcmm {
@@ -92,6 +94,11 @@ __global__ void __launch_bounds__(W * 32, 2) decode_kernel(const DecodeParams p)
   T *stages = qs + C::Q_ELEMS;
   uint64_t *bars = reinterpret_cast<uint64_t *>(stages + W * NS * C::STAGE);
   __shared__ int s_fail;
+  // Launched as a programmatic dependent of the previous kernel on the stream:
+  // nothing is read before that kernel has completed.  The merge launch that
+  // follows may be scheduled once every CTA of this grid has started.
+  ptx::grid_dependency_wait();
+  ptx::launch_dependents();
 
   const int split = blockIdx.x;
   const int kvh = blockIdx.y / p.n_head_tiles;
@@ -374,10 +381,15 @@ __global__ void __launch_bounds__(W * 32, 2) decode_kernel(const DecodeParams p)
 }
 
 // Second pass: combine the splits of each (sequence, head) through their
-// log-sum-exp.  Sequences that fit one split were written by the first pass.
+// log-sum-exp, one warp per row, 4-dimension slices per lane.  Sequences that fit
+// one split were written by the first pass.
 template <typename T>
-__global__ void merge_kernel(const DecodeParams p, int D) {
-  const int row = blockIdx.x;  // b * hq + h
+__global__ void merge_kernel(const DecodeParams p, int D, int rows) {
+  ptx::grid_dependency_wait();
+  ptx::launch_dependents();
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);  // b * hq + h
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
   const int b = row / p.hq;
   int seq_len = p.seq_lens[b];
   if (seq_len <= 0) return;
@@ -387,16 +399,31 @@ __global__ void merge_kernel(const DecodeParams p, int D) {
   if (ns <= 1) return;
   const float *lse = p.part_lse + int64_t(row) * p.num_splits;
   float M = -INFINITY;
-  for (int s = 0; s < ns; ++s) M = fmaxf(M, lse[s]);
+  for (int s = lane; s < ns; s += 32) M = fmaxf(M, lse[s]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   float wsum = 0.f;
-  for (int s = 0; s < ns; ++s) wsum += ptx::fast_exp2(lse[s] - M);
+  for (int s = lane; s < ns; s += 32) wsum += ptx::fast_exp2(lse[s] - M);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
   const float inv = 1.f / wsum;
   const float *po = p.part_o + int64_t(row) * p.num_splits * D;
   T *dst = static_cast<T *>(p.out) + int64_t(row) * D;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float acc = 0.f;
-    for (int s = 0; s < ns; ++s) acc += po[int64_t(s) * D + d] * ptx::fast_exp2(lse[s] - M);
-    dst[d] = ptx::from_f32<T>(acc * inv);
+  for (int d = lane * 4; d < D; d += 128) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int s = 0; s < ns; ++s) {
+      const float w = ptx::fast_exp2(lse[s] - M);
+      const float4 v = *reinterpret_cast<const float4 *>(po + int64_t(s) * D + d);
+      acc.x += v.x * w;
+      acc.y += v.y * w;
+      acc.z += v.z * w;
+      acc.w += v.w * w;
+    }
+    dst[d] = ptx::from_f32<T>(acc.x * inv);
+    dst[d + 1] = ptx::from_f32<T>(acc.y * inv);
+    dst[d + 2] = ptx::from_f32<T>(acc.z * inv);
+    dst[d + 3] = ptx::from_f32<T>(acc.w * inv);
   }
 }
 
@@ -844,6 +871,58 @@ size_t decode_scratch_bytes(const DecodeArgs &a) {
   return make_plan(a).scratch_bytes;
 }
 
+// Split scratch kept per (device, stream) between calls, so a call makes no
+// stream-ordered allocation between its kernels and the next call's launch can
+// overlap the previous merge (programmatic dependent launch).  Calls on one
+// stream run in order, and each kernel waits for the previous one before it
+// touches memory, so they can share one buffer; a larger call replaces it in
+// stream order.  Streams are keyed by cudaStreamGetId (never reused in a
+// process).  Returns null while the stream is being captured (a graph may be
+// replayed on any stream) or once kMaxCachedStreams streams hold a buffer: the
+// caller then allocates for the call alone.
+constexpr size_t kMaxCachedStreams = 16;
+
+void *stream_scratch(cudaStream_t stream, size_t bytes) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (cs != cudaStreamCaptureStatusNone) return nullptr;
+  unsigned long long id = 0;
+  int dev = 0;
+  if (cudaStreamGetId(stream, &id) != cudaSuccess || cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  struct Entry {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+  };
+  static std::mutex mu;
+  static std::map<std::pair<int, unsigned long long>, Entry> cache;
+  std::lock_guard<std::mutex> g(mu);
+  auto it = cache.find({dev, id});
+  if (it == cache.end()) {
+    if (cache.size() >= kMaxCachedStreams) return nullptr;
+    it = cache.emplace(std::make_pair(dev, id), Entry{}).first;
+  }
+  Entry &en = it->second;
+  if (en.bytes >= bytes) return en.ptr;
+  cudaMemPool_t mp = scratch_pool(dev);
+  if (!mp) return nullptr;
+  void *fresh = nullptr;
+  const size_t want = std::max(bytes, en.bytes + en.bytes / 2);
+  if (cudaMallocFromPoolAsync(&fresh, want, mp, stream) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (en.ptr) cudaFreeAsync(en.ptr, stream);
+  en.ptr = fresh;
+  en.bytes = want;
+  return fresh;
+}
+
 cudaError_t decode_attention(const DecodeArgs &a, cudaStream_t stream) {
   DecodeParams p = {};
   p.q = a.q;
@@ -887,6 +966,8 @@ cudaError_t decode_attention(const DecodeArgs &a, cudaStream_t stream) {
     if (a.scratch) {
       if (a.scratch_bytes < pl.scratch_bytes) return cudaErrorInvalidValue;
       scratch = a.scratch;
+    } else if ((scratch = stream_scratch(stream, pl.scratch_bytes)) != nullptr) {
+      // kept for the stream
     } else {
       int dev = 0;
       cudaGetDevice(&dev);
@@ -905,16 +986,15 @@ cudaError_t decode_attention(const DecodeArgs &a, cudaStream_t stream) {
                                        int(pl.smem));
   if (e != cudaSuccess) return e;
   dim3 grid(pl.num_splits, a.kv_heads * pl.n_head_tiles, a.batch);
-  pl.fn<<<grid, kWarps * 32, pl.smem, stream>>>(p);
-  e = cudaGetLastError();
+  e = launch_pdl(pl.fn, grid, dim3(kWarps * 32), pl.smem, stream, p);
   if (e == cudaSuccess && pl.num_splits > 1) {
     const int rows = a.batch * a.num_q_heads;
+    const dim3 mgrid((rows + 3) / 4);
     if (a.dtype == Dtype::BF16) {
-      merge_kernel<__nv_bfloat16><<<rows, 128, 0, stream>>>(p, a.head_dim);
+      e = launch_pdl(merge_kernel<__nv_bfloat16>, mgrid, dim3(128), 0, stream, p, a.head_dim, rows);
     } else {
-      merge_kernel<__half><<<rows, 128, 0, stream>>>(p, a.head_dim);
+      e = launch_pdl(merge_kernel<__half>, mgrid, dim3(128), 0, stream, p, a.head_dim, rows);
     }
-    e = cudaGetLastError();
   }
   if (owned) {
     cudaError_t f = cudaFreeAsync(scratch, stream);

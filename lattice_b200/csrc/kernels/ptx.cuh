@@ -234,5 +234,18 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start before the previous kernel on its stream has
+// finished; grid_dependency_wait blocks until that kernel has completed and its
+// memory operations are visible (it returns at once for an ordinary launch).
+// launch_dependents lets the next such kernel be scheduled once every CTA of
+// this grid has executed it or exited.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 }  // namespace ptx
 }  // namespace kcmm

@@ -112,7 +112,8 @@ SK = {"KCMM_DECODE_IMPL": "streamk"}   # persistent stream-K, per-warp cp.async 
     {"KCMM_DECODE_IMPL": "tma"},          # TMA producer-warp variant
     {"KCMM_DECODE_IMPL": "tma", "KCMM_SK_GRID": "3"},
     {"KCMM_DECODE_IMPL": "tma", "KCMM_SK_VARIANT": "2"},
-    {"KCMM_DECODE_SPLITS": "1"},          # split-K kernel (the default)
+    {"KCMM_PDL": "0"},                    # split-K, plain stream-ordered launches
+    {"KCMM_DECODE_SPLITS": "1"},          # split-K kernel (the default), forced splits
     {"KCMM_DECODE_SPLITS": "3"},
     {"KCMM_DECODE_SPLITS": "7"},
 ])
@@ -278,3 +279,79 @@ def test_calls_on_two_streams_and_in_a_graph(monkeypatch):
     finally:
         del graph
         wl.close()
+
+
+SPLIT_CASES = [
+    # batch, hq, hkv, D, lengths (None: random in [min_len, max_len])
+    (64, 32, 8, 128, None),                       # the bench shape
+    (40, 32, 8, 128, [1, 0, 17, 5, 0, 3] * 6 + [4096, 2048, 1, 0]),  # short and empty rows
+    (1, 32, 8, 128, [37]),
+    (3, 64, 2, 128, [0, 4000, 33]),               # GQA 32: two head tiles per kv head
+    (6, 8, 8, 64, None),                          # MHA, D 64
+    (4, 16, 2, 256, None),                        # D 256
+    (5, 12, 4, 80, None),
+]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("case", SPLIT_CASES)
+def test_default_split_matches_oracle_and_forced_splits(case, dtype, monkeypatch):
+    """Default plan (split heuristic, merge launched as a programmatic dependent, split
+    scratch kept per stream) against the oracle and against two forced splits."""
+    torch = _torch()
+    B, hq, hkv, D, lens = case
+    wl = make(batch=B, num_q_heads=hq, kv_heads=hkv, head_dim=D, dtype=dtype, min_len=1,
+              max_len=4096, pool_blocks=max(512, B * 300), seq_lens_override=lens,
+              seed=B + hq + D)
+    try:
+        wl.out.fill_(3.0)
+        for _ in range(2):  # the second call reuses the stream's scratch
+            wl.decode()
+        torch.cuda.synchronize()
+        first = wl.out.clone()
+        o = first.float().cpu().numpy()
+        dead = wl.seq_lens <= 0
+        assert (o[dead] == 3.0).all()  # zero-length rows untouched
+        check(wl, first)
+        monkeypatch.setenv("KCMM_DECODE_SPLITS", "2")
+        wl.decode()
+        torch.cuda.synchronize()
+        check(wl)
+        live = ~dead
+        a, b = first.float()[live], wl.out.float()[live]
+        assert torch.all((a - b).abs() <= 4e-3 + 1e-2 * b.abs())
+    finally:
+        wl.close()
+
+
+def test_many_sequences():
+    """2,100 short sequences in one call."""
+    wl = make(batch=2100, num_q_heads=8, kv_heads=2, head_dim=64, min_len=1, max_len=40,
+              pool_blocks=2100 * 3 + 64, seed=77)
+    try:
+        wl.decode()
+        _torch().cuda.synchronize()
+        check(wl)
+    finally:
+        wl.close()
+
+
+def test_back_to_back_calls_of_growing_size_on_one_stream():
+    """Calls with growing split scratch on one stream, launched back to back without a
+    host synchronisation: each call's kernels wait for the previous call's merge before
+    reusing (or replacing) the stream's scratch."""
+    torch = _torch()
+    wls = [make(batch=B, num_q_heads=32, kv_heads=8, head_dim=128, min_len=500, max_len=4096,
+                pool_blocks=B * 300, seed=90 + B) for B in (4, 16, 48)]
+    try:
+        outs = []
+        for _ in range(3):
+            for wl in wls:
+                wl.decode()
+                outs.append((wl, wl.out.clone()))
+        torch.cuda.synchronize()
+        for wl, out in outs:
+            check(wl, out)
+    finally:
+        for wl in wls:
+            wl.close()
