@@ -928,6 +928,123 @@ def run_headsplit_leg(args):
     return line
 
 
+def run_tables_leg(args):
+    """Block-table maintenance per decode step on the Llama-3-8B decode shape (64
+    sequences, contexts U[512, 4096], 32 layers): each step every sequence gains one
+    token (a new block every 16 tokens, as the reference scheduler appends them,
+    src/batch/continuous_scheduler.rs:692-712).
+
+    * ours: `kcmm_step_tables_sync_on_stream` on the device-resident tables (the
+      changed entries in one pinned copy and one scatter kernel), timed from the call
+      to the completion of its device work;
+    * reference pattern (src/model/llama_transformer.rs:277-303, :338-339): the host
+      builds the tables, lengths and offsets table, then copies the offsets once and
+      the tables and lengths once per layer from pageable memory.  Its host build runs
+      here through the C ABI from Python (ctypes calls; the Rust original makes the
+      same queries natively), so the build time is reported on its own and the copies
+      on their own.
+    Both ways read the same pool; the leg checks that they end with equal tables."""
+    import time
+
+    import numpy as np
+    import torch
+
+    from lattice_b200.kcmm import StepTables
+    from lattice_b200.workloads import DecodeWorkload, read_device, write_device
+
+    torch.cuda.set_device(0)
+    steps = min(args.steps, 256)
+    rng = np.random.default_rng(1000)
+    lens = [int(x) for x in rng.integers(512, 4097, 64)]
+    wl = DecodeWorkload(batch=64, num_q_heads=32, kv_heads=8, head_dim=128,
+                        pool_blocks=40000, max_len=4096 + 16 * (steps // 16 + 2),
+                        seq_lens_override=lens, seed=1000).build()
+    pool, seqs = wl.pool, list(wl.seq_indices)
+    layers, mbps = 32, wl.max_blocks_per_seq
+    # return the blocks no sequence holds, so the steps' appends find free blocks
+    used = {int(wl.tables[b, j]) for b, L in enumerate(lens) for j in range(max(1, -(-L // 16)))}
+    pool.free_blocks([int(b) for b in wl.block_ids if int(b) not in used][:4096])
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    tables = StepTables(pool, 64)
+    d_bt = torch.zeros(64 * mbps, dtype=torch.int32, device="cuda")
+    d_sl = torch.zeros(64, dtype=torch.int32, device="cuda")
+    d_off = torch.zeros(60000, dtype=torch.int64, device="cuda")
+
+    def advance():
+        for b, s in enumerate(seqs):
+            if lens[b] % 16 == 0:  # the next token starts a new block
+                pool.append_block_to_sequence(s, pool.alloc_blocks(1)[0])
+            lens[b] += 1
+            pool.update_seq_len(s, lens[b])
+
+    def reference_build():
+        bt = np.zeros((64, mbps), np.int32)
+        for b, s in enumerate(seqs):
+            t = pool.block_table(s)[:mbps]
+            bt[b, :len(t)] = t
+        sl = np.array([pool.seq_len(s) for s in seqs], np.int32)
+        off = np.array(pool.all_block_offsets_f16(), np.uint64)
+        return bt, sl, off
+
+    def reference_upload(bt, sl, off):
+        write_device(d_off.data_ptr(), off)
+        for _ in range(layers):
+            write_device(d_bt.data_ptr(), bt)
+            write_device(d_sl.data_ptr(), sl)
+
+    for _ in range(max(args.warmup, 3)):
+        advance()
+        tables.sync(seqs, sp)
+        reference_upload(*reference_build())
+    torch.cuda.synchronize()
+    st0 = tables.stats()
+    ours, build, upload, ref_bytes = [], [], [], 0
+    for _ in range(steps):
+        advance()
+        t0 = time.perf_counter()
+        tables.sync(seqs, sp)
+        stream.synchronize()
+        t1 = time.perf_counter()
+        bt, sl, off = reference_build()
+        t2 = time.perf_counter()
+        reference_upload(bt, sl, off)
+        t3 = time.perf_counter()
+        ours.append(t1 - t0)
+        build.append(t2 - t1)
+        upload.append(t3 - t2)
+        ref_bytes = off.nbytes + layers * (bt.nbytes + sl.nbytes)
+    st1 = tables.stats()
+    # both ways hold the same tables now
+    got_bt = read_device(tables.block_tables_ptr, 64 * mbps * 4).view(np.int32)
+    got_sl = read_device(tables.seq_lens_ptr, 64 * 4).view(np.int32)
+    got_off = read_device(tables.block_offsets_ptr, off.nbytes).view(np.uint64)
+    same = (np.array_equal(got_bt, bt.reshape(-1)) and np.array_equal(got_sl, sl)
+            and np.array_equal(got_off, off))
+    tables.destroy()
+    wl.close()
+    med = lambda v: float(np.median(v)) * 1e6  # noqa: E731
+    ours_us = med(ours)
+    out = _line(
+        "block-table maintenance per decode step (us, host + device)", ours_us, "us",
+        {"workload": "BASELINE config 2 decode step: 64 seqs, contexts U[512,4096] growing by "
+                     "one token per step, 40k-block pool, 32 layers",
+         "steps": steps},
+        None,
+        {"higher_is_better": False,
+         "ours": {"us_per_step": round(ours_us, 2),
+                  "bytes_per_step": round((st1["bytes"] - st0["bytes"]) / steps, 1),
+                  "entries_per_step": round((st1["table_entries"] - st0["table_entries"]
+                                             + st1["offset_entries"] - st0["offset_entries"])
+                                            / steps, 1)},
+         "reference_pattern": {"upload_us_per_step": round(med(upload), 2),
+                               "host_build_us_per_step_ctypes": round(med(build), 2),
+                               "bytes_per_step": ref_bytes,
+                               "copies_per_step": 1 + 2 * layers},
+         "tables_equal": bool(same)})
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -937,7 +1054,8 @@ def main():
     ap.add_argument("--profile", action="store_true",
                     help="profiling case for ncu: 12k-block pool, no CPU baseline / e2e legs")
     ap.add_argument("--workload",
-                    choices=["step", "append", "cow", "swap", "prefill", "headsplit"],
+                    choices=["step", "append", "cow", "swap", "prefill", "headsplit",
+                             "tables"],
                     default="step",
                     help="step = the headline (default); the others print one line for a "
                          "secondary BASELINE config")
@@ -954,6 +1072,8 @@ def main():
         run_prefill_leg(args)
     elif args.workload == "headsplit":
         run_headsplit_leg(args)
+    elif args.workload == "tables":
+        run_tables_leg(args)
     else:
         run_ours(args)
 

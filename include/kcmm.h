@@ -485,6 +485,50 @@ int kcmm_swap_in_blocks_on_stream(kcmm_pool_t *pool, const uint32_t *blocks,
  */
 int32_t kcmm_get_kernel_status(kcmm_pool_t *pool);
 
+/* --- device-resident step tables (no reference counterpart) --- */
+
+/*
+ * The block tables, sequence lengths and block offsets a decode step reads,
+ * kept on the device between steps.  They replace the per-step host build and
+ * per-layer upload of ref src/model/llama_transformer.rs:277-303 and :338-339
+ * (offsets: kcmm_get_all_block_offsets_f16).  A sync uploads only what changed
+ * since the previous sync: rows whose sequence or table changed, lengths that
+ * differ, and offsets of the blocks the pool installed, freed or swapped in.
+ * The contents equal the reference's host build: row b holds the first
+ * max_blocks_per_seq entries of seq_indices[b]'s table, zeros after it.
+ */
+typedef struct kcmm_step_tables kcmm_step_tables_t;
+
+typedef struct {
+    uint64_t syncs;          /* sync calls */
+    uint64_t table_entries;  /* 32-bit entries written (table entries and lengths) */
+    uint64_t offset_entries; /* 64-bit offsets entries written */
+    uint64_t bytes;          /* bytes copied host to device */
+    uint64_t full_offsets;   /* syncs that wrote the whole offsets array */
+} kcmm_step_tables_stats_t;
+
+/** Device tables for up to max_batch rows on the pool's device; NULL on error. */
+kcmm_step_tables_t *kcmm_step_tables_create(kcmm_pool_t *pool, uint32_t max_batch);
+/** Synchronises the device, then frees the tables. */
+void kcmm_step_tables_destroy(kcmm_step_tables_t *tables);
+/**
+ * Bring rows [0, batch) up to date for seq_indices[0..batch) (host array), and
+ * the offsets for every block of the pool.  Enqueues one copy and one kernel
+ * on stream_ptr when anything changed.  Syncs of one tables object must be
+ * ordered on the device (one stream, or events between streams).  -1 on a bad
+ * sequence index or batch > max_batch (message on the pool).
+ */
+int kcmm_step_tables_sync_on_stream(kcmm_step_tables_t *tables, const uint32_t *seq_indices,
+                                    uint32_t batch, uint64_t stream_ptr);
+/** Device int32 [max_batch, max_blocks_per_seq] block tables (block_tables_ptr of decode). */
+uint64_t kcmm_step_tables_block_tables(const kcmm_step_tables_t *tables);
+/** Device int32 [max_batch] sequence lengths (seq_lens_ptr of decode). */
+uint64_t kcmm_step_tables_seq_lens(const kcmm_step_tables_t *tables);
+/** Device u64 block offsets in 2-byte units; may move at a sync that grows it. */
+uint64_t kcmm_step_tables_block_offsets(const kcmm_step_tables_t *tables);
+/** Counters since creation; -1 on NULL arguments. */
+int kcmm_step_tables_stats(const kcmm_step_tables_t *tables, kcmm_step_tables_stats_t *out);
+
 /* --- library facts --- */
 
 /** Build tag of the library ("kcmm-b200 <version> sm_100a"). */

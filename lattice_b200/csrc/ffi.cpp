@@ -16,12 +16,18 @@
 #include "../../include/kcmm.h"
 #include "kcmm_internal.hpp"
 #include "launch.hpp"
+#include "step_tables.hpp"
 
 using kcmm::Error;
 using kcmm::Pool;
 
 struct kcmm_pool_t {
   Pool *pool;
+};
+
+struct kcmm_step_tables {
+  kcmm_pool_t *owner;
+  kcmm::StepTables *tables;
 };
 
 namespace {
@@ -959,5 +965,56 @@ int32_t kcmm_get_kernel_status(kcmm_pool_t *h) {
 }
 
 const char *kcmm_build_info(void) { return "kcmm-b200 0.1.0 sm_100a"; }
+
+// --- device-resident step tables -----------------------------------------------
+
+kcmm_step_tables_t *kcmm_step_tables_create(kcmm_pool_t *h, uint32_t max_batch) {
+  if (!h) return nullptr;
+  kcmm::StepTables *t = nullptr;
+  if (guarded(h, "kcmm_step_tables_create",
+              [&] { t = new kcmm::StepTables(P(h), max_batch); }) != 0)
+    return nullptr;
+  return new kcmm_step_tables{h, t};
+}
+
+void kcmm_step_tables_destroy(kcmm_step_tables_t *t) {
+  if (!t) return;
+  delete t->tables;
+  delete t;
+}
+
+int kcmm_step_tables_sync_on_stream(kcmm_step_tables_t *t, const uint32_t *seqs,
+                                    uint32_t batch, uint64_t stream) {
+  if (!t) return -1;
+  if (batch > 0 && !seqs) {
+    set_error(t->owner, "kcmm_step_tables_sync_on_stream: seq_indices is null");
+    return -1;
+  }
+  return guarded(t->owner, "kcmm_step_tables_sync_on_stream",
+                 [&] { t->tables->sync(seqs, batch, S(stream)); });
+}
+
+uint64_t kcmm_step_tables_block_tables(const kcmm_step_tables_t *t) {
+  return t ? reinterpret_cast<uint64_t>(t->tables->block_tables()) : 0;
+}
+
+uint64_t kcmm_step_tables_seq_lens(const kcmm_step_tables_t *t) {
+  return t ? reinterpret_cast<uint64_t>(t->tables->seq_lens()) : 0;
+}
+
+uint64_t kcmm_step_tables_block_offsets(const kcmm_step_tables_t *t) {
+  return t ? reinterpret_cast<uint64_t>(t->tables->block_offsets()) : 0;
+}
+
+int kcmm_step_tables_stats(const kcmm_step_tables_t *t, kcmm_step_tables_stats_t *out) {
+  if (!t || !out) return -1;
+  const kcmm::StepTableStats &s = t->tables->stats();
+  out->syncs = s.syncs;
+  out->table_entries = s.entries32;
+  out->offset_entries = s.entries64;
+  out->bytes = s.bytes;
+  out->full_offsets = s.full_offsets;
+  return 0;
+}
 
 }  // extern "C"

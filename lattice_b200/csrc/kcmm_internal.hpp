@@ -126,6 +126,34 @@ struct Sequence {
   bool active = true;
   uint64_t last_access = 0;
   Priority priority = Priority::Normal;
+  // Change stamps for device-resident step tables: `version` moves on every
+  // table change, `rewrite` only when entries other than the tail change
+  // (register, fork, copy-on-write, unregister), so an unchanged `rewrite`
+  // means the new entries are all past the old end.
+  uint64_t version = 0, rewrite = 0;
+};
+
+// What a StepTables object's device arrays hold, as the host last wrote them.
+struct StepTableState {
+  size_t max_batch = 0;
+  std::vector<int64_t> row_seq;  // -1: never written
+  std::vector<uint64_t> row_version, row_rewrite;
+  std::vector<uint32_t> row_blocks;  // table entries written (the rest are zero)
+  std::vector<int32_t> row_len;
+  uint64_t log_cursor = 0;  // block-log position the offsets reflect
+  size_t offsets_len = 0;   // entries valid in the device offsets array
+  bool offsets_init = false;
+};
+
+// One sync's changes: 32-bit entries of [tables (max_batch x max_blocks_per_seq) |
+// seq_lens (max_batch)] and 64-bit entries of the offsets array.
+struct TableUpdates {
+  std::vector<uint32_t> idx32;
+  std::vector<int32_t> val32;
+  std::vector<uint32_t> idx64;
+  std::vector<uint64_t> val64;
+  size_t offsets_needed = 0;  // entries the offsets array must hold
+  bool offsets_full = false;  // every entry was listed (first sync, grown, or log trimmed)
 };
 
 struct PoolConfig {
@@ -222,6 +250,10 @@ class Pool {
   const void *tensor_maps(size_t layer, int kv_heads, int head_dim);
   // The V page-box map of the layer (third map above), or null when unavailable.
   const void *v_page_map(size_t layer, int kv_heads, int head_dim);
+  // Changes since `st` for the rows seqs[0..batch) of a device step table, and
+  // `st` moved to the new state (step_tables.cpp).
+  void step_table_updates(const uint32_t *seqs, size_t batch, StepTableState *st,
+                          TableUpdates *up);
   void use_device() const;  // make the pool's device current
   void require_device(const char *what) const;
   int32_t *diag_word() const { return diag_; }  // device int32, sticky error bits
@@ -248,6 +280,10 @@ class Pool {
     return uint64_t(h.sb) * kSuperblockBytes + uint64_t(h.blk) * block_bytes;
   }
   void bump() { epoch_.fetch_add(1, std::memory_order_acq_rel); }
+  // Blocks whose offset-table entry (in_use ? va_offset / 2 : 0) changed, in
+  // order; entry i has global position block_log_base_ + i.
+  void log_block_locked(uint32_t blk);
+  void touch_table_locked(Sequence &s, bool rewrite);
   std::vector<uint32_t> select_victims_locked(size_t count);
   void swap_out_locked(const std::vector<uint32_t> &ids, void *stream);
   void swap_in_locked(const std::vector<uint32_t> &ids, void *stream);
@@ -276,6 +312,9 @@ class Pool {
   std::unique_ptr<SwapTier> tier_;
   std::atomic<uint64_t> epoch_{0};
   int32_t *diag_ = nullptr;
+  std::vector<uint32_t> block_log_;
+  uint64_t block_log_base_ = 0;
+  uint64_t table_stamp_ = 0;
 };
 
 // Best-fit range allocator over the swap buffer, merging on free

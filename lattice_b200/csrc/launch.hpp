@@ -79,6 +79,11 @@ struct PrefillArgs {
 // (kernels/prefill.cu).  head_dim 128; num_q_heads / kv_heads must divide 128.
 cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream);
 
+// Apply a packed step-table update list (kernels/tables.cu): 32-bit entries into
+// i32 and 64-bit entries into o64.
+cudaError_t apply_table_updates(const void *stage, int n32, int n64, size_t off64, int32_t *i32,
+                                uint64_t *o64, cudaStream_t stream);
+
 // Copy `rows` K and V rows of `row_elems` 16-bit elements from k_src/v_src
 // (row r at r*row_elems) to va_k/va_v + dst_elems[r]; dst_elems[r] < 0 skips.
 cudaError_t copy_rows(const void *k_src, const void *v_src, void *va_k, void *va_v,

@@ -289,7 +289,23 @@ uint32_t Pool::install_locked(BlockHandle h) {
     blocks_.push_back(bi);
   }
   bump();
+  log_block_locked(idx);
   return idx;
+}
+
+void Pool::log_block_locked(uint32_t blk) {
+  constexpr size_t kLogMax = size_t(1) << 20;
+  if (block_log_.size() >= kLogMax) {  // readers behind the cut reload the whole array
+    const size_t cut = block_log_.size() / 2;
+    block_log_.erase(block_log_.begin(), block_log_.begin() + long(cut));
+    block_log_base_ += cut;
+  }
+  block_log_.push_back(blk);
+}
+
+void Pool::touch_table_locked(Sequence &s, bool rewrite) {
+  s.version = ++table_stamp_;
+  if (rewrite) s.rewrite = s.version;
 }
 
 uint32_t Pool::alloc_block() {
@@ -310,6 +326,7 @@ std::vector<uint32_t> Pool::alloc_blocks(size_t n) {
 void Pool::release_block_locked(uint32_t blk, std::vector<BlockHandle> *gpu,
                                 std::vector<uint64_t> *cpu_slots) {
   BlockInfo &bi = blocks_[blk];
+  if (bi.loc == Loc::Gpu || bi.loc == Loc::Cpu || bi.loc == Loc::Nvme) log_block_locked(blk);
   switch (bi.loc) {
     case Loc::Gpu:
       bi.in_use = false;
@@ -367,6 +384,7 @@ uint32_t Pool::register_sequence(std::vector<uint32_t> table) {
   Sequence s;
   s.table = std::move(table);
   s.last_access = ++tick_;
+  touch_table_locked(s, true);
   seqs_.push_back(std::move(s));
   return uint32_t(seqs_.size() - 1);
 }
@@ -378,6 +396,7 @@ void Pool::unregister_sequence(size_t seq) {
     if (seq >= seqs_.size()) return;
     table.swap(seqs_[seq].table);
     seqs_[seq].seq_len = 0;
+    touch_table_locked(seqs_[seq], true);
   }
   if (!table.empty()) free_blocks(table.data(), table.size());
 }
@@ -418,6 +437,7 @@ bool Pool::append_block(size_t seq, uint32_t blk) {
   std::lock_guard<std::mutex> g(mu_);
   if (seq >= seqs_.size()) return false;
   seqs_[seq].table.push_back(blk);
+  touch_table_locked(seqs_[seq], false);
   return true;
 }
 
@@ -606,6 +626,7 @@ uint32_t Pool::fork_sequence(size_t src) {
   for (uint32_t b : s.table) blocks_[b].refcount += 1;
   s.last_access = ++tick_;
   s.active = true;
+  touch_table_locked(s, true);
   seqs_.push_back(std::move(s));
   return uint32_t(seqs_.size() - 1);
 }
@@ -627,6 +648,7 @@ std::vector<uint32_t> Pool::share_prefix(size_t src, size_t dst, size_t n) {
   for (uint32_t b : out) blocks_[b].refcount += 1;
   auto &dt = seqs_[dst].table;
   dt.insert(dt.end(), out.begin(), out.end());
+  touch_table_locked(seqs_[dst], false);
   return out;
 }
 
@@ -660,6 +682,7 @@ std::vector<uint32_t> Pool::cow_blocks(const uint32_t *seqs, const uint32_t *log
       dst_off.push_back(blocks_[nb].va_offset);
       blocks_[b].refcount -= 1;
       slot = nb;
+      touch_table_locked(seqs_[seqs[i]], true);
     }
     out[i] = slot;
   }
@@ -876,6 +899,7 @@ void Pool::swap_in_locked(const std::vector<uint32_t> &ids, void *stream) {
     bi.loc = Loc::Gpu;
     bi.access_tick = ++tick_;
     bump();
+    log_block_locked(ids[i]);
   }
   metrics_.restoration_count += 1;
   metrics_.restored_blocks += ids.size();

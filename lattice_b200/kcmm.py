@@ -223,8 +223,65 @@ SIGNATURES: dict[str, tuple] = {
     "kcmm_swap_out_blocks_on_stream": (i32, [P, pu32, u32, u64]),
     "kcmm_swap_in_blocks_on_stream": (i32, [P, pu32, u32, u64]),
     "kcmm_get_kernel_status": (i32, [P]),
+    "kcmm_step_tables_create": (P, [P, u32]),
+    "kcmm_step_tables_destroy": (None, [P]),
+    "kcmm_step_tables_sync_on_stream": (i32, [P, pu32, u32, u64]),
+    "kcmm_step_tables_block_tables": (u64, [P]),
+    "kcmm_step_tables_seq_lens": (u64, [P]),
+    "kcmm_step_tables_block_offsets": (u64, [P]),
+    "kcmm_step_tables_stats": (i32, [P, ctypes.c_void_p]),
     "kcmm_build_info": (ctypes.c_char_p, []),
 }
+
+
+class KcmmStepTablesStats(ctypes.Structure):
+    _fields_ = [("syncs", ctypes.c_uint64), ("table_entries", ctypes.c_uint64),
+                ("offset_entries", ctypes.c_uint64), ("bytes", ctypes.c_uint64),
+                ("full_offsets", ctypes.c_uint64)]
+
+
+class StepTables:
+    """Device-resident block tables / lengths / offsets of one ordered batch
+    (`kcmm_step_tables_*`); `sync` uploads only what changed."""
+
+    def __init__(self, pool: "KcmmPool", max_batch: int):
+        self.pool = pool
+        self.lib = pool.lib
+        h = self.lib.kcmm_step_tables_create(pool.handle, max_batch)
+        if not h:
+            raise KcmmError(f"kcmm_step_tables_create: {pool.last_error()}")
+        self.handle = ctypes.c_void_p(h)
+        self.max_batch = max_batch
+
+    def sync(self, seq_indices, stream_ptr: int = 0) -> None:
+        arr = _u32_array(seq_indices)
+        rc = self.lib.kcmm_step_tables_sync_on_stream(self.handle, arr, len(seq_indices),
+                                                      stream_ptr)
+        if rc != 0:
+            raise KcmmError(f"kcmm_step_tables_sync_on_stream: {self.pool.last_error()}")
+
+    @property
+    def block_tables_ptr(self) -> int:
+        return self.lib.kcmm_step_tables_block_tables(self.handle)
+
+    @property
+    def seq_lens_ptr(self) -> int:
+        return self.lib.kcmm_step_tables_seq_lens(self.handle)
+
+    @property
+    def block_offsets_ptr(self) -> int:
+        return self.lib.kcmm_step_tables_block_offsets(self.handle)
+
+    def stats(self) -> dict:
+        st = KcmmStepTablesStats()
+        if self.lib.kcmm_step_tables_stats(self.handle, ctypes.byref(st)) != 0:
+            raise KcmmError("kcmm_step_tables_stats failed")
+        return {f: getattr(st, f) for f, _ in st._fields_}
+
+    def destroy(self) -> None:
+        if self.handle:
+            self.lib.kcmm_step_tables_destroy(self.handle)
+            self.handle = None
 
 
 def _u32_array(values):

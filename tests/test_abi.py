@@ -190,3 +190,20 @@ def test_prefill_refuses_host_pool(host_pool_factory):
                            block_offsets_f16_ptr=16, batch=1, max_query_len=4, num_q_heads=8,
                            kv_heads=2, head_dim=128, block_size=16, max_blocks_per_seq=2,
                            scale=0.1)
+
+
+def test_step_tables_need_a_device_pool(kcmm_lib, host_pool_factory):
+    """On the host VMM backend (no device) creation fails with a message; NULL
+    handles are refused."""
+    from lattice_b200 import kcmm
+
+    lib = kcmm_lib.lib
+    pool = host_pool_factory(kv_heads=2, head_dim=64, max_batch=4, max_seq_len=256)
+    assert not lib.kcmm_step_tables_create(pool.handle, 8)
+    assert "kcmm_step_tables_create" in pool.last_error()
+    assert lib.kcmm_step_tables_sync_on_stream(None, None, 0, 0) == -1
+    assert lib.kcmm_step_tables_stats(None, None) == -1
+    assert lib.kcmm_step_tables_block_tables(None) == 0
+    lib.kcmm_step_tables_destroy(None)
+    with pytest.raises(kcmm.KcmmError):
+        kcmm.StepTables(pool, 8)
