@@ -295,6 +295,7 @@ uint32_t kcmm_total_blocks(kcmm_pool_t *pool);                         /* ref in
 uint32_t kcmm_free_physical_blocks(kcmm_pool_t *pool);                 /* ref include/kcmm.h:644 */
 int kcmm_has_free_blocks(kcmm_pool_t *pool);                           /* ref include/kcmm.h:647 */
 uint32_t kcmm_active_sequences(kcmm_pool_t *pool);                     /* ref include/kcmm.h:650 */
+/* Policy names: lru, lfu, fifo, arc, sink_window (ref src/kcmm/tiering.rs:877-895). */
 int kcmm_set_eviction_policy(kcmm_pool_t *pool, const char *policy);   /* ref include/kcmm.h:664 */
 uint32_t kcmm_get_eviction_policy(kcmm_pool_t *pool, char *out_policy,
                                   uint32_t max_len);                   /* ref include/kcmm.h:674 */
@@ -484,6 +485,26 @@ int kcmm_swap_in_blocks_on_stream(kcmm_pool_t *pool, const uint32_t *blocks,
  * Synchronises the pool's device.  -1 if the pool has no device.
  */
 int32_t kcmm_get_kernel_status(kcmm_pool_t *pool);
+
+/* --- background eviction and victim preview (no C counterpart in the reference) --- */
+
+/**
+ * Start the background eviction thread of ref src/kcmm/pool.rs:1308-1398 (Rust-only
+ * there): every background_evict_interval_ms, while the free physical block ratio
+ * is below low_watermark_threshold, swap out up to min(max_batch_blocks, 16)
+ * blocks of inactive (cooled) sequences chosen by the eviction policy.  A no-op
+ * when it runs already; -1 when tiering is disabled or the pool has no device.
+ */
+int kcmm_start_background_eviction(kcmm_pool_t *pool);
+/** Stop the thread and wait for it; 0 also when it was not running. */
+int kcmm_stop_background_eviction(kcmm_pool_t *pool);
+/**
+ * The victims kcmm_evict_blocks(pool, count) would take now, in eviction order,
+ * without moving anything; returns how many were written to out_blocks
+ * (at most max_out).  0 when tiering is disabled.
+ */
+uint32_t kcmm_preview_eviction_victims(kcmm_pool_t *pool, uint32_t count, uint32_t *out_blocks,
+                                       uint32_t max_out);
 
 /* --- device-resident step tables (no reference counterpart) --- */
 

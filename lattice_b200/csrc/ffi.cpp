@@ -7,6 +7,7 @@
 // points only force the CUDA module to load.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cctype>
 #include <cstdlib>
 #include <cstring>
@@ -965,6 +966,31 @@ int32_t kcmm_get_kernel_status(kcmm_pool_t *h) {
 }
 
 const char *kcmm_build_info(void) { return "kcmm-b200 0.1.0 sm_100a"; }
+
+// --- background eviction and victim preview ------------------------------------
+
+int kcmm_start_background_eviction(kcmm_pool_t *h) {
+  if (!h) return -1;
+  return guarded(h, "kcmm_start_background_eviction",
+                 [&] { P(h)->start_background_eviction(); });
+}
+
+int kcmm_stop_background_eviction(kcmm_pool_t *h) {
+  if (!h) return -1;
+  return guarded(h, "kcmm_stop_background_eviction", [&] { P(h)->stop_background_eviction(); });
+}
+
+uint32_t kcmm_preview_eviction_victims(kcmm_pool_t *h, uint32_t count, uint32_t *out,
+                                       uint32_t max_out) {
+  if (!h || !out || max_out == 0 || !P(h)->tiering_enabled()) return 0;
+  std::vector<uint32_t> v;
+  if (guarded(h, "kcmm_preview_eviction_victims",
+              [&] { v = P(h)->preview_victims(count); }) != 0)
+    return 0;
+  const uint32_t n = uint32_t(std::min<size_t>(v.size(), max_out));
+  std::memcpy(out, v.data(), n * sizeof(uint32_t));
+  return n;
+}
 
 // --- device-resident step tables -----------------------------------------------
 

@@ -12,13 +12,17 @@
 #pragma once
 
 #include <atomic>
+#include <condition_variable>
 #include <cstddef>
 #include <cstdint>
 #include <memory>
 #include <mutex>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <vector>
+
+#include "policy.hpp"
 
 namespace kcmm {
 
@@ -235,6 +239,15 @@ class Pool {
   void set_policy(const std::string &name);
   void note_access(uint32_t blk);
   size_t evict(size_t count);
+  // The victims evict(count) would take now, without moving anything.
+  std::vector<uint32_t> preview_victims(size_t count);
+  // Background eviction (ref src/kcmm/pool.rs:1308-1405): every
+  // evict_interval_ms, when the free-block ratio is below low_watermark, swap
+  // out up to min(max_batch_blocks, 16) policy-chosen blocks of inactive
+  // (cooled) sequences.  Start is a no-op when running; stop joins the thread.
+  void start_background_eviction();
+  void stop_background_eviction();
+  bool background_eviction_running();
   uint64_t restore_one(uint32_t blk);
   void restore_many(const uint32_t *ids, size_t n);
   void swap_out(const uint32_t *ids, size_t n, void *stream);
@@ -285,6 +298,8 @@ class Pool {
   void log_block_locked(uint32_t blk);
   void touch_table_locked(Sequence &s, bool rewrite);
   std::vector<uint32_t> select_victims_locked(size_t count);
+  void register_positions_locked(size_t seq, size_t from);
+  void background_evict_once(float threshold, size_t batch);
   void swap_out_locked(const std::vector<uint32_t> &ids, void *stream);
   void swap_in_locked(const std::vector<uint32_t> &ids, void *stream);
   SwapTier &tier_locked();
@@ -307,7 +322,11 @@ class Pool {
   std::vector<size_t> mapped_;  // superblocks backed so far, per region
   std::vector<Sequence> seqs_;
   uint64_t tick_ = 0;
-  std::string policy_ = "lru";
+  std::unique_ptr<EvictionPolicy> policy_;
+  std::mutex bg_mu_;
+  std::condition_variable bg_cv_;
+  std::thread bg_thread_;
+  bool bg_stop_ = false;
   Metrics metrics_;
   std::unique_ptr<SwapTier> tier_;
   std::atomic<uint64_t> epoch_{0};

@@ -21,6 +21,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cstring>
 #include <sstream>
 
@@ -158,7 +159,9 @@ Pool::Pool(const PoolConfig &cfg, std::unique_ptr<Vmm> vmm)
       region_bytes(align_up(max_blocks_total * block_bytes, kSuperblockBytes)),
       vmm_(std::move(vmm)),
       alloc_(block_bytes),
-      policy_(cfg.eviction_policy) {
+      policy_(make_policy(cfg.eviction_policy, cfg.max_blocks, cfg.sink_blocks,
+                          cfg.window_blocks)) {
+  if (!policy_) policy_ = make_policy("lru", 0, 0, 0);
   // ref src/kcmm/pool.rs:217-225: one K and one V region per layer.
   va_k.resize(num_layers);
   va_v.resize(num_layers);
@@ -184,6 +187,7 @@ Pool::Pool(const PoolConfig &cfg, std::unique_ptr<Vmm> vmm)
 }
 
 Pool::~Pool() {
+  stop_background_eviction();
   if (vmm_->is_device()) {
     use_device();
     cudaDeviceSynchronize();
@@ -290,7 +294,13 @@ uint32_t Pool::install_locked(BlockHandle h) {
   }
   bump();
   log_block_locked(idx);
+  if (cfg_.tiering) policy_->on_allocate(idx);  // ref src/kcmm/pool.rs:446-449
   return idx;
+}
+
+void Pool::register_positions_locked(size_t seq, size_t from) {
+  const auto &t = seqs_[seq].table;
+  for (size_t j = from; j < t.size(); ++j) policy_->register_block(t[j], seq, j);
 }
 
 void Pool::log_block_locked(uint32_t blk) {
@@ -386,6 +396,7 @@ uint32_t Pool::register_sequence(std::vector<uint32_t> table) {
   s.last_access = ++tick_;
   touch_table_locked(s, true);
   seqs_.push_back(std::move(s));
+  register_positions_locked(seqs_.size() - 1, 0);
   return uint32_t(seqs_.size() - 1);
 }
 
@@ -438,6 +449,7 @@ bool Pool::append_block(size_t seq, uint32_t blk) {
   if (seq >= seqs_.size()) return false;
   seqs_[seq].table.push_back(blk);
   touch_table_locked(seqs_[seq], false);
+  register_positions_locked(seq, seqs_[seq].table.size() - 1);
   return true;
 }
 
@@ -628,6 +640,7 @@ uint32_t Pool::fork_sequence(size_t src) {
   s.active = true;
   touch_table_locked(s, true);
   seqs_.push_back(std::move(s));
+  register_positions_locked(seqs_.size() - 1, 0);
   return uint32_t(seqs_.size() - 1);
 }
 
@@ -647,8 +660,10 @@ std::vector<uint32_t> Pool::share_prefix(size_t src, size_t dst, size_t n) {
   }
   for (uint32_t b : out) blocks_[b].refcount += 1;
   auto &dt = seqs_[dst].table;
+  const size_t old_len = dt.size();
   dt.insert(dt.end(), out.begin(), out.end());
   touch_table_locked(seqs_[dst], false);
+  register_positions_locked(dst, old_len);
   return out;
 }
 
@@ -683,6 +698,7 @@ std::vector<uint32_t> Pool::cow_blocks(const uint32_t *seqs, const uint32_t *log
       blocks_[b].refcount -= 1;
       slot = nb;
       touch_table_locked(seqs_[seqs[i]], true);
+      policy_->register_block(nb, seqs[i], logical[i]);
     }
     out[i] = slot;
   }
@@ -747,15 +763,22 @@ void Pool::slot_destinations(const int64_t *slots, size_t batch, std::vector<int
 
 std::string Pool::policy_name() {
   std::lock_guard<std::mutex> g(mu_);
-  return policy_;
+  return policy_->name();
 }
 
 void Pool::set_policy(const std::string &name) {
-  if (name != "lru" && name != "lfu" && name != "fifo") {
-    throw Error("unknown eviction policy '" + name + "' (expected lru, lfu or fifo)");
+  // ref src/kcmm/tiering.rs:877-895: a fresh policy object; ARC sized by the
+  // swap buffer over max_batch_blocks, sink-window protecting 1 + 4 blocks.
+  const size_t arc_cap = cfg_.max_blocks * num_layers * 2 * block_bytes /
+                         std::max<size_t>(cfg_.max_batch_blocks, 1);
+  auto p = make_policy(name, arc_cap, 1, 4);
+  if (!p) {
+    throw Error("unknown eviction policy '" + name +
+                "' (expected lru, lfu, fifo, arc, or sink_window)");
   }
   std::lock_guard<std::mutex> g(mu_);
-  policy_ = name;
+  policy_ = std::move(p);
+  for (size_t s = 0; s < seqs_.size(); ++s) register_positions_locked(s, 0);
 }
 
 void Pool::note_access(uint32_t blk) {
@@ -763,25 +786,97 @@ void Pool::note_access(uint32_t blk) {
   if (blk < blocks_.size() && blocks_[blk].in_use) {
     blocks_[blk].access_tick = ++tick_;
     blocks_[blk].access_count += 1;
+    // the reference reaches the policy through the block's physical handle,
+    // which only GPU-resident blocks have (ref src/kcmm/ffi.rs:2330-2336)
+    if (blocks_[blk].loc == Loc::Gpu) policy_->on_access(blk);
   }
 }
 
 std::vector<uint32_t> Pool::select_victims_locked(size_t count) {
   // Candidates are all live GPU-resident blocks in id order (ffi.rs:1913-1926);
-  // a stable sort on the policy key picks the victims (tiering.rs:79-200).
+  // the policy orders them (tiering.rs:32-540).
   std::vector<uint32_t> cand;
   for (uint32_t i = 0; i < blocks_.size(); ++i) {
     if (blocks_[i].in_use && blocks_[i].loc == Loc::Gpu) cand.push_back(i);
   }
-  auto key = [&](uint32_t i) -> uint64_t {
-    const BlockInfo &b = blocks_[i];
-    if (policy_ == "lfu") return b.access_count;
-    if (policy_ == "fifo") return b.alloc_tick;
-    return b.access_tick;
-  };
-  std::stable_sort(cand.begin(), cand.end(), [&](uint32_t a, uint32_t b) { return key(a) < key(b); });
-  if (cand.size() > count) cand.resize(count);
-  return cand;
+  return policy_->select_victims(cand, count);
+}
+
+std::vector<uint32_t> Pool::preview_victims(size_t count) {
+  std::lock_guard<std::mutex> g(mu_);
+  return select_victims_locked(count);
+}
+
+void Pool::start_background_eviction() {
+  if (!cfg_.tiering) throw Error("tiering is disabled");
+  require_device("background eviction");
+  std::lock_guard<std::mutex> g(bg_mu_);
+  if (bg_thread_.joinable()) return;
+  bg_stop_ = false;
+  bg_thread_ = std::thread([this] {
+    use_device();
+    const auto interval =
+        std::chrono::milliseconds(std::max<uint64_t>(cfg_.evict_interval_ms, 1));
+    const float threshold = cfg_.low_watermark;
+    const size_t batch = std::min<size_t>(cfg_.max_batch_blocks, 16);
+    std::unique_lock<std::mutex> lk(bg_mu_);
+    while (!bg_cv_.wait_for(lk, interval, [this] { return bg_stop_; })) {
+      lk.unlock();
+      try {
+        background_evict_once(threshold, batch);
+      } catch (const std::exception &) {
+        // a failed round (swap tier full, copy error) is counted in the
+        // metrics by the swap path; the next round tries again
+      }
+      lk.lock();
+    }
+  });
+}
+
+void Pool::stop_background_eviction() {
+  {
+    std::lock_guard<std::mutex> g(bg_mu_);
+    if (!bg_thread_.joinable()) return;
+    bg_stop_ = true;
+  }
+  bg_cv_.notify_all();
+  bg_thread_.join();
+}
+
+bool Pool::background_eviction_running() {
+  std::lock_guard<std::mutex> g(bg_mu_);
+  return bg_thread_.joinable();
+}
+
+void Pool::background_evict_once(float threshold, size_t batch) {
+  if (!below_low_watermark(threshold)) return;
+  std::lock_guard<std::mutex> g(mu_);
+  // candidates: live GPU-resident blocks of inactive sequences, in sequence
+  // and table order (ref src/kcmm/pool.rs:1351-1372), each block once
+  std::vector<uint32_t> cand;
+  std::vector<uint8_t> seen(blocks_.size(), 0);
+  for (const Sequence &s : seqs_) {
+    if (s.active) continue;
+    for (uint32_t b : s.table) {
+      if (b < blocks_.size() && !seen[b] && blocks_[b].in_use && blocks_[b].loc == Loc::Gpu) {
+        seen[b] = 1;
+        cand.push_back(b);
+      }
+    }
+  }
+  if (cand.empty()) return;
+  std::vector<uint32_t> victims = policy_->select_victims(cand, std::min(batch, cand.size()));
+  if (victims.empty()) return;
+  SwapTier &t = tier_locked();
+  const size_t slot_bytes = num_layers * 2 * block_bytes;
+  size_t fits = 0;
+  {
+    CpuSlotAllocator probe = t.slots;
+    size_t off;
+    while (fits < victims.size() && probe.allocate(slot_bytes, &off)) ++fits;
+  }
+  victims.resize(fits);
+  if (!victims.empty()) swap_out_locked(victims, nullptr);
 }
 
 SwapTier &Pool::tier_locked() {
@@ -857,6 +952,7 @@ void Pool::swap_out_locked(const std::vector<uint32_t> &ids, void *stream) {
     bi.loc = Loc::Cpu;
     bi.cpu_offset = host_off[i];
     bump();
+    policy_->on_evict(taken[i]);  // ref src/kcmm/tiering.rs:1177
   }
   metrics_.eviction_count += 1;
   metrics_.evicted_blocks += taken.size();
@@ -900,6 +996,7 @@ void Pool::swap_in_locked(const std::vector<uint32_t> &ids, void *stream) {
     bi.access_tick = ++tick_;
     bump();
     log_block_locked(ids[i]);
+    policy_->on_access(ids[i]);  // ref src/kcmm/tiering.rs:1871
   }
   metrics_.restoration_count += 1;
   metrics_.restored_blocks += ids.size();

@@ -223,6 +223,9 @@ SIGNATURES: dict[str, tuple] = {
     "kcmm_swap_out_blocks_on_stream": (i32, [P, pu32, u32, u64]),
     "kcmm_swap_in_blocks_on_stream": (i32, [P, pu32, u32, u64]),
     "kcmm_get_kernel_status": (i32, [P]),
+    "kcmm_start_background_eviction": (i32, [P]),
+    "kcmm_stop_background_eviction": (i32, [P]),
+    "kcmm_preview_eviction_victims": (u32, [P, u32, pu32, u32]),
     "kcmm_step_tables_create": (P, [P, u32]),
     "kcmm_step_tables_destroy": (None, [P]),
     "kcmm_step_tables_sync_on_stream": (i32, [P, pu32, u32, u64]),
@@ -647,6 +650,19 @@ class KcmmPool:
         self._check(self.lib.kcmm_swap_in_blocks_on_stream(self.handle, _u32_array(blocks),
                                                            len(blocks), stream_ptr),
                     "kcmm_swap_in_blocks_on_stream")
+
+    def start_background_eviction(self) -> None:
+        self._check(self.lib.kcmm_start_background_eviction(self.handle),
+                    "kcmm_start_background_eviction")
+
+    def stop_background_eviction(self) -> None:
+        self._check(self.lib.kcmm_stop_background_eviction(self.handle),
+                    "kcmm_stop_background_eviction")
+
+    def preview_eviction_victims(self, count: int) -> list[int]:
+        buf = (ctypes.c_uint32 * max(1, count))()
+        n = self.lib.kcmm_preview_eviction_victims(self.handle, count, buf, max(1, count))
+        return list(buf[:n])
 
     def set_eviction_policy(self, name: str) -> None:
         self._check(self.lib.kcmm_set_eviction_policy(self.handle, name.encode()),
