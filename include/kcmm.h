@@ -389,6 +389,42 @@ int kcmm_paged_prefill_bf16_on_stream(
     uint32_t num_q_heads, uint32_t kv_heads, uint32_t head_dim, uint32_t block_size,
     uint32_t max_blocks_per_seq, float scale, uint64_t stream_ptr);
 
+/*
+ * Strided twins for views into a fused QKV projection output (the vLLM seam of
+ * ref scripts/kcmm/kv_read_plan.py:830-838 and kv_write_mirror.py:536-537 copies
+ * such views to compact tensors first).  Strides are in elements; head_dim (and
+ * a token's kv_heads * head_dim row) must be contiguous.
+ *   q[b][h][:]   at query_ptr + b*q_stride_token + h*q_stride_head
+ *   out[b][h][:] at out_ptr   + b*out_stride_token + h*out_stride_head
+ *   table row b  at block_tables_ptr + b*block_tables_row_stride  (int32 entries)
+ * Head strides must be >= head_dim and the table row stride >= max_blocks_per_seq.
+ * Otherwise as kcmm_paged_attn_decode_bf16_on_stream.
+ */
+int kcmm_paged_attn_decode_bf16_strided_on_stream(
+    kcmm_pool_t *pool, uint32_t layer_idx, uint64_t query_ptr, int64_t q_stride_token,
+    int64_t q_stride_head, uint64_t out_ptr, int64_t out_stride_token, int64_t out_stride_head,
+    uint64_t block_tables_ptr, int64_t block_tables_row_stride, uint64_t seq_lens_ptr,
+    uint64_t block_offsets_f16_ptr, uint32_t batch, uint32_t num_q_heads, uint32_t kv_heads,
+    uint32_t head_dim, uint32_t block_size, uint32_t max_blocks_per_seq, float scale,
+    uint64_t stream_ptr);
+/** f16 twin of kcmm_paged_attn_decode_bf16_strided_on_stream. */
+int kcmm_paged_attn_decode_f16_strided_on_stream(
+    kcmm_pool_t *pool, uint32_t layer_idx, uint64_t query_ptr, int64_t q_stride_token,
+    int64_t q_stride_head, uint64_t out_ptr, int64_t out_stride_token, int64_t out_stride_head,
+    uint64_t block_tables_ptr, int64_t block_tables_row_stride, uint64_t seq_lens_ptr,
+    uint64_t block_offsets_f16_ptr, uint32_t batch, uint32_t num_q_heads, uint32_t kv_heads,
+    uint32_t head_dim, uint32_t block_size, uint32_t max_blocks_per_seq, float scale,
+    uint64_t stream_ptr);
+/**
+ * kcmm_append_kv_device_slots_on_stream with source rows k_src_ptr + b*k_row_stride
+ * and v_src_ptr + b*v_row_stride (elements; 0 = dense, else >= kv_heads*head_dim).
+ */
+int kcmm_append_kv_device_slots_strided_on_stream(
+    kcmm_pool_t *pool, uint32_t layer_idx, uint64_t slot_mapping_ptr,
+    uint64_t block_offsets_f16_ptr, uint64_t valid_blocks_ptr, uint32_t block_offsets_f16_len,
+    uint32_t batch, uint64_t k_src_ptr, int64_t k_row_stride, uint64_t v_src_ptr,
+    int64_t v_row_stride, uint64_t status_ptr, uint64_t stream_ptr);
+
 /** f16 twin of kcmm_paged_prefill_bf16_on_stream. */
 int kcmm_paged_prefill_f16_on_stream(
     kcmm_pool_t *pool, uint32_t layer_idx, uint64_t query_ptr, uint64_t out_ptr,

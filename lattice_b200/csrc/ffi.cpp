@@ -365,11 +365,11 @@ int kcmm_append_kv_slots_on_stream(kcmm_pool_t *h, uint32_t layer, const int64_t
   return append_slots(h, layer, slots, batch, k_src, v_src, stream);
 }
 
-int kcmm_append_kv_device_slots_on_stream(kcmm_pool_t *h, uint32_t layer, uint64_t slot_mapping,
-                                          uint64_t offsets, uint64_t valid, uint32_t offsets_len,
-                                          uint32_t batch, uint64_t k_src, uint64_t v_src,
-                                          uint64_t status, uint64_t stream) {
-  const char *op = "kcmm_append_kv_device_slots_on_stream";
+static int device_slots_impl(kcmm_pool_t *h, const char *op, uint32_t layer,
+                             uint64_t slot_mapping, uint64_t offsets, uint64_t valid,
+                             uint32_t offsets_len, uint32_t batch, uint64_t k_src,
+                             int64_t k_stride, uint64_t v_src, int64_t v_stride, uint64_t status,
+                             uint64_t stream) {
   if (!h || !slot_mapping || !offsets || !k_src || !v_src) {
     set_error(h, std::string(op) + ": null pointer argument");
     return -1;
@@ -387,8 +387,15 @@ int kcmm_append_kv_device_slots_on_stream(kcmm_pool_t *h, uint32_t layer, uint64
     set_error(h, std::string(op) + ": total_elements overflow");
     return -1;
   }
+  if (k_stride < 0 || v_stride < 0 || (k_stride && k_stride < int64_t(p->step_elems)) ||
+      (v_stride && v_stride < int64_t(p->step_elems))) {
+    set_error(h, std::string(op) + ": row strides must be 0 (dense) or >= kv_heads * head_dim");
+    return -1;
+  }
   if (guarded(h, op, [&] { p->require_device(op); })) return -1;
-  kcmm::dev::SlotWriteArgs a;
+  kcmm::dev::SlotWriteArgs a = {};
+  a.k_stride = k_stride;
+  a.v_stride = v_stride;
   a.va_k = reinterpret_cast<void *>(p->va_k[layer]);
   a.va_v = reinterpret_cast<void *>(p->va_v[layer]);
   a.slot_mapping = reinterpret_cast<const int64_t *>(slot_mapping);
@@ -404,6 +411,27 @@ int kcmm_append_kv_device_slots_on_stream(kcmm_pool_t *h, uint32_t layer, uint64
   a.region_elems = p->region_bytes / 2;
   p->use_device();
   return check_launch(h, op, kcmm::dev::device_slot_write(a, S(stream)));
+}
+
+int kcmm_append_kv_device_slots_on_stream(kcmm_pool_t *h, uint32_t layer, uint64_t slot_mapping,
+                                          uint64_t offsets, uint64_t valid, uint32_t offsets_len,
+                                          uint32_t batch, uint64_t k_src, uint64_t v_src,
+                                          uint64_t status, uint64_t stream) {
+  return device_slots_impl(h, "kcmm_append_kv_device_slots_on_stream", layer, slot_mapping,
+                           offsets, valid, offsets_len, batch, k_src, 0, v_src, 0, status,
+                           stream);
+}
+
+int kcmm_append_kv_device_slots_strided_on_stream(kcmm_pool_t *h, uint32_t layer,
+                                                  uint64_t slot_mapping, uint64_t offsets,
+                                                  uint64_t valid, uint32_t offsets_len,
+                                                  uint32_t batch, uint64_t k_src,
+                                                  int64_t k_row_stride, uint64_t v_src,
+                                                  int64_t v_row_stride, uint64_t status,
+                                                  uint64_t stream) {
+  return device_slots_impl(h, "kcmm_append_kv_device_slots_strided_on_stream", layer,
+                           slot_mapping, offsets, valid, offsets_len, batch, k_src,
+                           k_row_stride, v_src, v_row_stride, status, stream);
 }
 
 int kcmm_append_kv_device_slots_bf16_on_stream(kcmm_pool_t *h, uint32_t layer,
@@ -424,12 +452,19 @@ int kcmm_precompile_vllm_kv_write_f16(kcmm_pool_t *h) {
 // Paged decode attention (ref src/kcmm/ffi.rs:1569-1881)
 // ---------------------------------------------------------------------------
 
+// Element strides of the strided decode entry points (0 = dense).
+struct DecodeStrides {
+  int64_t q_token = 0, q_head = 0, out_token = 0, out_head = 0, tables_row = 0;
+};
+
 static int decode_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, uint64_t q,
                        uint64_t out, uint64_t tables, uint64_t seq_lens, uint64_t offsets,
                        uint32_t batch, uint32_t hq, uint32_t hkv, uint32_t hd, uint32_t bs,
                        uint32_t max_bps, float scale, uint64_t stream, bool sync,
-                       bool bind, bool noalloc = false) {
-  const char *op = noalloc ? "kcmm_paged_attn_decode_bf16_noalloc_on_stream"
+                       bool bind, bool noalloc = false, const DecodeStrides *st = nullptr) {
+  const char *op = st ? (dtype == kcmm::dev::Dtype::F16 ? "kcmm_paged_attn_decode_f16_strided"
+                                                        : "kcmm_paged_attn_decode_bf16_strided")
+                   : noalloc ? "kcmm_paged_attn_decode_bf16_noalloc_on_stream"
                    : dtype == kcmm::dev::Dtype::F16 ? "kcmm_paged_attn_decode_f16"
                                                     : "kcmm_paged_attn_decode_bf16";
   if (!h || !q || !out || !tables || !seq_lens || !offsets) {
@@ -457,9 +492,23 @@ static int decode_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, u
     set_error(h, std::string(op) + ": total_heads overflow");
     return -1;
   }
+  if (st && (st->q_token <= 0 || st->q_head < int64_t(hd) || st->out_token <= 0 ||
+             st->out_head < int64_t(hd) || st->tables_row < int64_t(max_bps))) {
+    set_error(h, std::string(op) +
+                     ": strides must be positive, head strides >= head_dim and the "
+                     "block-table row stride >= max_blocks_per_seq");
+    return -1;
+  }
   if (guarded(h, op, [&] { p->require_device(op); })) return -1;
   if (bind) p->use_device();
   kcmm::dev::DecodeArgs a = {};
+  if (st) {
+    a.q_stride_token = st->q_token;
+    a.q_stride_head = st->q_head;
+    a.out_stride_token = st->out_token;
+    a.out_stride_head = st->out_head;
+    a.tables_stride = st->tables_row;
+  }
   a.dtype = dtype;
   a.q = reinterpret_cast<const void *>(q);
   a.out = reinterpret_cast<void *>(out);
@@ -528,6 +577,36 @@ int kcmm_paged_attn_decode_f16_on_current_context_stream(
     uint32_t bs, uint32_t max_bps, float scale, uint64_t stream) {
   return decode_impl(h, kcmm::dev::Dtype::F16, layer, q, out, tables, seq_lens, offsets, batch,
                      hq, hkv, hd, bs, max_bps, scale, stream, false, false);
+}
+
+int kcmm_paged_attn_decode_bf16_strided_on_stream(
+    kcmm_pool_t *h, uint32_t layer, uint64_t q, int64_t q_stride_token, int64_t q_stride_head,
+    uint64_t out, int64_t out_stride_token, int64_t out_stride_head, uint64_t tables,
+    int64_t tables_row_stride, uint64_t seq_lens, uint64_t offsets, uint32_t batch, uint32_t hq,
+    uint32_t hkv, uint32_t hd, uint32_t bs, uint32_t max_bps, float scale, uint64_t stream) {
+  DecodeStrides st;
+  st.q_token = q_stride_token;
+  st.q_head = q_stride_head;
+  st.out_token = out_stride_token;
+  st.out_head = out_stride_head;
+  st.tables_row = tables_row_stride;
+  return decode_impl(h, kcmm::dev::Dtype::BF16, layer, q, out, tables, seq_lens, offsets, batch,
+                     hq, hkv, hd, bs, max_bps, scale, stream, false, true, false, &st);
+}
+
+int kcmm_paged_attn_decode_f16_strided_on_stream(
+    kcmm_pool_t *h, uint32_t layer, uint64_t q, int64_t q_stride_token, int64_t q_stride_head,
+    uint64_t out, int64_t out_stride_token, int64_t out_stride_head, uint64_t tables,
+    int64_t tables_row_stride, uint64_t seq_lens, uint64_t offsets, uint32_t batch, uint32_t hq,
+    uint32_t hkv, uint32_t hd, uint32_t bs, uint32_t max_bps, float scale, uint64_t stream) {
+  DecodeStrides st;
+  st.q_token = q_stride_token;
+  st.q_head = q_stride_head;
+  st.out_token = out_stride_token;
+  st.out_head = out_stride_head;
+  st.tables_row = tables_row_stride;
+  return decode_impl(h, kcmm::dev::Dtype::F16, layer, q, out, tables, seq_lens, offsets, batch,
+                     hq, hkv, hd, bs, max_bps, scale, stream, false, true, false, &st);
 }
 
 int kcmm_paged_attn_decode_bf16_on_stream(kcmm_pool_t *h, uint32_t layer, uint64_t q,

@@ -92,8 +92,10 @@ __global__ void slot_write_kernel(const SlotWriteArgs a) {
   __syncthreads();
   const int64_t dst = s_dst;
   if (dst < 0) return;
-  const uint16_t *ks = static_cast<const uint16_t *>(a.k_src) + int64_t(row) * a.step_elems;
-  const uint16_t *vs = static_cast<const uint16_t *>(a.v_src) + int64_t(row) * a.step_elems;
+  const uint16_t *ks = static_cast<const uint16_t *>(a.k_src) +
+                       int64_t(row) * (a.k_stride ? a.k_stride : a.step_elems);
+  const uint16_t *vs = static_cast<const uint16_t *>(a.v_src) +
+                       int64_t(row) * (a.v_stride ? a.v_stride : a.step_elems);
   uint16_t *kd = static_cast<uint16_t *>(a.va_k) + dst;
   uint16_t *vd = static_cast<uint16_t *>(a.va_v) + dst;
   const bool vec = ((reinterpret_cast<uintptr_t>(ks) | reinterpret_cast<uintptr_t>(vs) |

@@ -57,6 +57,10 @@ struct DecodeParams {
   float *part_o;
   float *part_lse;
   int32_t *diag;
+  // Element strides: q and out rows are q + b*q_sb + h*q_sh (head_dim contiguous),
+  // block-table rows tables + b*bt_stride.  Dense: (hq*D, D), (hq*D, D), max_bps.
+  int64_t q_sb, q_sh, o_sb, o_sh;
+  int64_t bt_stride;
 };
 
 __device__ __forceinline__ int ceil_div_dev(int a, int b) { return (a + b - 1) / b; }
@@ -120,12 +124,12 @@ __global__ void __launch_bounds__(W * 32, 2) decode_kernel(const DecodeParams p)
   const int n_splits_b = ceil_div_dev(n_units, p.units_per_split);
 
   // ---- stage Q (rows >= G are zero) and init barriers --------------------
-  const T *qg = static_cast<const T *>(p.q) + (int64_t(b) * p.hq + lo) * D;
+  const T *qg = static_cast<const T *>(p.q) + int64_t(b) * p.q_sb + int64_t(lo) * p.q_sh;
   for (int i = threadIdx.x; i < 16 * (D / 8); i += W * 32) {
     int r = i / (D / 8), c = (i % (D / 8)) * 8;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (r < G) {
-      const T *src = qg + int64_t(r) * D + c;
+      const T *src = qg + int64_t(r) * p.q_sh + c;
       if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
         v = *reinterpret_cast<const uint4 *>(src);
       } else {
@@ -167,7 +171,7 @@ __global__ void __launch_bounds__(W * 32, 2) decode_kernel(const DecodeParams p)
     int u = u_begin + warp + lane * W;
     int tok0 = u * kUnit;
     int page = tok0 / p.bs;
-    int blk = p.tables[int64_t(b) * p.max_bps + page];
+    int blk = p.tables[int64_t(b) * p.bt_stride + page];
     if (blk >= 0) {
       uint64_t off = p.offsets[blk];
       int64_t e = int64_t(off) + int64_t(tok0 % p.bs) * row_stride + int64_t(kvh) * D;
@@ -369,7 +373,7 @@ __global__ void __launch_bounds__(W * 32, 2) decode_kernel(const DecodeParams p)
     }
     const float inv = 1.f / L;
     if (n_splits_b == 1) {
-      T *dst = static_cast<T *>(p.out) + (head0 + h) * D + d;
+      T *dst = static_cast<T *>(p.out) + int64_t(b) * p.o_sb + int64_t(lo + h) * p.o_sh + d;
       dst[0] = ptx::from_f32<T>(x0 * inv);
       dst[1] = ptx::from_f32<T>(x1 * inv);
     } else {
@@ -408,7 +412,7 @@ __global__ void merge_kernel(const DecodeParams p, int D, int rows) {
   for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
   const float inv = 1.f / wsum;
   const float *po = p.part_o + int64_t(row) * p.num_splits * D;
-  T *dst = static_cast<T *>(p.out) + int64_t(row) * D;
+  T *dst = static_cast<T *>(p.out) + int64_t(b) * p.o_sb + int64_t(row % p.hq) * p.o_sh;
   for (int d = lane * 4; d < D; d += 128) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
@@ -440,7 +444,7 @@ __global__ void decode_generic_kernel(const DecodeParams p, int D) {
   int seq_len = p.seq_lens[b];
   if (seq_len <= 0) return;
   seq_len = min(seq_len, p.max_bps * p.bs);
-  const T *q = static_cast<const T *>(p.q) + (int64_t(b) * p.hq + h) * D;
+  const T *q = static_cast<const T *>(p.q) + int64_t(b) * p.q_sb + int64_t(h) * p.q_sh;
   float qv[8], acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -452,7 +456,7 @@ __global__ void decode_generic_kernel(const DecodeParams p, int D) {
   const T *vav = static_cast<const T *>(p.va_v);
   float m = -INFINITY, l = 0.f;
   for (int tok = 0; tok < seq_len; ++tok) {
-    int blk = p.tables[int64_t(b) * p.max_bps + tok / p.bs];
+    int blk = p.tables[int64_t(b) * p.bt_stride + tok / p.bs];
     int64_t e = blk < 0 ? -1
                         : int64_t(p.offsets[blk]) + int64_t(tok % p.bs) * p.hkv * D +
                               int64_t(kvh) * D;
@@ -480,7 +484,7 @@ __global__ void decode_generic_kernel(const DecodeParams p, int D) {
     }
   }
   if (l == 0.f) return;
-  T *out = static_cast<T *>(p.out) + (int64_t(b) * p.hq + h) * D;
+  T *out = static_cast<T *>(p.out) + int64_t(b) * p.o_sb + int64_t(h) * p.o_sh;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     int d = lane + 32 * i;
@@ -940,8 +944,17 @@ cudaError_t decode_attention(const DecodeArgs &a, cudaStream_t stream) {
   p.max_bps = a.max_blocks_per_seq;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.diag = a.diag;
+  const int64_t dense_row = int64_t(a.num_q_heads) * a.head_dim;
+  p.q_sb = a.q_stride_token ? a.q_stride_token : dense_row;
+  p.q_sh = a.q_stride_head ? a.q_stride_head : a.head_dim;
+  p.o_sb = a.out_stride_token ? a.out_stride_token : dense_row;
+  p.o_sh = a.out_stride_head ? a.out_stride_head : a.head_dim;
+  p.bt_stride = a.tables_stride ? a.tables_stride : a.max_blocks_per_seq;
+  const bool dense = p.q_sb == dense_row && p.q_sh == a.head_dim && p.o_sb == dense_row &&
+                     p.o_sh == a.head_dim && p.bt_stride == a.max_blocks_per_seq;
 
   SkPlan sp = make_sk_plan(a);
+  if (sp.forced && !dense) return cudaErrorNotSupported;  // stream-K reads dense rows only
   if (sp.ok) return decode_streamk(a, sp, stream);
   if (sp.forced) return cudaErrorNotSupported;
   Plan pl = make_plan(a);

@@ -41,6 +41,9 @@ struct DecodeArgs {
   // (kv_heads, head_dim), or null; region_tokens = tokens they span.
   const void *tensor_maps;
   uint64_t region_tokens;
+  // Element strides of q and out (token, head; head_dim is contiguous) and of the
+  // block-table rows; 0 = dense ([batch][Hq][D] and max_blocks_per_seq).
+  int64_t q_stride_token, q_stride_head, out_stride_token, out_stride_head, tables_stride;
 };
 
 // Bytes of split-K scratch decode_attention needs for these arguments
@@ -104,6 +107,7 @@ struct SlotWriteArgs {
   const void *v_src;
   int32_t *status;  // may be null
   uint64_t region_elems;
+  int64_t k_stride, v_stride;  // elements between source rows; 0 = step_elems
 };
 cudaError_t device_slot_write(const SlotWriteArgs &a, cudaStream_t stream);
 

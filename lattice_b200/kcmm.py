@@ -130,7 +130,8 @@ def library_path() -> Path:
     return path
 
 
-u32, u64, i32, f32 = ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int32, ctypes.c_float
+u32, u64, i32, i64, f32 = (ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int32, ctypes.c_int64,
+                         ctypes.c_float)
 P = ctypes.c_void_p
 pu32 = ctypes.POINTER(ctypes.c_uint32)
 pu64 = ctypes.POINTER(ctypes.c_uint64)
@@ -223,6 +224,14 @@ SIGNATURES: dict[str, tuple] = {
     "kcmm_swap_out_blocks_on_stream": (i32, [P, pu32, u32, u64]),
     "kcmm_swap_in_blocks_on_stream": (i32, [P, pu32, u32, u64]),
     "kcmm_get_kernel_status": (i32, [P]),
+    "kcmm_paged_attn_decode_bf16_strided_on_stream":
+        (i32, [P, u32, u64, i64, i64, u64, i64, i64, u64, i64, u64, u64, u32, u32, u32, u32, u32,
+               u32, f32, u64]),
+    "kcmm_paged_attn_decode_f16_strided_on_stream":
+        (i32, [P, u32, u64, i64, i64, u64, i64, i64, u64, i64, u64, u64, u32, u32, u32, u32, u32,
+               u32, f32, u64]),
+    "kcmm_append_kv_device_slots_strided_on_stream":
+        (i32, [P, u32, u64, u64, u64, u32, u32, u64, i64, u64, i64, u64, u64]),
     "kcmm_start_background_eviction": (i32, [P]),
     "kcmm_stop_background_eviction": (i32, [P]),
     "kcmm_preview_eviction_victims": (u32, [P, u32, pu32, u32]),

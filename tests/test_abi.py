@@ -207,3 +207,25 @@ def test_step_tables_need_a_device_pool(kcmm_lib, host_pool_factory):
     lib.kcmm_step_tables_destroy(None)
     with pytest.raises(kcmm.KcmmError):
         kcmm.StepTables(pool, 8)
+
+
+def test_strided_entry_points_check_strides(kcmm_lib, host_pool_factory):
+    """Head strides below head_dim and table rows shorter than max_blocks_per_seq are
+    refused before any device work (host pool: the checks run first)."""
+    lib = kcmm_lib.lib
+    pool = host_pool_factory(kv_heads=2, head_dim=64, max_batch=4, max_seq_len=256)
+    good = dict(qt=8 * 64, qh=64, ot=8 * 64, oh=64, tr=16)
+
+    def call(**kw):
+        a = {**good, **kw}
+        return lib.kcmm_paged_attn_decode_bf16_strided_on_stream(
+            pool.handle, 0, 1, a["qt"], a["qh"], 2, a["ot"], a["oh"], 3, a["tr"], 4, 5,
+            2, 8, 2, 64, 16, 16, 0.125, 0)
+
+    assert call(qh=32) == -1 and "strides" in pool.last_error()
+    assert call(oh=0) == -1
+    assert call(tr=15) == -1
+    assert call(qt=-1) == -1
+    assert lib.kcmm_append_kv_device_slots_strided_on_stream(
+        pool.handle, 0, 1, 2, 0, 4, 2, 3, 100, 4, 0, 0, 0) == -1  # k stride < kv_heads*D
+    assert "row strides" in pool.last_error()
