@@ -114,6 +114,39 @@ typedef struct {
     uint64_t restoration_count;
 } kcmm_metrics_t;
 
+/** Latency histogram in microseconds; buckets end at 100, 250, 500, 1000, 2500,
+ *  5000, 10000 us and above (ref src/kcmm/metrics.rs:29-74). */
+typedef struct {
+    uint64_t count;
+    uint64_t sum_us;
+    uint64_t min_us;
+    uint64_t max_us;
+    uint64_t buckets[9];
+} kcmm_latency_histogram_t;
+
+/** The reference's extended KcmmMetrics (ref src/kcmm/metrics.rs:77-114), which its C
+ *  ABI does not export: kcmm_metrics_t plus eviction observability. */
+typedef struct {
+    kcmm_metrics_t base;
+    uint64_t evicted_blocks_total;
+    uint64_t restored_blocks_total;
+    uint64_t eviction_failures;
+    uint64_t restoration_failures;
+    uint64_t background_eviction_count;
+    kcmm_latency_histogram_t eviction_latency;
+    kcmm_latency_histogram_t restoration_latency;
+} kcmm_metrics_ext_t;
+
+/** Per-policy counters (ref src/kcmm/metrics.rs:14-20), keyed by the policy active
+ *  when the operation ran. */
+typedef struct {
+    uint64_t eviction_count;
+    uint64_t restoration_count;
+    uint64_t evicted_blocks;
+    uint64_t restored_blocks;
+    double   avg_evict_batch_size;
+} kcmm_policy_stats_t;
+
 /** Pool statistics (ref include/kcmm.h:164-179). */
 typedef struct {
     uint32_t blocks_in_use;
@@ -521,6 +554,13 @@ int kcmm_swap_in_blocks_on_stream(kcmm_pool_t *pool, const uint32_t *blocks,
  * Synchronises the pool's device.  -1 if the pool has no device.
  */
 int32_t kcmm_get_kernel_status(kcmm_pool_t *pool);
+
+/* --- extended metrics (Rust-only in the reference) --- */
+
+/** Fill the extended metrics; -1 on NULL arguments. */
+int kcmm_get_metrics_ext(kcmm_pool_t *pool, kcmm_metrics_ext_t *out);
+/** Counters of one policy name; -1 when none were recorded for it. */
+int kcmm_get_policy_stats(kcmm_pool_t *pool, const char *policy, kcmm_policy_stats_t *out);
 
 /* --- background eviction and victim preview (no C counterpart in the reference) --- */
 

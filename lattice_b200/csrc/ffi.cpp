@@ -852,6 +852,43 @@ int kcmm_get_metrics(kcmm_pool_t *h, kcmm_metrics_t *out) {
   return 0;
 }
 
+static void copy_histogram(const kcmm::LatencyHistogram &h, kcmm_latency_histogram_t *out) {
+  out->count = h.count;
+  out->sum_us = h.sum_us;
+  out->min_us = h.min_us;
+  out->max_us = h.max_us;
+  for (int i = 0; i < 9; ++i) out->buckets[i] = h.buckets[i];
+}
+
+int kcmm_get_metrics_ext(kcmm_pool_t *h, kcmm_metrics_ext_t *out) {
+  if (!h || !out) return -1;
+  kcmm_metrics_ext_t m = {};
+  if (kcmm_get_metrics(h, &m.base) != 0) return -1;
+  kcmm::Metrics c = P(h)->metrics();
+  m.evicted_blocks_total = c.evicted_blocks;
+  m.restored_blocks_total = c.restored_blocks;
+  m.eviction_failures = c.eviction_failures;
+  m.restoration_failures = c.restoration_failures;
+  m.background_eviction_count = c.background_eviction_count;
+  copy_histogram(c.eviction_latency, &m.eviction_latency);
+  copy_histogram(c.restoration_latency, &m.restoration_latency);
+  *out = m;
+  return 0;
+}
+
+int kcmm_get_policy_stats(kcmm_pool_t *h, const char *policy, kcmm_policy_stats_t *out) {
+  if (!h || !policy || !out) return -1;
+  kcmm::Metrics c = P(h)->metrics();
+  auto it = c.policy_stats.find(policy);
+  if (it == c.policy_stats.end()) return -1;
+  out->eviction_count = it->second.eviction_count;
+  out->restoration_count = it->second.restoration_count;
+  out->evicted_blocks = it->second.evicted_blocks;
+  out->restored_blocks = it->second.restored_blocks;
+  out->avg_evict_batch_size = it->second.avg_evict_batch_size;
+  return 0;
+}
+
 int kcmm_get_pool_stats(kcmm_pool_t *h, kcmm_pool_stats_t *out) {
   if (!h || !out) return -1;
   Pool *p = P(h);

@@ -15,6 +15,7 @@
 #include <condition_variable>
 #include <cstddef>
 #include <cstdint>
+#include <map>
 #include <memory>
 #include <mutex>
 #include <stdexcept>
@@ -175,9 +176,27 @@ struct PoolConfig {
   size_t sink_blocks = 1, window_blocks = 4;
 };
 
+// Operation latencies in microseconds, bucketed at 100, 250, 500, 1000, 2500,
+// 5000, 10000 us and above (ref src/kcmm/metrics.rs:29-74).
+struct LatencyHistogram {
+  uint64_t count = 0, sum_us = 0, min_us = 0, max_us = 0;
+  uint64_t buckets[9] = {};
+  void record(uint64_t us);
+};
+
+// Per-policy counters, keyed by the policy active at the time
+// (ref src/kcmm/metrics.rs:14-20, src/kcmm/pool.rs:1263-1292).
+struct PolicyStats {
+  uint64_t eviction_count = 0, restoration_count = 0, evicted_blocks = 0, restored_blocks = 0;
+  double avg_evict_batch_size = 0.0;
+};
+
 struct Metrics {
   uint64_t eviction_count = 0, evicted_blocks = 0, eviction_failures = 0;
   uint64_t restoration_count = 0, restored_blocks = 0, restoration_failures = 0;
+  uint64_t background_eviction_count = 0;
+  LatencyHistogram eviction_latency, restoration_latency;
+  std::map<std::string, PolicyStats> policy_stats;
 };
 
 // Pinned, device-mapped host memory that backs the swap tier.
@@ -300,7 +319,7 @@ class Pool {
   std::vector<uint32_t> select_victims_locked(size_t count);
   void register_positions_locked(size_t seq, size_t from);
   void background_evict_once(float threshold, size_t batch);
-  void swap_out_locked(const std::vector<uint32_t> &ids, void *stream);
+  void swap_out_locked(const std::vector<uint32_t> &ids, void *stream, bool background = false);
   void swap_in_locked(const std::vector<uint32_t> &ids, void *stream);
   SwapTier &tier_locked();
 

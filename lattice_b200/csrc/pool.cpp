@@ -22,6 +22,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cstdint>
 #include <cstring>
 #include <sstream>
 
@@ -876,7 +877,7 @@ void Pool::background_evict_once(float threshold, size_t batch) {
     while (fits < victims.size() && probe.allocate(slot_bytes, &off)) ++fits;
   }
   victims.resize(fits);
-  if (!victims.empty()) swap_out_locked(victims, nullptr);
+  if (!victims.empty()) swap_out_locked(victims, nullptr, true);
 }
 
 SwapTier &Pool::tier_locked() {
@@ -918,8 +919,29 @@ SwapTier &Pool::tier_locked() {
   return *tier_;
 }
 
-void Pool::swap_out_locked(const std::vector<uint32_t> &ids, void *stream) {
+void LatencyHistogram::record(uint64_t us) {
+  // ref src/kcmm/metrics.rs:43-64
+  count += 1;
+  sum_us += us;
+  if (count == 1) {
+    min_us = max_us = us;
+  } else {
+    min_us = std::min(min_us, us);
+    max_us = std::max(max_us, us);
+  }
+  static const uint64_t kBounds[8] = {100, 250, 500, 1000, 2500, 5000, 10000, UINT64_MAX};
+  for (int i = 0; i < 8; ++i) {
+    if (us < kBounds[i]) {
+      buckets[i] += 1;
+      return;
+    }
+  }
+  buckets[8] += 1;
+}
+
+void Pool::swap_out_locked(const std::vector<uint32_t> &ids, void *stream, bool background) {
   if (ids.empty()) return;
+  const auto t0 = std::chrono::steady_clock::now();
   SwapTier &t = tier_locked();
   size_t slot_bytes = num_layers * 2 * block_bytes;
   std::vector<uint64_t> va_off, host_off;
@@ -954,13 +976,27 @@ void Pool::swap_out_locked(const std::vector<uint32_t> &ids, void *stream) {
     bump();
     policy_->on_evict(taken[i]);  // ref src/kcmm/tiering.rs:1177
   }
+  // ref src/kcmm/pool.rs:1255-1272
+  const uint64_t us = uint64_t(std::chrono::duration_cast<std::chrono::microseconds>(
+                                   std::chrono::steady_clock::now() - t0)
+                                   .count());
   metrics_.eviction_count += 1;
   metrics_.evicted_blocks += taken.size();
+  metrics_.eviction_latency.record(us);
+  if (background) metrics_.background_eviction_count += 1;
+  {
+    PolicyStats &ps = metrics_.policy_stats[policy_->name()];
+    ps.eviction_count += 1;
+    ps.evicted_blocks += taken.size();
+    const double n = double(ps.eviction_count);
+    ps.avg_evict_batch_size = (ps.avg_evict_batch_size * (n - 1.0) + double(taken.size())) / n;
+  }
   if (taken.size() < ids.size()) throw Error("swap tier is full");
 }
 
 void Pool::swap_in_locked(const std::vector<uint32_t> &ids, void *stream) {
   if (ids.empty()) return;
+  const auto t0 = std::chrono::steady_clock::now();
   SwapTier &t = tier_locked();
   size_t slot_bytes = num_layers * 2 * block_bytes;
   std::vector<uint64_t> va_off, host_off;
@@ -998,8 +1034,18 @@ void Pool::swap_in_locked(const std::vector<uint32_t> &ids, void *stream) {
     log_block_locked(ids[i]);
     policy_->on_access(ids[i]);  // ref src/kcmm/tiering.rs:1871
   }
+  // ref src/kcmm/pool.rs:1281-1293
+  const uint64_t us = uint64_t(std::chrono::duration_cast<std::chrono::microseconds>(
+                                   std::chrono::steady_clock::now() - t0)
+                                   .count());
   metrics_.restoration_count += 1;
   metrics_.restored_blocks += ids.size();
+  metrics_.restoration_latency.record(us);
+  {
+    PolicyStats &ps = metrics_.policy_stats[policy_->name()];
+    ps.restoration_count += 1;
+    ps.restored_blocks += ids.size();
+  }
 }
 
 size_t Pool::evict(size_t count) {

@@ -62,6 +62,28 @@ class KcmmMetrics(ctypes.Structure):
     ]
 
 
+class KcmmLatencyHistogram(ctypes.Structure):
+    _fields_ = [("count", ctypes.c_uint64), ("sum_us", ctypes.c_uint64),
+                ("min_us", ctypes.c_uint64), ("max_us", ctypes.c_uint64),
+                ("buckets", ctypes.c_uint64 * 9)]
+
+
+class KcmmMetricsExt(ctypes.Structure):
+    _fields_ = [("base", KcmmMetrics), ("evicted_blocks_total", ctypes.c_uint64),
+                ("restored_blocks_total", ctypes.c_uint64),
+                ("eviction_failures", ctypes.c_uint64),
+                ("restoration_failures", ctypes.c_uint64),
+                ("background_eviction_count", ctypes.c_uint64),
+                ("eviction_latency", KcmmLatencyHistogram),
+                ("restoration_latency", KcmmLatencyHistogram)]
+
+
+class KcmmPolicyStats(ctypes.Structure):
+    _fields_ = [("eviction_count", ctypes.c_uint64), ("restoration_count", ctypes.c_uint64),
+                ("evicted_blocks", ctypes.c_uint64), ("restored_blocks", ctypes.c_uint64),
+                ("avg_evict_batch_size", ctypes.c_double)]
+
+
 class KcmmPoolStats(ctypes.Structure):
     _fields_ = [
         ("blocks_in_use", ctypes.c_uint32),
@@ -232,6 +254,8 @@ SIGNATURES: dict[str, tuple] = {
                u32, f32, u64]),
     "kcmm_append_kv_device_slots_strided_on_stream":
         (i32, [P, u32, u64, u64, u64, u32, u32, u64, i64, u64, i64, u64, u64]),
+    "kcmm_get_metrics_ext": (i32, [P, ctypes.c_void_p]),
+    "kcmm_get_policy_stats": (i32, [P, ctypes.c_char_p, ctypes.c_void_p]),
     "kcmm_start_background_eviction": (i32, [P]),
     "kcmm_stop_background_eviction": (i32, [P]),
     "kcmm_preview_eviction_victims": (u32, [P, u32, pu32, u32]),
@@ -659,6 +683,26 @@ class KcmmPool:
         self._check(self.lib.kcmm_swap_in_blocks_on_stream(self.handle, _u32_array(blocks),
                                                            len(blocks), stream_ptr),
                     "kcmm_swap_in_blocks_on_stream")
+
+    def metrics_ext(self) -> dict:
+        m = KcmmMetricsExt()
+        self._check(self.lib.kcmm_get_metrics_ext(self.handle, ctypes.byref(m)),
+                    "kcmm_get_metrics_ext")
+
+        def hist(h):
+            return {"count": h.count, "sum_us": h.sum_us, "min_us": h.min_us,
+                    "max_us": h.max_us, "buckets": list(h.buckets)}
+        out = {name: getattr(m.base, name) for name, _ in m.base._fields_}
+        out.update({name: getattr(m, name) for name, _ in m._fields_[1:6]})
+        out["eviction_latency"] = hist(m.eviction_latency)
+        out["restoration_latency"] = hist(m.restoration_latency)
+        return out
+
+    def policy_stats(self, policy: str) -> dict | None:
+        st = KcmmPolicyStats()
+        if self.lib.kcmm_get_policy_stats(self.handle, policy.encode(), ctypes.byref(st)) != 0:
+            return None
+        return {name: getattr(st, name) for name, _ in st._fields_}
 
     def start_background_eviction(self) -> None:
         self._check(self.lib.kcmm_start_background_eviction(self.handle),

@@ -229,3 +229,39 @@ def test_strided_entry_points_check_strides(kcmm_lib, host_pool_factory):
     assert lib.kcmm_append_kv_device_slots_strided_on_stream(
         pool.handle, 0, 1, 2, 0, 4, 2, 3, 100, 4, 0, 0, 0) == -1  # k stride < kv_heads*D
     assert "row strides" in pool.last_error()
+
+
+def test_extended_metrics_layout_and_host_values(kcmm_lib, host_pool_factory, tmp_path):
+    """kcmm_metrics_ext_t / kcmm_policy_stats_t as a C compiler lays them out equal the
+    ctypes mirrors; a pool that never swapped reports zeros and no policy stats."""
+    from lattice_b200 import kcmm
+
+    src = tmp_path / "layout.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include <stddef.h>
+#include "kcmm.h"
+int main(void) {
+  printf("%zu %zu %zu %zu %zu\n", sizeof(kcmm_metrics_ext_t),
+         offsetof(kcmm_metrics_ext_t, background_eviction_count),
+         offsetof(kcmm_metrics_ext_t, eviction_latency),
+         offsetof(kcmm_metrics_ext_t, restoration_latency), sizeof(kcmm_policy_stats_t));
+  return 0;
+}
+''')
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", f"-I{ROOT / 'include'}", str(src), "-o", str(exe)],
+                   check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True,
+                                          check=True).stdout.split()]
+    E = kcmm.KcmmMetricsExt
+    assert got == [ctypes.sizeof(E), E.background_eviction_count.offset,
+                   E.eviction_latency.offset, E.restoration_latency.offset,
+                   ctypes.sizeof(kcmm.KcmmPolicyStats)]
+    pool = host_pool_factory(kv_heads=2, head_dim=64, max_batch=4, max_seq_len=256,
+                             tiering=True, max_blocks=16)
+    m = pool.metrics_ext()
+    assert m["evicted_blocks_total"] == 0 and m["background_eviction_count"] == 0
+    assert m["eviction_latency"]["count"] == 0 and m["restoration_latency"]["count"] == 0
+    assert pool.policy_stats("lru") is None
+    assert kcmm_lib.lib.kcmm_get_metrics_ext(None, None) == -1

@@ -83,6 +83,19 @@ def test_evict_takes_the_policy_victims_and_restores_bit_exact(policy):
                    if pool.all_block_valid_flags()[b] and pool.block_location(b) == "cpu"]
         assert sorted(evicted) == sorted(preview)
         pool.restore_evicted_blocks(preview)
+        # ref src/kcmm/pool.rs:1255-1293: one eviction and one restoration, under the
+        # policy that was active
+        st = pool.policy_stats(policy)
+        assert st["eviction_count"] == 1 and st["evicted_blocks"] == n
+        assert st["avg_evict_batch_size"] == pytest.approx(n)
+        assert st["restoration_count"] == 1 and st["restored_blocks"] == n
+        m = pool.metrics_ext()
+        for key in ("eviction_latency", "restoration_latency"):
+            h = m[key]
+            assert h["count"] == 1 and sum(h["buckets"]) == 1
+            assert h["min_us"] == h["max_us"] == h["sum_us"]
+        assert m["evicted_blocks_total"] == n and m["restored_blocks_total"] == n
+        assert m["background_eviction_count"] == 0
         for b in preview:
             assert pool.block_location(b) == "gpu"
             got = _block_bytes(pool, layers, b, pool.block_va_offset(b))
@@ -122,6 +135,11 @@ def test_background_thread_evicts_only_inactive_sequences():
         m = pool.metrics()
         assert m["cpu_blocks"] == len(cold_blocks)
         assert m["eviction_count"] >= 2  # at most 16 blocks per round
+        ext = pool.metrics_ext()
+        assert ext["background_eviction_count"] == m["eviction_count"]
+        assert ext["evicted_blocks_total"] == len(cold_blocks)
+        st = pool.policy_stats("lru")
+        assert st["avg_evict_batch_size"] == pytest.approx(len(cold_blocks) / st["eviction_count"])
         pool.restore_evicted_blocks(cold_blocks)
         for b in cold_blocks:
             got = _block_bytes(pool, layers, b, pool.block_va_offset(b))[(0, "k")]
