@@ -853,12 +853,17 @@ def run_headsplit_leg(args):
     """Llama-3-70B decode with KV heads sharded across the N ranks:
     8 sequences of 32,768 tokens, 64 q heads / 8 kv heads, D 128, bf16.  Rank r holds
     kv heads [r*8/N, (r+1)*8/N) and their query heads for every sequence; a step is the
-    paged decode of the rank's heads followed by an NCCL all-gather of the per-head
-    outputs ([8, 64/N, 128] bf16 per rank) so every rank holds the full [8, 64, 128].
-    Strong scaling: the total work is fixed as N grows."""
+    paged decode of the rank's heads followed by an all-gather of the per-head outputs
+    ([8, 64/N, 128] bf16 per rank) so every rank holds the full [8, 64, 128].  The
+    all-gather runs two ways: `kcmm_peer_allgather_on_stream` + `kcmm_peer_wait_on_stream`
+    (stores into the peers' buffers over NVLink and per-CTA flags) and NCCL
+    all_gather_into_tensor; the value line counts the faster one, both are reported, and
+    the leg checks that both gather the same bytes.  Strong scaling: the total work is fixed as N grows."""
+    import ctypes
+
     import torch
 
-    from lattice_b200.workloads import DecodeWorkload
+    from lattice_b200.workloads import DecodeWorkload, PeerBuffers, library
 
     world, rank, local = dist_setup(args)
     torch.cuda.set_device(local)
@@ -875,24 +880,57 @@ def run_headsplit_leg(args):
     sp = stream.cuda_stream
     import torch.distributed as dist
 
-    def step():
+    lib = library().lib
+    slice_bytes = wl.out.numel() * wl.out.element_size()
+    pb = PeerBuffers(slice_bytes, rank, world, local) if world > 1 else None
+    status = torch.zeros(1, dtype=torch.int32, device=f"cuda:{local}")
+    if pb is not None:
+        dst = (ctypes.c_uint64 * world)(*pb.buf_ptrs)
+        sig = (ctypes.c_uint64 * world)(*pb.sig_ptrs)
+
+    def step_nccl():
         wl.decode(stream_ptr=sp)
         if world > 1:
             dist.all_gather_into_tensor(gathered, wl.out)
         else:
             gathered[0].copy_(wl.out)
 
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize()
-    barrier()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for _ in range(args.steps):
-        step()
-    t1.record(stream)
-    torch.cuda.synchronize()
-    ms = max_over_ranks(t0.elapsed_time(t1)) / args.steps
+    def step_p2p():
+        wl.decode(stream_ptr=sp)
+        pb.epoch += 1
+        assert lib.kcmm_peer_allgather_on_stream(wl.out.data_ptr(), slice_bytes, dst, sig, rank,
+                                                 world, pb.epoch, sp) == 0
+        assert lib.kcmm_peer_wait_on_stream(pb.signal_ptr, world, pb.epoch, status.data_ptr(),
+                                            sp) == 0
+
+    def timed(step):
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        return max_over_ranks(t0.elapsed_time(t1)) / args.steps
+
+    ms_nccl = timed(step_nccl)
+    same = True
+    ms_p2p = None
+    if pb is not None:
+        ms_p2p = timed(step_p2p)
+        torch.cuda.synchronize()
+        from lattice_b200.workloads import read_device
+        import numpy as np
+
+        got = read_device(pb.gathered_ptr, slice_bytes * world)
+        ref = gathered.view(torch.int16).cpu().numpy().view(np.uint8).reshape(-1)
+        same = bool((got == ref).all()) and int(status.item()) == 0
+    # the value line uses the faster of the two gathers; both are reported
+    ms = min(ms_p2p, ms_nccl) if ms_p2p is not None else ms_nccl
+    used = "p2p" if ms_p2p is not None and ms_p2p <= ms_nccl else "nccl"
     # attention alone, for the split of the step
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a0.record(stream)
@@ -902,7 +940,10 @@ def run_headsplit_leg(args):
     torch.cuda.synchronize()
     attn_ms = max_over_ranks(a0.elapsed_time(a1)) / args.steps
     kv_total = wl.kv_bytes() * world  # every rank reads its own heads' pages
-    status = wl.pool.kernel_status()
+    status_word = wl.pool.kernel_status()
+    if pb is not None:
+        barrier()
+        pb.close()
     wl.close()
     peak, kind = peaks()
     line = None
@@ -913,15 +954,21 @@ def run_headsplit_leg(args):
             "GB/s",
             {"workload": "BASELINE config 5 decode: 8 seqs x 32768 tokens, Hq 64 / Hkv 8, "
                          "D 128, bf16; kv heads sharded over the ranks, outputs all-gathered "
-                         "(NCCL)", "ranks": world, "scaling": "strong"},
+                         "(NVLink peer stores and NCCL, the faster one counted)", "ranks": world,
+             "scaling": "strong"},
             {"bound": "hbm", "achieved": round(gbs / world, 1), "peak": peak, "unit": "GB/s",
              "frac": round(gbs / world / peak, 4), "traffic": None, "peak_kind": kind,
              "per": "GPU"},
             {"n_gpus": world, "ms_per_step": round(ms, 4),
              "attention_ms": round(attn_ms, 4),
              "allgather_ms": round(max(ms - attn_ms, 0.0), 4),
+             "allgather_used": used,
+             "ms_per_step_p2p_allgather": round(ms_p2p, 4) if ms_p2p is not None else None,
+             "ms_per_step_nccl_allgather": round(ms_nccl, 4),
+             "allgather_ms_nccl": round(max(ms_nccl - attn_ms, 0.0), 4),
+             "p2p_equals_nccl": same,
              "tokens_per_s_80_layers": round(seqs / (80 * ms * 1e-3), 1),
-             "status": status})
+             "status": status_word})
     if world > 1:
         barrier()
         dist.destroy_process_group()

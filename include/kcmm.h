@@ -555,6 +555,28 @@ int kcmm_swap_in_blocks_on_stream(kcmm_pool_t *pool, const uint32_t *blocks,
  */
 int32_t kcmm_get_kernel_status(kcmm_pool_t *pool);
 
+/* --- all-gather over NVLink peer memory (KV-head split, no reference counterpart) --- */
+
+/*
+ * The KV-head split of the decode (each GPU attends its own kv heads) needs every
+ * rank's output on every rank; the reference plan uses ncclAllGather.  These
+ * two calls do it with plain stores into peers' memory and per-CTA flags:
+ *   dst_ptrs[r]    rank r's gathered buffer (world slices of nbytes), mapped on
+ *                  this device (CUDA IPC or P2P); slice `rank` is written here;
+ *   signal_ptrs[r] rank r's signal array, kcmm_peer_signal_words(world) u64
+ *                  flags, zeroed once; every call raises this rank's flags there
+ *                  to `epoch`, which must grow by one per call on every rank.
+ * kcmm_peer_wait_on_stream then waits (bounded, 1 s) until all ranks' flags in
+ * this rank's signal array reached epoch; on a timeout it writes 1 to *status.
+ * nbytes must be a multiple of 16 and world <= 8.  -1 on invalid arguments.
+ */
+uint32_t kcmm_peer_signal_words(uint32_t world);
+int kcmm_peer_allgather_on_stream(uint64_t src_ptr, uint64_t nbytes, const uint64_t *dst_ptrs,
+                                  const uint64_t *signal_ptrs, uint32_t rank, uint32_t world,
+                                  uint64_t epoch, uint64_t stream_ptr);
+int kcmm_peer_wait_on_stream(uint64_t signal_ptr, uint32_t world, uint64_t epoch,
+                             uint64_t status_ptr, uint64_t stream_ptr);
+
 /* --- extended metrics (Rust-only in the reference) --- */
 
 /** Fill the extended metrics; -1 on NULL arguments. */

@@ -28,7 +28,8 @@ ALIAS = PKG / "libbaseline_llm_os.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CU_SOURCES = ["kernels/decode.cu", "kernels/decode_noalloc.cu", "kernels/append.cu",
-              "kernels/copy.cu", "kernels/prefill.cu", "kernels/tables.cu"]
+              "kernels/copy.cu", "kernels/prefill.cu", "kernels/tables.cu",
+              "kernels/peer.cu"]
 CPP_SOURCES = ["pool.cpp", "vmm.cpp", "ffi.cpp", "step_tables.cpp", "policy.cpp"]
 HEADERS = ["kcmm_internal.hpp", "launch.hpp", "kernels/ptx.cuh", "kernels/decode_streamk.cuh",
            "kernels/tcgen05.cuh", "kernels/pdl.cuh",

@@ -1083,6 +1083,44 @@ int32_t kcmm_get_kernel_status(kcmm_pool_t *h) {
 
 const char *kcmm_build_info(void) { return "kcmm-b200 0.1.0 sm_100a"; }
 
+// --- all-gather over NVLink peer memory -------------------------------------------
+
+uint32_t kcmm_peer_signal_words(uint32_t world) {
+  return world >= 1 && world <= uint32_t(kcmm::dev::kMaxPeers)
+             ? world * uint32_t(kcmm::dev::kGatherBlocks)
+             : 0;
+}
+
+int kcmm_peer_allgather_on_stream(uint64_t src, uint64_t nbytes, const uint64_t *dst_ptrs,
+                                  const uint64_t *sig_ptrs, uint32_t rank, uint32_t world,
+                                  uint64_t epoch, uint64_t stream) {
+  if (!src || !dst_ptrs || !sig_ptrs || world == 0 || world > uint32_t(kcmm::dev::kMaxPeers) ||
+      rank >= world || nbytes == 0 || nbytes % 16 != 0 || epoch == 0)
+    return -1;
+  void *dst[kcmm::dev::kMaxPeers];
+  unsigned long long *sig[kcmm::dev::kMaxPeers];
+  for (uint32_t r = 0; r < world; ++r) {
+    if (!dst_ptrs[r] || !sig_ptrs[r] || dst_ptrs[r] % 16 != 0 || sig_ptrs[r] % 8 != 0) return -1;
+    dst[r] = reinterpret_cast<void *>(dst_ptrs[r]);
+    sig[r] = reinterpret_cast<unsigned long long *>(sig_ptrs[r]);
+  }
+  return kcmm::dev::peer_allgather(reinterpret_cast<const void *>(src), nbytes, dst, sig,
+                                   int(rank), int(world), epoch, S(stream)) == cudaSuccess
+             ? 0
+             : -1;
+}
+
+int kcmm_peer_wait_on_stream(uint64_t sig, uint32_t world, uint64_t epoch, uint64_t status,
+                             uint64_t stream) {
+  if (!sig || sig % 8 != 0 || world == 0 || world > uint32_t(kcmm::dev::kMaxPeers) || epoch == 0)
+    return -1;
+  return kcmm::dev::peer_wait(reinterpret_cast<const unsigned long long *>(sig), int(world),
+                              epoch, reinterpret_cast<int32_t *>(status),
+                              S(stream)) == cudaSuccess
+             ? 0
+             : -1;
+}
+
 // --- background eviction and victim preview ------------------------------------
 
 int kcmm_start_background_eviction(kcmm_pool_t *h) {

@@ -82,6 +82,19 @@ struct PrefillArgs {
 // (kernels/prefill.cu).  head_dim 128; num_q_heads / kv_heads must divide 128.
 cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream);
 
+// All-gather over NVLink peer memory (kernels/peer.cu).  dst[r] is rank r's
+// gathered buffer (world slices of nbytes, P2P-accessible from this device),
+// sig[r] rank r's signal array of world * kGatherBlocks u64 flags.
+constexpr int kMaxPeers = 8;
+constexpr int kGatherBlocks = 16;
+cudaError_t peer_allgather(const void *src, uint64_t nbytes, void *const *dst,
+                           unsigned long long *const *sig, int rank, int world,
+                           unsigned long long epoch, cudaStream_t stream);
+// Wait (bounded, 1 s) until every flag of this rank's signal array reaches epoch;
+// a timeout writes 1 to *status.
+cudaError_t peer_wait(const unsigned long long *sig, int world, unsigned long long epoch,
+                      int32_t *status, cudaStream_t stream);
+
 // Apply a packed step-table update list (kernels/tables.cu): 32-bit entries into
 // i32 and 64-bit entries into o64.
 cudaError_t apply_table_updates(const void *stage, int n32, int n64, size_t off64, int32_t *i32,

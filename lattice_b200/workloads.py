@@ -349,3 +349,75 @@ def cuda_stream_ptr() -> int:
 
 
 _ = ctypes  # keep ctypes imported for users building raw pointers
+
+
+class PeerBuffers:
+    """A gathered-output buffer and a signal array per rank, mapped on every rank
+    through CUDA IPC, for `kcmm_peer_allgather_on_stream` / `kcmm_peer_wait_on_stream`.
+
+    Collective over the default process group: every rank allocates its own buffer
+    (world slices of `slice_bytes`) and signal array, publishes their IPC handles
+    with `all_gather_object`, and opens the peers'.  Pointers are indexed by rank;
+    this rank's entries are its own allocations."""
+
+    def __init__(self, slice_bytes: int, rank: int, world: int, device: int):
+        import torch.distributed as dist
+
+        rt = _cudart()
+        torch = _torch()
+        torch.cuda.set_device(device)
+        self.rank, self.world, self.slice_bytes = rank, world, slice_bytes
+        self.sig_words = int(library().lib.kcmm_peer_signal_words(world))
+        self._own = []
+        self._opened = []
+        handles = []
+        for nbytes in (slice_bytes * world, self.sig_words * 8):
+            err, ptr = rt.cudaMalloc(nbytes)
+            if int(err) != 0:
+                raise RuntimeError(f"cudaMalloc failed: {err}")
+            (err,) = rt.cudaMemset(ptr, 0, nbytes)
+            if int(err) != 0:
+                raise RuntimeError(f"cudaMemset failed: {err}")
+            err, h = rt.cudaIpcGetMemHandle(ptr)
+            if int(err) != 0:
+                raise RuntimeError(f"cudaIpcGetMemHandle failed: {err}")
+            self._own.append(int(ptr))
+            handles.append(bytes(h.reserved))
+        (err,) = rt.cudaDeviceSynchronize()
+        everyone = [None] * world
+        dist.all_gather_object(everyone, handles)
+        self.buf_ptrs, self.sig_ptrs = [], []
+        for r in range(world):
+            if r == rank:
+                self.buf_ptrs.append(self._own[0])
+                self.sig_ptrs.append(self._own[1])
+                continue
+            opened = []
+            for raw in everyone[r]:
+                h = rt.cudaIpcMemHandle_t()
+                h.reserved = raw
+                err, ptr = rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess)
+                if int(err) != 0:
+                    raise RuntimeError(f"cudaIpcOpenMemHandle failed: {err}")
+                opened.append(int(ptr))
+                self._opened.append(int(ptr))
+            self.buf_ptrs.append(opened[0])
+            self.sig_ptrs.append(opened[1])
+        self.epoch = 0
+
+    @property
+    def gathered_ptr(self) -> int:
+        return self._own[0]
+
+    @property
+    def signal_ptr(self) -> int:
+        return self._own[1]
+
+    def close(self) -> None:
+        rt = _cudart()
+        rt.cudaDeviceSynchronize()
+        for p in self._opened:
+            rt.cudaIpcCloseMemHandle(p)
+        for p in self._own:
+            rt.cudaFree(p)
+        self._opened, self._own = [], []

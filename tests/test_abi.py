@@ -265,3 +265,18 @@ int main(void) {
     assert m["eviction_latency"]["count"] == 0 and m["restoration_latency"]["count"] == 0
     assert pool.policy_stats("lru") is None
     assert kcmm_lib.lib.kcmm_get_metrics_ext(None, None) == -1
+
+
+def test_peer_allgather_argument_checks(kcmm_lib):
+    """Checked before any device work: NULL pointers, world outside 1..8, a rank outside
+    the world, sizes that are not whole 16-byte chunks, epoch 0."""
+    lib = kcmm_lib.lib
+    assert lib.kcmm_peer_signal_words(2) == 32 and lib.kcmm_peer_signal_words(9) == 0
+    ptrs = (ctypes.c_uint64 * 2)(16, 32)
+    assert lib.kcmm_peer_allgather_on_stream(0, 16, ptrs, ptrs, 0, 2, 1, 0) == -1
+    assert lib.kcmm_peer_allgather_on_stream(16, 16, ptrs, ptrs, 2, 2, 1, 0) == -1
+    assert lib.kcmm_peer_allgather_on_stream(16, 24, ptrs, ptrs, 0, 2, 1, 0) == -1
+    assert lib.kcmm_peer_allgather_on_stream(16, 16, ptrs, ptrs, 0, 9, 1, 0) == -1
+    assert lib.kcmm_peer_allgather_on_stream(16, 16, ptrs, ptrs, 0, 2, 0, 0) == -1
+    assert lib.kcmm_peer_wait_on_stream(0, 2, 1, 0, 0) == -1
+    assert lib.kcmm_peer_wait_on_stream(8, 0, 1, 0, 0) == -1

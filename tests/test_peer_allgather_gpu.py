@@ -1,0 +1,105 @@
+"""All-gather over NVLink peer memory (`kcmm_peer_allgather_on_stream` and
+`kcmm_peer_wait_on_stream`) with two ranks, one GPU each; skipped with fewer than two
+GPUs.  Every rank's gathered buffer must hold every rank's slice after the wait, over
+several epochs with changing data.  A wait for a rank that never raises its flags
+returns after its 1 s bound with status 1, and the GPU stays usable."""
+from __future__ import annotations
+
+import json
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
+    import ctypes
+    import datetime
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(ROOT))
+    from lattice_b200.workloads import PeerBuffers, library, read_device
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=60))
+    lib = library().lib
+    result = {"ok": True}
+    pb = None
+    try:
+        slice_bytes = 8 * 32 * 128 * 2  # one rank's [8, 32, 128] bf16 output
+        pb = PeerBuffers(slice_bytes, rank, world, rank)
+        dst = (ctypes.c_uint64 * world)(*pb.buf_ptrs)
+        sig = (ctypes.c_uint64 * world)(*pb.sig_ptrs)
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        sp = torch.cuda.current_stream().cuda_stream
+        for epoch in range(1, 5):
+            src = torch.full((slice_bytes // 2,), float(rank * 10 + epoch), device="cuda")
+            src = src.bfloat16()
+            assert lib.kcmm_peer_allgather_on_stream(src.data_ptr(), slice_bytes, dst, sig, rank,
+                                                     world, epoch, sp) == 0
+            assert lib.kcmm_peer_wait_on_stream(pb.signal_ptr, world, epoch, status.data_ptr(),
+                                                sp) == 0
+            torch.cuda.synchronize()
+            got = read_device(pb.gathered_ptr, slice_bytes * world).view(np.uint16)
+            for r in range(world):
+                want = torch.full((1,), float(r * 10 + epoch)).bfloat16().view(torch.int16)
+                part = got[r * slice_bytes // 2:(r + 1) * slice_bytes // 2]
+                if not (part == np.uint16(want.item() & 0xFFFF)).all():
+                    result["ok"] = False
+            result[f"status_{epoch}"] = int(status.item())
+            dist.barrier()
+        # rank 1 skips epoch 5: rank 0's wait runs out and reports it
+        if rank == 0:
+            assert lib.kcmm_peer_allgather_on_stream(src.data_ptr(), slice_bytes, dst, sig, rank,
+                                                     world, 5, sp) == 0
+            assert lib.kcmm_peer_wait_on_stream(pb.signal_ptr, world, 5, status.data_ptr(),
+                                                sp) == 0
+            torch.cuda.synchronize()
+            result["timeout_status"] = int(status.item())
+            # the context is still usable
+            result["after"] = float((torch.ones(4, device="cuda") * 2).sum().item())
+        dist.barrier()
+        # argument checks
+        result["bad_world"] = lib.kcmm_peer_allgather_on_stream(
+            src.data_ptr(), slice_bytes, dst, sig, rank, 9, 6, sp)
+        result["bad_bytes"] = lib.kcmm_peer_allgather_on_stream(
+            src.data_ptr(), 24, dst, sig, rank, world, 6, sp)
+    finally:
+        if pb is not None:
+            dist.barrier()
+            pb.close()
+        Path(out_dir, f"rank{rank}.json").write_text(json.dumps(result))
+        dist.destroy_process_group()
+
+
+def test_two_rank_peer_allgather(tmp_path):
+    import torch
+
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    port = _free_port()
+    mp.start_processes(_rank_main, args=(2, port, str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    r0 = json.loads((tmp_path / "rank0.json").read_text())
+    r1 = json.loads((tmp_path / "rank1.json").read_text())
+    for r in (r0, r1):
+        assert r["ok"]
+        assert all(r[f"status_{e}"] == 0 for e in range(1, 5))
+        assert r["bad_world"] == -1 and r["bad_bytes"] == -1
+    assert r0["timeout_status"] == 1 and r0["after"] == 8.0
