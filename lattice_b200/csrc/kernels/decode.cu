@@ -516,22 +516,6 @@ KernelFn fast_kernel() {
   return decode_kernel<T, D, kWarps, kStages>;
 }
 
-constexpr int kDeepStages = 6;
-
-template <typename T>
-KernelFn deep_kernel() {
-  return decode_kernel<T, 128, kWarps, kDeepStages>;
-}
-
-// KCMM_DECODE_DEEP=0 keeps the 3-stage kernel for every grid (read once).
-bool deep_ring_enabled() {
-  static const bool on = [] {
-    const char *v = std::getenv("KCMM_DECODE_DEEP");
-    return !(v && std::strcmp(v, "0") == 0);
-  }();
-  return on;
-}
-
 template <typename T>
 bool pick_fast(int D, KernelFn *fn, size_t *smem) {
   switch (D) {
@@ -615,13 +599,6 @@ Plan make_plan(const DecodeArgs &a) {
   if (a.force_splits > 0) ups = std::max(1, std::min((max_units + a.force_splits - 1) / a.force_splits, 32 * kWarps));
   pl.units_per_split = ups;
   pl.num_splits = (max_units + ups - 1) / ups;
-  // A grid that fits in one wave at one CTA per SM (few items, long contexts)
-  // takes the deep-ring variant: 6 stages per warp fill the SM's shared memory,
-  // so each CTA keeps twice the bytes in flight.
-  if (D == 128 && items * pl.num_splits <= sm_count() && deep_ring_enabled()) {
-    pl.fn = a.dtype == Dtype::BF16 ? deep_kernel<__nv_bfloat16>() : deep_kernel<__half>();
-    pl.smem = Cfg<__nv_bfloat16, 128, kWarps, kDeepStages>::SMEM;
-  }
   if (pl.num_splits > 1) {
     size_t rows = size_t(a.batch) * a.num_q_heads * pl.num_splits;
     pl.scratch_bytes = rows * size_t(D) * 4 + rows * 4;
