@@ -855,10 +855,13 @@ def run_headsplit_leg(args):
     kv heads [r*8/N, (r+1)*8/N) and their query heads for every sequence; a step is the
     paged decode of the rank's heads followed by an all-gather of the per-head outputs
     ([8, 64/N, 128] bf16 per rank) so every rank holds the full [8, 64, 128].  The
-    all-gather runs two ways: `kcmm_peer_allgather_on_stream` + `kcmm_peer_wait_on_stream`
-    (stores into the peers' buffers over NVLink and per-CTA flags) and NCCL
-    all_gather_into_tensor; the value line counts the faster one, both are reported, and
-    the leg checks that both gather the same bytes.  Strong scaling: the total work is fixed as N grows."""
+    all-gather runs three ways: NCCL all_gather_into_tensor after the decode;
+    `kcmm_peer_allgather_on_stream` + `kcmm_peer_wait_on_stream` after the decode (stores
+    into the peers' buffers over NVLink and per-CTA flags); and
+    `kcmm_paged_attn_decode_bf16_allgather_on_stream` + the wait, where the decode's
+    merge kernel stores the rows into the peers' buffers itself.  The value line counts
+    the fastest, all are reported, and the leg checks that all gather the same bytes.
+    Strong scaling: the total work is fixed as N grows."""
     import ctypes
 
     import torch
@@ -887,6 +890,14 @@ def run_headsplit_leg(args):
     if pb is not None:
         dst = (ctypes.c_uint64 * world)(*pb.buf_ptrs)
         sig = (ctypes.c_uint64 * world)(*pb.sig_ptrs)
+        sig_local = pb.signal_ptr
+    else:  # one rank: the fused decode gathers into its own buffer
+        own_sig = torch.zeros(lib.kcmm_peer_signal_words(1), dtype=torch.int64,
+                              device=f"cuda:{local}")
+        dst = (ctypes.c_uint64 * 1)(gathered.data_ptr())
+        sig = (ctypes.c_uint64 * 1)(own_sig.data_ptr())
+        sig_local = own_sig.data_ptr()
+    epoch = [0]
 
     def step_nccl():
         wl.decode(stream_ptr=sp)
@@ -903,6 +914,17 @@ def run_headsplit_leg(args):
         assert lib.kcmm_peer_wait_on_stream(pb.signal_ptr, world, pb.epoch, status.data_ptr(),
                                             sp) == 0
 
+    def step_fused():
+        # the split merge stores the rows straight into every rank's buffer
+        epoch[0] += 1
+        assert lib.kcmm_paged_attn_decode_bf16_allgather_on_stream(
+            wl.pool.handle, 0, wl.q.data_ptr(), wl.out.data_ptr(), wl.d_tables.data_ptr(),
+            wl.d_seq_lens.data_ptr(), wl.d_offsets.data_ptr(), wl.batch, wl.num_q_heads,
+            wl.kv_heads, wl.head_dim, wl.block_size, wl.max_blocks_per_seq, wl.scale, dst, sig,
+            rank, world, epoch[0], sp) == 0, wl.pool.last_error()
+        assert lib.kcmm_peer_wait_on_stream(sig_local, world, epoch[0], status.data_ptr(),
+                                            sp) == 0
+
     def timed(step):
         for _ in range(max(args.warmup, 3)):
             step()
@@ -916,21 +938,32 @@ def run_headsplit_leg(args):
         torch.cuda.synchronize()
         return max_over_ranks(t0.elapsed_time(t1)) / args.steps
 
+    from lattice_b200.workloads import read_device
+    import numpy as np
+
     ms_nccl = timed(step_nccl)
+    ref = gathered.view(torch.int16).cpu().numpy().view(np.uint8).reshape(-1).copy()
     same = True
     ms_p2p = None
     if pb is not None:
+        # the p2p epochs share the signal arrays with the fused epochs
+        pb.epoch = epoch[0]
         ms_p2p = timed(step_p2p)
+        epoch[0] = pb.epoch
         torch.cuda.synchronize()
-        from lattice_b200.workloads import read_device
-        import numpy as np
-
         got = read_device(pb.gathered_ptr, slice_bytes * world)
-        ref = gathered.view(torch.int16).cpu().numpy().view(np.uint8).reshape(-1)
         same = bool((got == ref).all()) and int(status.item()) == 0
-    # the value line uses the faster of the two gathers; both are reported
-    ms = min(ms_p2p, ms_nccl) if ms_p2p is not None else ms_nccl
-    used = "p2p" if ms_p2p is not None and ms_p2p <= ms_nccl else "nccl"
+    ms_fused = timed(step_fused)
+    torch.cuda.synchronize()
+    got = (read_device(pb.gathered_ptr, slice_bytes * world) if pb is not None
+           else gathered.view(torch.int16).cpu().numpy().view(np.uint8).reshape(-1))
+    fused_same = bool((got == ref).all()) and int(status.item()) == 0
+    # the value line uses the fastest of the gathers; all are reported
+    options = {"nccl": ms_nccl, "fused_p2p": ms_fused}
+    if ms_p2p is not None:
+        options["p2p"] = ms_p2p
+    used = min(options, key=options.get)
+    ms = options[used]
     # attention alone, for the split of the step
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a0.record(stream)
@@ -954,7 +987,8 @@ def run_headsplit_leg(args):
             "GB/s",
             {"workload": "BASELINE config 5 decode: 8 seqs x 32768 tokens, Hq 64 / Hkv 8, "
                          "D 128, bf16; kv heads sharded over the ranks, outputs all-gathered "
-                         "(NVLink peer stores and NCCL, the faster one counted)", "ranks": world,
+                         "(NCCL, NVLink peer stores, and peer stores fused into the decode's "
+                         "merge; the fastest counted)", "ranks": world,
              "scaling": "strong"},
             {"bound": "hbm", "achieved": round(gbs / world, 1), "peak": peak, "unit": "GB/s",
              "frac": round(gbs / world / peak, 4), "traffic": None, "peak_kind": kind,
@@ -965,6 +999,8 @@ def run_headsplit_leg(args):
              "allgather_used": used,
              "ms_per_step_p2p_allgather": round(ms_p2p, 4) if ms_p2p is not None else None,
              "ms_per_step_nccl_allgather": round(ms_nccl, 4),
+             "ms_per_step_fused_decode_allgather": round(ms_fused, 4),
+             "fused_equals_nccl": fused_same,
              "allgather_ms_nccl": round(max(ms_nccl - attn_ms, 0.0), 4),
              "p2p_equals_nccl": same,
              "tokens_per_s_80_layers": round(seqs / (80 * ms * 1e-3), 1),

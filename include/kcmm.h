@@ -577,6 +577,34 @@ int kcmm_peer_allgather_on_stream(uint64_t src_ptr, uint64_t nbytes, const uint6
 int kcmm_peer_wait_on_stream(uint64_t signal_ptr, uint32_t world, uint64_t epoch,
                              uint64_t status_ptr, uint64_t stream_ptr);
 
+/*
+ * The decode of kcmm_paged_attn_decode_{bf16,f16}_on_stream fused with the
+ * all-gather above: the kernel that merges the split partials also stores every
+ * finished output row into slot `rank` of every rank's gathered buffer
+ * (gathered_ptrs[r], [world][batch][num_q_heads][head_dim] 16-bit values, 16-byte
+ * aligned) and then raises this rank's flags in signal_ptrs[r] to `epoch`, as
+ * kcmm_peer_allgather_on_stream does, so no separate gather kernel runs.
+ * `output_ptr` receives this rank's rows as usual.  Follow with
+ * kcmm_peer_wait_on_stream.  Sequences of length 0 leave their rows untouched
+ * everywhere.  Only the tensor-core decode path takes peers (head_dim 32, 64, 80,
+ * 96, 112, 128, 160, 192 or 256 and block_size a multiple of 16); -1 otherwise.
+ * Replaces the decode + ncclAllGather pair of the reference's KV-head split plan.
+ */
+int kcmm_paged_attn_decode_bf16_allgather_on_stream(
+    kcmm_pool_t *pool, uint32_t layer_idx, uint64_t query_ptr, uint64_t output_ptr,
+    uint64_t block_tables_ptr, uint64_t seq_lens_ptr, uint64_t block_offsets_ptr,
+    uint32_t batch_size, uint32_t num_q_heads, uint32_t num_kv_heads, uint32_t head_dim,
+    uint32_t block_size, uint32_t max_blocks_per_seq, float scale, const uint64_t *gathered_ptrs,
+    const uint64_t *signal_ptrs, uint32_t rank, uint32_t world, uint64_t epoch,
+    uint64_t stream_ptr);
+int kcmm_paged_attn_decode_f16_allgather_on_stream(
+    kcmm_pool_t *pool, uint32_t layer_idx, uint64_t query_ptr, uint64_t output_ptr,
+    uint64_t block_tables_ptr, uint64_t seq_lens_ptr, uint64_t block_offsets_ptr,
+    uint32_t batch_size, uint32_t num_q_heads, uint32_t num_kv_heads, uint32_t head_dim,
+    uint32_t block_size, uint32_t max_blocks_per_seq, float scale, const uint64_t *gathered_ptrs,
+    const uint64_t *signal_ptrs, uint32_t rank, uint32_t world, uint64_t epoch,
+    uint64_t stream_ptr);
+
 /* --- extended metrics (Rust-only in the reference) --- */
 
 /** Fill the extended metrics; -1 on NULL arguments. */

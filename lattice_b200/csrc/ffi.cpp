@@ -457,12 +457,22 @@ struct DecodeStrides {
   int64_t q_token = 0, q_head = 0, out_token = 0, out_head = 0, tables_row = 0;
 };
 
+// Peer outputs of the decode fused with the KV-head all-gather.
+struct DecodePeers {
+  const uint64_t *gathered = nullptr, *signals = nullptr;
+  uint32_t rank = 0, world = 0;
+  uint64_t epoch = 0;
+};
+
 static int decode_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, uint64_t q,
                        uint64_t out, uint64_t tables, uint64_t seq_lens, uint64_t offsets,
                        uint32_t batch, uint32_t hq, uint32_t hkv, uint32_t hd, uint32_t bs,
                        uint32_t max_bps, float scale, uint64_t stream, bool sync,
-                       bool bind, bool noalloc = false, const DecodeStrides *st = nullptr) {
-  const char *op = st ? (dtype == kcmm::dev::Dtype::F16 ? "kcmm_paged_attn_decode_f16_strided"
+                       bool bind, bool noalloc = false, const DecodeStrides *st = nullptr,
+                       const DecodePeers *peers = nullptr) {
+  const char *op = peers ? (dtype == kcmm::dev::Dtype::F16 ? "kcmm_paged_attn_decode_f16_allgather"
+                                                           : "kcmm_paged_attn_decode_bf16_allgather")
+                   : st ? (dtype == kcmm::dev::Dtype::F16 ? "kcmm_paged_attn_decode_f16_strided"
                                                         : "kcmm_paged_attn_decode_bf16_strided")
                    : noalloc ? "kcmm_paged_attn_decode_bf16_noalloc_on_stream"
                    : dtype == kcmm::dev::Dtype::F16 ? "kcmm_paged_attn_decode_f16"
@@ -499,9 +509,34 @@ static int decode_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, u
                      "block-table row stride >= max_blocks_per_seq");
     return -1;
   }
+  if (peers) {
+    if (!peers->gathered || !peers->signals || peers->world < 1 ||
+        peers->world > uint32_t(kcmm::dev::kMaxPeers) || peers->rank >= peers->world ||
+        peers->epoch == 0) {
+      set_error(h, std::string(op) + ": need 1 <= world <= " +
+                       std::to_string(kcmm::dev::kMaxPeers) +
+                       ", rank < world, epoch >= 1 and non-null gathered / signal pointer arrays");
+      return -1;
+    }
+    for (uint32_t r = 0; r < peers->world; ++r) {
+      if (!peers->gathered[r] || (peers->gathered[r] & 15) || !peers->signals[r] ||
+          (peers->signals[r] & 7)) {
+        set_error(h, std::string(op) + ": gathered buffer " + std::to_string(r) +
+                         " must be non-null and 16-byte aligned, signal array 8-byte aligned");
+        return -1;
+      }
+    }
+  }
   if (guarded(h, op, [&] { p->require_device(op); })) return -1;
   if (bind) p->use_device();
   kcmm::dev::DecodeArgs a = {};
+  if (peers) {
+    a.peer_out = peers->gathered;
+    a.peer_sig = peers->signals;
+    a.peer_rank = int(peers->rank);
+    a.peer_world = int(peers->world);
+    a.peer_epoch = peers->epoch;
+  }
   if (st) {
     a.q_stride_token = st->q_token;
     a.q_stride_head = st->q_head;
@@ -607,6 +642,42 @@ int kcmm_paged_attn_decode_f16_strided_on_stream(
   st.tables_row = tables_row_stride;
   return decode_impl(h, kcmm::dev::Dtype::F16, layer, q, out, tables, seq_lens, offsets, batch,
                      hq, hkv, hd, bs, max_bps, scale, stream, false, true, false, &st);
+}
+
+static int decode_allgather(kcmm_pool_t *h, kcmm::dev::Dtype dt, uint32_t layer, uint64_t q,
+                            uint64_t out, uint64_t tables, uint64_t seq_lens, uint64_t offsets,
+                            uint32_t batch, uint32_t hq, uint32_t hkv, uint32_t hd, uint32_t bs,
+                            uint32_t max_bps, float scale, const uint64_t *gathered,
+                            const uint64_t *signals, uint32_t rank, uint32_t world,
+                            uint64_t epoch, uint64_t stream) {
+  DecodePeers pe;
+  pe.gathered = gathered;
+  pe.signals = signals;
+  pe.rank = rank;
+  pe.world = world;
+  pe.epoch = epoch;
+  return decode_impl(h, dt, layer, q, out, tables, seq_lens, offsets, batch, hq, hkv, hd, bs,
+                     max_bps, scale, stream, false, true, false, nullptr, &pe);
+}
+
+int kcmm_paged_attn_decode_bf16_allgather_on_stream(
+    kcmm_pool_t *h, uint32_t layer, uint64_t q, uint64_t out, uint64_t tables, uint64_t seq_lens,
+    uint64_t offsets, uint32_t batch, uint32_t hq, uint32_t hkv, uint32_t hd, uint32_t bs,
+    uint32_t max_bps, float scale, const uint64_t *gathered_ptrs, const uint64_t *signal_ptrs,
+    uint32_t rank, uint32_t world, uint64_t epoch, uint64_t stream) {
+  return decode_allgather(h, kcmm::dev::Dtype::BF16, layer, q, out, tables, seq_lens, offsets,
+                          batch, hq, hkv, hd, bs, max_bps, scale, gathered_ptrs, signal_ptrs,
+                          rank, world, epoch, stream);
+}
+
+int kcmm_paged_attn_decode_f16_allgather_on_stream(
+    kcmm_pool_t *h, uint32_t layer, uint64_t q, uint64_t out, uint64_t tables, uint64_t seq_lens,
+    uint64_t offsets, uint32_t batch, uint32_t hq, uint32_t hkv, uint32_t hd, uint32_t bs,
+    uint32_t max_bps, float scale, const uint64_t *gathered_ptrs, const uint64_t *signal_ptrs,
+    uint32_t rank, uint32_t world, uint64_t epoch, uint64_t stream) {
+  return decode_allgather(h, kcmm::dev::Dtype::F16, layer, q, out, tables, seq_lens, offsets,
+                          batch, hq, hkv, hd, bs, max_bps, scale, gathered_ptrs, signal_ptrs,
+                          rank, world, epoch, stream);
 }
 
 int kcmm_paged_attn_decode_bf16_on_stream(kcmm_pool_t *h, uint32_t layer, uint64_t q,

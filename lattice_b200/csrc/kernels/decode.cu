@@ -431,6 +431,90 @@ __global__ void merge_kernel(const DecodeParams p, int D, int rows) {
   }
 }
 
+// Peer outputs of merge_gather_kernel: rank r's gathered buffer holds
+// [world][batch][hq][D] 16-bit values; this rank's rows go to slot `rank` of every
+// buffer, then this CTA's flag in every rank's signal array is raised to epoch.
+struct PeerOut {
+  uint16_t *dst[kMaxPeers];
+  unsigned long long *sig[kMaxPeers];
+  int rank, world;
+  unsigned long long epoch;
+};
+
+// merge_kernel fused with the all-gather of the KV-head split: kGatherBlocks
+// CTAs of 32 warps walk all rows, one warp per row (the per-CTA flags fix the
+// CTA count, so the parallelism comes from wide CTAs; with 4-warp CTAs the
+// 70B head-split merge was latency-bound at 45 us).  A row that needed merging is merged as in merge_kernel
+// and written to the local output and to every rank's buffer; a row that the
+// first pass finished (one split) is copied from the local output to the
+// buffers.  The stores to other GPUs are plain stores over NVLink; the CTA's
+// flags follow a system-scope fence (kernels/peer.cu has the waiting side).
+constexpr int kMergeGatherThreads = 1024;
+
+template <typename T>
+__global__ void __launch_bounds__(kMergeGatherThreads) merge_gather_kernel(const DecodeParams p, int D, int rows, const PeerOut g) {
+  ptx::grid_dependency_wait();
+  ptx::launch_dependents();
+  const int lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
+  const int64_t slice = int64_t(p.batch) * p.hq * D;
+  for (int row = blockIdx.x * wpb + (threadIdx.x >> 5); row < rows; row += gridDim.x * wpb) {
+    const int b = row / p.hq;
+    int seq_len = p.seq_lens[b];
+    if (seq_len <= 0) continue;  // left untouched, here and in the peers' buffers
+    seq_len = min(seq_len, p.max_bps * p.bs);
+    const int n_units = ceil_div_dev(seq_len, kUnit);
+    const int ns = ceil_div_dev(n_units, p.units_per_split);
+    T *local = static_cast<T *>(p.out) + int64_t(b) * p.o_sb + int64_t(row % p.hq) * p.o_sh;
+    const int64_t goff = int64_t(g.rank) * slice + int64_t(row) * D;
+    if (ns <= 1) {
+      for (int d = lane * 4; d < D; d += 128) {
+        const uint16_t *src = reinterpret_cast<const uint16_t *>(local) + d;
+        const uint2 v = make_uint2(uint32_t(src[0]) | (uint32_t(src[1]) << 16),
+                                   uint32_t(src[2]) | (uint32_t(src[3]) << 16));
+        for (int r = 0; r < g.world; ++r) *reinterpret_cast<uint2 *>(g.dst[r] + goff + d) = v;
+      }
+      continue;
+    }
+    const float *lse = p.part_lse + int64_t(row) * p.num_splits;
+    float M = -INFINITY;
+    for (int s = lane; s < ns; s += 32) M = fmaxf(M, lse[s]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float wsum = 0.f;
+    for (int s = lane; s < ns; s += 32) wsum += ptx::fast_exp2(lse[s] - M);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+    const float inv = 1.f / wsum;
+    const float *po = p.part_o + int64_t(row) * p.num_splits * D;
+    for (int d = lane * 4; d < D; d += 128) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+      for (int s = 0; s < ns; ++s) {
+        const float w = ptx::fast_exp2(lse[s] - M);
+        const float4 v = *reinterpret_cast<const float4 *>(po + int64_t(s) * D + d);
+        acc.x += v.x * w;
+        acc.y += v.y * w;
+        acc.z += v.z * w;
+        acc.w += v.w * w;
+      }
+      T o[4] = {ptx::from_f32<T>(acc.x * inv), ptx::from_f32<T>(acc.y * inv),
+                ptx::from_f32<T>(acc.z * inv), ptx::from_f32<T>(acc.w * inv)};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) local[d + k] = o[k];
+      const uint16_t *u = reinterpret_cast<const uint16_t *>(o);
+      const uint2 v = make_uint2(uint32_t(u[0]) | (uint32_t(u[1]) << 16),
+                                 uint32_t(u[2]) | (uint32_t(u[3]) << 16));
+      for (int r = 0; r < g.world; ++r) *reinterpret_cast<uint2 *>(g.dst[r] + goff + d) = v;
+    }
+  }
+  __threadfence_system();  // this thread's stores (peers' memory included) before the flags
+  __syncthreads();
+  if (int(threadIdx.x) < g.world) {
+    unsigned long long *f = g.sig[threadIdx.x] + g.rank * kGatherBlocks + blockIdx.x;
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(g.epoch) : "memory");
+  }
+}
+
 // Fallback for shapes outside the tensor-core path (head_dim not a multiple
 // of 16, block_size not a multiple of 16): one warp per (sequence, head),
 // plain loads, same math.
@@ -959,10 +1043,12 @@ cudaError_t decode_attention(const DecodeArgs &a, cudaStream_t stream) {
                      p.o_sh == a.head_dim && p.bt_stride == a.max_blocks_per_seq;
 
   SkPlan sp = make_sk_plan(a);
-  if (sp.forced && !dense) return cudaErrorNotSupported;  // stream-K reads dense rows only
+  // stream-K reads dense rows only and has no gather
+  if (sp.forced && (!dense || a.peer_world > 0)) return cudaErrorNotSupported;
   if (sp.ok) return decode_streamk(a, sp, stream);
   if (sp.forced) return cudaErrorNotSupported;
   Plan pl = make_plan(a);
+  if (!pl.fast && a.peer_world > 0) return cudaErrorNotSupported;  // tensor-core path only
   if (!pl.fast) {
     const int threads = 256;
     const int64_t warps = int64_t(a.batch) * a.num_q_heads;
@@ -1005,7 +1091,26 @@ cudaError_t decode_attention(const DecodeArgs &a, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   dim3 grid(pl.num_splits, a.kv_heads * pl.n_head_tiles, a.batch);
   e = launch_pdl(pl.fn, grid, dim3(kWarps * 32), pl.smem, stream, p);
-  if (e == cudaSuccess && pl.num_splits > 1) {
+  if (e == cudaSuccess && a.peer_world > 0) {
+    // merge fused with the all-gather: always launched (it also forwards the
+    // rows the first pass finished)
+    PeerOut g = {};
+    for (int r = 0; r < a.peer_world; ++r) {
+      g.dst[r] = reinterpret_cast<uint16_t *>(a.peer_out[r]);
+      g.sig[r] = reinterpret_cast<unsigned long long *>(a.peer_sig[r]);
+    }
+    g.rank = a.peer_rank;
+    g.world = a.peer_world;
+    g.epoch = a.peer_epoch;
+    const int rows = a.batch * a.num_q_heads;
+    if (a.dtype == Dtype::BF16) {
+      e = launch_pdl(merge_gather_kernel<__nv_bfloat16>, dim3(kGatherBlocks),
+                     dim3(kMergeGatherThreads), 0, stream, p, a.head_dim, rows, g);
+    } else {
+      e = launch_pdl(merge_gather_kernel<__half>, dim3(kGatherBlocks),
+                     dim3(kMergeGatherThreads), 0, stream, p, a.head_dim, rows, g);
+    }
+  } else if (e == cudaSuccess && pl.num_splits > 1) {
     const int rows = a.batch * a.num_q_heads;
     const dim3 mgrid((rows + 3) / 4);
     if (a.dtype == Dtype::BF16) {

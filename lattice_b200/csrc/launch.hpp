@@ -44,6 +44,14 @@ struct DecodeArgs {
   // Element strides of q and out (token, head; head_dim is contiguous) and of the
   // block-table rows; 0 = dense ([batch][Hq][D] and max_blocks_per_seq).
   int64_t q_stride_token, q_stride_head, out_stride_token, out_stride_head, tables_stride;
+  // All-gather of the KV-head split (kernels/decode.cu, merge_gather_kernel):
+  // peer_world > 0 writes every output row also to slot peer_rank of each
+  // rank's gathered buffer peer_out[r] ([world][batch][Hq][D]) and raises this
+  // rank's flags in peer_sig[r] to peer_epoch (host arrays of device addresses).
+  const uint64_t *peer_out;
+  const uint64_t *peer_sig;
+  int peer_rank, peer_world;
+  uint64_t peer_epoch;
 };
 
 // Bytes of split-K scratch decode_attention needs for these arguments

@@ -257,6 +257,12 @@ SIGNATURES: dict[str, tuple] = {
     "kcmm_peer_signal_words": (u32, [u32]),
     "kcmm_peer_allgather_on_stream": (i32, [u64, u64, pu64, pu64, u32, u32, u64, u64]),
     "kcmm_peer_wait_on_stream": (i32, [u64, u32, u64, u64, u64]),
+    "kcmm_paged_attn_decode_bf16_allgather_on_stream": (
+        i32, [P, u32, u64, u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, f32, pu64, pu64,
+              u32, u32, u64, u64]),
+    "kcmm_paged_attn_decode_f16_allgather_on_stream": (
+        i32, [P, u32, u64, u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, f32, pu64, pu64,
+              u32, u32, u64, u64]),
     "kcmm_get_metrics_ext": (i32, [P, ctypes.c_void_p]),
     "kcmm_get_policy_stats": (i32, [P, ctypes.c_char_p, ctypes.c_void_p]),
     "kcmm_start_background_eviction": (i32, [P]),

@@ -280,3 +280,28 @@ def test_peer_allgather_argument_checks(kcmm_lib):
     assert lib.kcmm_peer_allgather_on_stream(16, 16, ptrs, ptrs, 0, 2, 0, 0) == -1
     assert lib.kcmm_peer_wait_on_stream(0, 2, 1, 0, 0) == -1
     assert lib.kcmm_peer_wait_on_stream(8, 0, 1, 0, 0) == -1
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_decode_allgather_argument_checks(kcmm_lib, host_pool_factory, dtype):
+    """The decode fused with the peer all-gather checks its peer arguments before any
+    device work (host pool: the checks run first): world outside 1..8, a rank outside
+    the world, epoch 0, NULL or misaligned buffers."""
+    lib = kcmm_lib.lib
+    pool = host_pool_factory(kv_heads=2, head_dim=64, max_batch=4, max_seq_len=256)
+    fn = getattr(lib, f"kcmm_paged_attn_decode_{dtype}_allgather_on_stream")
+
+    def call(bufs=(256, 512), sigs=(1024, 2048), rank=0, world=2, epoch=1):
+        b = (ctypes.c_uint64 * len(bufs))(*bufs)
+        s = (ctypes.c_uint64 * len(sigs))(*sigs)
+        return fn(pool.handle, 0, 1, 2, 3, 4, 5, 2, 8, 2, 64, 16, 16, 0.125, b, s, rank,
+                  world, epoch, 0)
+
+    for kw in (dict(world=0), dict(world=9, bufs=(256,) * 9, sigs=(1024,) * 9),
+               dict(rank=2), dict(epoch=0)):
+        assert call(**kw) == -1
+        assert "allgather" in pool.last_error() and "world" in pool.last_error()
+    assert call(bufs=(256, 520)) == -1 and "16-byte aligned" in pool.last_error()
+    assert call(sigs=(1024, 0)) == -1 and "signal" in pool.last_error()
+    # valid peer arguments get as far as the device check
+    assert call() == -1 and "device" in pool.last_error().lower()

@@ -2,7 +2,9 @@
 `kcmm_peer_wait_on_stream`) with two ranks, one GPU each; skipped with fewer than two
 GPUs.  Every rank's gathered buffer must hold every rank's slice after the wait, over
 several epochs with changing data.  A wait for a rank that never raises its flags
-returns after its 1 s bound with status 1, and the GPU stays usable."""
+returns after its 1 s bound with status 1, and the GPU stays usable.  The decode fused
+with the gather (`kcmm_paged_attn_decode_bf16_allgather_on_stream`) must fill every
+rank's buffer with all ranks' outputs the same way."""
 from __future__ import annotations
 
 import json
@@ -84,6 +86,85 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
             pb.close()
         Path(out_dir, f"rank{rank}.json").write_text(json.dumps(result))
         dist.destroy_process_group()
+
+
+def _fused_rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
+    """Each rank decodes its own kv heads with the fused decode + gather; every
+    rank's gathered buffer must hold all ranks' outputs, bit for bit."""
+    import ctypes
+    import datetime
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(ROOT))
+    from lattice_b200.workloads import DecodeWorkload, PeerBuffers, read_device
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=60))
+    result = {"ok": True, "close": True}
+    pb = wl = None
+    try:
+        wl = DecodeWorkload(batch=4, num_q_heads=16, kv_heads=2, head_dim=128,
+                            pool_blocks=2200, seq_lens_override=[0, 40, 3000, 8000],
+                            max_len=8000, seed=90 + rank, device=rank).build()
+        slice_bytes = wl.out.numel() * 2
+        pb = PeerBuffers(slice_bytes, rank, world, rank)
+        dst = (ctypes.c_uint64 * world)(*pb.buf_ptrs)
+        sig = (ctypes.c_uint64 * world)(*pb.sig_ptrs)
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        sp = torch.cuda.current_stream().cuda_stream
+        lib = wl.pool.lib
+        live = torch.from_numpy(wl.seq_lens > 0).cuda()
+        for epoch in range(1, 4):
+            wl.q.copy_(torch.randn_like(wl.q.float()).bfloat16())
+            wl.decode(stream_ptr=sp)
+            ref = wl.out.clone()
+            wl.out.zero_()
+            pb.epoch += 1
+            assert lib.kcmm_paged_attn_decode_bf16_allgather_on_stream(
+                wl.pool.handle, 0, wl.q.data_ptr(), wl.out.data_ptr(), wl.d_tables.data_ptr(),
+                wl.d_seq_lens.data_ptr(), wl.d_offsets.data_ptr(), wl.batch, wl.num_q_heads,
+                wl.kv_heads, wl.head_dim, wl.block_size, wl.max_blocks_per_seq, wl.scale,
+                dst, sig, rank, world, pb.epoch, sp) == 0, wl.pool.last_error()
+            assert lib.kcmm_peer_wait_on_stream(pb.signal_ptr, world, pb.epoch,
+                                                status.data_ptr(), sp) == 0
+            torch.cuda.synchronize()
+            err = (wl.out[live].float() - ref[live].float()).abs()
+            if not bool((err <= 2e-3 + 1e-2 * ref[live].float().abs()).all()):
+                result["close"] = False
+            mine = wl.out.view(torch.int16).cpu().numpy().view(np.uint8).reshape(-1)
+            everyone = [None] * world
+            dist.all_gather_object(everyone, mine)
+            got = read_device(pb.gathered_ptr, slice_bytes * world)
+            if not (got == np.concatenate(everyone)).all() or int(status.item()) != 0:
+                result["ok"] = False
+            dist.barrier()
+    finally:
+        if pb is not None:
+            dist.barrier()
+            pb.close()
+        if wl is not None:
+            wl.close()
+        Path(out_dir, f"fused{rank}.json").write_text(json.dumps(result))
+        dist.destroy_process_group()
+
+
+def test_two_rank_decode_fused_with_allgather(tmp_path):
+    import torch
+
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    port = _free_port()
+    mp.start_processes(_fused_rank_main, args=(2, port, str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    for r in range(2):
+        res = json.loads((tmp_path / f"fused{r}.json").read_text())
+        assert res["ok"] and res["close"], res
 
 
 def test_two_rank_peer_allgather(tmp_path):

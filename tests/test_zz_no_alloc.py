@@ -41,7 +41,7 @@ def _close(got, ref):
 
 
 CASES = [
-    # Llama-3-8B heads, contexts 512..4096 (many stream-K pieces per sequence)
+    # Llama-3-8B heads, contexts 512..4096 (several splits per sequence, merged)
     dict(batch=64, pool_blocks=17000, min_len=512, max_len=4096, seed=3),
     # mixed short and empty rows, GQA 8, two head tiles not needed
     dict(batch=5, num_q_heads=8, kv_heads=1, pool_blocks=256,
@@ -68,10 +68,11 @@ def test_noalloc_matches_regular_twice(case):
         wl.close()
 
 
-def test_noalloc_split_fallback(monkeypatch):
-    """The split-K kernel (not the default stream-K) through the same static scratch."""
+def test_noalloc_streamk(monkeypatch):
+    """The opt-in persistent stream-K kernel (KCMM_DECODE_IMPL=streamk) through the same
+    static scratch: its partial rows and its per-call prefix arrays live there too."""
     torch = _torch()
-    monkeypatch.setenv("KCMM_DECODE_IMPL", "split")
+    monkeypatch.setenv("KCMM_DECODE_IMPL", "streamk")
     wl = _make(batch=8, pool_blocks=1200, min_len=100, max_len=2500, seed=5)
     try:
         ref = torch.empty_like(wl.q)
