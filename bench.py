@@ -623,9 +623,14 @@ def run_cow_leg(args):
             memcpy(base, t.data_ptr(), used, "d2d")
     del t
     sp = torch.cuda.current_stream().cuda_stream
-    copy_ms, attn_ms = [], []
+    copy_ms, attn_ms, shared_ms = [], [], []
     q = torch.randn(reqs * beams, 32, 128, device="cuda", generator=gen).to(torch.bfloat16)
     out = torch.empty_like(q)
+    out_shared = torch.empty_like(q)
+    # the beams of a request form a group sharing the 2048-token prefix
+    g_starts = torch.arange(0, reqs * beams + 1, beams, dtype=torch.int32, device="cuda")
+    g_prefix = torch.full((reqs,), 2048, dtype=torch.int32, device="cuda")
+    max_diff = 0.0
     copies = 0
     for it in range(max(args.warmup, 3) + args.steps):
         forks = [pool.fork_sequence(p) for p in parents for _ in range(beams)]
@@ -652,10 +657,21 @@ def run_cow_leg(args):
                                max_blocks_per_seq=tables.shape[1], scale=128 ** -0.5,
                                stream_ptr=sp)
         c.record()
+        _gate(torch)
+        c2, d = (torch.cuda.Event(enable_timing=True) for _ in range(2))
+        c2.record()
+        assert pool.lib.kcmm_paged_attn_decode_shared_prefix_bf16_on_stream(
+            pool.handle, 0, q.data_ptr(), out_shared.data_ptr(), d_tables.data_ptr(),
+            d_lens.data_ptr(), d_offs.data_ptr(), len(forks), 32, 8, 128, 16, tables.shape[1],
+            128 ** -0.5, g_starts.data_ptr(), g_prefix.data_ptr(), reqs, beams, sp) == 0, \
+            pool.last_error()
+        d.record()
         torch.cuda.synchronize()
+        max_diff = max(max_diff, float((out_shared.float() - out.float()).abs().max()))
         if it >= max(args.warmup, 3):
             copy_ms.append(a.elapsed_time(b))
             attn_ms.append(b2.elapsed_time(c))
+            shared_ms.append(c2.elapsed_time(d))
         copies = sum(1 for n, o in zip(new, shared) if n != o)
         for f in forks:
             pool.unregister_sequence(f)
@@ -663,6 +679,7 @@ def run_cow_leg(args):
     pool.destroy()
     tc = statistics.median(copy_ms)
     ta = statistics.median(attn_ms)
+    ts = statistics.median(shared_ms)
     # unique bytes: each request's 4 beams copy the same parent tail, so a step reads 16
     # distinct source blocks and writes 64 new ones (per region); the 3 repeat reads of a
     # source come from L2 and are not counted as HBM work
@@ -688,6 +705,15 @@ def run_cow_leg(args):
                             "unique_bytes": unique,
                             "logical_gbs": round(logical / (ta * 1e-3) / 1e9, 1),
                             "unique_gbs": round(unique / (ta * 1e-3) / 1e9, 1)},
+         "beam_attention_shared_prefix": {
+             "call": "kcmm_paged_attn_decode_shared_prefix_bf16_on_stream (the 4 beams of a "
+                     "request form a group sharing 2048 tokens)",
+             "us": round(ts * 1e3, 2),
+             "unique_gbs": round(unique / (ts * 1e-3) / 1e9, 1),
+             "unique_frac_of_hbm": round(unique / (ts * 1e-3) / 1e9 / peak, 4),
+             "logical_gbs": round(logical / (ts * 1e-3) / 1e9, 1),
+             "speedup_vs_plain": round(ta / ts, 2),
+             "max_abs_diff_vs_plain": round(max_diff, 6)},
          "status": status})
 
 

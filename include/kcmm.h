@@ -550,10 +550,49 @@ int kcmm_swap_in_blocks_on_stream(kcmm_pool_t *pool, const uint32_t *blocks,
 /**
  * Sticky device-side diagnostics of the pool's kernels, then cleared:
  * bit 0 = a bounded wait for a KV page gave up (no data arrived),
- * bit 1 = a block offset was misaligned or outside the layer region.
+ * bit 1 = a block offset was misaligned or outside the layer region,
+ * bit 2 = launch arguments the kernel found inconsistent (a prefill context
+ *         shorter than its chunk; members of a shared-prefix group whose shared
+ *         table entries differ).
  * Synchronises the pool's device.  -1 if the pool has no device.
  */
 int32_t kcmm_get_kernel_status(kcmm_pool_t *pool);
+
+/*
+ * Decode attention over sequences that share a prefix of their pages (no
+ * counterpart in the reference: its kernel reads every sequence's pages on its
+ * own, also where kcmm_share_prefix / kcmm_fork_sequence made them the same
+ * blocks).  Same arguments and result as kcmm_paged_attn_decode_bf16_on_stream,
+ * plus groups of consecutive sequences:
+ *   group_starts_ptr  device int32[n_groups + 1], ascending, 0 .. batch_size:
+ *                     group g is the sequences [starts[g], starts[g+1]);
+ *   prefix_lens_ptr   device int32[n_groups]: the first prefix_lens[g] tokens of
+ *                     every member are the same blocks (same ids in the first
+ *                     ceil(prefix_lens[g] / block_size) table entries).
+ * The shared pages are read once per group (and kv head) for all members' query
+ * rows together, each member's remaining tokens on their own, and the two
+ * partial results merge through their log-sum-exp.  The prefix used is the
+ * group's length capped by every member's context, in whole 16-token units.
+ * At most max_group_size members of a group share (the rest attend alone); a
+ * malformed group attends alone.  A member whose table differs from the first
+ * member's inside the shared pages sets bit 2 of kcmm_get_kernel_status (the
+ * result is then undefined for that group).  Needs num_q_heads a multiple of
+ * num_kv_heads with at most 16 query heads per kv head, head_dim 64, 128 or 256,
+ * and at most 16384 sequences; -1 otherwise.  Each call first resolves the groups
+ * in one small kernel, so the attention kernels read two words per item.
+ */
+int kcmm_paged_attn_decode_shared_prefix_bf16_on_stream(
+    kcmm_pool_t *pool, uint32_t layer_idx, uint64_t query_ptr, uint64_t output_ptr,
+    uint64_t block_tables_ptr, uint64_t seq_lens_ptr, uint64_t block_offsets_ptr,
+    uint32_t batch_size, uint32_t num_q_heads, uint32_t num_kv_heads, uint32_t head_dim,
+    uint32_t block_size, uint32_t max_blocks_per_seq, float scale, uint64_t group_starts_ptr,
+    uint64_t prefix_lens_ptr, uint32_t n_groups, uint32_t max_group_size, uint64_t stream_ptr);
+int kcmm_paged_attn_decode_shared_prefix_f16_on_stream(
+    kcmm_pool_t *pool, uint32_t layer_idx, uint64_t query_ptr, uint64_t output_ptr,
+    uint64_t block_tables_ptr, uint64_t seq_lens_ptr, uint64_t block_offsets_ptr,
+    uint32_t batch_size, uint32_t num_q_heads, uint32_t num_kv_heads, uint32_t head_dim,
+    uint32_t block_size, uint32_t max_blocks_per_seq, float scale, uint64_t group_starts_ptr,
+    uint64_t prefix_lens_ptr, uint32_t n_groups, uint32_t max_group_size, uint64_t stream_ptr);
 
 /* --- all-gather over NVLink peer memory (KV-head split, no reference counterpart) --- */
 

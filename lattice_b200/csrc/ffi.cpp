@@ -457,6 +457,12 @@ struct DecodeStrides {
   int64_t q_token = 0, q_head = 0, out_token = 0, out_head = 0, tables_row = 0;
 };
 
+// Groups of the shared-prefix decode (device arrays).
+struct DecodeGroups {
+  uint64_t group_starts = 0, prefix_lens = 0;
+  uint32_t n_groups = 0, max_group_size = 0;
+};
+
 // Peer outputs of the decode fused with the KV-head all-gather.
 struct DecodePeers {
   const uint64_t *gathered = nullptr, *signals = nullptr;
@@ -469,8 +475,12 @@ static int decode_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, u
                        uint32_t batch, uint32_t hq, uint32_t hkv, uint32_t hd, uint32_t bs,
                        uint32_t max_bps, float scale, uint64_t stream, bool sync,
                        bool bind, bool noalloc = false, const DecodeStrides *st = nullptr,
-                       const DecodePeers *peers = nullptr) {
-  const char *op = peers ? (dtype == kcmm::dev::Dtype::F16 ? "kcmm_paged_attn_decode_f16_allgather"
+                       const DecodePeers *peers = nullptr,
+                       const DecodeGroups *groups = nullptr) {
+  const char *op = groups ? (dtype == kcmm::dev::Dtype::F16
+                                 ? "kcmm_paged_attn_decode_shared_prefix_f16"
+                                 : "kcmm_paged_attn_decode_shared_prefix_bf16")
+                   : peers ? (dtype == kcmm::dev::Dtype::F16 ? "kcmm_paged_attn_decode_f16_allgather"
                                                            : "kcmm_paged_attn_decode_bf16_allgather")
                    : st ? (dtype == kcmm::dev::Dtype::F16 ? "kcmm_paged_attn_decode_f16_strided"
                                                         : "kcmm_paged_attn_decode_bf16_strided")
@@ -527,6 +537,25 @@ static int decode_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, u
       }
     }
   }
+  if (groups) {
+    if (!groups->group_starts || !groups->prefix_lens || groups->n_groups == 0 ||
+        groups->n_groups > batch || groups->max_group_size == 0 ||
+        groups->max_group_size > batch) {
+      set_error(h, std::string(op) +
+                       ": need non-null group_starts / prefix_lens, 1 <= n_groups <= batch "
+                       "and 1 <= max_group_size <= batch");
+      return -1;
+    }
+    if (batch > 16384) {
+      set_error(h, std::string(op) + ": at most 16384 sequences per call");
+      return -1;
+    }
+    if (hq % hkv != 0 || hq / hkv > 16) {
+      set_error(h, std::string(op) + ": needs num_q_heads a multiple of num_kv_heads with at "
+                                     "most 16 query heads per kv head");
+      return -1;
+    }
+  }
   if (guarded(h, op, [&] { p->require_device(op); })) return -1;
   if (bind) p->use_device();
   kcmm::dev::DecodeArgs a = {};
@@ -575,6 +604,15 @@ static int decode_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, u
       return -1;
     }
     if (check_launch(h, op, kcmm::dev::decode_attention_noalloc(a, S(stream)))) return -1;
+    return 0;
+  }
+  if (groups) {
+    if (check_launch(h, op,
+                     kcmm::dev::decode_attention_shared_prefix(
+                         a, reinterpret_cast<const int32_t *>(groups->group_starts),
+                         reinterpret_cast<const int32_t *>(groups->prefix_lens),
+                         int(groups->n_groups), int(groups->max_group_size), S(stream))))
+      return -1;
     return 0;
   }
   a.tensor_maps = p->tensor_maps(layer, int(hkv), int(hd));
@@ -678,6 +716,41 @@ int kcmm_paged_attn_decode_f16_allgather_on_stream(
   return decode_allgather(h, kcmm::dev::Dtype::F16, layer, q, out, tables, seq_lens, offsets,
                           batch, hq, hkv, hd, bs, max_bps, scale, gathered_ptrs, signal_ptrs,
                           rank, world, epoch, stream);
+}
+
+static int decode_shared_prefix(kcmm_pool_t *h, kcmm::dev::Dtype dt, uint32_t layer, uint64_t q,
+                                uint64_t out, uint64_t tables, uint64_t seq_lens,
+                                uint64_t offsets, uint32_t batch, uint32_t hq, uint32_t hkv,
+                                uint32_t hd, uint32_t bs, uint32_t max_bps, float scale,
+                                uint64_t group_starts, uint64_t prefix_lens, uint32_t n_groups,
+                                uint32_t max_group_size, uint64_t stream) {
+  DecodeGroups g;
+  g.group_starts = group_starts;
+  g.prefix_lens = prefix_lens;
+  g.n_groups = n_groups;
+  g.max_group_size = max_group_size;
+  return decode_impl(h, dt, layer, q, out, tables, seq_lens, offsets, batch, hq, hkv, hd, bs,
+                     max_bps, scale, stream, false, true, false, nullptr, nullptr, &g);
+}
+
+int kcmm_paged_attn_decode_shared_prefix_bf16_on_stream(
+    kcmm_pool_t *h, uint32_t layer, uint64_t q, uint64_t out, uint64_t tables, uint64_t seq_lens,
+    uint64_t offsets, uint32_t batch, uint32_t hq, uint32_t hkv, uint32_t hd, uint32_t bs,
+    uint32_t max_bps, float scale, uint64_t group_starts, uint64_t prefix_lens,
+    uint32_t n_groups, uint32_t max_group_size, uint64_t stream) {
+  return decode_shared_prefix(h, kcmm::dev::Dtype::BF16, layer, q, out, tables, seq_lens,
+                              offsets, batch, hq, hkv, hd, bs, max_bps, scale, group_starts,
+                              prefix_lens, n_groups, max_group_size, stream);
+}
+
+int kcmm_paged_attn_decode_shared_prefix_f16_on_stream(
+    kcmm_pool_t *h, uint32_t layer, uint64_t q, uint64_t out, uint64_t tables, uint64_t seq_lens,
+    uint64_t offsets, uint32_t batch, uint32_t hq, uint32_t hkv, uint32_t hd, uint32_t bs,
+    uint32_t max_bps, float scale, uint64_t group_starts, uint64_t prefix_lens,
+    uint32_t n_groups, uint32_t max_group_size, uint64_t stream) {
+  return decode_shared_prefix(h, kcmm::dev::Dtype::F16, layer, q, out, tables, seq_lens,
+                              offsets, batch, hq, hkv, hd, bs, max_bps, scale, group_starts,
+                              prefix_lens, n_groups, max_group_size, stream);
 }
 
 int kcmm_paged_attn_decode_bf16_on_stream(kcmm_pool_t *h, uint32_t layer, uint64_t q,

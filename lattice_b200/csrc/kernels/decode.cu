@@ -73,6 +73,128 @@ __device__ __forceinline__ void head_range(int kvh, int ht, int hq, int hkv, int
   *hi = min(g_hi, *lo + 16);
 }
 
+// Shared-prefix (cascade) decode: sequences in batch order form groups
+// [group_starts[g], group_starts[g+1]) whose first prefix_lens[g] tokens are the
+// same pages (beams of one request, or requests on one system prompt).  The
+// prefix is attended once per group with all members' query rows stacked in the
+// CTA's 16 rows (members_per_tile = 16 / G members per tile, tiles_per_group
+// tiles), each member's own tokens by a second kind of CTA, and the two sets of
+// partials merge through their log-sum-exp.
+struct CascadeParams {
+  const int32_t *group_starts;  // [n_groups + 1]
+  const int32_t *prefix_lens;   // [n_groups], tokens
+  int n_groups, max_group_size, members_per_tile, tiles_per_group;
+  int fit;          // CTAs per prefix tile that one wave of the GPU holds (>= 1)
+  int max_a;        // prefix slots of a row: at most this many prefix splits
+  // Written by shared_prefix_prep_kernel (scratch):
+  int32_t *seq_slots;  // [batch]: partial slots of sequence b (prefix + own splits)
+  int32_t *count;      // [1]: CTAs with work
+  int4 *work;          // [2 per CTA] the work entries, prefix work first
+};
+
+// One work entry (two int4): what a CTA of the shared-prefix decode attends.
+//   a = {mode (1 prefix, 2 own tokens), table row b, first unit, end unit}
+//   c = {first member (mode 1), member mask (mode 1), partial slot, tokens}
+// Mode 1 rows are (member m of the mask, query head); mode 2 rows are sequence
+// b's heads.  `tokens` bounds the keys (the shared units, or the context).
+
+// One CTA resolves the groups and writes the work list, so the attention CTAs
+// start from one entry, as the plain decode starts from its sequence.  A
+// sequence shares its group's prefix when the group is well formed (0 <= start <
+// end <= batch, and its start maps back to it), the sequence lies in the group's
+// range and is among its first max_group_size members.  Starts are meant to
+// ascend; where they do not, the search below still gives every sequence at most
+// one group.  A group's units are its prefix length capped by every sharing
+// member's context, in whole 16-token units; they are split into
+// max(fit, units / (32 * 4)) pieces (at most max_a), each sequence's own
+// units into pieces of DecodeParams.units_per_split.
+__global__ void shared_prefix_prep_kernel(const DecodeParams p, const CascadeParams c) {
+  ptx::grid_dependency_wait();
+  ptx::launch_dependents();
+  extern __shared__ int32_t prep_smem[];
+  int32_t *gs = prep_smem;                      // [n_groups + 1]
+  int32_t *sg = prep_smem + c.n_groups + 1;     // [batch]: group shared, or -1
+  int32_t *gu = sg + p.batch;                   // [n_groups]: units shared
+  int32_t *gn = gu + c.n_groups;                // [n_groups]: prefix splits
+  __shared__ int n_work;
+  for (int i = threadIdx.x; i <= c.n_groups; i += blockDim.x) gs[i] = c.group_starts[i];
+  if (threadIdx.x == 0) n_work = 0;
+  __syncthreads();
+  auto group_of = [&](int b) {  // the last group whose start is <= b
+    int lo = 0, hi = c.n_groups - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (gs[mid] <= b) {
+        lo = mid;
+      } else {
+        hi = mid - 1;
+      }
+    }
+    return lo;
+  };
+  auto well_formed = [&](int g) {
+    const int s0 = gs[g], s1 = gs[g + 1];
+    return s0 >= 0 && s1 <= p.batch && s0 < s1 && group_of(s0) == g;
+  };
+  for (int b = threadIdx.x; b < p.batch; b += blockDim.x) {
+    const int g = group_of(b);
+    const bool in = well_formed(g) && b >= gs[g] && b < gs[g + 1] && b - gs[g] < c.max_group_size;
+    sg[b] = in ? g : -1;
+  }
+  __syncthreads();
+  const int cap = p.max_bps * p.bs;
+  for (int g = threadIdx.x; g < c.n_groups; g += blockDim.x) {
+    int pl = 0;
+    if (well_formed(g)) {
+      pl = c.prefix_lens[g];
+      const int s_end = min(gs[g + 1], gs[g] + c.max_group_size);
+      for (int m = gs[g]; m < s_end; ++m) {
+        if (sg[m] == g) pl = min(pl, min(p.seq_lens[m], cap));
+      }
+    }
+    const int pu = max(pl, 0) / kUnit;
+    const int want = pu > 0 ? min(c.max_a, min(pu, max(c.fit, ceil_div_dev(pu, 32 * 4)))) : 0;
+    const int ups = want > 0 ? ceil_div_dev(pu, want) : 1;  // <= 32 units per warp
+    const int ns = want > 0 ? ceil_div_dev(pu, ups) : 0;    // every piece non-empty
+    gu[g] = pu;
+    gn[g] = ns;
+    if (ns == 0) continue;
+    for (int t = 0; t < c.tiles_per_group; ++t) {
+      int mask = 0;
+      for (int m = 0; m < c.members_per_tile; ++m) {
+        const int bm = gs[g] + t * c.members_per_tile + m;
+        if (bm < p.batch && sg[bm] == g) mask |= 1 << m;
+      }
+      if (!mask) continue;
+      const int at = atomicAdd(&n_work, ns);
+      for (int k = 0; k < ns; ++k) {
+        c.work[2 * (at + k)] = make_int4(1, gs[g], k * ups, min(k * ups + ups, pu));
+        c.work[2 * (at + k) + 1] =
+            make_int4(gs[g] + t * c.members_per_tile, mask, k, pu * kUnit);
+      }
+    }
+  }
+  __syncthreads();  // prefix work first: the long items start first
+  for (int b = threadIdx.x; b < p.batch; b += blockDim.x) {
+    const int len = min(p.seq_lens[b], cap);
+    const int g = sg[b];
+    const int pu = g >= 0 ? gu[g] : 0;
+    const int na = g >= 0 ? gn[g] : 0;
+    const int n_units = len > 0 ? ceil_div_dev(len, kUnit) : 0;
+    const int nb = n_units > pu ? ceil_div_dev(n_units - pu, p.units_per_split) : 0;
+    c.seq_slots[b] = len > 0 ? na + nb : 0;
+    if (nb == 0) continue;
+    const int at = atomicAdd(&n_work, nb);
+    for (int k = 0; k < nb; ++k) {
+      const int u0 = pu + k * p.units_per_split;
+      c.work[2 * (at + k)] = make_int4(2, b, u0, min(u0 + p.units_per_split, n_units));
+      c.work[2 * (at + k) + 1] = make_int4(0, 0, na + k, len);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *c.count = n_work;
+}
+
 template <typename T, int D, int W, int NS>
 struct Cfg {
   static constexpr int RS = D + 8;                  // padded row (elements)
@@ -89,8 +211,18 @@ struct Cfg {
 // registers.  Without it ptxas may aim at 3 CTAs per SM (at most 168 registers)
 // after unrelated edits to the kernel, and the loop then runs about 10% slower on
 // the Llama-3-8B decode shape (measured: 129.8 us against 117.3 us per call).
-template <typename T, int D, int W, int NS>
-__global__ void __launch_bounds__(W * 32, 2) decode_kernel(const DecodeParams p) {
+//
+// MODE 0: the plain decode, item = blockIdx.z = sequence.
+// MODE 1: a prefix item of the shared-prefix decode (item = group * tiles_per_group
+//         + tile): rows are (member, query head) pairs, keys the group's shared
+//         units read through its first member's block table; always partials, slot
+//         = split.
+// MODE 2: a suffix item (item = sequence): the units past the sequence's shared
+//         prefix; always partials, slots after the prefix ones.
+template <typename T, int D, int W, int NS, int MODE>
+__device__ __forceinline__ void decode_body(const DecodeParams &p, const int item,
+                                            const int split, const int4 ea = int4{},
+                                            const int4 ec = int4{}) {
   using C = Cfg<T, D, W, NS>;
   using MMA = ptx::Mma<T>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -104,32 +236,63 @@ __global__ void __launch_bounds__(W * 32, 2) decode_kernel(const DecodeParams p)
   ptx::grid_dependency_wait();
   ptx::launch_dependents();
 
-  const int split = blockIdx.x;
   const int kvh = blockIdx.y / p.n_head_tiles;
   const int ht = blockIdx.y % p.n_head_tiles;
-  const int b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  int seq_len = p.seq_lens[b];
-  if (seq_len <= 0) return;
-  seq_len = min(seq_len, p.max_bps * p.bs);
-  const int n_units = ceil_div_dev(seq_len, kUnit);
-  const int u_begin = split * p.units_per_split;
-  if (u_begin >= n_units) return;
-  const int u_end = min(u_begin + p.units_per_split, n_units);
-  int lo, hi;
-  head_range(kvh, ht, p.hq, p.hkv, &lo, &hi);
-  const int G = hi - lo;
-  if (G <= 0) return;
-  const int n_splits_b = ceil_div_dev(n_units, p.units_per_split);
+  int b, seq_len, u_begin, u_end, n_splits_b, G, lo, hi;
+  int NR = 0, slot0 = 0, mbase = 0;  // MODE 1/2 only
+  unsigned members = 0;              // MODE 1: bit m = member m of the tile is a row source
+  if constexpr (MODE == 0) {
+    b = item;
+    seq_len = p.seq_lens[b];
+    if (seq_len <= 0) return;
+    seq_len = min(seq_len, p.max_bps * p.bs);
+    const int n_units = ceil_div_dev(seq_len, kUnit);
+    u_begin = split * p.units_per_split;
+    if (u_begin >= n_units) return;
+    u_end = min(u_begin + p.units_per_split, n_units);
+    head_range(kvh, ht, p.hq, p.hkv, &lo, &hi);
+    G = hi - lo;
+    if (G <= 0) return;
+    n_splits_b = ceil_div_dev(n_units, p.units_per_split);
+  } else {
+    // the work entry of the shared-prefix decode
+    b = ea.y;
+    u_begin = ea.z;
+    u_end = ea.w;
+    slot0 = ec.z;
+    seq_len = ec.w;
+    head_range(kvh, 0, p.hq, p.hkv, &lo, &hi);
+    G = hi - lo;
+    if (G <= 0 || u_begin >= u_end) return;
+    if constexpr (MODE == 1) {
+      mbase = ec.x;
+      members = unsigned(ec.y);
+      NR = (32 - __clz(int(members))) * G;  // up to the last member in the mask
+    } else {
+      NR = G;
+    }
+    n_splits_b = 2;  // partials only
+  }
 
   // ---- stage Q (rows >= G are zero) and init barriers --------------------
   const T *qg = static_cast<const T *>(p.q) + int64_t(b) * p.q_sb + int64_t(lo) * p.q_sh;
   for (int i = threadIdx.x; i < 16 * (D / 8); i += W * 32) {
     int r = i / (D / 8), c = (i % (D / 8)) * 8;
     uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < G) {
-      const T *src = qg + int64_t(r) * p.q_sh + c;
+    bool row_live;
+    const T *src;
+    if constexpr (MODE == 1) {  // row r = (member r / G, head lo + r % G)
+      const int m = r / G;
+      row_live = r < NR && ((members >> m) & 1u);
+      src = static_cast<const T *>(p.q) + int64_t(mbase + m) * p.q_sb +
+            int64_t(lo + r - m * G) * p.q_sh + c;
+    } else {
+      row_live = r < G;
+      src = qg + int64_t(r) * p.q_sh + c;
+    }
+    if (row_live) {
       if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
         v = *reinterpret_cast<const uint4 *>(src);
       } else {
@@ -172,6 +335,12 @@ __global__ void __launch_bounds__(W * 32, 2) decode_kernel(const DecodeParams p)
     int tok0 = u * kUnit;
     int page = tok0 / p.bs;
     int blk = p.tables[int64_t(b) * p.bt_stride + page];
+    if constexpr (MODE == 1) {  // the caller's promise: every member holds the same block
+      for (int m = 0; m < 16; ++m) {
+        if (((members >> m) & 1u) && p.tables[int64_t(mbase + m) * p.bt_stride + page] != blk)
+          atomicOr(p.diag, int32_t(kDiagBadLaunch));
+      }
+    }
     if (blk >= 0) {
       uint64_t off = p.offsets[blk];
       int64_t e = int64_t(off) + int64_t(tok0 % p.bs) * row_stride + int64_t(kvh) * D;
@@ -344,8 +513,9 @@ __global__ void __launch_bounds__(W * 32, 2) decode_kernel(const DecodeParams p)
 #pragma unroll
     for (int i = 0; i < C::ND; ++i) {
       int d = i * 8 + 2 * t;
-      if (g < G) *reinterpret_cast<float2 *>(wo + g * D + d) = make_float2(o[i][0], o[i][1]);
-      if (g + 8 < G) *reinterpret_cast<float2 *>(wo + (g + 8) * D + d) = make_float2(o[i][2], o[i][3]);
+      const int nr = MODE == 0 ? G : NR;
+      if (g < nr) *reinterpret_cast<float2 *>(wo + g * D + d) = make_float2(o[i][0], o[i][1]);
+      if (g + 8 < nr) *reinterpret_cast<float2 *>(wo + (g + 8) * D + d) = make_float2(o[i][2], o[i][3]);
     }
     if (t == 0) {
       cm[warp * 16 + g] = m0;
@@ -356,8 +526,11 @@ __global__ void __launch_bounds__(W * 32, 2) decode_kernel(const DecodeParams p)
   }
   __syncthreads();
   const int64_t head0 = int64_t(b) * p.hq + lo;
-  for (int i = threadIdx.x; i < G * (D / 2); i += W * 32) {
+  for (int i = threadIdx.x; i < (MODE == 0 ? G : NR) * (D / 2); i += W * 32) {
     const int h = i / (D / 2), d = (i % (D / 2)) * 2;
+    if constexpr (MODE == 1) {
+      if (!((members >> (h / G)) & 1u)) continue;
+    }
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < W; ++w) M = fmaxf(M, cm[w * 16 + h]);
@@ -377,10 +550,44 @@ __global__ void __launch_bounds__(W * 32, 2) decode_kernel(const DecodeParams p)
       dst[0] = ptx::from_f32<T>(x0 * inv);
       dst[1] = ptx::from_f32<T>(x1 * inv);
     } else {
-      const int64_t row = (head0 + h) * p.num_splits + split;
+      int64_t row;
+      if constexpr (MODE == 1) {
+        const int m = h / G;
+        row = (int64_t(mbase + m) * p.hq + lo + (h - m * G)) * p.num_splits + slot0;
+      } else if constexpr (MODE == 2) {
+        row = (head0 + h) * p.num_splits + slot0;
+      } else {
+        row = (head0 + h) * p.num_splits + split;
+      }
       *reinterpret_cast<float2 *>(p.part_o + row * D + d) = make_float2(x0 * inv, x1 * inv);
       if (d == 0) p.part_lse[row] = M + log2f(L);
     }
+  }
+}
+
+template <typename T, int D, int W, int NS>
+__global__ void __launch_bounds__(W * 32, 2) decode_kernel(const DecodeParams p) {
+  decode_body<T, D, W, NS, 0>(p, blockIdx.z, blockIdx.x);
+}
+
+// Shared-prefix decode: blockIdx.x walks the prep kernel's work list (prefix
+// work first, so the long items start first), blockIdx.y is the kv head.  The
+// grid is sized for the most work the arguments allow; CTAs past the list's
+// count exit after one load.
+template <typename T, int D, int W, int NS>
+__global__ void __launch_bounds__(W * 32, 2)
+    decode_shared_prefix_kernel(const DecodeParams p, const CascadeParams cp) {
+  ptx::grid_dependency_wait();  // the work list is the prep kernel's output
+  const int n = *cp.count;
+  const int4 ea = cp.work[2 * blockIdx.x], ec = cp.work[2 * blockIdx.x + 1];
+  if (int(blockIdx.x) >= n) {
+    ptx::launch_dependents();
+    return;
+  }
+  if (ea.x == 1) {
+    decode_body<T, D, W, NS, 1>(p, 0, 0, ea, ec);
+  } else {
+    decode_body<T, D, W, NS, 2>(p, 0, 0, ea, ec);
   }
 }
 
@@ -401,6 +608,49 @@ __global__ void merge_kernel(const DecodeParams p, int D, int rows) {
   const int n_units = ceil_div_dev(seq_len, kUnit);
   const int ns = ceil_div_dev(n_units, p.units_per_split);
   if (ns <= 1) return;
+  const float *lse = p.part_lse + int64_t(row) * p.num_splits;
+  float M = -INFINITY;
+  for (int s = lane; s < ns; s += 32) M = fmaxf(M, lse[s]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float wsum = 0.f;
+  for (int s = lane; s < ns; s += 32) wsum += ptx::fast_exp2(lse[s] - M);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+  const float inv = 1.f / wsum;
+  const float *po = p.part_o + int64_t(row) * p.num_splits * D;
+  T *dst = static_cast<T *>(p.out) + int64_t(b) * p.o_sb + int64_t(row % p.hq) * p.o_sh;
+  for (int d = lane * 4; d < D; d += 128) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int s = 0; s < ns; ++s) {
+      const float w = ptx::fast_exp2(lse[s] - M);
+      const float4 v = *reinterpret_cast<const float4 *>(po + int64_t(s) * D + d);
+      acc.x += v.x * w;
+      acc.y += v.y * w;
+      acc.z += v.z * w;
+      acc.w += v.w * w;
+    }
+    dst[d] = ptx::from_f32<T>(acc.x * inv);
+    dst[d + 1] = ptx::from_f32<T>(acc.y * inv);
+    dst[d + 2] = ptx::from_f32<T>(acc.z * inv);
+    dst[d + 3] = ptx::from_f32<T>(acc.w * inv);
+  }
+}
+
+// Merge of the shared-prefix decode: every row's slots are its group's prefix
+// splits followed by its own suffix splits, all of them partials.
+template <typename T>
+__global__ void merge_shared_prefix_kernel(const DecodeParams p, const CascadeParams cp, int D,
+                                           int rows) {
+  ptx::grid_dependency_wait();
+  ptx::launch_dependents();
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);  // b * hq + h
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int b = row / p.hq;
+  const int ns = cp.seq_slots[b];  // 0 for an empty sequence: left untouched
+  if (ns <= 0) return;
   const float *lse = p.part_lse + int64_t(row) * p.num_splits;
   float M = -INFINITY;
   for (int s = lane; s < ns; s += 32) M = fmaxf(M, lse[s]);
@@ -1117,6 +1367,180 @@ cudaError_t decode_attention(const DecodeArgs &a, cudaStream_t stream) {
       e = launch_pdl(merge_kernel<__nv_bfloat16>, mgrid, dim3(128), 0, stream, p, a.head_dim, rows);
     } else {
       e = launch_pdl(merge_kernel<__half>, mgrid, dim3(128), 0, stream, p, a.head_dim, rows);
+    }
+  }
+  if (owned) {
+    cudaError_t f = cudaFreeAsync(scratch, stream);
+    if (e == cudaSuccess) e = f;
+  }
+  return e;
+}
+
+namespace {
+
+using SharedPrefixFn = void (*)(const DecodeParams, const CascadeParams);
+
+template <typename T>
+bool pick_shared_prefix(int D, SharedPrefixFn *fn, size_t *smem) {
+  switch (D) {
+#define KCMM_CASE(DD)                                                  \
+  case DD:                                                             \
+    *fn = decode_shared_prefix_kernel<T, DD, kWarps, kStages>;         \
+    *smem = Cfg<T, DD, kWarps, kStages>::SMEM;                         \
+    return true;
+    KCMM_CASE(64)
+    KCMM_CASE(128)
+    KCMM_CASE(256)
+#undef KCMM_CASE
+    default:
+      return false;
+  }
+}
+
+// Units per split for `items` work items over at most max_units units, aiming
+// at `waves` waves of 2 CTAs per SM (16..32*W units, at most 16 splits).  The
+// plain decode's rule is 6 waves, which balances contexts of unequal length;
+// the prefix items of a group are few and equally long, and there CTAs of 4
+// units per warp spend most of their time starting up and draining their ring
+// (measured on the beam-search shape: 63 us at 8 splits of 16 units).
+int units_per_split_for(int64_t items, int max_units, int waves) {
+  const int64_t target = int64_t(sm_count()) * 2 * waves;
+  const int64_t want = std::max<int64_t>(1, (target + items - 1) / std::max<int64_t>(items, 1));
+  int ups = int((max_units + want - 1) / want);
+  ups = std::max(ups, (max_units + 15) / 16);
+  ups = std::max(ups, 16);
+  return std::min(ups, 32 * kWarps);
+}
+
+struct SharedPrefixPlan {
+  SharedPrefixFn fn = nullptr;
+  size_t smem = 0, scratch_bytes = 0, resolved_off = 0;
+  int mt = 0, tiles = 0, fit = 1, max_a = 0, b_ups = 0, b_splits = 0;
+  int64_t max_work = 0;
+};
+
+// Groups resolved in one CTA's shared memory: group_starts, and one word per
+// sequence and two per group.
+constexpr int kSharedPrefixMaxBatch = 16384;
+
+SharedPrefixPlan make_shared_prefix_plan(const DecodeArgs &a, int n_groups, int max_group) {
+  SharedPrefixPlan pl;
+  const int G = (a.num_q_heads + a.kv_heads - 1) / a.kv_heads;
+  if (a.head_dim % 16 != 0 || a.block_size % kUnit != 0 || G > 16 ||
+      a.num_q_heads % a.kv_heads != 0)
+    return pl;
+  const bool ok = a.dtype == Dtype::BF16
+                      ? pick_shared_prefix<__nv_bfloat16>(a.head_dim, &pl.fn, &pl.smem)
+                      : pick_shared_prefix<__half>(a.head_dim, &pl.fn, &pl.smem);
+  if (!ok) {
+    pl.fn = nullptr;
+    return pl;
+  }
+  const int max_units =
+      int((int64_t(a.max_blocks_per_seq) * a.block_size + kUnit - 1) / kUnit);
+  pl.mt = 16 / G;
+  pl.tiles = (max_group + pl.mt - 1) / pl.mt;
+  // Prefix tiles are few and equally long: split each into as many pieces as
+  // one wave of 2 CTAs per SM holds for all of them (at least one; at most 32
+  // units per warp), so every piece starts at once and none waits for a slot.
+  const int64_t prefix_ctas = int64_t(n_groups) * pl.tiles * a.kv_heads;
+  pl.fit = int(std::max<int64_t>(1, std::min<int64_t>(16, int64_t(sm_count()) * 2 / prefix_ctas)));
+  pl.max_a = std::max(pl.fit, (max_units + 32 * kWarps - 1) / (32 * kWarps));
+  pl.b_ups = units_per_split_for(int64_t(a.batch) * a.kv_heads, max_units, 6);
+  pl.b_splits = (max_units + pl.b_ups - 1) / pl.b_ups;
+  const size_t rows = size_t(a.batch) * a.num_q_heads * size_t(pl.max_a + pl.b_splits);
+  pl.resolved_off = (rows * size_t(a.head_dim) * 4 + rows * 4 + 15) & ~size_t(15);
+  pl.max_work = int64_t(n_groups) * pl.tiles * pl.max_a + int64_t(a.batch) * pl.b_splits;
+  // seq_slots and the count, then the 32-byte work entries (16-byte aligned)
+  pl.scratch_bytes = pl.resolved_off + ((size_t(a.batch) + 1) * 4 + 15) / 16 * 16 +
+                     size_t(pl.max_work) * 32;
+  return pl;
+}
+
+}  // namespace
+
+size_t decode_shared_prefix_scratch_bytes(const DecodeArgs &a, int n_groups, int max_group) {
+  return make_shared_prefix_plan(a, n_groups, max_group).scratch_bytes;
+}
+
+cudaError_t decode_attention_shared_prefix(const DecodeArgs &a, const int32_t *group_starts,
+                                           const int32_t *prefix_lens, int n_groups,
+                                           int max_group, cudaStream_t stream) {
+  const SharedPrefixPlan pl = make_shared_prefix_plan(a, n_groups, max_group);
+  if (!pl.fn) return cudaErrorNotSupported;
+  if (a.batch > kSharedPrefixMaxBatch || pl.max_work > 0x7fffffff) return cudaErrorInvalidValue;
+  DecodeParams p = {};
+  p.q = a.q;
+  p.out = a.out;
+  p.tables = a.block_tables;
+  p.seq_lens = a.seq_lens;
+  p.offsets = a.block_offsets;
+  p.va_k = a.va_k;
+  p.va_v = a.va_v;
+  p.region_elems = a.region_elems;
+  p.batch = a.batch;
+  p.hq = a.num_q_heads;
+  p.hkv = a.kv_heads;
+  p.bs = a.block_size;
+  p.max_bps = a.max_blocks_per_seq;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.diag = a.diag;
+  p.q_sb = int64_t(a.num_q_heads) * a.head_dim;
+  p.q_sh = a.head_dim;
+  p.o_sb = p.q_sb;
+  p.o_sh = a.head_dim;
+  p.bt_stride = a.max_blocks_per_seq;
+  p.units_per_split = pl.b_ups;
+  p.num_splits = pl.max_a + pl.b_splits;  // slot stride of a row
+  p.n_head_tiles = 1;
+  CascadeParams cp = {};
+  cp.group_starts = group_starts;
+  cp.prefix_lens = prefix_lens;
+  cp.n_groups = n_groups;
+  cp.max_group_size = max_group;
+  cp.members_per_tile = pl.mt;
+  cp.tiles_per_group = pl.tiles;
+  cp.fit = pl.fit;
+  cp.max_a = pl.max_a;
+
+  void *scratch = nullptr;
+  bool owned = false;
+  cudaError_t e = cudaSuccess;
+  if (a.scratch) {
+    if (a.scratch_bytes < pl.scratch_bytes) return cudaErrorInvalidValue;
+    scratch = a.scratch;
+  } else if ((scratch = stream_scratch(stream, pl.scratch_bytes)) == nullptr) {
+    e = scratch_acquire(a, pl.scratch_bytes, stream, &scratch, &owned);
+    if (e != cudaSuccess) return e;
+  }
+  const size_t rows = size_t(a.batch) * a.num_q_heads * size_t(p.num_splits);
+  p.part_o = static_cast<float *>(scratch);
+  p.part_lse = p.part_o + rows * size_t(a.head_dim);
+  char *res = static_cast<char *>(scratch) + pl.resolved_off;
+  cp.seq_slots = reinterpret_cast<int32_t *>(res);
+  cp.count = cp.seq_slots + a.batch;
+  cp.work = reinterpret_cast<int4 *>(res + ((size_t(a.batch) + 1) * 4 + 15) / 16 * 16);
+
+  const size_t prep_smem = (size_t(n_groups) * 3 + 1 + size_t(a.batch)) * 4;
+  e = cudaFuncSetAttribute(shared_prefix_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           int(prep_smem));
+  if (e == cudaSuccess)
+    e = launch_pdl(shared_prefix_prep_kernel, dim3(1), dim3(1024), prep_smem, stream, p, cp);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(pl.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pl.smem));
+  if (e == cudaSuccess) {
+    dim3 grid(unsigned(pl.max_work), a.kv_heads, 1);
+    e = launch_pdl(pl.fn, grid, dim3(kWarps * 32), pl.smem, stream, p, cp);
+  }
+  if (e == cudaSuccess) {
+    const int nrows = a.batch * a.num_q_heads;
+    const dim3 mgrid((nrows + 3) / 4);
+    if (a.dtype == Dtype::BF16) {
+      e = launch_pdl(merge_shared_prefix_kernel<__nv_bfloat16>, mgrid, dim3(128), 0, stream, p,
+                     cp, a.head_dim, nrows);
+    } else {
+      e = launch_pdl(merge_shared_prefix_kernel<__half>, mgrid, dim3(128), 0, stream, p, cp,
+                     a.head_dim, nrows);
     }
   }
   if (owned) {

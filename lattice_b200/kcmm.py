@@ -257,6 +257,12 @@ SIGNATURES: dict[str, tuple] = {
     "kcmm_peer_signal_words": (u32, [u32]),
     "kcmm_peer_allgather_on_stream": (i32, [u64, u64, pu64, pu64, u32, u32, u64, u64]),
     "kcmm_peer_wait_on_stream": (i32, [u64, u32, u64, u64, u64]),
+    "kcmm_paged_attn_decode_shared_prefix_bf16_on_stream": (
+        i32, [P, u32, u64, u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, f32, u64, u64,
+              u32, u32, u64]),
+    "kcmm_paged_attn_decode_shared_prefix_f16_on_stream": (
+        i32, [P, u32, u64, u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, f32, u64, u64,
+              u32, u32, u64]),
     "kcmm_paged_attn_decode_bf16_allgather_on_stream": (
         i32, [P, u32, u64, u64, u64, u64, u64, u32, u32, u32, u32, u32, u32, f32, pu64, pu64,
               u32, u32, u64, u64]),

@@ -305,3 +305,23 @@ def test_decode_allgather_argument_checks(kcmm_lib, host_pool_factory, dtype):
     assert call(sigs=(1024, 0)) == -1 and "signal" in pool.last_error()
     # valid peer arguments get as far as the device check
     assert call() == -1 and "device" in pool.last_error().lower()
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_shared_prefix_decode_argument_checks(kcmm_lib, host_pool_factory, dtype):
+    """Group arguments are checked before any device work (host pool): NULL group
+    arrays, no groups, more groups than sequences, max_group_size 0, and more than 16
+    query heads per kv head."""
+    lib = kcmm_lib.lib
+    pool = host_pool_factory(kv_heads=2, head_dim=64, max_batch=4, max_seq_len=256)
+    fn = getattr(lib, f"kcmm_paged_attn_decode_shared_prefix_{dtype}_on_stream")
+
+    def call(starts=6, lens=7, n=1, mx=2, hq=8, hkv=2):
+        return fn(pool.handle, 0, 1, 2, 3, 4, 5, 2, hq, hkv, 64, 16, 16, 0.125, starts, lens,
+                  n, mx, 0)
+
+    for kw in (dict(starts=0), dict(lens=0), dict(n=0), dict(n=3), dict(mx=0), dict(mx=3)):
+        assert call(**kw) == -1
+        assert "shared_prefix" in pool.last_error() and "group" in pool.last_error()
+    assert call(hq=34, hkv=2) == -1 and "16 query heads" in pool.last_error()
+    assert call() == -1 and "device" in pool.last_error().lower()
