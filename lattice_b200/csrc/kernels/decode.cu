@@ -222,7 +222,7 @@ struct Cfg {
 template <typename T, int D, int W, int NS, int MODE>
 __device__ __forceinline__ void decode_body(const DecodeParams &p, const int item,
                                             const int split, const int4 ea = int4{},
-                                            const int4 ec = int4{}) {
+                                            const int4 ec = int4{}, const int kvh_in = 0) {
   using C = Cfg<T, D, W, NS>;
   using MMA = ptx::Mma<T>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -236,8 +236,8 @@ __device__ __forceinline__ void decode_body(const DecodeParams &p, const int ite
   ptx::grid_dependency_wait();
   ptx::launch_dependents();
 
-  const int kvh = blockIdx.y / p.n_head_tiles;
-  const int ht = blockIdx.y % p.n_head_tiles;
+  const int kvh = MODE == 0 ? int(blockIdx.y) / p.n_head_tiles : kvh_in;
+  const int ht = MODE == 0 ? int(blockIdx.y) % p.n_head_tiles : 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   int b, seq_len, u_begin, u_end, n_splits_b, G, lo, hi;
@@ -570,24 +570,26 @@ __global__ void __launch_bounds__(W * 32, 2) decode_kernel(const DecodeParams p)
   decode_body<T, D, W, NS, 0>(p, blockIdx.z, blockIdx.x);
 }
 
-// Shared-prefix decode: blockIdx.x walks the prep kernel's work list (prefix
-// work first, so the long items start first), blockIdx.y is the kv head.  The
+// Shared-prefix decode: blockIdx.x = entry * Hkv + kv head walks the prep
+// kernel's work list with the kv head fastest, so CTAs start in list order
+// (prefix work first: the long items start together in the first wave).  The
 // grid is sized for the most work the arguments allow; CTAs past the list's
 // count exit after one load.
 template <typename T, int D, int W, int NS>
 __global__ void __launch_bounds__(W * 32, 2)
     decode_shared_prefix_kernel(const DecodeParams p, const CascadeParams cp) {
   ptx::grid_dependency_wait();  // the work list is the prep kernel's output
+  const int entry = int(blockIdx.x) / p.hkv, kvh = int(blockIdx.x) % p.hkv;
   const int n = *cp.count;
-  const int4 ea = cp.work[2 * blockIdx.x], ec = cp.work[2 * blockIdx.x + 1];
-  if (int(blockIdx.x) >= n) {
+  const int4 ea = cp.work[2 * entry], ec = cp.work[2 * entry + 1];
+  if (entry >= n) {
     ptx::launch_dependents();
     return;
   }
   if (ea.x == 1) {
-    decode_body<T, D, W, NS, 1>(p, 0, 0, ea, ec);
+    decode_body<T, D, W, NS, 1>(p, 0, 0, ea, ec, kvh);
   } else {
-    decode_body<T, D, W, NS, 2>(p, 0, 0, ea, ec);
+    decode_body<T, D, W, NS, 2>(p, 0, 0, ea, ec, kvh);
   }
 }
 
@@ -1468,7 +1470,8 @@ cudaError_t decode_attention_shared_prefix(const DecodeArgs &a, const int32_t *g
                                            int max_group, cudaStream_t stream) {
   const SharedPrefixPlan pl = make_shared_prefix_plan(a, n_groups, max_group);
   if (!pl.fn) return cudaErrorNotSupported;
-  if (a.batch > kSharedPrefixMaxBatch || pl.max_work > 0x7fffffff) return cudaErrorInvalidValue;
+  if (a.batch > kSharedPrefixMaxBatch || pl.max_work * a.kv_heads > 0x7fffffff)
+    return cudaErrorInvalidValue;
   DecodeParams p = {};
   p.q = a.q;
   p.out = a.out;
@@ -1529,7 +1532,7 @@ cudaError_t decode_attention_shared_prefix(const DecodeArgs &a, const int32_t *g
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(pl.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pl.smem));
   if (e == cudaSuccess) {
-    dim3 grid(unsigned(pl.max_work), a.kv_heads, 1);
+    dim3 grid(unsigned(pl.max_work * a.kv_heads), 1, 1);
     e = launch_pdl(pl.fn, grid, dim3(kWarps * 32), pl.smem, stream, p, cp);
   }
   if (e == cudaSuccess) {
