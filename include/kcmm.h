@@ -578,7 +578,7 @@ int32_t kcmm_get_kernel_status(kcmm_pool_t *pool);
  * member's inside the shared pages sets bit 2 of kcmm_get_kernel_status (the
  * result is then undefined for that group).  Needs num_q_heads a multiple of
  * num_kv_heads with at most 16 query heads per kv head, head_dim 64, 128 or 256,
- * and at most 16384 sequences; -1 otherwise.  Each call first resolves the groups
+ * and at most 8192 sequences; -1 otherwise.  Each call first resolves the groups
  * in one small kernel, so the attention kernels read two words per item.
  */
 int kcmm_paged_attn_decode_shared_prefix_bf16_on_stream(

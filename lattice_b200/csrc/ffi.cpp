@@ -546,8 +546,8 @@ static int decode_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, u
                        "and 1 <= max_group_size <= batch");
       return -1;
     }
-    if (batch > 16384) {
-      set_error(h, std::string(op) + ": at most 16384 sequences per call");
+    if (batch > 8192) {
+      set_error(h, std::string(op) + ": at most 8192 sequences per call");
       return -1;
     }
     if (hq % hkv != 0 || hq / hkv > 16) {

@@ -116,8 +116,14 @@ __global__ void shared_prefix_prep_kernel(const DecodeParams p, const CascadePar
   int32_t *sg = prep_smem + c.n_groups + 1;     // [batch]: group shared, or -1
   int32_t *gu = sg + p.batch;                   // [n_groups]: units shared
   int32_t *gn = gu + c.n_groups;                // [n_groups]: prefix splits
+  int32_t *sl = gn + c.n_groups;                // [batch]: seq_lens, capped
+  int32_t *gp = sl + p.batch;                   // [n_groups]: prefix_lens
   __shared__ int n_work;
+  const int cap = p.max_bps * p.bs;
+  // every global input in one pass: the rest of the kernel works from shared memory
   for (int i = threadIdx.x; i <= c.n_groups; i += blockDim.x) gs[i] = c.group_starts[i];
+  for (int i = threadIdx.x; i < c.n_groups; i += blockDim.x) gp[i] = c.prefix_lens[i];
+  for (int i = threadIdx.x; i < p.batch; i += blockDim.x) sl[i] = min(p.seq_lens[i], cap);
   if (threadIdx.x == 0) n_work = 0;
   __syncthreads();
   auto group_of = [&](int b) {  // the last group whose start is <= b
@@ -142,14 +148,13 @@ __global__ void shared_prefix_prep_kernel(const DecodeParams p, const CascadePar
     sg[b] = in ? g : -1;
   }
   __syncthreads();
-  const int cap = p.max_bps * p.bs;
   for (int g = threadIdx.x; g < c.n_groups; g += blockDim.x) {
     int pl = 0;
     if (well_formed(g)) {
-      pl = c.prefix_lens[g];
+      pl = gp[g];
       const int s_end = min(gs[g + 1], gs[g] + c.max_group_size);
       for (int m = gs[g]; m < s_end; ++m) {
-        if (sg[m] == g) pl = min(pl, min(p.seq_lens[m], cap));
+        if (sg[m] == g) pl = min(pl, sl[m]);
       }
     }
     const int pu = max(pl, 0) / kUnit;
@@ -176,7 +181,7 @@ __global__ void shared_prefix_prep_kernel(const DecodeParams p, const CascadePar
   }
   __syncthreads();  // prefix work first: the long items start first
   for (int b = threadIdx.x; b < p.batch; b += blockDim.x) {
-    const int len = min(p.seq_lens[b], cap);
+    const int len = sl[b];
     const int g = sg[b];
     const int pu = g >= 0 ? gu[g] : 0;
     const int na = g >= 0 ? gn[g] : 0;
@@ -1421,9 +1426,9 @@ struct SharedPrefixPlan {
   int64_t max_work = 0;
 };
 
-// Groups resolved in one CTA's shared memory: group_starts, and one word per
-// sequence and two per group.
-constexpr int kSharedPrefixMaxBatch = 16384;
+// Groups resolved in one CTA's shared memory: group_starts, two words per
+// sequence and three per group (at most 192 KB).
+constexpr int kSharedPrefixMaxBatch = 8192;
 
 SharedPrefixPlan make_shared_prefix_plan(const DecodeArgs &a, int n_groups, int max_group) {
   SharedPrefixPlan pl;
@@ -1524,7 +1529,7 @@ cudaError_t decode_attention_shared_prefix(const DecodeArgs &a, const int32_t *g
   cp.count = cp.seq_slots + a.batch;
   cp.work = reinterpret_cast<int4 *>(res + ((size_t(a.batch) + 1) * 4 + 15) / 16 * 16);
 
-  const size_t prep_smem = (size_t(n_groups) * 3 + 1 + size_t(a.batch)) * 4;
+  const size_t prep_smem = (size_t(n_groups) * 4 + 1 + size_t(a.batch) * 2) * 4;
   e = cudaFuncSetAttribute(shared_prefix_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            int(prep_smem));
   if (e == cudaSuccess)

@@ -133,6 +133,14 @@ def test_eight_heads_per_kv_head():
     _run_case([5, 4], [32, 32], [512, 500], lens, 5, hq=16, hkv=2, seed=3)
 
 
+def test_more_sequences_than_prep_threads():
+    """1500 sequences in groups of 3 (500 groups): the prep kernel's thread-stride
+    loops and a long work list."""
+    rng = np.random.default_rng(7)
+    lens = [40 + int(x) for x in rng.integers(0, 60, 1500)]
+    _run_case([3] * 500, [2] * 500, [32] * 500, lens, 3, hq=8, hkv=2, seed=7)
+
+
 def test_malformed_groups_keep_the_result():
     torch = _torch()
     wl = _build([4, 4], [20, 20], [400, 380, 330, 390, 350, 341, 399, 333], seed=4)
