@@ -764,9 +764,12 @@ __global__ void __launch_bounds__(kMergeGatherThreads) merge_gather_kernel(const
       for (int r = 0; r < g.world; ++r) *reinterpret_cast<uint2 *>(g.dst[r] + goff + d) = v;
     }
   }
-  __threadfence_system();  // this thread's stores (peers' memory included) before the flags
+  // The CTA barrier orders every thread's stores (peers' memory included) before
+  // the flag threads' system-scope fence and release store, which carry them to
+  // the other GPUs (cumulativity: the pattern of a cooperative grid barrier).
   __syncthreads();
   if (int(threadIdx.x) < g.world) {
+    __threadfence_system();
     unsigned long long *f = g.sig[threadIdx.x] + g.rank * kGatherBlocks + blockIdx.x;
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(g.epoch) : "memory");
   }

@@ -6,8 +6,8 @@
 // rank's buffer (its own included) with plain stores through CUDA IPC
 // mappings, then raises its flags in every rank's signal array:
 //   signal[r][src * kGatherBlocks + blk] = epoch   (u64, system scope, release)
-// one flag per CTA, written by the CTA's thread 0 after the CTA's stores are
-// fenced at system scope.  peer_wait spins, bounded, until every flag of its own
+// one flag per CTA and rank, written by thread r after the CTA barrier and a
+// system-scope fence.  peer_wait spins, bounded, until every flag of its own
 // signal array has reached `epoch`; the gathered buffer is then complete.  A
 // wait that runs out writes 1 to `status` and returns (no trap), so a missing
 // rank is reported instead of hanging the GPU.
@@ -47,9 +47,12 @@ __global__ void __launch_bounds__(512) peer_allgather_kernel(const GatherArgs a)
     const uint4 v = a.src[i];
     for (int r = 0; r < a.world; ++r) a.dst[r][uint64_t(a.rank) * a.n16 + i] = v;
   }
-  __threadfence_system();  // this thread's peer stores before the CTA's flags
+  // The CTA barrier orders every thread's peer stores before the flag threads'
+  // system-scope fence and release store (cumulativity: the pattern of a
+  // cooperative grid barrier), so one fence per flag replaces one per thread.
   __syncthreads();
   if (threadIdx.x < a.world) {
+    __threadfence_system();
     unsigned long long *f = a.sig[threadIdx.x] + a.rank * kGatherBlocks + blockIdx.x;
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(a.epoch) : "memory");
   }
