@@ -218,12 +218,12 @@ struct Cfg {
 // the Llama-3-8B decode shape (measured: 129.8 us against 117.3 us per call).
 //
 // MODE 0: the plain decode, item = blockIdx.z = sequence.
-// MODE 1: a prefix item of the shared-prefix decode (item = group * tiles_per_group
-//         + tile): rows are (member, query head) pairs, keys the group's shared
-//         units read through its first member's block table; always partials, slot
-//         = split.
-// MODE 2: a suffix item (item = sequence): the units past the sequence's shared
-//         prefix; always partials, slots after the prefix ones.
+// MODE 1: a prefix entry of the shared-prefix decode (ea / ec, written by
+//         shared_prefix_prep_kernel): rows are (member, query head) pairs of the
+//         entry's member mask, keys the group's shared units read through its
+//         first member's block table; a partial into the entry's slot.
+// MODE 2: an own-tokens entry: one sequence's units past its shared prefix; a
+//         partial into the entry's slot, after the prefix ones.
 template <typename T, int D, int W, int NS, int MODE>
 __device__ __forceinline__ void decode_body(const DecodeParams &p, const int item,
                                             const int split, const int4 ea = int4{},
@@ -1468,10 +1468,6 @@ SharedPrefixPlan make_shared_prefix_plan(const DecodeArgs &a, int n_groups, int 
 }
 
 }  // namespace
-
-size_t decode_shared_prefix_scratch_bytes(const DecodeArgs &a, int n_groups, int max_group) {
-  return make_shared_prefix_plan(a, n_groups, max_group).scratch_bytes;
-}
 
 cudaError_t decode_attention_shared_prefix(const DecodeArgs &a, const int32_t *group_starts,
                                            const int32_t *prefix_lens, int n_groups,

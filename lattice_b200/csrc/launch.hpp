@@ -62,8 +62,8 @@ cudaError_t decode_attention(const DecodeArgs &a, cudaStream_t stream);
 // [group_starts[g], group_starts[g+1]) share their first prefix_lens[g] tokens'
 // pages (device arrays); at most max_group members of a group share, the rest
 // attend alone.  Dense q / out / tables only; the strides and peer fields of `a`
-// are ignored.  cudaErrorNotSupported outside the tensor-core shapes or G > 16.
-size_t decode_shared_prefix_scratch_bytes(const DecodeArgs &a, int n_groups, int max_group);
+// are ignored.  cudaErrorNotSupported outside head_dim 64 / 128 / 256, a block
+// size that is a multiple of 16, or G > 16.
 cudaError_t decode_attention_shared_prefix(const DecodeArgs &a, const int32_t *group_starts,
                                            const int32_t *prefix_lens, int n_groups,
                                            int max_group, cudaStream_t stream);
