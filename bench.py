@@ -596,7 +596,10 @@ def run_cow_leg(args):
     """Beam-search CoW (BASELINE config 4 shapes, 32 layers): 16 requests x 4 beams share a
     2048-token prefix plus a partly filled tail block; a step forks the 4 beams from their
     request and copies each beam's shared tail (64 whole-block copies across all 64
-    regions), then runs decode attention of the 64 beams over the shared pages."""
+    regions), then runs decode attention of the 64 beams over the shared pages twice:
+    the plain decode (every beam reads the prefix pages) and the shared-prefix decode
+    (the 4 beams of a request form a group that reads them once).  Both are reported
+    against the unique bytes; the leg checks that they agree."""
     import torch
 
     from lattice_b200 import kcmm
