@@ -191,6 +191,21 @@ def max_over_ranks(ms: float) -> float:
     return float(t.item())
 
 
+def gather_over_ranks(values: list[float]) -> list[list[float]]:
+    """Every rank's `values`, as a list indexed by rank (the local list alone
+    without a process group)."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return [list(values)]
+    dev = (f"cuda:{torch.cuda.current_device()}" if dist.get_backend() == "nccl" else "cpu")
+    t = torch.tensor(values, dtype=torch.float64, device=dev)
+    rows = [torch.zeros_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(rows, t)
+    return [r.cpu().tolist() for r in rows]
+
+
 def barrier() -> None:
     import torch.distributed as dist
 
@@ -213,7 +228,12 @@ def run_ours(args):
     # --profile: same batch, heads and length distribution with the tables drawn
     # from a 12k-block pool, so that an ncu capture saves/restores < 1 GB per pass.
     pool_blocks = 12000 if args.profile else 40000
-    wl = DecodeWorkload(seed=1000 + rank, device=local, pool_blocks=pool_blocks).build()
+    # Every rank draws the same context lengths (one shared seed), so each rank moves
+    # the same bytes and the 1 -> N curve measures the hardware; pages, tables and
+    # queries come from a per-rank seed.
+    lens = np.random.default_rng(1000).integers(512, 4097, 64).astype(np.int32).tolist()
+    wl = DecodeWorkload(seed=1000 + rank, device=local, pool_blocks=pool_blocks,
+                        seq_lens_override=lens).build()
     # the step's new token of sequence b sits at position L_b - 1 of its table
     slots = np.array([int(wl.tables[b, (L - 1) // 16]) * 16 + (L - 1) % 16
                       for b, L in enumerate(wl.seq_lens)], np.int64)
@@ -271,14 +291,19 @@ def run_ours(args):
     peak, peak_kind = peaks()
     from lattice_b200.kcmm import KcmmError  # noqa: F401  (import check)
 
-    splits = int(os.environ.get("KCMM_DECODE_SPLITS", "0"))
     launches_per_step = 1 + 2  # fused append + decode main + split merge
     e2e = run_e2e(args, wl, fa, stream, world) if not args.profile else None
     status = wl.pool.kernel_status()
+    per_rank = gather_over_ranks([attn_avg, attn_bytes, float(status)])
+    cpu_baseline_sample = (cpu_baseline(wl) if rank == 0 and world == 1 and not args.profile
+                           else None)
+    wl.close()
+    # BASELINE config 5's KV-head split on the same ranks (strong scaling)
+    hs = headsplit_measure(args, world, rank, local) if not args.profile else None
 
     result = None
     if rank == 0:
-        cpu = cpu_baseline(wl) if world == 1 and not args.profile else None
+        cpu = cpu_baseline_sample if world == 1 and not args.profile else None
         result = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_step, 5),
@@ -299,10 +324,17 @@ def run_ours(args):
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clk,
-            "device_status": status,
+            "device_status": int(max(r[2] for r in per_rank)),
+            "per_rank": {
+                "attn_us_min_max": [round(min(r[0] for r in per_rank) * 1e3, 2),
+                                    round(max(r[0] for r in per_rank) * 1e3, 2)],
+                "roofline_frac_min_max": [
+                    round(min(r[1] / (r[0] * 1e-3) / 1e9 for r in per_rank) / peak, 4),
+                    round(max(r[1] / (r[0] * 1e-3) / 1e9 for r in per_rank) / peak, 4)],
+                "bytes_equal": len({r[1] for r in per_rank}) == 1},
+            "headsplit": hs,
         }
         print(json.dumps(result))
-    wl.close()
     if world > 1:
         import torch.distributed as dist
 
@@ -878,7 +910,10 @@ def run_prefill_leg(args):
          "status": status})
 
 
-def run_headsplit_leg(args):
+HEADSPLIT = {"num_q_heads": 64, "kv_heads": 8, "seqs": 8, "context": 32768}
+
+
+def headsplit_measure(args, world: int, rank: int, local: int) -> dict | None:
     """Llama-3-70B decode with KV heads sharded across the N ranks:
     8 sequences of 32,768 tokens, 64 q heads / 8 kv heads, D 128, bf16.  Rank r holds
     kv heads [r*8/N, (r+1)*8/N) and their query heads for every sequence; a step is the
@@ -888,26 +923,31 @@ def run_headsplit_leg(args):
     `kcmm_peer_allgather_on_stream` + `kcmm_peer_wait_on_stream` after the decode (stores
     into the peers' buffers over NVLink and per-CTA flags); and
     `kcmm_paged_attn_decode_bf16_allgather_on_stream` + the wait, where the decode's
-    merge kernel stores the rows into the peers' buffers itself.  The value line counts
-    the fastest, all are reported, and the leg checks that all gather the same bytes.
-    Strong scaling: the total work is fixed as N grows."""
+    merge kernel stores the rows into the peers' buffers itself.  Steps run back to
+    back with no host barrier (the gathered buffers alternate halves by epoch).
+
+    Parity, on every rank: the rank's own rows of two sampled sequences against a
+    torch fp32 reference of the same pages (max-abs 2e-3 / max-rel 1e-2), and every
+    peer-store gather bit-identical to NCCL's; the flags reduced over ranks.
+    Strong scaling: the total work is fixed as N grows.  Returns the summary on rank 0
+    (None elsewhere); every rank takes the same collective steps."""
     import ctypes
 
     import torch
 
-    from lattice_b200.workloads import DecodeWorkload, PeerBuffers, library
+    from lattice_b200.workloads import DecodeWorkload, PeerBuffers, library, read_device
 
-    world, rank, local = dist_setup(args)
     torch.cuda.set_device(local)
-    hq, hkv, seqs, ctx = 64, 8, 8, 32768
+    hq, hkv = HEADSPLIT["num_q_heads"], HEADSPLIT["kv_heads"]
+    seqs, ctx = HEADSPLIT["seqs"], HEADSPLIT["context"]
     if hkv % world:
-        raise SystemExit(f"headsplit needs a rank count dividing {hkv}")
+        return {"skipped": f"{world} ranks do not divide {hkv} kv heads"} if rank == 0 else None
     hkv_l, hq_l = hkv // world, hq // world
     wl = DecodeWorkload(batch=seqs, num_q_heads=hq_l, kv_heads=hkv_l, head_dim=128,
                         min_len=ctx, max_len=ctx, pool_blocks=seqs * ctx // 16,
                         seed=3000 + rank, device=local).build()
-    gathered = torch.empty((world,) + tuple(wl.out.shape), dtype=wl.out.dtype,
-                           device=f"cuda:{local}")
+    dev = f"cuda:{local}"
+    gathered = torch.empty((world,) + tuple(wl.out.shape), dtype=wl.out.dtype, device=dev)
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
     import torch.distributed as dist
@@ -915,17 +955,19 @@ def run_headsplit_leg(args):
     lib = library().lib
     slice_bytes = wl.out.numel() * wl.out.element_size()
     pb = PeerBuffers(slice_bytes, rank, world, local) if world > 1 else None
-    status = torch.zeros(1, dtype=torch.int32, device=f"cuda:{local}")
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
     if pb is not None:
         dst = (ctypes.c_uint64 * world)(*pb.buf_ptrs)
         sig = (ctypes.c_uint64 * world)(*pb.sig_ptrs)
         sig_local = pb.signal_ptr
-    else:  # one rank: the fused decode gathers into its own buffer
-        own_sig = torch.zeros(lib.kcmm_peer_signal_words(1), dtype=torch.int64,
-                              device=f"cuda:{local}")
-        dst = (ctypes.c_uint64 * 1)(gathered.data_ptr())
+        half = pb.half_ptr
+    else:  # one rank: the fused decode gathers into its own buffer (two halves)
+        own = torch.empty((2,) + tuple(gathered.shape), dtype=wl.out.dtype, device=dev)
+        own_sig = torch.zeros(lib.kcmm_peer_signal_words(1), dtype=torch.int64, device=dev)
+        dst = (ctypes.c_uint64 * 1)(own.data_ptr())
         sig = (ctypes.c_uint64 * 1)(own_sig.data_ptr())
         sig_local = own_sig.data_ptr()
+        half = lambda e: own[e & 1].data_ptr()  # noqa: E731
     epoch = [0]
 
     def step_nccl():
@@ -937,10 +979,10 @@ def run_headsplit_leg(args):
 
     def step_p2p():
         wl.decode(stream_ptr=sp)
-        pb.epoch += 1
+        epoch[0] += 1
         assert lib.kcmm_peer_allgather_on_stream(wl.out.data_ptr(), slice_bytes, dst, sig, rank,
-                                                 world, pb.epoch, sp) == 0
-        assert lib.kcmm_peer_wait_on_stream(pb.signal_ptr, world, pb.epoch, status.data_ptr(),
+                                                 world, epoch[0], sp) == 0
+        assert lib.kcmm_peer_wait_on_stream(sig_local, world, epoch[0], status.data_ptr(),
                                             sp) == 0
 
     def step_fused():
@@ -965,76 +1007,106 @@ def run_headsplit_leg(args):
             step()
         t1.record(stream)
         torch.cuda.synchronize()
-        return max_over_ranks(t0.elapsed_time(t1)) / args.steps
-
-    from lattice_b200.workloads import read_device
-    import numpy as np
+        return t0.elapsed_time(t1) / args.steps
 
     ms_nccl = timed(step_nccl)
     ref = gathered.view(torch.int16).cpu().numpy().view(np.uint8).reshape(-1).copy()
-    same = True
-    ms_p2p = None
-    if pb is not None:
-        # the p2p epochs share the signal arrays with the fused epochs
-        pb.epoch = epoch[0]
+    # this rank's rows of two sequences against the torch fp32 reference
+    sample = [0, seqs - 1]
+    want = wl.torch_reference(sample)
+    got = gathered[rank][sample].float()
+    err = (got - want).abs()
+    close = bool((err <= 2e-3 + 1e-2 * want.abs()).all())
+    max_err = float(err.max().item())
+    ms_p2p, p2p_same = None, True
+    if world > 1:
         ms_p2p = timed(step_p2p)
-        epoch[0] = pb.epoch
         torch.cuda.synchronize()
-        got = read_device(pb.gathered_ptr, slice_bytes * world)
-        same = bool((got == ref).all()) and int(status.item()) == 0
+        p2p_same = bool((read_device(half(epoch[0]), slice_bytes * world) == ref).all())
     ms_fused = timed(step_fused)
     torch.cuda.synchronize()
-    got = (read_device(pb.gathered_ptr, slice_bytes * world) if pb is not None
-           else gathered.view(torch.int16).cpu().numpy().view(np.uint8).reshape(-1))
-    fused_same = bool((got == ref).all()) and int(status.item()) == 0
-    # the value line uses the fastest of the gathers; all are reported
-    options = {"nccl": ms_nccl, "fused_p2p": ms_fused}
-    if ms_p2p is not None:
-        options["p2p"] = ms_p2p
-    used = min(options, key=options.get)
-    ms = options[used]
+    fused_same = bool((read_device(half(epoch[0]), slice_bytes * world) == ref).all())
+    gather_status = int(status.item())
     # attention alone, for the split of the step
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
     a0.record(stream)
     for _ in range(args.steps):
         wl.decode(stream_ptr=sp)
     a1.record(stream)
     torch.cuda.synchronize()
-    attn_ms = max_over_ranks(a0.elapsed_time(a1)) / args.steps
-    kv_total = wl.kv_bytes() * world  # every rank reads its own heads' pages
-    status_word = wl.pool.kernel_status()
-    if pb is not None:
+    attn_ms = a0.elapsed_time(a1) / args.steps
+    kv_rank = wl.kv_bytes()
+    dev_status = wl.pool.kernel_status()
+    # one row per rank: times, parity flags, status words
+    mine = torch.tensor([ms_nccl, ms_p2p if ms_p2p is not None else 0.0, ms_fused, attn_ms,
+                         float(close and p2p_same and fused_same), float(gather_status),
+                         float(dev_status), max_err], dtype=torch.float64, device=dev)
+    rows = [torch.zeros_like(mine) for _ in range(world)]
+    if world > 1:
+        dist.all_gather(rows, mine)
         barrier()
         pb.close()
+    else:
+        rows = [mine]
     wl.close()
+    if rank != 0:
+        return None
+    r = torch.stack(rows).cpu().numpy()
+    ms = {"nccl": float(r[:, 0].max()), "fused_p2p": float(r[:, 2].max())}
+    if world > 1:
+        ms["p2p"] = float(r[:, 1].max())
+    used = min(ms, key=ms.get)
+    attn = r[:, 3]
     peak, kind = peaks()
+    kv_total = kv_rank * world  # every rank reads its own heads' pages (equal shards)
+    gbs = kv_total / (ms[used] * 1e-3) / 1e9
+    per_rank_frac = kv_rank / (attn * 1e-3) / 1e9 / peak
+    return {
+        "workload": "BASELINE config 5 decode: 8 seqs x 32768 tokens, Hq 64 / Hkv 8, D 128, "
+                    "bf16; kv heads sharded over the ranks, outputs all-gathered",
+        "scaling": "strong", "ranks": world, "kv_heads_per_rank": hkv_l,
+        "value": round(gbs, 1), "unit": "GB/s (whole job, KV bytes / max-over-ranks step)",
+        "ms_per_step": round(ms[used], 4), "allgather_used": used,
+        "ms_per_step_nccl_allgather": round(ms["nccl"], 4),
+        "ms_per_step_p2p_allgather": round(ms["p2p"], 4) if "p2p" in ms else None,
+        "ms_per_step_fused_decode_allgather": round(ms["fused_p2p"], 4),
+        "attention_ms": round(float(attn.max()), 4),
+        "attention_ms_min_max_over_ranks": [round(float(attn.min()), 4),
+                                            round(float(attn.max()), 4)],
+        "allgather_ms": {k: round(max(v - float(attn.max()), 0.0), 4) for k, v in ms.items()},
+        "roofline_frac_per_rank_min_max": [round(float(per_rank_frac.min()), 4),
+                                           round(float(per_rank_frac.max()), 4)],
+        "peak_gbs": peak, "peak_kind": kind,
+        "tokens_per_s_80_layers": round(seqs / (80 * ms[used] * 1e-3), 1),
+        "parity": bool((r[:, 4] == 1.0).all()),
+        "parity_check": "every rank: own rows of sequences 0 and 7 vs a torch fp32 reference "
+                        "(max-abs 2e-3 / max-rel 1e-2); peer-store and fused gathers "
+                        "bit-identical to NCCL's",
+        "max_abs_err": float(r[:, 7].max()),
+        "status": int(max(r[:, 5].max(), r[:, 6].max())),
+    }
+
+
+def run_headsplit_leg(args):
+    """`--workload headsplit`: the KV-head split of config 5 alone, one JSON line."""
+    world, rank, local = dist_setup(args)
+    hs = headsplit_measure(args, world, rank, local)
     line = None
     if rank == 0:
-        gbs = kv_total / (ms * 1e-3) / 1e9
-        line = _line(
-            "70B decode, KV heads sharded: KV GB/s (whole job) and decode tokens/s", gbs,
-            "GB/s",
-            {"workload": "BASELINE config 5 decode: 8 seqs x 32768 tokens, Hq 64 / Hkv 8, "
-                         "D 128, bf16; kv heads sharded over the ranks, outputs all-gathered "
-                         "(NCCL, NVLink peer stores, and peer stores fused into the decode's "
-                         "merge; the fastest counted)", "ranks": world,
-             "scaling": "strong"},
-            {"bound": "hbm", "achieved": round(gbs / world, 1), "peak": peak, "unit": "GB/s",
-             "frac": round(gbs / world / peak, 4), "traffic": None, "peak_kind": kind,
-             "per": "GPU"},
-            {"n_gpus": world, "ms_per_step": round(ms, 4),
-             "attention_ms": round(attn_ms, 4),
-             "allgather_ms": round(max(ms - attn_ms, 0.0), 4),
-             "allgather_used": used,
-             "ms_per_step_p2p_allgather": round(ms_p2p, 4) if ms_p2p is not None else None,
-             "ms_per_step_nccl_allgather": round(ms_nccl, 4),
-             "ms_per_step_fused_decode_allgather": round(ms_fused, 4),
-             "fused_equals_nccl": fused_same,
-             "allgather_ms_nccl": round(max(ms_nccl - attn_ms, 0.0), 4),
-             "p2p_equals_nccl": same,
-             "tokens_per_s_80_layers": round(seqs / (80 * ms * 1e-3), 1),
-             "status": status_word})
+        roof = None
+        if "value" in hs:
+            frac = hs["value"] / world / hs["peak_gbs"]
+            roof = {"bound": "hbm", "achieved": round(hs["value"] / world, 1),
+                    "peak": hs["peak_gbs"], "unit": "GB/s", "frac": round(frac, 4),
+                    "traffic": None, "peak_kind": hs["peak_kind"], "per": "GPU"}
+        line = _line("70B decode, KV heads sharded: KV GB/s (whole job) and decode tokens/s",
+                     hs.get("value", 0.0), "GB/s", {"workload": hs.get("workload"),
+                                                    "ranks": world, "scaling": "strong"},
+                     roof, {"n_gpus": world, "headsplit": hs})
     if world > 1:
+        import torch.distributed as dist
+
         barrier()
         dist.destroy_process_group()
     return line

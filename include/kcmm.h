@@ -600,13 +600,20 @@ int kcmm_paged_attn_decode_shared_prefix_f16_on_stream(
  * The KV-head split of the decode (each GPU attends its own kv heads) needs every
  * rank's output on every rank; the reference plan uses ncclAllGather.  These
  * two calls do it with plain stores into peers' memory and per-CTA flags:
- *   dst_ptrs[r]    rank r's gathered buffer (world slices of nbytes), mapped on
- *                  this device (CUDA IPC or P2P); slice `rank` is written here;
+ *   dst_ptrs[r]    rank r's gathered buffer, mapped on this device (CUDA IPC or
+ *                  P2P): two halves of world slices of nbytes, 2*world*nbytes in
+ *                  all.  Epoch e writes slice `rank` of half (e & 1);
  *   signal_ptrs[r] rank r's signal array, kcmm_peer_signal_words(world) u64
  *                  flags, zeroed once; every call raises this rank's flags there
  *                  to `epoch`, which must grow by one per call on every rank.
  * kcmm_peer_wait_on_stream then waits (bounded, 1 s) until all ranks' flags in
  * this rank's signal array reached epoch; on a timeout it writes 1 to *status.
+ * After the wait for epoch e, half (e & 1) of this rank's buffer holds every
+ * rank's slice.
+ * Ordering rule: on every rank, issue gather(e), wait(e), then every read of
+ * half (e & 1), all before gather(e+1), in stream order.  A peer can be one
+ * epoch ahead and writes the other half meanwhile; it writes half (e & 1) again
+ * only at epoch e+2, after it has seen this rank's epoch e+1 flags.
  * nbytes must be a multiple of 16 and world <= 8.  -1 on invalid arguments.
  */
 uint32_t kcmm_peer_signal_words(uint32_t world);
@@ -619,9 +626,10 @@ int kcmm_peer_wait_on_stream(uint64_t signal_ptr, uint32_t world, uint64_t epoch
 /*
  * The decode of kcmm_paged_attn_decode_{bf16,f16}_on_stream fused with the
  * all-gather above: the kernel that merges the split partials also stores every
- * finished output row into slot `rank` of every rank's gathered buffer
- * (gathered_ptrs[r], [world][batch][num_q_heads][head_dim] 16-bit values, 16-byte
- * aligned) and then raises this rank's flags in signal_ptrs[r] to `epoch`, as
+ * finished output row into slot `rank` of half (epoch & 1) of every rank's
+ * gathered buffer (gathered_ptrs[r], [2][world][batch][num_q_heads][head_dim]
+ * 16-bit values, 16-byte aligned), then raises this rank's flags in
+ * signal_ptrs[r] to `epoch`, under the same ordering rule and as
  * kcmm_peer_allgather_on_stream does, so no separate gather kernel runs.
  * `output_ptr` receives this rank's rows as usual.  Follow with
  * kcmm_peer_wait_on_stream.  Sequences of length 0 leave their rows untouched

@@ -31,7 +31,7 @@ CU_SOURCES = ["kernels/decode.cu", "kernels/decode_noalloc.cu", "kernels/append.
               "kernels/copy.cu", "kernels/prefill.cu", "kernels/tables.cu",
               "kernels/peer.cu"]
 CPP_SOURCES = ["pool.cpp", "vmm.cpp", "ffi.cpp", "step_tables.cpp", "policy.cpp"]
-HEADERS = ["kcmm_internal.hpp", "launch.hpp", "kernels/ptx.cuh", "kernels/decode_streamk.cuh",
+HEADERS = ["kcmm_internal.hpp", "launch.hpp", "kernels/ptx.cuh",
            "kernels/tcgen05.cuh", "kernels/pdl.cuh",
            "step_tables.hpp", "policy.hpp"]
 

@@ -591,10 +591,7 @@ static int decode_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, u
   a.scale = scale;
   a.diag = p->diag_word();
   if (const char *fs = std::getenv("KCMM_DECODE_SPLITS")) a.force_splits = std::atoi(fs);
-  a.region_tokens = p->region_bytes / (uint64_t(hkv) * hd * 2);
   if (noalloc) {
-    // No tensor maps: encoding them fills a host-side cache, and only the
-    // TMA-producer kernel (opt-in) reads them.
     const size_t need = kcmm::dev::decode_scratch_bytes(a);
     const size_t limit = kcmm::dev::decode_noalloc_scratch_limit();
     if (need > limit) {
@@ -615,7 +612,6 @@ static int decode_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, u
       return -1;
     return 0;
   }
-  a.tensor_maps = p->tensor_maps(layer, int(hkv), int(hd));
   if (check_launch(h, op, kcmm::dev::decode_attention(a, S(stream)))) return -1;
   if (sync) {
     cudaError_t e = cudaDeviceSynchronize();

@@ -689,8 +689,9 @@ __global__ void merge_shared_prefix_kernel(const DecodeParams p, const CascadePa
 }
 
 // Peer outputs of merge_gather_kernel: rank r's gathered buffer holds
-// [world][batch][hq][D] 16-bit values; this rank's rows go to slot `rank` of every
-// buffer, then this CTA's flag in every rank's signal array is raised to epoch.
+// [2][world][batch][hq][D] 16-bit values; epoch e writes this rank's rows to slot
+// `rank` of half e & 1 of every buffer (kernels/peer.cu says why two halves), then
+// this CTA's flag in every rank's signal array is raised to epoch.
 struct PeerOut {
   uint16_t *dst[kMaxPeers];
   unsigned long long *sig[kMaxPeers];
@@ -722,7 +723,7 @@ __global__ void __launch_bounds__(kMergeGatherThreads) merge_gather_kernel(const
     const int n_units = ceil_div_dev(seq_len, kUnit);
     const int ns = ceil_div_dev(n_units, p.units_per_split);
     T *local = static_cast<T *>(p.out) + int64_t(b) * p.o_sb + int64_t(row % p.hq) * p.o_sh;
-    const int64_t goff = int64_t(g.rank) * slice + int64_t(row) * D;
+    const int64_t goff = (int64_t(g.epoch & 1ull) * g.world + g.rank) * slice + int64_t(row) * D;
     if (ns <= 1) {
       for (int d = lane * 4; d < D; d += 128) {
         const uint16_t *src = reinterpret_cast<const uint16_t *>(local) + d;
@@ -836,15 +837,6 @@ __global__ void decode_generic_kernel(const DecodeParams p, int D) {
   }
 }
 
-}  // namespace
-}  // namespace dev
-}  // namespace kcmm
-
-#include "decode_streamk.cuh"
-
-namespace kcmm {
-namespace dev {
-namespace {
 
 // ---------------------------------------------------------------------------
 // Host side
@@ -967,190 +959,6 @@ cudaMemPool_t scratch_pool(int dev) {
   return pools[dev];
 }
 
-// --- stream-K plan -------------------------------------------------------------
-
-using SkFn = void (*)(const sk::Params, int);
-
-struct SkPlan {
-  bool ok = false;
-  bool forced = false;  // requested through KCMM_DECODE_IMPL: no silent fallback
-  SkFn fn = nullptr;
-  void (*merge)(const sk::Params, int) = nullptr;
-  size_t smem = 0;
-  int grid = 0, threads = 160, ring = 0, n_head_tiles = 1, g_max = 16;
-  size_t scratch_bytes = 0;
-  size_t off_lse = 0, off_cum = 0, off_segcum = 0;
-};
-
-constexpr int kSlots = 2;
-
-// Ring depth that fills the shared memory left for `per_sm` CTAs per SM.
-template <int D, int C>
-int ring_depth(int batch, int g_max, int per_sm) {
-  const size_t budget = size_t(227 * 1024) / size_t(per_sm) - 1024;
-  const size_t fixed = sk::layout<D, C, kSlots>(batch, g_max, 0).total;
-  const size_t stage = size_t(2) * 16 * D * 2 + 2 * 8 + 4 + 16;
-  if (fixed >= budget) return 0;
-  int r = int((budget - fixed) / stage);
-  r = std::min(r, 48);
-  r -= r % C;
-  while (r >= C && sk::layout<D, C, kSlots>(batch, g_max, r).total > budget) r -= C;
-  return r;
-}
-
-template <typename T, int D, int C, int NP>
-void sk_pick(SkPlan *pl, int batch, int per_sm) {
-  pl->fn = sk::sk_decode_kernel<T, D, C, NP, kSlots>;
-  pl->merge = sk::merge<T, D>;
-  pl->threads = (C + NP) * 32;
-  pl->ring = ring_depth<D, C>(batch, pl->g_max, per_sm);
-  if (const char *r = std::getenv("KCMM_SK_RING")) {
-    int want = std::atoi(r);
-    want -= want % C;
-    if (want >= C && want < pl->ring) pl->ring = want;
-  }
-  pl->smem = sk::layout<D, C, kSlots>(batch, pl->g_max, pl->ring).total;
-}
-
-template <typename T>
-bool sk_select(SkPlan *pl, int D, int batch, int variant) {
-  // variant: 0 = 4 consumers + 2 producers, 1 CTA/SM;  1 = 4 + 1, 2 CTAs/SM;
-  //          2 = 6 consumers + 2 producers, 1 CTA/SM;  3 = 4 + 3, 1 CTA/SM
-  switch (D) {
-#define KCMM_SK(DD)                                             \
-  case DD:                                                      \
-    if (variant == 1) sk_pick<T, DD, 4, 1>(pl, batch, 2);       \
-    else if (variant == 2) sk_pick<T, DD, 6, 2>(pl, batch, 1);  \
-    else if (variant == 3) sk_pick<T, DD, 4, 3>(pl, batch, 1);  \
-    else sk_pick<T, DD, 4, 2>(pl, batch, 1);                    \
-    return true;
-    KCMM_SK(64)
-    KCMM_SK(128)
-#undef KCMM_SK
-#define KCMM_SK1(DD)                     \
-  case DD:                               \
-    sk_pick<T, DD, 4, 2>(pl, batch, 1);  \
-    return true;
-    KCMM_SK1(192)
-    KCMM_SK1(256)
-#undef KCMM_SK1
-    default:
-      return false;
-  }
-}
-
-// --- stream-K with per-warp cp.async rings (default) -----------------------------
-
-template <int D, int W>
-int ld_stages(int batch, int g_max) {
-  for (int ns = 4; ns >= 2; --ns) {
-    if (sk::layout_ld<D, W, kSlots>(batch, g_max, ns).total <= size_t(227 * 1024 - 1024)) return ns;
-  }
-  return 0;
-}
-
-template <typename T, int D, int W>
-void ld_pick(SkPlan *pl, int batch) {
-  pl->fn = sk::sk_ld_kernel<T, D, W, kSlots>;
-  pl->merge = sk::merge<T, D>;
-  pl->threads = W * 32;
-  pl->ring = ld_stages<D, W>(batch, pl->g_max);
-  if (const char *r = std::getenv("KCMM_SK_RING")) {
-    const int want = std::atoi(r);
-    if (want >= 2 && want < pl->ring) pl->ring = want;
-  }
-  pl->smem = sk::layout_ld<D, W, kSlots>(batch, pl->g_max, pl->ring).total;
-}
-
-template <typename T>
-bool ld_select(SkPlan *pl, int D, int batch, int warps) {
-  // warps per CTA (1 CTA per SM): 6, 8 (default), 10 or 12; a ring of at least
-  // two stages per warp must fit next to the merge slots.
-  switch (D) {
-#define KCMM_LD(DD)                                         \
-  case DD:                                                  \
-    if (warps == 6) ld_pick<T, DD, 6>(pl, batch);           \
-    else if (warps == 10) ld_pick<T, DD, 10>(pl, batch);    \
-    else if (warps == 12) ld_pick<T, DD, 12>(pl, batch);    \
-    else if (warps == 8) ld_pick<T, DD, 8>(pl, batch);      \
-    else return false;                                      \
-    return true;
-    KCMM_LD(64)
-    KCMM_LD(128)
-#undef KCMM_LD
-#define KCMM_LD1(DD)                 \
-  case DD:                           \
-    if (warps != 8) return false;    \
-    ld_pick<T, DD, 8>(pl, batch);    \
-    return true;
-    KCMM_LD1(32)
-    KCMM_LD1(80)
-    KCMM_LD1(96)
-    KCMM_LD1(112)
-    KCMM_LD1(160)
-    KCMM_LD1(192)
-    KCMM_LD1(256)
-#undef KCMM_LD1
-    default:
-      return false;
-  }
-}
-
-// The split-K kernel is the default: on the Llama-3-8B decode shape it runs at
-// the same speed as the best stream-K configuration that fits in shared memory
-// or faster.  KCMM_DECODE_IMPL=streamk (per-warp cp.async rings, warps from
-// KCMM_SK_WARPS) or =tma (TMA producer warps, KCMM_SK_VARIANT) selects a
-// persistent stream-K kernel instead; when the shapes rule the requested
-// kernel out the call fails rather than running another kernel.
-SkPlan make_sk_plan(const DecodeArgs &a) {
-  SkPlan pl;
-  const char *impl = std::getenv("KCMM_DECODE_IMPL");
-  const bool tma = impl && std::strcmp(impl, "tma") == 0;
-  const bool streamk = impl && std::strcmp(impl, "streamk") == 0;
-  if (!tma && !streamk) return pl;
-  pl.forced = true;
-  const int D = a.head_dim;
-  if (D % 16 != 0 || a.block_size % 16 != 0 || a.batch > 2048) return pl;
-  if ((reinterpret_cast<uintptr_t>(a.q) & 15) != 0) return pl;
-  if (tma && (D % 64 != 0 || !a.tensor_maps)) return pl;
-  int variant = 0;
-  if (const char *v = std::getenv("KCMM_SK_VARIANT")) variant = std::atoi(v);
-  int warps = 8;
-  if (const char *w = std::getenv("KCMM_SK_WARPS")) warps = std::atoi(w);
-  const int g_all = (a.num_q_heads + a.kv_heads - 1) / a.kv_heads;
-  pl.n_head_tiles = (g_all + 15) / 16;
-  pl.g_max = std::min(16, g_all);
-  bool found;
-  if (tma) {
-    found = a.dtype == Dtype::BF16 ? sk_select<__nv_bfloat16>(&pl, D, a.batch, variant)
-                                   : sk_select<__half>(&pl, D, a.batch, variant);
-    if (pl.ring < 8) found = false;
-  } else {
-    found = a.dtype == Dtype::BF16 ? ld_select<__nv_bfloat16>(&pl, D, a.batch, warps)
-                                   : ld_select<__half>(&pl, D, a.batch, warps);
-    if (pl.ring < 2) found = false;
-  }
-  if (!found || pl.smem > 227 * 1024) return pl;
-  if (cudaFuncSetAttribute(pl.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pl.smem)) !=
-      cudaSuccess)
-    return pl;
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pl.fn, pl.threads, pl.smem) !=
-          cudaSuccess ||
-      per_sm <= 0)
-    return pl;
-  pl.grid = sm_count() * per_sm;
-  if (const char *gs = std::getenv("KCMM_SK_GRID")) pl.grid = std::max(1, std::atoi(gs));
-  const size_t segs = size_t(a.batch) * a.kv_heads * pl.n_head_tiles;
-  const size_t rows = (segs + size_t(pl.grid)) * size_t(pl.g_max);
-  pl.off_lse = rows * size_t(D) * 4;
-  pl.off_cum = (pl.off_lse + rows * 4 + 15) & ~size_t(15);
-  pl.off_segcum = pl.off_cum + (size_t(a.batch) + 1) * 8;
-  pl.scratch_bytes = pl.off_segcum + (size_t(a.batch) + 1) * 4;
-  pl.ok = true;
-  return pl;
-}
-
 cudaError_t scratch_acquire(const DecodeArgs &a, size_t bytes, cudaStream_t stream, void **out,
                             bool *owned) {
   *owned = false;
@@ -1168,61 +976,9 @@ cudaError_t scratch_acquire(const DecodeArgs &a, size_t bytes, cudaStream_t stre
   return e;
 }
 
-cudaError_t decode_streamk(const DecodeArgs &a, const SkPlan &pl, cudaStream_t stream) {
-  void *scratch = nullptr;
-  bool owned = false;
-  cudaError_t e = scratch_acquire(a, pl.scratch_bytes, stream, &scratch, &owned);
-  if (e != cudaSuccess) return e;
-  sk::Params p;
-  std::memset(static_cast<void *>(&p), 0, sizeof(p));
-  if (a.tensor_maps) {  // only the TMA variant reads them
-    std::memcpy(&p.tmk, a.tensor_maps, sizeof(CUtensorMap));
-    std::memcpy(&p.tmv, static_cast<const char *>(a.tensor_maps) + 128, sizeof(CUtensorMap));
-  }
-  p.region_tokens = a.region_tokens;
-  p.q = a.q;
-  p.out = a.out;
-  p.tables = a.block_tables;
-  p.seq_lens = a.seq_lens;
-  p.offsets = a.block_offsets;
-  p.va_k = a.va_k;
-  p.va_v = a.va_v;
-  p.region_elems = a.region_elems;
-  p.batch = a.batch;
-  p.hq = a.num_q_heads;
-  p.hkv = a.kv_heads;
-  p.bs = a.block_size;
-  p.max_bps = a.max_blocks_per_seq;
-  p.scale_log2 = a.scale * 1.4426950408889634f;
-  p.n_head_tiles = pl.n_head_tiles;
-  p.g_max = pl.g_max;
-  char *base = static_cast<char *>(scratch);
-  p.part_o = reinterpret_cast<float *>(base);
-  p.part_lse = reinterpret_cast<float *>(base + pl.off_lse);
-  p.cum_out = reinterpret_cast<int64_t *>(base + pl.off_cum);
-  p.segcum_out = reinterpret_cast<int32_t *>(base + pl.off_segcum);
-  p.diag = a.diag;
-  pl.fn<<<pl.grid, pl.threads, pl.smem, stream>>>(p, pl.ring);
-  e = cudaGetLastError();
-  if (e == cudaSuccess) {
-    pl.merge<<<a.batch * a.num_q_heads, 128, 0, stream>>>(p, pl.grid);
-    e = cudaGetLastError();
-  }
-  if (owned) {
-    cudaError_t f = cudaFreeAsync(scratch, stream);
-    if (e == cudaSuccess) e = f;
-  }
-  return e;
-}
-
 }  // namespace
 
-size_t decode_scratch_bytes(const DecodeArgs &a) {
-  SkPlan sp = make_sk_plan(a);
-  if (sp.ok) return sp.scratch_bytes;
-  if (sp.forced) return 0;  // the launch fails with cudaErrorNotSupported
-  return make_plan(a).scratch_bytes;
-}
+size_t decode_scratch_bytes(const DecodeArgs &a) { return make_plan(a).scratch_bytes; }
 
 // Split scratch kept per (device, stream) between calls, so a call makes no
 // stream-ordered allocation between its kernels and the next call's launch can
@@ -1299,14 +1055,7 @@ cudaError_t decode_attention(const DecodeArgs &a, cudaStream_t stream) {
   p.o_sb = a.out_stride_token ? a.out_stride_token : dense_row;
   p.o_sh = a.out_stride_head ? a.out_stride_head : a.head_dim;
   p.bt_stride = a.tables_stride ? a.tables_stride : a.max_blocks_per_seq;
-  const bool dense = p.q_sb == dense_row && p.q_sh == a.head_dim && p.o_sb == dense_row &&
-                     p.o_sh == a.head_dim && p.bt_stride == a.max_blocks_per_seq;
 
-  SkPlan sp = make_sk_plan(a);
-  // stream-K reads dense rows only and has no gather
-  if (sp.forced && (!dense || a.peer_world > 0)) return cudaErrorNotSupported;
-  if (sp.ok) return decode_streamk(a, sp, stream);
-  if (sp.forced) return cudaErrorNotSupported;
   Plan pl = make_plan(a);
   if (!pl.fast && a.peer_world > 0) return cudaErrorNotSupported;  // tensor-core path only
   if (!pl.fast) {

@@ -1,16 +1,26 @@
 // All-gather over NVLink peer memory, for the KV-head split of the decode
 // (each rank attends its own kv heads; every rank needs all heads' outputs).
 //
-// A rank's gathered buffer holds world slices of `nbytes`; slice r comes from
-// rank r.  peer_allgather copies this rank's slice into slot `rank` of every
-// rank's buffer (its own included) with plain stores through CUDA IPC
-// mappings, then raises its flags in every rank's signal array:
+// A rank's gathered buffer holds two halves of world slices of `nbytes`; epoch
+// e fills half e & 1, and slice r of a half comes from rank r.  peer_allgather
+// copies this rank's slice into slot `rank` of that half of every rank's buffer
+// (its own included) with plain stores through CUDA IPC mappings, then raises
+// its flags in every rank's signal array:
 //   signal[r][src * kGatherBlocks + blk] = epoch   (u64, system scope, release)
 // one flag per CTA and rank, written by thread r after the CTA barrier and a
 // system-scope fence.  peer_wait spins, bounded, until every flag of its own
 // signal array has reached `epoch`; the gathered buffer is then complete.  A
 // wait that runs out writes 1 to `status` and returns (no trap), so a missing
 // rank is reported instead of hanging the GPU.
+//
+// Why two halves: once a rank's wait for epoch e has passed, it may start
+// epoch e+1 while a slower peer is still reading epoch e's rows.  Epoch e+1
+// goes to the other half, and a rank can only reach epoch e+2 (the same half
+// again) after its wait for e+1 saw every peer's e+1 flags.  A peer raises
+// those after everything it ordered before its epoch e+1 gather on its stream,
+// including its reads of epoch e.  So with gather(e) -> wait(e) -> reads of
+// half e & 1 -> gather(e+1) in stream order on every rank, no half is
+// overwritten while a rank may still read it.
 //
 // No TMA and no multicast: remote memory is only ever the target of ordinary
 // stores, and flags are read from this GPU's own memory.
@@ -43,9 +53,10 @@ __global__ void __launch_bounds__(512) peer_allgather_kernel(const GatherArgs a)
   const uint64_t per = (a.n16 + gridDim.x - 1) / gridDim.x;
   const uint64_t lo = uint64_t(blockIdx.x) * per;
   const uint64_t hi = lo + per < a.n16 ? lo + per : a.n16;
+  const uint64_t base = ((a.epoch & 1ull) * uint64_t(a.world) + uint64_t(a.rank)) * a.n16;
   for (uint64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
     const uint4 v = a.src[i];
-    for (int r = 0; r < a.world; ++r) a.dst[r][uint64_t(a.rank) * a.n16 + i] = v;
+    for (int r = 0; r < a.world; ++r) a.dst[r][base + i] = v;
   }
   // The CTA barrier orders every thread's peer stores before the flag threads'
   // system-scope fence and release store (cumulativity: the pattern of a

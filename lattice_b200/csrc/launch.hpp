@@ -37,17 +37,14 @@ struct DecodeArgs {
   float *scratch;
   size_t scratch_bytes;
   int force_splits;  // >0 overrides the split heuristic (tests)
-  // Two 128-byte TMA descriptors (K then V region) for this layer and
-  // (kv_heads, head_dim), or null; region_tokens = tokens they span.
-  const void *tensor_maps;
-  uint64_t region_tokens;
   // Element strides of q and out (token, head; head_dim is contiguous) and of the
   // block-table rows; 0 = dense ([batch][Hq][D] and max_blocks_per_seq).
   int64_t q_stride_token, q_stride_head, out_stride_token, out_stride_head, tables_stride;
   // All-gather of the KV-head split (kernels/decode.cu, merge_gather_kernel):
   // peer_world > 0 writes every output row also to slot peer_rank of each
-  // rank's gathered buffer peer_out[r] ([world][batch][Hq][D]) and raises this
-  // rank's flags in peer_sig[r] to peer_epoch (host arrays of device addresses).
+  // rank's gathered buffer peer_out[r] ([2][world][batch][Hq][D]; half
+  // peer_epoch & 1) and raises this rank's flags in peer_sig[r] to peer_epoch
+  // (host arrays of device addresses).
   const uint64_t *peer_out;
   const uint64_t *peer_sig;
   int peer_rank, peer_world;
@@ -100,8 +97,9 @@ struct PrefillArgs {
 cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream);
 
 // All-gather over NVLink peer memory (kernels/peer.cu).  dst[r] is rank r's
-// gathered buffer (world slices of nbytes, P2P-accessible from this device),
-// sig[r] rank r's signal array of world * kGatherBlocks u64 flags.
+// gathered buffer (two halves of world slices of nbytes, P2P-accessible from
+// this device; epoch e fills half e & 1), sig[r] rank r's signal array of
+// world * kGatherBlocks u64 flags.
 constexpr int kMaxPeers = 8;
 constexpr int kGatherBlocks = 16;
 cudaError_t peer_allgather(const void *src, uint64_t nbytes, void *const *dst,

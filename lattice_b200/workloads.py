@@ -172,6 +172,46 @@ class DecodeWorkload:
         qo = self.batch * self.num_q_heads * self.head_dim * e * 2
         return kv + tables + qo + 4 * self.batch
 
+    def region_tensor(self, layer: int, kind: str):
+        """A torch view (16-bit words, no copy) of the used part of a K or V region."""
+        torch = _torch()
+        base = self.pool.va_k(layer) if kind == "k" else self.pool.va_v(layer)
+
+        class _View:
+            __cuda_array_interface__ = {"shape": (self.region_used // 2,), "typestr": "<i2",
+                                        "data": (base, False), "version": 3}
+
+        return torch.as_tensor(_View(), device=f"cuda:{self.device}").view(self.tdtype)
+
+    def torch_reference(self, rows: list[int], layer: int = 0):
+        """fp32 paged decode attention of sequences `rows` in plain torch on the device
+        ([len(rows), Hq, D] float32): every key of the sequence through its block table
+        and the offsets table, softmax(scale * q.k) v with kv head h * Hkv // Hq.  An
+        independent check of the kernels for callers that cannot run the CPU oracle."""
+        torch = _torch()
+        dev = f"cuda:{self.device}"
+        kr, vr = self.region_tensor(layer, "k"), self.region_tensor(layer, "v")
+        step = self.kv_heads * self.head_dim
+        outs = []
+        for b in rows:
+            L = int(self.seq_lens[b])
+            if L <= 0:
+                outs.append(torch.full((self.num_q_heads, self.head_dim), float("nan"), device=dev))
+                continue
+            t = torch.arange(L, device=dev)
+            blk = torch.from_numpy(self.tables[b].astype(np.int64)).to(dev)[t // self.block_size]
+            off = torch.from_numpy(self.offsets.view(np.int64)).to(dev)[blk]
+            base = off + (t % self.block_size) * step
+            idx = base[:, None] + torch.arange(step, device=dev)[None, :]
+            k = kr[idx].float().view(L, self.kv_heads, self.head_dim)
+            v = vr[idx].float().view(L, self.kv_heads, self.head_dim)
+            q = self.q[b].float()
+            kvh = torch.arange(self.num_q_heads, device=dev) * self.kv_heads // self.num_q_heads
+            s = torch.einsum("hd,lhd->hl", q, k[:, kvh, :]) * self.scale
+            p = torch.softmax(s, dim=-1)
+            outs.append(torch.einsum("hl,lhd->hd", p, v[:, kvh, :]))
+        return torch.stack(outs)
+
     def host_region(self, layer: int, kind: str) -> np.ndarray:
         """Current bytes of a region (16-bit words), read back from the device."""
         base = self.pool.va_k(layer) if kind == "k" else self.pool.va_v(layer)
@@ -356,9 +396,10 @@ class PeerBuffers:
     through CUDA IPC, for `kcmm_peer_allgather_on_stream` / `kcmm_peer_wait_on_stream`.
 
     Collective over the default process group: every rank allocates its own buffer
-    (world slices of `slice_bytes`) and signal array, publishes their IPC handles
-    with `all_gather_object`, and opens the peers'.  Pointers are indexed by rank;
-    this rank's entries are its own allocations."""
+    (two halves of world slices of `slice_bytes`; epoch e fills half e & 1) and
+    signal array, publishes their IPC handles with `all_gather_object`, and opens
+    the peers'.  Pointers are indexed by rank; this rank's entries are its own
+    allocations."""
 
     def __init__(self, slice_bytes: int, rank: int, world: int, device: int):
         import torch.distributed as dist
@@ -371,7 +412,7 @@ class PeerBuffers:
         self._own = []
         self._opened = []
         handles = []
-        for nbytes in (slice_bytes * world, self.sig_words * 8):
+        for nbytes in (2 * slice_bytes * world, self.sig_words * 8):
             err, ptr = rt.cudaMalloc(nbytes)
             if int(err) != 0:
                 raise RuntimeError(f"cudaMalloc failed: {err}")
@@ -407,7 +448,12 @@ class PeerBuffers:
 
     @property
     def gathered_ptr(self) -> int:
+        """This rank's whole gathered buffer (both halves)."""
         return self._own[0]
+
+    def half_ptr(self, epoch: int) -> int:
+        """The half of this rank's gathered buffer that epoch `epoch` fills."""
+        return self._own[0] + (epoch & 1) * self.slice_bytes * self.world
 
     @property
     def signal_ptr(self) -> int:

@@ -21,14 +21,25 @@ REF_LIB = HERE / "_ref" / "libref_kernels.so"
 DT = {"f16": 0, "bf16": 1, "f32": 2}
 
 
+def reference_root() -> Path | None:
+    """The reference checkout whose kernel sources oracle/_ref compiles: $REF_ROOT,
+    else a checkout named `reference` beside this repository; None when neither
+    holds `src/cuda/kernels` (GPU machines carry no reference tree)."""
+    env = os.environ.get("REF_ROOT")
+    cand = Path(env) if env else HERE.parent.parent / "reference"
+    return cand if (cand / "src" / "cuda" / "kernels").is_dir() else None
+
+
 def build(ref: bool | None = None) -> None:
-    """Build liboracle (always) and oracle/_ref (when the reference tree exists)."""
+    """Build liboracle (always) and oracle/_ref (when a reference checkout is found)."""
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
-    ref_root = os.environ.get("REF_ROOT", "/root/reference")
+    root = reference_root()
     if ref is None:
-        ref = Path(ref_root, "src/cuda/kernels").is_dir()
+        ref = root is not None
     if ref:
-        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF_ROOT={ref_root}"], check=True)
+        if root is None:
+            raise RuntimeError("oracle/_ref needs the reference checkout: set REF_ROOT")
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF_ROOT={root}"], check=True)
 
 
 def _ptr(a: np.ndarray | None):
@@ -182,9 +193,13 @@ def fused_norm_rope_append(x, w, q, k, v, positions, slots, offsets, valid, va_k
 
 def ref_paged_attn(dtype: str, q, va_k, va_v, tables, seq_lens, offsets, *, hq, hkv, d, bs,
                    max_bps, scale, out=None, workers: int = 1):
+    """dtype "f16"/"bf16": 16-bit bit arrays; "f32": float32 arrays, the reference
+    source built over fp32 storage, which reads `offsets` as element indices."""
     B = len(seq_lens)
-    out = np.zeros((B, hq, d), np.uint16) if out is None else out
-    fn = ref_lib().ref_paged_attn_bf16 if dtype == "bf16" else ref_lib().ref_paged_attn_f16
+    if out is None:
+        out = np.zeros((B, hq, d), np.float32 if dtype == "f32" else np.uint16)
+    fn = {"bf16": ref_lib().ref_paged_attn_bf16, "f16": ref_lib().ref_paged_attn_f16,
+          "f32": ref_lib().ref_paged_attn_f32}[dtype]
     fn(_ptr(q), _ptr(va_k), _ptr(va_v), _ptr(np.ascontiguousarray(tables, np.int32)),
        _ptr(np.ascontiguousarray(seq_lens, np.int32)), _ptr(np.ascontiguousarray(offsets, np.uint64)),
        _ptr(out), ctypes.c_int(B), ctypes.c_int(hq), ctypes.c_int(hkv), ctypes.c_int(d),

@@ -14,7 +14,10 @@
  *   src/cuda/kernels/rope.cu                  rope_f16
  *   src/cuda/kernels/kv_gather.cu             gather_kv_layer / scatter_kv_layer
  * With KCMM_SHIM_BF16 the same attention source is built over bfloat16 storage
- * (exported as ref_paged_attn_bf16) for the bf16 CPU baseline.
+ * (exported as ref_paged_attn_bf16) for the bf16 CPU baseline, and with
+ * KCMM_SHIM_F32 over fp32 storage (ref_paged_attn_f32) for the fp32 CPU toy.
+ * Those two builds carry only the attention kernel; the executor's globals
+ * come from the default build.
  */
 #include <ucontext.h>
 
@@ -26,7 +29,11 @@
 
 #include "cuda_fp16.h"
 
-#ifndef KCMM_SHIM_BF16
+#if defined(KCMM_SHIM_BF16) || defined(KCMM_SHIM_F32)
+#define KCMM_SHIM_ALT 1
+#endif
+
+#ifndef KCMM_SHIM_ALT
 thread_local kcmm_shim_dim3 blockIdx, threadIdx, blockDim, gridDim;
 #endif
 
@@ -117,7 +124,7 @@ void launch(unsigned grid, unsigned block, int workers, bool barriers,
 
 }  // namespace
 
-#ifndef KCMM_SHIM_BF16
+#ifndef KCMM_SHIM_ALT
 void __syncthreads() {
   FiberSched *s = g_sched;
   if (!s) return;
@@ -130,6 +137,10 @@ void __syncthreads() {
 
 #ifdef KCMM_SHIM_BF16
 #define kcmm_vllm_paged_attn_decode_f16 ref_body_attn_bf16
+#include "kcmm_vllm_paged_attn.cu"
+#undef kcmm_vllm_paged_attn_decode_f16
+#elif defined(KCMM_SHIM_F32)
+#define kcmm_vllm_paged_attn_decode_f16 ref_body_attn_f32
 #include "kcmm_vllm_paged_attn.cu"
 #undef kcmm_vllm_paged_attn_decode_f16
 #else
@@ -159,6 +170,20 @@ void ref_paged_attn_bf16(const uint16_t *q, const uint16_t *va_k, const uint16_t
   launch((total + 127) / 128, 128, workers, false, [&] {
     ref_body_attn_bf16(u64(q), u64(va_k), u64(va_v), u64(tables), u64(seq_lens), u64(offsets),
                        u64(out), total, packed_heads, d, packed_blocks, scale);
+  });
+}
+#elif defined(KCMM_SHIM_F32)
+// block_offsets_f16 is read as an element index into the float regions
+void ref_paged_attn_f32(const float *q, const float *va_k, const float *va_v,
+                        const int32_t *tables, const int32_t *seq_lens, const uint64_t *offsets,
+                        float *out, int batch, int hq, int hkv, int d, int bs, int max_bps,
+                        float scale, int workers) {
+  const int total = batch * hq;
+  const int packed_heads = (hkv << 16) | hq;
+  const int packed_blocks = (max_bps << 16) | bs;
+  launch((total + 127) / 128, 128, workers, false, [&] {
+    ref_body_attn_f32(u64(q), u64(va_k), u64(va_v), u64(tables), u64(seq_lens), u64(offsets),
+                      u64(out), total, packed_heads, d, packed_blocks, scale);
   });
 }
 #else

@@ -4,7 +4,10 @@
  * as host C++ (oracle/ref_host.cpp).  Only oracle/_ref is built with it.
  *
  *   __half            16-bit storage; IEEE binary16 by default, bfloat16
- *                     when KCMM_SHIM_BF16 is defined (bf16 timing builds).
+ *                     when KCMM_SHIM_BF16 is defined (bf16 timing builds),
+ *                     and a plain float when KCMM_SHIM_F32 is defined (the
+ *                     fp32 CPU toy: the kernels index elements through
+ *                     `__half *`, so the same source then runs on fp32 data).
  *   blockIdx/...      per-OS-thread launch coordinates set by the executor.
  *   __syncthreads     a barrier implemented with ucontext fibers.
  */
@@ -23,11 +26,16 @@ extern thread_local kcmm_shim_dim3 blockIdx, threadIdx, blockDim, gridDim;
 #define __forceinline__ inline
 #define __shared__ thread_local
 
+#ifdef KCMM_SHIM_F32
+struct __half {
+  float v;
+};
+static inline float __half2float(__half h) { return h.v; }
+static inline __half __float2half(float f) { return __half{f}; }
+#elif defined(KCMM_SHIM_BF16)
 struct __half {
   uint16_t bits;
 };
-
-#ifdef KCMM_SHIM_BF16
 static inline float __half2float(__half h) {
   uint32_t u = uint32_t(h.bits) << 16;
   float f;
@@ -41,6 +49,9 @@ static inline __half __float2half(float f) {
   return __half{uint16_t(u >> 16)};
 }
 #else
+struct __half {
+  uint16_t bits;
+};
 static inline float __half2float(__half h) {
   _Float16 v;
   std::memcpy(&v, &h.bits, 2);

@@ -162,6 +162,54 @@ def test_fused_norm_rope_append_matches_oracle(mode):
         wl.close()
 
 
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_config3_fused_norm_rope_append_full_size(mode):
+    """BASELINE config 3 exactly: 256 decode tokens, hidden 4096, eps 1e-5, weight
+    U(0.5, 1.5), rope theta 500000 on head_dim 128 at positions uniform in [0, 8191],
+    8 kv heads, block_size 16, seeded distinct slots.  normed, q and the rotated K
+    rows within the bf16 tolerance of the oracle composition; V pages bit-exact; no
+    byte outside the written rows changes."""
+    torch = _torch()
+    from lattice_b200.workloads import FusedAppendWorkload, tensor_bits
+    from oracle import native as N
+
+    wl = FusedAppendWorkload(tokens=256, rope_mode=mode, seed=30 + mode).build()
+    try:
+        assert (wl.hidden, wl.eps, wl.theta, wl.kv_heads, wl.head_dim, wl.block_size) == \
+            (4096, 1e-5, 500000.0, 8, 128, 16)
+        assert len(set(wl.slots.tolist())) == 256
+        assert wl.positions.min() >= 0 and wl.positions.max() <= 8191
+        x, w, q0 = tensor_bits(wl.x), tensor_bits(wl.w), tensor_bits(wl.q)
+        k, v = tensor_bits(wl.k), tensor_bits(wl.v)
+        nbytes = int(wl.offsets.max()) * 2 + wl.pool.stats()["block_bytes"]
+        va_k0, va_v0 = region(wl.pool, 0, "k", nbytes).copy(), region(wl.pool, 0, "v", nbytes).copy()
+        wl.run()
+        torch.cuda.synchronize()
+        assert int(wl.status.item()) == 0
+        want_norm, want_q, st = N.fused_norm_rope_append(
+            x, w, q0, k, v, wl.positions, wl.slots, wl.offsets, wl.valid, va_k0, va_v0,
+            eps=wl.eps, base=wl.theta, mode=mode, hkv=wl.kv_heads, d=wl.head_dim,
+            bs=wl.block_size)
+        assert st == 0
+        f = N.bf16_bits_to_f32
+        for got, want in ((tensor_bits(wl.normed), want_norm), (tensor_bits(wl.q), want_q)):
+            g, r = f(got), f(want)
+            assert (np.abs(g - r) <= 2e-3 + 1e-2 * np.abs(r)).all()
+        got_k, got_v = region(wl.pool, 0, "k", nbytes), region(wl.pool, 0, "v", nbytes)
+        assert np.array_equal(got_v, va_v0)
+        gk, rk = f(got_k), f(va_k0)
+        assert (np.abs(gk - rk) <= 2e-3 + 1e-2 * np.abs(rk)).all()
+        # rows no token writes keep their bytes exactly (K included)
+        step = wl.kv_heads * wl.head_dim
+        written = np.zeros(nbytes // 2, bool)
+        for slot in wl.slots:
+            start = int(wl.offsets[slot // 16]) + (slot % 16) * step
+            written[start:start + step] = True
+        assert np.array_equal(got_k[~written], va_k0[~written])
+    finally:
+        wl.close()
+
+
 def test_fused_status_codes():
     torch = _torch()
     from lattice_b200.workloads import FusedAppendWorkload

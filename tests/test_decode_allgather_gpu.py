@@ -58,7 +58,7 @@ def test_two_ranks_on_one_gpu(case, dtype):
     wls = [DecodeWorkload(dtype=dtype, seed=70 + r, **CASES[case]).build() for r in range(world)]
     try:
         wl0 = wls[0]
-        shape = (world,) + tuple(wl0.out.shape)
+        shape = (2, world) + tuple(wl0.out.shape)  # two halves, by epoch parity
         sentinel = 5.0
         bufs = [torch.full(shape, sentinel, device="cuda").to(wl0.out.dtype)
                 for _ in range(world)]
@@ -90,8 +90,9 @@ def test_two_ranks_on_one_gpu(case, dtype):
                 assert bool(((got - ref).abs() <= ATOL + RTOL * ref.abs()).all()), (
                     f"rank {r} epoch {epoch}: max err {(got - ref).abs().max().item()}")
                 for b in bufs:
-                    assert torch.equal(b[r][live], wl.out[live])
-                    assert bool((b[r][~live] == sentinel).all())
+                    half = b[epoch & 1]
+                    assert torch.equal(half[r][live], wl.out[live])
+                    assert bool((half[r][~live] == sentinel).all())
         for wl in wls:
             assert wl.pool.kernel_status() == 0
     finally:
@@ -107,7 +108,7 @@ def test_one_rank_gathers_into_its_own_buffer():
     wl = DecodeWorkload(batch=8, num_q_heads=32, kv_heads=8, head_dim=128, pool_blocks=2200,
                         min_len=100, max_len=4000, seed=77).build()
     try:
-        buf = torch.zeros((1,) + tuple(wl.out.shape), dtype=wl.out.dtype, device="cuda")
+        buf = torch.zeros((2, 1) + tuple(wl.out.shape), dtype=wl.out.dtype, device="cuda")
         sg = torch.zeros(16, dtype=torch.int64, device="cuda")
         dst = (ctypes.c_uint64 * 1)(buf.data_ptr())
         sig = (ctypes.c_uint64 * 1)(sg.data_ptr())
@@ -120,7 +121,8 @@ def test_one_rank_gathers_into_its_own_buffer():
                                                     sp) == 0
         torch.cuda.synchronize()
         assert int(status.item()) == 0 and all(int(v) == 7 for v in sg.tolist())
-        assert torch.equal(buf[0], wl.out)
+        assert torch.equal(buf[7 & 1][0], wl.out)
+        assert bool((buf[0] == 0).all())  # epoch 7 writes half 1 only
         assert bool(((wl.out.float() - ref.float()).abs() <= ATOL + RTOL * ref.float().abs())
                     .all())
     finally:

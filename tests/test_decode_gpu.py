@@ -97,21 +97,7 @@ def test_zero_length_rows_untouched():
         wl.close()
 
 
-SK = {"KCMM_DECODE_IMPL": "streamk"}   # persistent stream-K, per-warp cp.async rings
-
-
 @pytest.mark.parametrize("env", [
-    {**SK},                               # 8 warps
-    {**SK, "KCMM_SK_GRID": "1"},          # one CTA walks every segment
-    {**SK, "KCMM_SK_GRID": "3"},          # slices cut segments into pieces
-    {**SK, "KCMM_SK_GRID": "37"},
-    {**SK, "KCMM_SK_GRID": "5000"},       # more CTAs than units: empty slices
-    {**SK, "KCMM_SK_WARPS": "6"},
-    {**SK, "KCMM_SK_WARPS": "10"},
-    {**SK, "KCMM_SK_RING": "2"},          # shallow rings
-    {"KCMM_DECODE_IMPL": "tma"},          # TMA producer-warp variant
-    {"KCMM_DECODE_IMPL": "tma", "KCMM_SK_GRID": "3"},
-    {"KCMM_DECODE_IMPL": "tma", "KCMM_SK_VARIANT": "2"},
     {"KCMM_PDL": "0"},                    # split-K, plain stream-ordered launches
     {"KCMM_DECODE_SPLITS": "1"},          # split-K kernel (the default), forced splits
     {"KCMM_DECODE_SPLITS": "3"},
@@ -131,12 +117,9 @@ def test_work_split_does_not_change_result(env, monkeypatch):
 
 
 @pytest.mark.parametrize("seed", [0, 2, 9])
-@pytest.mark.parametrize("impl", ["split", "streamk"])
-def test_short_rows_within_tolerance(seed, impl, monkeypatch):
+def test_short_rows_within_tolerance(seed):
     """64 rows of 1..47 keys: few keys dominate each row, so a P rounded once to 16 bits
-    would miss the tolerance; the kernels carry P as a hi + lo pair."""
-    if impl == "streamk":
-        monkeypatch.setenv("KCMM_DECODE_IMPL", "streamk")
+    would miss the tolerance; the kernel carries P as a hi + lo pair."""
     lens = list(np.random.default_rng(seed).integers(1, 48, 64))
     wl = make(batch=64, num_q_heads=32, kv_heads=8, head_dim=128, seq_lens_override=lens,
               max_len=64, pool_blocks=512, seed=seed)
@@ -186,29 +169,13 @@ def test_v_row_kat():
         wl.close()
 
 
-def test_requested_streamk_that_does_not_fit_fails(monkeypatch):
-    """12 warps x 2 ring stages of 16x128 K/V tiles plus the merge slots exceed shared
-    memory at head_dim 128: the call reports an error instead of running split-K."""
-    from lattice_b200.kcmm import KcmmError
-
-    wl = make(batch=2, num_q_heads=32, kv_heads=8, head_dim=128, seq_lens_override=[5, 9])
-    try:
-        monkeypatch.setenv("KCMM_DECODE_IMPL", "streamk")
-        monkeypatch.setenv("KCMM_SK_WARPS", "12")
-        with pytest.raises(KcmmError, match="not supported"):
-            wl.decode()
-    finally:
-        wl.close()
-
-
-@pytest.mark.parametrize("grid", ["2", "11"])
-def test_piece_merging_with_gqa_tiles_and_empty_rows(grid, monkeypatch):
-    """Head tiles (GQA 32), zero-length rows and pieces that straddle slices together."""
-    monkeypatch.setenv("KCMM_DECODE_IMPL", "streamk")
-    monkeypatch.setenv("KCMM_SK_WARPS", "6")  # 16-head merge slots: 8 warps do not fit
-    monkeypatch.setenv("KCMM_SK_GRID", grid)
+@pytest.mark.parametrize("splits", ["1", "2", "11"])
+def test_gqa_head_tiles_with_empty_rows(splits, monkeypatch):
+    """Two head tiles per kv head (GQA 32), zero-length rows and forced split counts
+    together: empty rows stay untouched, the rest match the oracle."""
+    monkeypatch.setenv("KCMM_DECODE_SPLITS", splits)
     wl = make(batch=6, num_q_heads=64, kv_heads=2, head_dim=128,
-              seq_lens_override=[0, 33, 700, 1, 0, 257], seed=int(grid))
+              seq_lens_override=[0, 33, 700, 1, 0, 257], seed=int(splits))
     try:
         wl.out.fill_(5.0)
         wl.decode()

@@ -68,24 +68,6 @@ def test_noalloc_matches_regular_twice(case):
         wl.close()
 
 
-def test_noalloc_streamk(monkeypatch):
-    """The opt-in persistent stream-K kernel (KCMM_DECODE_IMPL=streamk) through the same
-    static scratch: its partial rows and its per-call prefix arrays live there too."""
-    torch = _torch()
-    monkeypatch.setenv("KCMM_DECODE_IMPL", "streamk")
-    wl = _make(batch=8, pool_blocks=1200, min_len=100, max_len=2500, seed=5)
-    try:
-        ref = torch.empty_like(wl.q)
-        wl.decode(out=ref)
-        for _ in range(2):
-            got = torch.full_like(wl.q, float("nan"))
-            wl.decode(out=got, noalloc=True)
-            torch.cuda.synchronize()
-            _close(got, ref)
-    finally:
-        wl.close()
-
-
 def test_noalloc_leaves_free_memory_unchanged():
     """After the first call, further calls take no device memory."""
     torch = _torch()
