@@ -511,6 +511,227 @@ __global__ void __launch_bounds__(kFusedThreads) fused_fast_kernel(const FusedAp
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fused RMSNorm + RoPE + KV append, split form: three CTAs per token, one per
+// independent part of the op.
+//   blockIdx.y == 0  rotary of the k heads into the page, V row copied
+//   blockIdx.y == 1  rotary of the q heads, in place
+//   blockIdx.y == 2  RMSNorm of the hidden row (x, w -> normed)
+// Only the K/V CTA waits for the two dependent lookups of the slot (slot
+// mapping, then the offsets / valid tables).  Its CTAs come first in the grid,
+// so those lookups are issued before the bulk of the loads; the norm and q CTAs
+// store as soon as their own loads land.
+// Rotary factors: theta_i comes from the launcher (the same fp32
+// 1/powf(base, e_i) as the reference formula, ref src/cuda/kernels/rope.cu:18);
+// every thread forms angle = pos * theta_i in fp32 like the reference, reduces it
+// exactly to [-pi, pi] in double precision, and takes __sinf/__cosf there
+// (absolute error below 2^-21 on that interval).  No table, no barrier in the
+// q CTA, and none of sincosf's large-argument code.
+// Requirements (checked by the launcher): 16-byte aligned rows, head_dim % 16 ==
+// 0, head_dim <= 256, and hidden, num_q_heads * head_dim and kv_heads * head_dim
+// at most C * 8 * kSplitThreads for the chunk budget C (8-element chunks per
+// thread) the launcher picks: 4 when they fit 4096, else 8.
+// ---------------------------------------------------------------------------
+
+constexpr int kSplitThreads = 128;
+
+// Slot resolution with the device-slot write's status rules; -1 = write nothing.
+__device__ __forceinline__ int64_t resolve_slot(const FusedAppendArgs &a, int64_t slot,
+                                                int step) {
+  if (slot < 0) return -1;
+  const int64_t blk = slot / a.block_size;
+  if (blk >= a.offsets_len) {
+    if (a.status) atomicCAS(a.status, 0, 1);
+    return -1;
+  }
+  if (a.valid && a.valid[blk] == 0) {
+    if (a.status) atomicCAS(a.status, 0, 2);
+    return -1;
+  }
+  const int64_t d = int64_t(a.block_offsets[blk]) + (slot % a.block_size) * step;
+  if (uint64_t(d) + uint64_t(step) > a.region_elems) {
+    if (a.status) atomicCAS(a.status, 0, 3);
+    return -1;
+  }
+  return d;
+}
+
+// cos / sin of the fp32 angle pos * theta: the angle minus the nearest multiple
+// of 2 pi, formed in double precision (|angle| <= 2^24 keeps it exact to well
+// below the fp32 ulp of the result), then the hardware approximations.
+__device__ __forceinline__ void rotary(float pos, float theta, float &c, float &s) {
+  const float ang = pos * theta;
+  constexpr double kTwoPi = 6.283185307179586476925286766559;
+  constexpr double kInvTwoPi = 0.15915494309189533576888376337251;
+  const double k = rint(double(ang) * kInvTwoPi);
+  const float r = float(fma(-k, kTwoPi, double(ang)));
+  s = __sinf(r);
+  c = __cosf(r);
+}
+
+// Rotate the 8-element chunk `lo` whose first element is element d0 of a head
+// row: interleaved pairs inside the chunk, or (neox) the low halves of pairs
+// (i, i + D/2) with the high halves in `hi`.
+__device__ __forceinline__ void rotate_chunk(uint4 &lo, uint4 &hi, int d0, float pos,
+                                             const float *inv_freq, bool neox) {
+  uint16_t *e = reinterpret_cast<uint16_t *>(&lo);
+  if (!neox) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float c, s;
+      rotary(pos, inv_freq[d0 / 2 + j], c, s);
+      const float x0 = bf(e[2 * j]), x1 = bf(e[2 * j + 1]);
+      e[2 * j] = to_bf(x0 * c - x1 * s);
+      e[2 * j + 1] = to_bf(x0 * s + x1 * c);
+    }
+  } else {
+    uint16_t *f = reinterpret_cast<uint16_t *>(&hi);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float c, s;
+      rotary(pos, inv_freq[d0 + j], c, s);
+      const float x0 = bf(e[j]), x1 = bf(f[j]);
+      e[j] = to_bf(x0 * c - x1 * s);
+      f[j] = to_bf(x0 * s + x1 * c);
+    }
+  }
+}
+
+template <int C>
+__global__ void __launch_bounds__(kSplitThreads) fused_split_kernel(const FusedAppendArgs a) {
+  __shared__ float red[kSplitThreads / 32];
+  __shared__ int64_t s_dst;
+  ptx::grid_dependency_wait();  // a programmatic dependent: see pdl.cuh
+  ptx::launch_dependents();
+  const int t = blockIdx.x, role = blockIdx.y, tid = threadIdx.x;
+  const int D = a.head_dim, half = D / 2, cph = D / 8;
+  const bool neox = a.rope_mode == 2;
+  if (role == 0) {
+    const int step = a.kv_heads * D, nk = step / 8;
+    int64_t slot = -1;
+    if (tid == 0) slot = a.slot_mapping[t];
+    const float pos = float(a.positions[t]);
+    const uint4 *k = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(a.k) + int64_t(t) * step);
+    const uint4 *v = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(a.v) + int64_t(t) * step);
+    uint4 kr[C], kh[C], vr[C];
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      const int c = tid + i * kSplitThreads;
+      if (c < nk) {
+        kr[i] = k[c];
+        vr[i] = v[c];
+        if (neox && (c % cph) * 8 < half) kh[i] = k[c + half / 8];
+      }
+    }
+    if (tid == 0) s_dst = resolve_slot(a, slot, step);
+    // rotate while the slot lookups are in flight
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      const int c = tid + i * kSplitThreads;
+      const int d0 = (c % cph) * 8;
+      if (c < nk && (!neox || d0 < half)) rotate_chunk(kr[i], kh[i], d0, pos, a.inv_freq, neox);
+    }
+    __syncthreads();
+    const int64_t dst = s_dst;
+    if (dst < 0) return;
+    uint4 *kd = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.va_k) + dst);
+    uint4 *vd = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.va_v) + dst);
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      const int c = tid + i * kSplitThreads;
+      if (c < nk) {
+        vd[c] = vr[i];
+        const int d0 = (c % cph) * 8;
+        if (!neox) {
+          kd[c] = kr[i];
+        } else if (d0 < half) {
+          kd[c] = kr[i];
+          kd[c + half / 8] = kh[i];
+        }
+      }
+    }
+    return;
+  }
+  if (role == 1) {
+    const float pos = float(a.positions[t]);
+    const int nq = a.num_q_heads * D / 8;
+    uint4 *q = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.q) + int64_t(t) * a.num_q_heads * D);
+    uint4 qr[C];
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      const int c = tid + i * kSplitThreads;
+      if (c < nq) qr[i] = q[c];
+    }
+    // A thread stores only the chunks it rotates (neox: a low-half chunk and its
+    // high partner, which no other thread writes), so the in-place update needs
+    // no barrier.
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      const int c = tid + i * kSplitThreads;
+      if (c < nq) {
+        const int d0 = (c % cph) * 8;
+        if (!neox) {
+          rotate_chunk(qr[i], qr[i], d0, pos, a.inv_freq, false);
+          q[c] = qr[i];
+        } else if (d0 < half) {
+          uint4 hi = q[c + half / 8];
+          rotate_chunk(qr[i], hi, d0, pos, a.inv_freq, true);
+          q[c] = qr[i];
+          q[c + half / 8] = hi;
+        }
+      }
+    }
+    return;
+  }
+  // RMSNorm (ref src/cuda/kernels/rms_norm.cu:14-35): bf16((x * inv_rms) * w)
+  const int H = a.hidden, nx = H / 8;
+  const uint4 *x = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(a.x) + int64_t(t) * H);
+  const uint4 *w = reinterpret_cast<const uint4 *>(a.norm_weight);
+  uint4 xr[C], wr[C];
+#pragma unroll
+  for (int i = 0; i < C; ++i) {
+    const int c = tid + i * kSplitThreads;
+    if (c < nx) {
+      xr[i] = x[c];
+      wr[i] = w[c];
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < C; ++i) {
+    if (tid + i * kSplitThreads < nx) {
+      const uint16_t *e = reinterpret_cast<const uint16_t *>(&xr[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float f = bf(e[j]);
+        ss += f * f;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float total = 0.f;
+#pragma unroll
+  for (int i = 0; i < kSplitThreads / 32; ++i) total += red[i];
+  const float inv_rms = 1.0f / sqrtf(total / float(H) + a.eps);
+  uint4 *y = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.normed_out) + int64_t(t) * H);
+#pragma unroll
+  for (int i = 0; i < C; ++i) {
+    const int c = tid + i * kSplitThreads;
+    if (c < nx) {
+      const uint16_t *xe = reinterpret_cast<const uint16_t *>(&xr[i]);
+      const uint16_t *we = reinterpret_cast<const uint16_t *>(&wr[i]);
+      uint4 out;
+      uint16_t *oe = reinterpret_cast<uint16_t *>(&out);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) oe[j] = to_bf((bf(xe[j]) * inv_rms) * bf(we[j]));
+      y[c] = out;
+    }
+  }
+}
+
 }  // namespace
 
 cudaError_t copy_rows(const void *k_src, const void *v_src, void *va_k, void *va_v,
@@ -540,7 +761,15 @@ cudaError_t device_slot_write(const SlotWriteArgs &a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-cudaError_t fused_norm_rope_append(const FusedAppendArgs &a, cudaStream_t stream) {
+cudaError_t fused_norm_rope_append(const FusedAppendArgs &args, cudaStream_t stream) {
+  FusedAppendArgs a = args;
+  // theta_i = 1 / base^e_i in fp32, the reference formula (ref src/cuda/kernels/rope.cu:18
+  // with the base as a parameter); e_i = 2 floor(i/2) / D (reference mode) or 2i / D
+  for (int i = 0; i < a.head_dim / 2 && i < 128; ++i) {
+    const float e = a.rope_mode == 0 ? float(2 * (i / 2)) / float(a.head_dim)
+                                     : float(2 * i) / float(a.head_dim);
+    a.inv_freq[i] = 1.0f / powf(a.rope_theta, e);
+  }
   const uintptr_t align = reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.norm_weight) |
                           reinterpret_cast<uintptr_t>(a.normed_out) | reinterpret_cast<uintptr_t>(a.q) |
                           reinterpret_cast<uintptr_t>(a.k) | reinterpret_cast<uintptr_t>(a.v) |
@@ -553,6 +782,16 @@ cudaError_t fused_norm_rope_append(const FusedAppendArgs &a, cudaStream_t stream
                     !(std::getenv("KCMM_FUSED_IMPL") &&
                       std::strcmp(std::getenv("KCMM_FUSED_IMPL"), "table") == 0);
   const size_t smem = size_t(a.head_dim) * sizeof(float);
+  const char *impl = std::getenv("KCMM_FUSED_IMPL");
+  const int widest = std::max(a.hidden, std::max(a.num_q_heads * a.head_dim, step));
+  const bool split = fast && a.head_dim <= 256 && widest <= 8 * 8 * kSplitThreads &&
+                     impl && std::strcmp(impl, "split") == 0;
+  if (split) {
+    const dim3 grid(a.num_tokens, 3);
+    if (widest <= 4 * 8 * kSplitThreads)
+      return launch_pdl(fused_split_kernel<4>, grid, dim3(kSplitThreads), 0, stream, a);
+    return launch_pdl(fused_split_kernel<8>, grid, dim3(kSplitThreads), 0, stream, a);
+  }
   if (fast)
     return launch_pdl(fused_fast_kernel, dim3(a.num_tokens), dim3(kFusedThreads), smem, stream, a);
   return launch_pdl(fused_kernel, dim3(a.num_tokens), dim3(kFusedThreads), smem, stream, a);

@@ -164,6 +164,9 @@ struct FusedAppendArgs {
   void *va_v;
   uint64_t region_elems;
   int32_t *status;
+  // Rotary frequencies theta_i = 1 / base^e_i per pair index (head_dim/2 <= 128
+  // entries), filled by the launcher from rope_theta, rope_mode and head_dim.
+  float inv_freq[128];
 };
 cudaError_t fused_norm_rope_append(const FusedAppendArgs &a, cudaStream_t stream);
 
