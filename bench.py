@@ -518,11 +518,11 @@ def run_reference(args):
 # --- secondary legs (one JSON line each; `--workload` selects one) -----------------
 
 
-def _gate(torch):
-    """Hold the stream for ~1 ms so that the host-side work of the next ABI call
-    (allocator bookkeeping, launch) overlaps it and the following event pair times
-    only the device work."""
-    torch.cuda._sleep(2_000_000)
+def _gate(torch, cycles: int = 2_000_000):
+    """Hold the stream (~1 ms by default) so that the host-side work of the next ABI
+    call (allocator bookkeeping, launch) overlaps it and the following event pair
+    times only the device work."""
+    torch.cuda._sleep(cycles)
 
 
 def _line(metric, value, unit, config, roofline, extra=None):
@@ -797,12 +797,12 @@ def run_swap_leg(args):
     out_ms, in_ms = [], []
     for it in range(max(2, min(args.warmup, 3)) + min(args.steps, 10)):
         victims = [int(b) for b in rng.choice(blocks, nv, replace=False)]
-        _gate(torch)
+        _gate(torch, 20_000_000)  # ~10 ms: covers the host bookkeeping of 3276 blocks
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         pool.swap_out(victims, stream_ptr=sp)
         b.record()
-        _gate(torch)
+        _gate(torch, 20_000_000)  # ~10 ms: covers the host bookkeeping of 3276 blocks
         c, d = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         c.record()
         pool.swap_in(victims, stream_ptr=sp)

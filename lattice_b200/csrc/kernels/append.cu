@@ -74,12 +74,16 @@ __global__ void slot_write_kernel(const SlotWriteArgs a) {
     const int64_t slot = a.slot_mapping[row];
     if (slot >= 0) {
       const int64_t blk = slot / a.block_size;
-      if (blk >= a.offsets_len) {
+      // both lookups in flight together when the block id is in range
+      const bool in_range = blk < a.offsets_len;
+      const uint8_t live = in_range && a.valid ? a.valid[blk] : uint8_t(1);
+      const uint64_t off = in_range ? a.block_offsets[blk] : 0;
+      if (!in_range) {
         if (a.status) atomicCAS(a.status, 0, 1);
-      } else if (a.valid && a.valid[blk] == 0) {
+      } else if (live == 0) {
         if (a.status) atomicCAS(a.status, 0, 2);
       } else {
-        const int64_t d = int64_t(a.block_offsets[blk]) + (slot % a.block_size) * a.step_elems;
+        const int64_t d = int64_t(off) + (slot % a.block_size) * a.step_elems;
         if (uint64_t(d) + uint64_t(a.step_elems) > a.region_elems) {
           if (a.status) atomicCAS(a.status, 0, 3);
         } else {
@@ -319,20 +323,8 @@ __global__ void __launch_bounds__(kFusedThreads) fused_kernel(const FusedAppendA
 }
 
 // ---------------------------------------------------------------------------
-// Fused RMSNorm + RoPE + KV append, latency-oriented form (one CTA per token).
-// Every global load of the token is issued at entry -- the slot lookup chain, x,
-// the norm weight, q, k and v -- so their DRAM round trips overlap.  The first
-// head_dim/2 threads then compute the token's rotary factors into shared memory
-// while the loads are in flight; the one barrier of the RMS reduction also
-// publishes the table.  Same arithmetic as fused_kernel: normed =
-// bf16((x * inv_rms) * w), rotation in fp32, one rounding per element.
-// Requirements (checked by the launcher): 16-byte aligned rows, head_dim % 16 ==
-// 0, and the per-thread chunk budgets below.
+// Rotation of one 16-byte chunk with a cos/sin table.
 // ---------------------------------------------------------------------------
-
-constexpr int kFastX = 4;  // x chunks (8 elements) per thread: hidden <= 8192
-constexpr int kFastQ = 4;  // q chunks per thread: num_q_heads * head_dim <= 8192
-constexpr int kFastK = 2;  // k / v chunks per thread: kv_heads * head_dim <= 4096
 
 // Rotate the 8-element chunk `in` of a head row starting at element d0.
 // Interleaved modes rotate pairs (2i, 2i+1) inside the chunk; for neox the chunk
@@ -360,173 +352,25 @@ __device__ __forceinline__ void rot_chunk(uint4 &lo, uint4 *partner, int pair0, 
   }
 }
 
-__global__ void __launch_bounds__(kFusedThreads) fused_fast_kernel(const FusedAppendArgs a) {
-  extern __shared__ float fsm[];  // cs[D/2], sn[D/2]
-  __shared__ float red[kFusedThreads / 32];
-  __shared__ int64_t s_dst;
-  ptx::grid_dependency_wait();  // a programmatic dependent: see pdl.cuh
-  ptx::launch_dependents();
-  const int t = blockIdx.x, tid = threadIdx.x;
-  const int D = a.head_dim, H = a.hidden, half = D / 2;
-  const int step = a.kv_heads * D;
-  const int qelems = a.num_q_heads * D;
-  const bool neox = a.rope_mode == 2;
-  float *cs = fsm;
-  float *sn = fsm + half;
-
-  int64_t slot = -1;
-  if (tid == 0) slot = a.slot_mapping[t];
-  const float pos = float(a.positions[t]);
-  const uint4 *x = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(a.x) + int64_t(t) * H);
-  const uint4 *w = reinterpret_cast<const uint4 *>(a.norm_weight);
-  uint4 *q = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.q) + int64_t(t) * qelems);
-  const uint4 *k = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(a.k) + int64_t(t) * step);
-  const uint4 *v = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(a.v) + int64_t(t) * step);
-  const int nx = H / 8, nq = qelems / 8, nk = step / 8;
-  const int cph = D / 8;  // chunks per head row
-  uint4 xr[kFastX], wr[kFastX], qr[kFastQ], kr[kFastK], vr[kFastK];
-#pragma unroll
-  for (int i = 0; i < kFastX; ++i) {
-    const int c = tid + i * kFusedThreads;
-    if (c < nx) {
-      xr[i] = x[c];
-      wr[i] = w[c];
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < kFastQ; ++i) {
-    const int c = tid + i * kFusedThreads;
-    if (c < nq) qr[i] = q[c];
-  }
-#pragma unroll
-  for (int i = 0; i < kFastK; ++i) {
-    const int c = tid + i * kFusedThreads;
-    if (c < nk) {
-      kr[i] = k[c];
-      vr[i] = v[c];
-    }
-  }
-  if (tid == 0) {
-    int64_t dst = -1;
-    if (slot >= 0) {
-      const int64_t blk = slot / a.block_size;
-      if (blk >= a.offsets_len) {
-        if (a.status) atomicCAS(a.status, 0, 1);
-      } else if (a.valid && a.valid[blk] == 0) {
-        if (a.status) atomicCAS(a.status, 0, 2);
-      } else {
-        const int64_t d = int64_t(a.block_offsets[blk]) + (slot % a.block_size) * step;
-        if (uint64_t(d) + uint64_t(step) > a.region_elems) {
-          if (a.status) atomicCAS(a.status, 0, 3);
-        } else {
-          dst = d;
-        }
-      }
-    }
-    s_dst = dst;
-  }
-  // Rotary table for this token (ref src/cuda/kernels/rope.cu:18, base as a parameter)
-  if (tid < half) {
-    const float e = a.rope_mode == 0 ? float(2 * (tid / 2)) / float(D) : float(2 * tid) / float(D);
-    const float theta = 1.0f / powf(a.rope_theta, e);
-    float sv, cv;
-    sincosf(pos * theta, &sv, &cv);
-    cs[tid] = cv;
-    sn[tid] = sv;
-  }
-  // RMSNorm partial sum (ref src/cuda/kernels/rms_norm.cu:14-35)
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < kFastX; ++i) {
-    if (tid + i * kFusedThreads < nx) {
-      const uint16_t *e = reinterpret_cast<const uint16_t *>(&xr[i]);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float f = bf(e[j]);
-        ss += f * f;
-      }
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if ((tid & 31) == 0) red[tid >> 5] = ss;
-  __syncthreads();  // red[], s_dst and the rotary table
-  float total = 0.f;
-#pragma unroll
-  for (int i = 0; i < kFusedThreads / 32; ++i) total += red[i];
-  const float inv_rms = 1.0f / sqrtf(total / float(H) + a.eps);
-  uint4 *y = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.normed_out) + int64_t(t) * H);
-#pragma unroll
-  for (int i = 0; i < kFastX; ++i) {
-    const int c = tid + i * kFusedThreads;
-    if (c < nx) {
-      const uint16_t *xe = reinterpret_cast<const uint16_t *>(&xr[i]);
-      const uint16_t *we = reinterpret_cast<const uint16_t *>(&wr[i]);
-      uint4 out;
-      uint16_t *oe = reinterpret_cast<uint16_t *>(&out);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) oe[j] = to_bf((bf(xe[j]) * inv_rms) * bf(we[j]));
-      y[c] = out;
-    }
-  }
-  // q: interleaved pairs rotate inside a chunk; neox chunks of the low half of a
-  // head pair with the chunk half/8 further on (read again, it is in L1)
-#pragma unroll
-  for (int i = 0; i < kFastQ; ++i) {
-    const int c = tid + i * kFusedThreads;
-    if (c < nq) {
-      const int d0 = (c % cph) * 8;
-      if (!neox) {
-        rot_chunk(qr[i], nullptr, d0 / 2, cs, sn, false);
-        q[c] = qr[i];
-      } else if (d0 < half) {
-        uint4 hi = q[c + half / 8];
-        rot_chunk(qr[i], &hi, d0, cs, sn, true);
-        q[c] = qr[i];
-        q[c + half / 8] = hi;
-      }
-    }
-  }
-  const int64_t dst = s_dst;
-  if (dst >= 0) {
-    uint4 *kd = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.va_k) + dst);
-    uint4 *vd = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.va_v) + dst);
-#pragma unroll
-    for (int i = 0; i < kFastK; ++i) {
-      const int c = tid + i * kFusedThreads;
-      if (c < nk) {
-        const int d0 = (c % cph) * 8;
-        if (!neox) {
-          rot_chunk(kr[i], nullptr, d0 / 2, cs, sn, false);
-          kd[c] = kr[i];
-        } else if (d0 < half) {
-          uint4 hi = k[c + half / 8];
-          rot_chunk(kr[i], &hi, d0, cs, sn, true);
-          kd[c] = kr[i];
-          kd[c + half / 8] = hi;
-        }
-        vd[c] = vr[i];
-      }
-    }
-  }
-}
-
 // ---------------------------------------------------------------------------
-// Fused RMSNorm + RoPE + KV append, split form: three CTAs per token, one per
-// independent part of the op.
+// Fused RMSNorm + RoPE + KV append, split form (the default for aligned rows):
+// three CTAs per token, one per independent part of the op.
 //   blockIdx.y == 0  rotary of the k heads into the page, V row copied
 //   blockIdx.y == 1  rotary of the q heads, in place
 //   blockIdx.y == 2  RMSNorm of the hidden row (x, w -> normed)
 // Only the K/V CTA waits for the two dependent lookups of the slot (slot
-// mapping, then the offsets / valid tables).  Its CTAs come first in the grid,
-// so those lookups are issued before the bulk of the loads; the norm and q CTAs
-// store as soon as their own loads land.
-// Rotary factors: theta_i comes from the launcher (the same fp32
-// 1/powf(base, e_i) as the reference formula, ref src/cuda/kernels/rope.cu:18);
-// every thread forms angle = pos * theta_i in fp32 like the reference, reduces it
-// exactly to [-pi, pi] in double precision, and takes __sinf/__cosf there
-// (absolute error below 2^-21 on that interval).  No table, no barrier in the
-// q CTA, and none of sincosf's large-argument code.
+// mapping, then the offsets / valid tables); its CTAs come first in the grid,
+// so those lookups are issued before the bulk of the loads.  The norm and q
+// CTAs store as soon as their own loads land.  Against one CTA per token that
+// does all three parts, this cut 32 layers of config 3 (one CUDA graph) from
+// 169 to 137 us on B200.
+// Rotary factors: theta_i comes from the launcher (the reference formula
+// 1/powf(base, e_i) in fp32, ref src/cuda/kernels/rope.cu:18).  The first
+// head_dim/2 threads of a rotary CTA form angle = pos * theta_i in fp32 like the
+// reference, reduce it exactly to [-pi, pi] in double precision and put
+// __cosf/__sinf of it (absolute error below 2^-21 on that interval) in a shared
+// table.  Every thread evaluating the factors of its own pairs instead was
+// slower in the 32-layer graph (167 us).
 // Requirements (checked by the launcher): 16-byte aligned rows, head_dim % 16 ==
 // 0, head_dim <= 256, and hidden, num_q_heads * head_dim and kv_heads * head_dim
 // at most C * 8 * kSplitThreads for the chunk budget C (8-element chunks per
@@ -544,11 +388,14 @@ __device__ __forceinline__ int64_t resolve_slot(const FusedAppendArgs &a, int64_
     if (a.status) atomicCAS(a.status, 0, 1);
     return -1;
   }
-  if (a.valid && a.valid[blk] == 0) {
+  // both lookups in flight together (one round trip, not two)
+  const uint8_t live = a.valid ? a.valid[blk] : uint8_t(1);
+  const uint64_t off = a.block_offsets[blk];
+  if (live == 0) {
     if (a.status) atomicCAS(a.status, 0, 2);
     return -1;
   }
-  const int64_t d = int64_t(a.block_offsets[blk]) + (slot % a.block_size) * step;
+  const int64_t d = int64_t(off) + (slot % a.block_size) * step;
   if (uint64_t(d) + uint64_t(step) > a.region_elems) {
     if (a.status) atomicCAS(a.status, 0, 3);
     return -1;
@@ -569,41 +416,15 @@ __device__ __forceinline__ void rotary(float pos, float theta, float &c, float &
   c = __cosf(r);
 }
 
-// Rotate the 8-element chunk `lo` whose first element is element d0 of a head
-// row: interleaved pairs inside the chunk, or (neox) the low halves of pairs
-// (i, i + D/2) with the high halves in `hi`.
-__device__ __forceinline__ void rotate_chunk(uint4 &lo, uint4 &hi, int d0, float pos,
-                                             const float *inv_freq, bool neox) {
-  uint16_t *e = reinterpret_cast<uint16_t *>(&lo);
-  if (!neox) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float c, s;
-      rotary(pos, inv_freq[d0 / 2 + j], c, s);
-      const float x0 = bf(e[2 * j]), x1 = bf(e[2 * j + 1]);
-      e[2 * j] = to_bf(x0 * c - x1 * s);
-      e[2 * j + 1] = to_bf(x0 * s + x1 * c);
-    }
-  } else {
-    uint16_t *f = reinterpret_cast<uint16_t *>(&hi);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float c, s;
-      rotary(pos, inv_freq[d0 + j], c, s);
-      const float x0 = bf(e[j]), x1 = bf(f[j]);
-      e[j] = to_bf(x0 * c - x1 * s);
-      f[j] = to_bf(x0 * s + x1 * c);
-    }
-  }
-}
-
 template <int C>
 __global__ void __launch_bounds__(kSplitThreads) fused_split_kernel(const FusedAppendArgs a) {
   __shared__ float red[kSplitThreads / 32];
   __shared__ int64_t s_dst;
+  __shared__ float tcs[128], tsn[128];  // cos / sin per pair index
   ptx::grid_dependency_wait();  // a programmatic dependent: see pdl.cuh
   ptx::launch_dependents();
-  const int t = blockIdx.x, role = blockIdx.y, tid = threadIdx.x;
+  const int t = blockIdx.x, tid = threadIdx.x;
+  const int role = blockIdx.y;
   const int D = a.head_dim, half = D / 2, cph = D / 8;
   const bool neox = a.rope_mode == 2;
   if (role == 0) {
@@ -624,14 +445,14 @@ __global__ void __launch_bounds__(kSplitThreads) fused_split_kernel(const FusedA
       }
     }
     if (tid == 0) s_dst = resolve_slot(a, slot, step);
-    // rotate while the slot lookups are in flight
+    for (int i = tid; i < half; i += kSplitThreads) rotary(pos, a.inv_freq[i], tcs[i], tsn[i]);
+    __syncthreads();  // the table and s_dst
 #pragma unroll
     for (int i = 0; i < C; ++i) {
       const int c = tid + i * kSplitThreads;
       const int d0 = (c % cph) * 8;
-      if (c < nk && (!neox || d0 < half)) rotate_chunk(kr[i], kh[i], d0, pos, a.inv_freq, neox);
+      if (c < nk && (!neox || d0 < half)) rot_chunk(kr[i], &kh[i], neox ? d0 : d0 / 2, tcs, tsn, neox);
     }
-    __syncthreads();
     const int64_t dst = s_dst;
     if (dst < 0) return;
     uint4 *kd = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.va_k) + dst);
@@ -662,20 +483,22 @@ __global__ void __launch_bounds__(kSplitThreads) fused_split_kernel(const FusedA
       const int c = tid + i * kSplitThreads;
       if (c < nq) qr[i] = q[c];
     }
+    for (int i = tid; i < half; i += kSplitThreads) rotary(pos, a.inv_freq[i], tcs[i], tsn[i]);
+    __syncthreads();
     // A thread stores only the chunks it rotates (neox: a low-half chunk and its
     // high partner, which no other thread writes), so the in-place update needs
-    // no barrier.
+    // no second barrier.
 #pragma unroll
     for (int i = 0; i < C; ++i) {
       const int c = tid + i * kSplitThreads;
       if (c < nq) {
         const int d0 = (c % cph) * 8;
         if (!neox) {
-          rotate_chunk(qr[i], qr[i], d0, pos, a.inv_freq, false);
+          rot_chunk(qr[i], nullptr, d0 / 2, tcs, tsn, false);
           q[c] = qr[i];
         } else if (d0 < half) {
           uint4 hi = q[c + half / 8];
-          rotate_chunk(qr[i], hi, d0, pos, a.inv_freq, true);
+          rot_chunk(qr[i], &hi, d0, tcs, tsn, true);
           q[c] = qr[i];
           q[c + half / 8] = hi;
         }
@@ -775,25 +598,18 @@ cudaError_t fused_norm_rope_append(const FusedAppendArgs &args, cudaStream_t str
                           reinterpret_cast<uintptr_t>(a.k) | reinterpret_cast<uintptr_t>(a.v) |
                           reinterpret_cast<uintptr_t>(a.va_k) | reinterpret_cast<uintptr_t>(a.va_v);
   const int step = a.kv_heads * a.head_dim;
-  const bool fast = (align & 15) == 0 && a.head_dim % 16 == 0 && a.hidden % 8 == 0 &&
-                    a.hidden <= 8 * kFusedThreads * kFastX &&
-                    a.num_q_heads * a.head_dim <= 8 * kFusedThreads * kFastQ &&
-                    step <= 8 * kFusedThreads * kFastK &&
-                    !(std::getenv("KCMM_FUSED_IMPL") &&
-                      std::strcmp(std::getenv("KCMM_FUSED_IMPL"), "table") == 0);
-  const size_t smem = size_t(a.head_dim) * sizeof(float);
-  const char *impl = std::getenv("KCMM_FUSED_IMPL");
   const int widest = std::max(a.hidden, std::max(a.num_q_heads * a.head_dim, step));
-  const bool split = fast && a.head_dim <= 256 && widest <= 8 * 8 * kSplitThreads &&
-                     impl && std::strcmp(impl, "split") == 0;
+  const bool split = (align & 15) == 0 && a.head_dim % 16 == 0 && a.head_dim <= 256 &&
+                     a.hidden % 8 == 0 && widest <= 8 * 8 * kSplitThreads &&
+                     !(std::getenv("KCMM_FUSED_IMPL") &&
+                       std::strcmp(std::getenv("KCMM_FUSED_IMPL"), "table") == 0);
   if (split) {
     const dim3 grid(a.num_tokens, 3);
     if (widest <= 4 * 8 * kSplitThreads)
       return launch_pdl(fused_split_kernel<4>, grid, dim3(kSplitThreads), 0, stream, a);
     return launch_pdl(fused_split_kernel<8>, grid, dim3(kSplitThreads), 0, stream, a);
   }
-  if (fast)
-    return launch_pdl(fused_fast_kernel, dim3(a.num_tokens), dim3(kFusedThreads), smem, stream, a);
+  const size_t smem = size_t(a.head_dim) * sizeof(float);
   return launch_pdl(fused_kernel, dim3(a.num_tokens), dim3(kFusedThreads), smem, stream, a);
 }
 

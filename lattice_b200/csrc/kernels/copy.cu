@@ -5,16 +5,23 @@
 // and move the block with 16-byte accesses.
 //   * copy_blocks: device -> device (CoW fork of a shared block; the
 //     reference has only a refcount seam, ref scripts/kcmm/shadow_allocator.py).
+//   * swap_blocks_staged (the default swap path): the swap kernel packs a
+//     chunk of blocks into half of a device staging buffer, in host-slot
+//     layout, and the copy engines move each run of consecutive host slots
+//     with one cudaMemcpyAsync; the two halves alternate so packing overlaps
+//     the previous chunk's copy (restores run the same steps backwards).  The
+//     reference also stages (ref src/kcmm/tiering.rs:1207-1798: a gather
+//     kernel, one D2H per layer and a CPU memcpy scatter); here one copy
+//     covers every layer of a run of blocks and nothing is scattered on the CPU.
 //   * swap_blocks: device <-> pinned host memory mapped into the device
-//     address space.  The kernel reads/writes the host bytes directly, so a
-//     whole eviction or restore batch is one launch with no staging buffer
-//     and no host-side scatter (ref src/kcmm/tiering.rs:1207-1798 stages
-//     through a gather kernel, one D2H per layer and a CPU memcpy scatter).
-//     Host slot layout: [K0][V0][K1][V1]...[K(L-1)][V(L-1)], each block_bytes
-//     (ref src/kcmm/tiering.rs:1414-1421).
+//     address space; the kernel reads/writes the host bytes directly
+//     (KCMM_SWAP_IMPL=sm).
+//   Host slot layout: [K0][V0][K1][V1]...[K(L-1)][V(L-1)], each block_bytes
+//   (ref src/kcmm/tiering.rs:1414-1421).
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <vector>
 
 #include "../launch.hpp"
 
@@ -111,6 +118,72 @@ cudaError_t swap_blocks(const uint64_t *d_layer_bases, int num_layers, const uin
                         uint8_t *host_base_dev, int dir, cudaStream_t stream) {
   return launch_pairs(swap_blocks_kernel, d_layer_bases, host_base_dev, num_layers, va_off,
                       host_off, count, block_bytes, dir, stream);
+}
+
+cudaError_t swap_blocks_staged(const SwapStaging &st, const uint64_t *d_layer_bases,
+                               int num_layers, const uint64_t *va_off, const uint64_t *host_off,
+                               int count, uint64_t block_bytes, uint8_t *host, int dir,
+                               cudaStream_t stream) {
+  const uint64_t slot = uint64_t(2) * num_layers * block_bytes;
+  const uint64_t half_bytes = st.bytes / 2;
+  if (half_bytes < slot || !st.copy_stream) return cudaErrorInvalidValue;
+  const int per = int(half_bytes / slot);
+  std::vector<uint64_t> local(size_t(std::min(per, count)));
+  for (size_t j = 0; j < local.size(); ++j) local[j] = j * slot;
+  const cudaMemcpyKind kind = dir == 0 ? cudaMemcpyDeviceToHost : cudaMemcpyHostToDevice;
+  cudaStream_t cs = st.copy_stream;
+  // The copy stream starts behind everything already queued on the caller's stream.
+  cudaError_t e = cudaEventRecord(st.ev_kernel[0], stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, st.ev_kernel[0], 0);
+  if (e == cudaSuccess) e = cudaEventRecord(st.ev_copy[0], cs);
+  if (e == cudaSuccess) e = cudaEventRecord(st.ev_copy[1], cs);
+  if (e == cudaSuccess) e = cudaEventRecord(st.ev_kernel[1], stream);
+  for (int base = 0, chunk = 0; e == cudaSuccess && base < count; base += per, ++chunk) {
+    const int n = std::min(per, count - base);
+    const int h = chunk & 1;
+    uint8_t *half = st.buffer + uint64_t(h) * half_bytes;
+    // one cudaMemcpyAsync per run of consecutive host slots, on the copy stream
+    auto copy_runs = [&]() -> cudaError_t {
+      int j0 = 0;
+      while (j0 < n) {
+        int j1 = j0 + 1;
+        while (j1 < n && host_off[base + j1] == host_off[base + j1 - 1] + slot) ++j1;
+        uint8_t *hp = host + host_off[base + j0];
+        uint8_t *dp = half + uint64_t(j0) * slot;
+        const uint64_t bytes = uint64_t(j1 - j0) * slot;
+        cudaError_t r = dir == 0 ? cudaMemcpyAsync(hp, dp, bytes, kind, cs)
+                                 : cudaMemcpyAsync(dp, hp, bytes, kind, cs);
+        if (r != cudaSuccess) return r;
+        j0 = j1;
+      }
+      return cudaSuccess;
+    };
+    if (dir == 0) {
+      // pack on the caller's stream once the half's previous copy has left it
+      e = cudaStreamWaitEvent(stream, st.ev_copy[h], 0);
+      if (e == cudaSuccess)
+        e = launch_pairs(swap_blocks_kernel, d_layer_bases, half, num_layers, va_off + base,
+                         local.data(), n, block_bytes, 0, stream);
+      if (e == cudaSuccess) e = cudaEventRecord(st.ev_kernel[h], stream);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, st.ev_kernel[h], 0);
+      if (e == cudaSuccess) e = copy_runs();
+      if (e == cudaSuccess) e = cudaEventRecord(st.ev_copy[h], cs);
+    } else {
+      // fill the half once its previous unpack has read it
+      e = cudaStreamWaitEvent(cs, st.ev_kernel[h], 0);
+      if (e == cudaSuccess) e = copy_runs();
+      if (e == cudaSuccess) e = cudaEventRecord(st.ev_copy[h], cs);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, st.ev_copy[h], 0);
+      if (e == cudaSuccess)
+        e = launch_pairs(swap_blocks_kernel, d_layer_bases, half, num_layers, va_off + base,
+                         local.data(), n, block_bytes, 1, stream);
+      if (e == cudaSuccess) e = cudaEventRecord(st.ev_kernel[h], stream);
+    }
+  }
+  // the caller's stream ends behind the last copy
+  if (e == cudaSuccess) e = cudaEventRecord(st.ev_copy[0], cs);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, st.ev_copy[0], 0);
+  return e;
 }
 
 }  // namespace dev

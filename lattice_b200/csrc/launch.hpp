@@ -181,6 +181,23 @@ cudaError_t copy_blocks(const uint64_t *d_layer_bases, int num_layers, const uin
 cudaError_t swap_blocks(const uint64_t *d_layer_bases, int num_layers, const uint64_t *va_off,
                         const uint64_t *host_off, int count, uint64_t block_bytes,
                         uint8_t *host_base_dev, int dir, cudaStream_t stream);
+// The same move through the copy engines.  The swap kernel packs blocks into
+// (or unpacks them from) one half of a device staging buffer on the caller's
+// stream; every run of consecutive host slots crosses the host link as one
+// cudaMemcpyAsync between that half and `host` (the host view of the
+// registered tier) on copy_stream.  The two halves alternate, so packing one
+// chunk overlaps the copy of the previous one; events order the halves' reuse,
+// and the caller's stream ends behind the last copy.
+struct SwapStaging {
+  uint8_t *buffer;  // device, `bytes` long, two halves
+  uint64_t bytes;
+  cudaStream_t copy_stream;
+  cudaEvent_t ev_kernel[2], ev_copy[2];  // per half: last pack / unpack, last copy
+};
+cudaError_t swap_blocks_staged(const SwapStaging &st, const uint64_t *d_layer_bases,
+                               int num_layers, const uint64_t *va_off, const uint64_t *host_off,
+                               int count, uint64_t block_bytes, uint8_t *host, int dir,
+                               cudaStream_t stream);
 
 }  // namespace dev
 }  // namespace kcmm

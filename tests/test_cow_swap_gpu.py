@@ -118,3 +118,74 @@ def test_evict_and_restore_reference_api():
         assert pool.eviction_policy() == "fifo"
     finally:
         wl.close()
+
+
+def _many_chunks_roundtrip() -> dict:
+    """Swap batches that span several halves of the staging buffer, with host slots
+    fragmented between batches.  Every block's bytes in every region must come back
+    exactly, wherever the block lands.  Returns a summary for the caller to check."""
+    import torch
+
+    from lattice_b200.workloads import DecodeWorkload
+
+    # kv_heads 8 x head_dim 128 -> 32 KiB blocks; 2 layers -> 128 KiB host slots, so
+    # 256 blocks fill one 32 MiB staging half and 1000 blocks take four chunks
+    wl = DecodeWorkload(batch=4, num_q_heads=32, kv_heads=8, head_dim=128, pool_blocks=1200,
+                        min_len=40, max_len=200, num_layers=2, tiering=True, seed=12).build()
+    try:
+        pool = wl.pool
+        rng = np.random.default_rng(12)
+        ids = [int(b) for b in wl.block_ids]
+        bb = pool.stats()["block_bytes"] // 2
+        before = regions(wl)
+        offs = {b: pool.block_va_offset(b) // 2 for b in ids}
+        first = [int(b) for b in rng.choice(ids, 1000, replace=False)]
+        pool.swap_out(first)
+        back = first[::2]  # frees every other host slot: the next batch's runs are short
+        pool.swap_in(back)
+        rest = [b for b in ids if b not in set(first)]
+        second = [int(b) for b in rng.choice(rest + back, 400, replace=False)]
+        pool.swap_out(second)
+        cpu = [b for b in ids if pool.block_location(b) == "cpu"]
+        pool.swap_in(cpu)
+        torch.cuda.synchronize()
+        after = regions(wl)
+        bad = 0
+        for b in ids:
+            dst = pool.block_va_offset(b) // 2
+            for key in before:
+                if not np.array_equal(after[key][dst:dst + bb], before[key][offs[b]:offs[b] + bb]):
+                    bad += 1
+        return {"bad": bad, "on_cpu": sum(pool.block_location(b) == "cpu" for b in ids),
+                "status": pool.kernel_status(), "moved": len(first) + len(second)}
+    finally:
+        wl.close()
+
+
+def test_swap_many_chunks_fragmented_slots_bit_exact():
+    """The default path (copy engines through the staging buffer)."""
+    _torch()
+    res = _many_chunks_roundtrip()
+    assert res == {"bad": 0, "on_cpu": 0, "status": 0, "moved": 1400}, res
+
+
+def test_swap_sm_store_path_bit_exact():
+    """KCMM_SWAP_IMPL=sm (the swap kernel stores into the mapped host tier); the switch
+    is read once per process, so the same round trip runs in a child process."""
+    import json
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    _torch()
+    root = Path(__file__).resolve().parents[1]
+    code = ("import json, sys; sys.path.insert(0, %r); sys.path.insert(0, %r); "
+            "import test_cow_swap_gpu as t; print(json.dumps(t._many_chunks_roundtrip()))"
+            % (str(root), str(root / "tests")))
+    env = dict(os.environ, KCMM_SWAP_IMPL="sm")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         env=env, timeout=600, cwd=root)
+    assert out.returncode == 0, out.stderr[-2000:]
+    res = json.loads(out.stdout.strip().splitlines()[-1])
+    assert res == {"bad": 0, "on_cpu": 0, "status": 0, "moved": 1400}, res
