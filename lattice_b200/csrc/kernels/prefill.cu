@@ -205,6 +205,40 @@ __device__ __forceinline__ void store_p_tmem(const float (&s)[N], uint32_t t_hi,
   tc::wait_st();
 }
 
+// The 128 P values of one row -> TMEM as 16-bit pairs, 16 columns per store so that
+// few packed words are live at once: P_hi at columns t_hi .. t_hi + 63, P_lo =
+// round(P - P_hi) at t_lo .. t_lo + 63.
+template <typename T>
+__device__ __forceinline__ void store_p_row128(const float (&s)[128], uint32_t t_hi,
+                                               uint32_t t_lo) {
+#pragma unroll
+  for (int part = 0; part < 4; ++part) {
+    uint32_t w[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) w[i] = pack2<T>(s[32 * part + 2 * i], s[32 * part + 2 * i + 1]);
+    tc::st16u(t_hi + 16 * part, w);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float a = s[32 * part + 2 * i], b = s[32 * part + 2 * i + 1];
+      const float2 hv = unpack2<T>(pack2<T>(a, b));
+      w[i] = pack2<T>(a - hv.x, b - hv.y);
+    }
+    tc::st16u(t_lo + 16 * part, w);
+  }
+  tc::wait_st();
+}
+
+// The P_hi half of store_p_row128 alone.
+template <typename T>
+__device__ __forceinline__ void store_p_hi128(const float (&s)[128], uint32_t t_hi) {
+#pragma unroll
+  for (int part = 0; part < 4; ++part) {
+    uint32_t w[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) w[i] = pack2<T>(s[32 * part + 2 * i], s[32 * part + 2 * i + 1]);
+    tc::st16u(t_hi + 16 * part, w);
+  }
+}
 // Store N columns of one row of O (fp32 in TMEM) / l to global memory.
 template <typename T, int N = 128>
 __device__ __forceinline__ void store_o_row(uint32_t t_row, float inv, uint16_t *dst, bool ok) {
@@ -864,6 +898,349 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
   }
 }
 
+// --- two query tiles per CTA: the pair kernel (the default) ------------------------------
+//
+// A CTA owns 256 query rows of one kv head: tile 0 = rows 0-127, tile 1 = rows 128-255
+// (row = token * G + head, as above), so every K/V tile that crosses from L2 feeds both
+// tiles' MMAs: half the TMA boxes per FLOP of prefill_ws_kernel.
+// warps 0-3  softmax of tile 0, warps 4-7 softmax of tile 1: one thread per row, all
+//            128 keys of a KV tile (warp w reads its TMEM lane quarter w % 4)
+// warp 8     Q (both tiles), then K boxes 0-3 of every KV tile (all 8 without TMA)
+// warp 9     MMA issuer and TMEM owner
+// warp 10    V (all 8 page boxes of a tile)
+// warp 11    K boxes 4-7 (TMA variant; idle otherwise)
+// TMEM: S/P of tile 0 [0,128), S/P of tile 1 [128,256), O of tile 0 [256,384), O of
+// tile 1 [384,512).  Per KV tile j the issue order is
+//   P.V(0, j), QK(0, j+1), P.V(1, j), QK(1, j+1)
+// so the tensor pipe works on one tile while the other tile's softmax runs.  QK(x, j+1)
+// overwrites S/P of tile x after P.V(x, j) read it (tensor-core operations of a CTA
+// execute in issue order), and its completion also covers P.V(x, j), so the softmax
+// may rescale O(x) as soon as S(x, j+1) is ready.
+// P_lo: a single rounding of P to 16 bits leaves a relative error of up to 2^-9 per
+// weight.  Over a row with many comparable weights the errors average out; over few
+// dominant weights (short rows, peaked rows, cancelling values) they do not.  Each
+// softmax thread bounds its row's tile: with s2 = sum(P^2) over the tile and L the
+// running sum including it, sqrt(s2) <= L / 64 keeps the tile's rounding error
+// (standard deviation) within about 2^-9 / sqrt(3) / 64 of the largest |v|.  s2 is
+// bounded by max(P) * sum(P), both known without a pass over the values.  A row above
+// the bound marks the tile; the tile's four warps then agree (named barrier) and
+// compute and store P_lo only for marked tiles, whose P_lo MMAs run.  On a long
+// context that is the first few KV tiles of every row.
+constexpr int kPrThreads = 12 * 32;
+constexpr int kPrKStages = 3;
+constexpr int kPrVStages = 2;
+constexpr uint32_t kPrOffQ = 0;  // two Q tiles
+constexpr uint32_t kPrOffK = 2 * kTile;
+constexpr uint32_t kPrOffV = kPrOffK + kPrKStages * kTile;
+constexpr uint32_t kPrOffBar = kPrOffV + kPrVStages * kTile;
+constexpr size_t kPrSmem = kPrOffBar + 256 + 1024;  // barriers and flags + alignment slack
+constexpr float kLoTau2 = 1.0f / 4096.0f;            // (1/64)^2
+// Register split of the pair kernel: the launch gives every thread kPrLaunchRegs
+// (__launch_bounds__(384, 1)); the softmax warpgroups then take kPrSoftmaxRegs and the
+// producer / MMA warpgroup keeps kPrOtherRegs.  setmaxnreg.inc waits until the
+// warpgroup's registers are free in the CTA's pool, so the split must not exceed the
+// pool: 256 * 200 + 128 * 96 = 63,488 <= 384 * 168 = 64,512.  The launcher checks the
+// compiled kernel's register count against it before every launch.
+constexpr int kPrLaunchRegs = 168;
+constexpr int kPrSoftmaxRegs = 200;
+constexpr int kPrOtherRegs = 96;
+static_assert(256 * kPrSoftmaxRegs + 128 * kPrOtherRegs <= kPrThreads * kPrLaunchRegs,
+              "register split exceeds the launch pool");
+enum PrBar { kPrQFull = 0, kPrKFull = 1, kPrKEmpty = 4, kPrVFull = 7, kPrVEmpty = 9,
+             kPrSFull = 11, kPrPFull = 13, kPrOFinal = 15, kPrSlot = 17, kPrLoFlags = 18 };
+
+template <typename T, bool TMA>
+__global__ void __launch_bounds__(kPrThreads, 1)
+    prefill_pair_kernel(const __grid_constant__ WsParams P) {
+  const PrefillParams &p = P.p;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw = ptx::smem_u32(smem_raw);
+  const uint32_t sb = (raw + 1023u) & ~1023u;
+  unsigned char *smem = smem_raw + (sb - raw);
+  __shared__ int s_fail;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tt = 2 * p.tt;  // tokens per CTA (p.tt per tile)
+  const int q0 = p.q_start[b];
+  const int qlen = p.q_start[b + 1] - q0;
+  const int ctx = p.ctx_lens[b];
+  if (qt * tt >= qlen) return;
+  if (ctx < qlen || ctx > p.max_bps * p.bs) {
+    if (tid == 0) atomicOr(p.diag, int32_t(kDiagBadLaunch));
+    return;
+  }
+  const int base_pos = ctx - qlen;
+  const int ti_hi = min((qt + 1) * tt, qlen);
+  const int kv_hi = base_pos + ti_hi;
+  const int nt = (kv_hi + kKvTile - 1) / kKvTile;
+  auto bar = [&](int i) { return sb + kPrOffBar + uint32_t(i) * 8; };
+  volatile int *lo_flag = reinterpret_cast<volatile int *>(smem + kPrOffBar + kPrLoFlags * 8);
+
+  if (tid == 0) {
+    ptx::mbar_init(bar(kPrQFull), 32);
+    for (int i = 0; i < kPrKStages; ++i) {
+      ptx::mbar_init(bar(kPrKFull + i), TMA ? 2 : 32);
+      ptx::mbar_init(bar(kPrKEmpty + i), 1);
+    }
+    for (int i = 0; i < kPrVStages; ++i) {
+      ptx::mbar_init(bar(kPrVFull + i), 32);
+      ptx::mbar_init(bar(kPrVEmpty + i), 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      ptx::mbar_init(bar(kPrSFull + x), 1);
+      ptx::mbar_init(bar(kPrPFull + x), 128);
+      ptx::mbar_init(bar(kPrOFinal + x), 1);
+    }
+    for (int i = 0; i < 8; ++i) lo_flag[i] = -1;  // [tile][j % 4] = j when tile j needs P_lo
+    ptx::fence_mbarrier_init();
+    s_fail = 0;
+  }
+  if (warp == 9) {
+    tc::tmem_alloc(bar(kPrSlot), kWsTmemCols);
+    tc::tmem_relinquish();
+    tc::fence_before_sync();
+  }
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + kPrOffBar + kPrSlot * 8);
+  volatile int *fail = &s_fail;
+  const int32_t *table = p.tables + size_t(b) * p.max_bps;
+  const uint32_t row_stride = uint32_t(p.hkv) * kHd;  // elements per token row
+  if (warp >= 8) {
+  // producer / MMA warpgroup: gives registers back to the softmax warpgroups
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPrOtherRegs));
+  if (warp == 8 || (TMA && warp == 11)) {
+    // ---------------- K producers (warp 8 loads Q first) ----------------
+    if (warp == 8) {
+      for (int it = 0; it < 128; ++it) {
+        const int idx = it * 32 + lane, r = idx >> 4, c = idx & 15;  // r: CTA row 0..255
+        const int t_r = qt * tt + r / p.G, h_r = h * p.G + r % p.G;
+        const bool ok = t_r < qlen;
+        const uint16_t *src = ok ? p.q + (size_t(q0 + t_r) * p.hq + h_r) * kHd + c * 8 : p.q;
+        ptx::cp_async16(sb + kPrOffQ + uint32_t(r >> 7) * kTile + swz(r & 127, c), src,
+                        ok ? 16u : 0u);
+      }
+      ptx::cp_async_mbar_arrive(bar(kPrQFull));
+    }
+    const int part = warp == 8 ? 0 : 1;
+    if (TMA && lane == 0) ptx::prefetch_tensormap(&P.tmk);
+    bool bad = false;
+    BoxLookup lk(table, p.offsets, p.bs, kv_hi, nt, lane);
+    for (int j = 0; j < nt; ++j) {
+      const int st = j % kPrKStages;
+      int64_t e0 = 0;
+      bool live = lk.next(row_stride, p.region_elems, &e0, &bad);
+      // both tiles' QK of tile j - kPrKStages must have finished reading this stage
+      if (j >= kPrKStages &&
+          !ws_wait(bar(kPrKEmpty + st), uint32_t((j / kPrKStages - 1) & 1), fail))
+        break;
+      const uint32_t dst = sb + kPrOffK + st * kTile;
+      if constexpr (TMA) {
+        if (live && (e0 & (row_stride - 1)) != 0) {  // not a whole token row: no TMA box
+          live = false;
+          bad = true;
+        }
+        const bool mine = ((lane & 7) >> 2) == part;
+        const uint32_t lm = __ballot_sync(0xffffffffu, live && mine && lane < 8);
+        if (lane == 0) ptx::mbar_arrive_expect_tx(bar(kPrKFull + st), uint32_t(__popc(lm)) * 4096u);
+        __syncwarp();
+        if (lane < 16 && live && mine) {  // lanes 8..15: second head_dim half of the boxes
+          const int bx = lane & 7, half = lane >> 3;
+          ptx::tma_load_3d(dst + half * kHalf + bx * 2048, &P.tmk, half * 64, h,
+                           int(e0 >> P.row_shift), bar(kPrKFull + st));
+        }
+      } else {
+        gather_tile(p.va_k, dst, e0, live, j, kv_hi, row_stride, h, lane);
+        ptx::cp_async_mbar_arrive(bar(kPrKFull + st));
+      }
+    }
+    ptx::cp_async_wait<0>();
+    if (bad) atomicOr(p.diag, int32_t(kDiagBadOffset));
+  } else if (warp == 10) {
+    // ---------------- V producer ----------------
+    if (TMA && lane == 0) ptx::prefetch_tensormap(&P.tmv);
+    bool bad = false;
+    BoxLookup lk(table, p.offsets, p.bs, kv_hi, nt, lane);
+    for (int j = 0; j < nt; ++j) {
+      const int st = j % kPrVStages;
+      int64_t e0 = 0;
+      bool live = lk.next(row_stride, p.region_elems, &e0, &bad);
+      // both tiles' P.V of tile j - kPrVStages must have finished reading this stage
+      if (j >= kPrVStages &&
+          !ws_wait(bar(kPrVEmpty + st), uint32_t((j / kPrVStages - 1) & 1), fail))
+        break;
+      const uint32_t dst = sb + kPrOffV + st * kTile;
+      bool boxes = false;
+      if constexpr (TMA) {
+        const bool aligned = (e0 & (row_stride - 1)) == 0;
+        const uint32_t lm = __ballot_sync(0xffffffffu, live && aligned && lane < 8);
+        // whole tile inside the context and all 8 boxes loadable: TMA, else zero-filling copies
+        boxes = j * kKvTile + kKvTile <= kv_hi && __popc(lm) == 8;
+      }
+      if (boxes) {
+        if (lane == 0) {
+          ptx::mbar_arrive_expect_tx(bar(kPrVFull + st), 8u * 4096u);
+        } else {
+          ptx::mbar_arrive(bar(kPrVFull + st));
+        }
+        __syncwarp();
+        if (lane < 8) {  // one box = 16 token rows x both head_dim halves
+          ptx::tma_load_4d(dst + lane * 4096, &P.tmv, 0, int(e0 >> P.row_shift), 0, h,
+                           bar(kPrVFull + st));
+        }
+      } else {
+        gather_tile<true>(p.va_v, dst, e0, live, j, kv_hi, row_stride, h, lane);
+        ptx::cp_async_mbar_arrive(bar(kPrVFull + st));
+      }
+    }
+    ptx::cp_async_wait<0>();
+    if (bad) atomicOr(p.diag, int32_t(kDiagBadOffset));
+  } else if (warp == 9) {
+    // ---------------- MMA issuer ----------------
+    auto issue_qk = [&](int x, int j) {
+      const uint32_t qa = sb + kPrOffQ + uint32_t(x) * kTile;
+      const uint32_t ka = sb + kPrOffK + (j % kPrKStages) * kTile;
+      const uint32_t tS = tmem + uint32_t(x) * 128;
+      if (lane == 0) {
+        tc::fence_after_sync();
+        ptx::fence_proxy_async_smem();  // cp.async-written K (and Q) -> tensor-core reads
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t o = uint32_t((k >> 2) * kHalf + (k & 3) * 32);
+          tc::mma_ss(tS, tc::sw128_desc(qa + o, 16, 1024), tc::sw128_desc(ka + o, 16, 1024),
+                     p.idesc_qk, k > 0);
+        }
+        tc::commit(bar(kPrSFull + x));
+      }
+      __syncwarp();
+    };
+    auto issue_pv = [&](int x, int j) {
+      if (lane == 0) {
+        tc::fence_after_sync();
+        ptx::fence_proxy_async_smem();  // cp.async-written V -> tensor-core reads
+        const uint32_t va = sb + kPrOffV + (j % kPrVStages) * kTile;
+        const uint32_t tp = tmem + uint32_t(x) * 128;  // P_hi columns [0,64), P_lo [64,128)
+        const uint32_t tO = tmem + 256 + uint32_t(x) * 128;
+        const bool lo = lo_flag[x * 4 + (j & 3)] == j;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          // V box k: 16 keys (K) x head_dim (N), the two halves 2048 B apart
+          const uint64_t vd = tc::sw128_desc(va + uint32_t(k) * 4096, 2048, 1024);
+          tc::mma_ts(tO, tp + k * 8, vd, p.idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        if (lo) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint64_t vd = tc::sw128_desc(va + uint32_t(k) * 4096, 2048, 1024);
+            tc::mma_ts(tO, tp + 64 + k * 8, vd, p.idesc_pv, 1u);
+          }
+        }
+        if (j == nt - 1) tc::commit(bar(kPrOFinal + x));
+      }
+      __syncwarp();
+    };
+    bool ok = ws_wait(bar(kPrQFull), 0, fail) && ws_wait(bar(kPrKFull), 0, fail);
+    if (ok) {
+      issue_qk(0, 0);
+      issue_qk(1, 0);
+      if (lane == 0) tc::commit(bar(kPrKEmpty));
+      __syncwarp();
+    }
+    for (int j = 0; ok && j < nt; ++j) {
+      const uint32_t ph = uint32_t(j & 1);
+      if (!ws_wait(bar(kPrPFull), ph, fail)) break;
+      if (!ws_wait(bar(kPrVFull + j % kPrVStages), uint32_t((j / kPrVStages) & 1), fail)) break;
+      issue_pv(0, j);
+      const bool more = j + 1 < nt;
+      if (more) {
+        if (!ws_wait(bar(kPrKFull + (j + 1) % kPrKStages), uint32_t(((j + 1) / kPrKStages) & 1),
+                     fail))
+          break;
+        issue_qk(0, j + 1);
+      }
+      if (!ws_wait(bar(kPrPFull + 1), ph, fail)) break;
+      issue_pv(1, j);
+      if (lane == 0) tc::commit(bar(kPrVEmpty + j % kPrVStages));
+      __syncwarp();
+      if (more) {
+        issue_qk(1, j + 1);
+        if (lane == 0) tc::commit(bar(kPrKEmpty + (j + 1) % kPrKStages));
+        __syncwarp();
+      }
+    }
+  }
+  } else {
+    // ---------------- softmax warps ----------------
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kPrSoftmaxRegs));
+    const int x = warp >> 2, q4 = warp & 3;
+    const int row = q4 * 32 + lane;           // TMEM lane = row of tile x
+    const int crow = x * 128 + row;           // row of the CTA
+    const int ti = qt * tt + crow / p.G;
+    const bool row_ok = ti < qlen;
+    const int qpos = row_ok ? base_pos + ti : kv_hi - 1;
+    const uint32_t lane_base = uint32_t(q4 * 32) << 16;
+    const uint32_t tS = tmem + uint32_t(x) * 128 + lane_base;
+    const uint32_t tO = tmem + 256 + uint32_t(x) * 128 + lane_base;
+    const int first_pos = base_pos + qt * tt + x * p.tt;  // position of the tile's first row
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      if (!ws_wait(bar(kPrSFull + x), uint32_t(j & 1), fail)) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::ld32(tS + 32 * c, s + 32 * c);
+      tc::wait_ld();
+      const bool need_mask = j * kKvTile + kKvTile - 1 > first_pos;
+      const float mx = masked_max<128>(s, j * kKvTile, qpos, need_mask) * p.scale_log2;
+      float alpha;
+      bool rescale;
+      const float sum = exp_given_max<128>(s, mx, p.scale_log2, j > 0, m_run, alpha, rescale);
+      l_run = l_run * alpha + sum;
+      // sum(P^2) <= max(P) * sum(P), with max(P) = 2^(mx - m_run) from the tile's max
+      const float pmax = ptx::fast_exp2(mx - m_run);
+      if (__any_sync(0xffffffffu, pmax * sum > kLoTau2 * l_run * l_run) && lane == 0)
+        lo_flag[x * 4 + (j & 3)] = j;
+      // the tile's four warps agree whether its P_lo MMAs run (named barrier 1 + x)
+      if (x == 0) {
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      } else {
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+      }
+      if (lo_flag[x * 4 + (j & 3)] == j) {
+        store_p_row128<T>(s, tS, tS + 64);
+      } else {
+        store_p_hi128<T>(s, tS);
+        tc::wait_st();
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O(x) *= alpha: P.V(x, j-1) completed before S(x, j) (same issuer, in order)
+        scale_o_row<128>(tO, rescale ? alpha : 1.f);
+      }
+      tc::fence_before_sync();
+      ptx::mbar_arrive(bar(kPrPFull + x));
+    }
+    if (ok && ws_wait(bar(kPrOFinal + x), 0, fail)) {
+      tc::fence_after_sync();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + crow % p.G) * kHd;
+      store_o_row<T, 128>(tO, inv, dst, row_ok);
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (s_fail && tid == 0) atomicOr(p.diag, int32_t(kDiagWaitTimeout));
+  if (warp == 9) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kWsTmemCols);
+  }
+}
+
 }  // namespace
 
 cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
@@ -914,6 +1291,25 @@ cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
     if (tma) {
       std::memcpy(&wp.tmk, a.tensor_maps, sizeof(CUtensorMap));
       std::memcpy(&wp.tmv, a.v_page_map, sizeof(CUtensorMap));
+    }
+    const bool ws = impl && std::strcmp(impl, "ws") == 0;
+    auto pfn = tma ? (bf16 ? prefill_pair_kernel<__nv_bfloat16, true>
+                           : prefill_pair_kernel<__half, true>)
+                   : (bf16 ? prefill_pair_kernel<__nv_bfloat16, false>
+                           : prefill_pair_kernel<__half, false>);
+    // the pair kernel's register split needs the launch register count it was built
+    // for (a smaller pool would leave setmaxnreg.inc waiting): otherwise the one-tile kernel
+    cudaFuncAttributes fa;
+    const bool regs_ok = cudaFuncGetAttributes(&fa, pfn) == cudaSuccess &&
+                         fa.numRegs * kPrThreads >= 256 * kPrSoftmaxRegs + 128 * kPrOtherRegs;
+    if (!ws && regs_ok) {  // two query tiles per CTA (prefill_pair_kernel)
+      auto fn = pfn;
+      cudaError_t e =
+          cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kPrSmem));
+      if (e != cudaSuccess) return e;
+      const dim3 pgrid((a.max_q_len + 2 * p.tt - 1) / (2 * p.tt), a.kv_heads, a.batch);
+      fn<<<pgrid, kPrThreads, kPrSmem, stream>>>(wp);
+      return cudaGetLastError();
     }
     auto fn = tma ? (bf16 ? prefill_ws_kernel<__nv_bfloat16, true> : prefill_ws_kernel<__half, true>)
                   : (bf16 ? prefill_ws_kernel<__nv_bfloat16, false> : prefill_ws_kernel<__half, false>);

@@ -74,13 +74,15 @@ def test_prefill_matches_oracle(case, dtype):
         wl.close()
 
 
-@pytest.mark.parametrize("impl,bs", [("cpasync", 16), ("ws", 32), ("ws", 8)])
+@pytest.mark.parametrize("impl,bs", [("cpasync", 16), ("pair", 32), ("pair", 8), ("ws", 16),
+                                     ("ws", 32), ("gather", 16)])
 def test_prefill_kernel_paths(impl, bs, monkeypatch):
-    """The single-role kernel (forced, and chosen for 8-token pages) and the
-    warp-specialised kernel with 32-token pages (two boxes per page) agree with the
-    oracle."""
-    if impl == "cpasync":
-        monkeypatch.setenv("KCMM_PREFILL_IMPL", "cpasync")
+    """Every kernel path agrees with the oracle: the two-tile kernel (the default) with
+    32-token pages (two boxes per page); the single-role kernel (forced, and chosen for
+    8-token pages); the one-tile warp-specialised kernel (forced); the copy-gather
+    variant (forced) for layouts without tensor maps."""
+    if impl != "pair":
+        monkeypatch.setenv("KCMM_PREFILL_IMPL", impl)
     wl = make(ctx_lens=[700, 260], chunk_lens=[300, 260], num_q_heads=16, kv_heads=2,
               block_size=bs, seed=bs)
     try:
@@ -147,5 +149,25 @@ def test_prefill_rejects_unsupported_shapes():
             wl.pool.paged_prefill(0, num_q_heads=8, kv_heads=1, head_dim=64, **base)
         with pytest.raises(KcmmError, match="dividing 128"):
             wl.pool.paged_prefill(0, num_q_heads=6, kv_heads=2, head_dim=128, **base)
+    finally:
+        wl.close()
+
+
+@pytest.mark.parametrize("impl", ["pair", "ws"])
+def test_prefill_peaked_rows(impl, monkeypatch):
+    """Queries scaled by 6: each row's softmax is dominated by a few keys, so a P rounded
+    once to 16 bits is not accurate enough there.  The two-tile kernel must keep the
+    P_lo correction on those tiles (its per-row test of sum(P^2) against the running
+    sum) and stay within the tolerance."""
+    if impl != "pair":
+        monkeypatch.setenv("KCMM_PREFILL_IMPL", impl)
+    torch = _torch()
+    wl = make(ctx_lens=[2600, 900], chunk_lens=[700, 900], num_q_heads=8, kv_heads=1, seed=21)
+    try:
+        wl.q.mul_(6.0)
+        wl.run()
+        torch.cuda.synchronize()
+        check(wl)
+        assert wl.pool.kernel_status() == 0
     finally:
         wl.close()
