@@ -922,10 +922,11 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
 // softmax thread bounds its row's tile: with s2 = sum(P^2) over the tile and L the
 // running sum including it, sqrt(s2) <= L / 64 keeps the tile's rounding error
 // (standard deviation) within about 2^-9 / sqrt(3) / 64 of the largest |v|.  s2 is
-// bounded by max(P) * sum(P), both known without a pass over the values.  A row above
-// the bound marks the tile; the tile's four warps then agree (named barrier) and
-// compute and store P_lo only for marked tiles, whose P_lo MMAs run.  On a long
-// context that is the first few KV tiles of every row.
+// bounded by max(P) * sum(P), both known without a pass over the values.  A warp with a
+// row above the bound marks the tile and stores its rows' P_lo; the other warps store
+// zeros in the P_lo columns, so a marked tile's P_lo MMAs see P_lo where it is needed
+// and nothing elsewhere, and an unmarked tile runs no P_lo MMAs.  On a long context
+// only the first few KV tiles of every row are marked.
 constexpr int kPrThreads = 12 * 32;
 constexpr int kPrKStages = 3;
 constexpr int kPrVStages = 2;
@@ -939,11 +940,11 @@ constexpr float kLoTau2 = 1.0f / 4096.0f;            // (1/64)^2
 // (__launch_bounds__(384, 1)); the softmax warpgroups then take kPrSoftmaxRegs and the
 // producer / MMA warpgroup keeps kPrOtherRegs.  setmaxnreg.inc waits until the
 // warpgroup's registers are free in the CTA's pool, so the split must not exceed the
-// pool: 256 * 200 + 128 * 96 = 63,488 <= 384 * 168 = 64,512.  The launcher checks the
+// pool: 256 * 208 + 128 * 80 = 63,488 <= 384 * 168 = 64,512.  The launcher checks the
 // compiled kernel's register count against it before every launch.
 constexpr int kPrLaunchRegs = 168;
-constexpr int kPrSoftmaxRegs = 200;
-constexpr int kPrOtherRegs = 96;
+constexpr int kPrSoftmaxRegs = 208;
+constexpr int kPrOtherRegs = 80;
 static_assert(256 * kPrSoftmaxRegs + 128 * kPrOtherRegs <= kPrThreads * kPrLaunchRegs,
               "register split exceeds the launch pool");
 enum PrBar { kPrQFull = 0, kPrKFull = 1, kPrKEmpty = 4, kPrVFull = 7, kPrVEmpty = 9,
@@ -1203,18 +1204,17 @@ __global__ void __launch_bounds__(kPrThreads, 1)
       l_run = l_run * alpha + sum;
       // sum(P^2) <= max(P) * sum(P), with max(P) = 2^(mx - m_run) from the tile's max
       const float pmax = ptx::fast_exp2(mx - m_run);
-      if (__any_sync(0xffffffffu, pmax * sum > kLoTau2 * l_run * l_run) && lane == 0)
-        lo_flag[x * 4 + (j & 3)] = j;
-      // the tile's four warps agree whether its P_lo MMAs run (named barrier 1 + x)
-      if (x == 0) {
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-      } else {
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-      }
-      if (lo_flag[x * 4 + (j & 3)] == j) {
+      // A warp whose rows need P_lo marks the tile and stores it; the others store
+      // zeros there, which is what skipping P_lo gives their rows if another warp's
+      // rows make the tile run its P_lo MMAs.
+      if (__any_sync(0xffffffffu, pmax * sum > kLoTau2 * l_run * l_run)) {
+        if (lane == 0) lo_flag[x * 4 + (j & 3)] = j;
         store_p_row128<T>(s, tS, tS + 64);
       } else {
         store_p_hi128<T>(s, tS);
+        const uint32_t z[16] = {};
+#pragma unroll
+        for (int part = 0; part < 4; ++part) tc::st16u(tS + 64 + 16 * part, z);
         tc::wait_st();
       }
       if (__any_sync(0xffffffffu, rescale)) {
