@@ -965,8 +965,15 @@ def headsplit_measure(args, world: int, rank: int, local: int) -> dict | None:
     lib = library().lib
     slice_bytes = wl.out.numel() * wl.out.element_size()
     pb = PeerBuffers(slice_bytes, rank, world, local) if world > 1 else None
+    peer_error = None
+    if pb is not None and not pb.ok:  # the same on every rank: NCCL is still measured
+        peer_error, pb = pb.error, None
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    if pb is not None:
+    if world > 1 and pb is None:
+        dst = sig = None
+        sig_local = 0
+        half = None
+    elif pb is not None:
         dst = (ctypes.c_uint64 * world)(*pb.buf_ptrs)
         sig = (ctypes.c_uint64 * world)(*pb.sig_ptrs)
         sig_local = pb.signal_ptr
@@ -1028,14 +1035,15 @@ def headsplit_measure(args, world: int, rank: int, local: int) -> dict | None:
     err = (got - want).abs()
     close = bool((err <= 2e-3 + 1e-2 * want.abs()).all())
     max_err = float(err.max().item())
-    ms_p2p, p2p_same = None, True
-    if world > 1:
+    ms_p2p, p2p_same, ms_fused, fused_same = None, True, None, True
+    if world > 1 and pb is not None:
         ms_p2p = timed(step_p2p)
         torch.cuda.synchronize()
         p2p_same = bool((read_device(half(epoch[0]), slice_bytes * world) == ref).all())
-    ms_fused = timed(step_fused)
-    torch.cuda.synchronize()
-    fused_same = bool((read_device(half(epoch[0]), slice_bytes * world) == ref).all())
+    if world == 1 or pb is not None:
+        ms_fused = timed(step_fused)
+        torch.cuda.synchronize()
+        fused_same = bool((read_device(half(epoch[0]), slice_bytes * world) == ref).all())
     gather_status = int(status.item())
     # attention alone, for the split of the step
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1049,22 +1057,26 @@ def headsplit_measure(args, world: int, rank: int, local: int) -> dict | None:
     kv_rank = wl.kv_bytes()
     dev_status = wl.pool.kernel_status()
     # one row per rank: times, parity flags, status words
-    mine = torch.tensor([ms_nccl, ms_p2p if ms_p2p is not None else 0.0, ms_fused, attn_ms,
+    mine = torch.tensor([ms_nccl, ms_p2p if ms_p2p is not None else 0.0,
+                         ms_fused if ms_fused is not None else 0.0, attn_ms,
                          float(close and p2p_same and fused_same), float(gather_status),
                          float(dev_status), max_err], dtype=torch.float64, device=dev)
     rows = [torch.zeros_like(mine) for _ in range(world)]
     if world > 1:
         dist.all_gather(rows, mine)
         barrier()
-        pb.close()
+        if pb is not None:
+            pb.close()
     else:
         rows = [mine]
     wl.close()
     if rank != 0:
         return None
     r = torch.stack(rows).cpu().numpy()
-    ms = {"nccl": float(r[:, 0].max()), "fused_p2p": float(r[:, 2].max())}
-    if world > 1:
+    ms = {"nccl": float(r[:, 0].max())}
+    if ms_fused is not None:
+        ms["fused_p2p"] = float(r[:, 2].max())
+    if ms_p2p is not None:
         ms["p2p"] = float(r[:, 1].max())
     used = min(ms, key=ms.get)
     attn = r[:, 3]
@@ -1080,7 +1092,9 @@ def headsplit_measure(args, world: int, rank: int, local: int) -> dict | None:
         "ms_per_step": round(ms[used], 4), "allgather_used": used,
         "ms_per_step_nccl_allgather": round(ms["nccl"], 4),
         "ms_per_step_p2p_allgather": round(ms["p2p"], 4) if "p2p" in ms else None,
-        "ms_per_step_fused_decode_allgather": round(ms["fused_p2p"], 4),
+        "ms_per_step_fused_decode_allgather": (round(ms["fused_p2p"], 4)
+                                               if "fused_p2p" in ms else None),
+        "peer_buffers_error": peer_error,
         "attention_ms": round(float(attn.max()), 4),
         "attention_ms_min_max_over_ranks": [round(float(attn.min()), 4),
                                             round(float(attn.max()), 4)],

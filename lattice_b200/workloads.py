@@ -399,7 +399,10 @@ class PeerBuffers:
     (two halves of world slices of `slice_bytes`; epoch e fills half e & 1) and
     signal array, publishes their IPC handles with `all_gather_object`, and opens
     the peers'.  Pointers are indexed by rank; this rank's entries are its own
-    allocations."""
+    allocations.  Every rank takes part in both exchanges even when its own step
+    failed, and `ok` is the same on every rank: False when any rank could not
+    allocate or open a mapping (the reason is in `error`), so callers skip the peer
+    gathers together instead of one rank leaving the others waiting."""
 
     def __init__(self, slice_bytes: int, rank: int, world: int, device: int):
         import torch.distributed as dist
@@ -411,39 +414,58 @@ class PeerBuffers:
         self.sig_words = int(library().lib.kcmm_peer_signal_words(world))
         self._own = []
         self._opened = []
+        self.error = None
         handles = []
-        for nbytes in (2 * slice_bytes * world, self.sig_words * 8):
-            err, ptr = rt.cudaMalloc(nbytes)
-            if int(err) != 0:
-                raise RuntimeError(f"cudaMalloc failed: {err}")
-            (err,) = rt.cudaMemset(ptr, 0, nbytes)
-            if int(err) != 0:
-                raise RuntimeError(f"cudaMemset failed: {err}")
-            err, h = rt.cudaIpcGetMemHandle(ptr)
-            if int(err) != 0:
-                raise RuntimeError(f"cudaIpcGetMemHandle failed: {err}")
-            self._own.append(int(ptr))
-            handles.append(bytes(h.reserved))
-        (err,) = rt.cudaDeviceSynchronize()
+        try:
+            for nbytes in (2 * slice_bytes * world, self.sig_words * 8):
+                err, ptr = rt.cudaMalloc(nbytes)
+                if int(err) != 0:
+                    raise RuntimeError(f"cudaMalloc failed: {err}")
+                self._own.append(int(ptr))
+                (err,) = rt.cudaMemset(ptr, 0, nbytes)
+                if int(err) != 0:
+                    raise RuntimeError(f"cudaMemset failed: {err}")
+                err, h = rt.cudaIpcGetMemHandle(ptr)
+                if int(err) != 0:
+                    raise RuntimeError(f"cudaIpcGetMemHandle failed: {err}")
+                handles.append(bytes(h.reserved))
+            rt.cudaDeviceSynchronize()
+        except Exception as e:  # noqa: BLE001 - reported to every rank below
+            self.error = f"rank {rank}: {e}"
+            handles = None
         everyone = [None] * world
         dist.all_gather_object(everyone, handles)
         self.buf_ptrs, self.sig_ptrs = [], []
-        for r in range(world):
-            if r == rank:
-                self.buf_ptrs.append(self._own[0])
-                self.sig_ptrs.append(self._own[1])
-                continue
-            opened = []
-            for raw in everyone[r]:
-                h = rt.cudaIpcMemHandle_t()
-                h.reserved = raw
-                err, ptr = rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess)
-                if int(err) != 0:
-                    raise RuntimeError(f"cudaIpcOpenMemHandle failed: {err}")
-                opened.append(int(ptr))
-                self._opened.append(int(ptr))
-            self.buf_ptrs.append(opened[0])
-            self.sig_ptrs.append(opened[1])
+        failed = [r for r in range(world) if everyone[r] is None]
+        if not failed:
+            try:
+                for r in range(world):
+                    if r == rank:
+                        self.buf_ptrs.append(self._own[0])
+                        self.sig_ptrs.append(self._own[1])
+                        continue
+                    opened = []
+                    for raw in everyone[r]:
+                        h = rt.cudaIpcMemHandle_t()
+                        h.reserved = raw
+                        err, ptr = rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess)
+                        if int(err) != 0:
+                            raise RuntimeError(f"cudaIpcOpenMemHandle of rank {r} failed: {err}")
+                        opened.append(int(ptr))
+                        self._opened.append(int(ptr))
+                    self.buf_ptrs.append(opened[0])
+                    self.sig_ptrs.append(opened[1])
+            except Exception as e:  # noqa: BLE001 - reported to every rank below
+                self.error = f"rank {rank}: {e}"
+        errors = [None] * world
+        dist.all_gather_object(errors, self.error)
+        bad = [e for e in errors if e is not None]
+        if failed and not bad:
+            bad = [f"rank {r} could not allocate its buffers" for r in failed]
+        self.ok = not bad
+        if not self.ok:
+            self.error = "; ".join(bad)
+            self.close()
         self.epoch = 0
 
     @property
