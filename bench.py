@@ -14,6 +14,11 @@ the 126 MB L2, so no flush is needed between steps ("inputs larger than L2").
 / max-over-ranks step time).  `tokens_per_s` = decode tokens/s of a 32-layer
 model's KV path = B_total / (32 * t_step).
 
+On one GPU the line also carries `secondary`: the other BASELINE configurations
+(fused append, beam CoW + shared-prefix decode, swap, chunked prefill, step tables)
+run after the headline with their own step counts (`--no-secondary` skips them;
+`--workload <leg>` runs one alone and prints its own line).
+
 Usage:
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 For N > 1 launch with torch.distributed.run (one rank per GPU, weak scaling:
@@ -300,6 +305,9 @@ def run_ours(args):
     wl.close()
     # BASELINE config 5's KV-head split on the same ranks (strong scaling)
     hs = headsplit_measure(args, world, rank, local) if not args.profile else None
+    # the other BASELINE configurations, one GPU only
+    secondary = (run_secondary_legs(args) if world == 1 and not args.profile
+                 and not args.no_secondary else None)
 
     result = None
     if rank == 0:
@@ -333,6 +341,7 @@ def run_ours(args):
                     round(max(r[1] / (r[0] * 1e-3) / 1e9 for r in per_rank) / peak, 4)],
                 "bytes_equal": len({r[1] for r in per_rank}) == 1},
             "headsplit": hs,
+            "secondary": secondary,
         }
         print(json.dumps(result))
     if world > 1:
@@ -525,12 +534,45 @@ def _gate(torch, cycles: int = 2_000_000):
     torch.cuda._sleep(cycles)
 
 
+_QUIET = [False]  # set while the secondary legs run inside the headline bench
+
+
 def _line(metric, value, unit, config, roofline, extra=None):
     out = {"metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": 1,
            "higher_is_better": True, "dtype": "bf16", "data": "synthetic", "config": config,
            "roofline": roofline}
     out.update(extra or {})
-    print(json.dumps(out))
+    if not _QUIET[0]:
+        print(json.dumps(out))
+    return out
+
+
+def run_secondary_legs(args) -> dict:
+    """The secondary BASELINE configurations, run after the headline on one GPU so that
+    their numbers sit in the headline line too: the fused append (config 3), beam
+    CoW and shared-prefix decode (config 4), swap and chunked prefill (config 5), and
+    the device-resident step tables (config 2).  Each leg is one process-local
+    measurement with its own steps; a leg that fails records its error instead."""
+    legs = {"append": (run_append_leg, 50, 5), "cow": (run_cow_leg, 20, 3),
+            "swap": (run_swap_leg, 5, 2), "prefill": (run_prefill_leg, 3, 2),
+            "tables": (run_tables_leg, 64, 3)}
+    out = {}
+    _QUIET[0] = True
+    try:
+        for name, (fn, steps, warmup) in legs.items():
+            leg_args = argparse.Namespace(**vars(args))
+            leg_args.steps, leg_args.warmup = steps, warmup
+            t0 = time.perf_counter()
+            try:
+                res = fn(leg_args)
+                res = {k: v for k, v in res.items()
+                       if k not in ("n_gpus", "higher_is_better", "dtype", "data")}
+            except Exception as e:  # noqa: BLE001 - one leg's failure is reported, not fatal
+                res = {"error": f"{type(e).__name__}: {e}"}
+            res["leg_wall_s"] = round(time.perf_counter() - t0, 1)
+            out[name] = res
+    finally:
+        _QUIET[0] = False
     return out
 
 
@@ -1261,6 +1303,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--profile", action="store_true",
                     help="profiling case for ncu: 12k-block pool, no CPU baseline / e2e legs")
+    ap.add_argument("--no-secondary", dest="no_secondary", action="store_true",
+                    help="skip the secondary configurations after the headline (one GPU)")
     ap.add_argument("--workload",
                     choices=["step", "append", "cow", "swap", "prefill", "headsplit",
                              "tables"],
