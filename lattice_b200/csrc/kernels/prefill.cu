@@ -239,6 +239,20 @@ __device__ __forceinline__ void store_p_hi128(const float (&s)[128], uint32_t t_
     tc::st16u(t_hi + 16 * part, w);
   }
 }
+// One row of O (128 fp32 columns in TMEM) to global memory as it is.
+__device__ __forceinline__ void store_o_row_f32(uint32_t t_row, float *dst) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float o[32];
+    tc::ld32(t_row + c * 32, o);
+    tc::wait_ld();
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      *reinterpret_cast<float4 *>(dst + c * 32 + q * 4) =
+          make_float4(o[q * 4], o[q * 4 + 1], o[q * 4 + 2], o[q * 4 + 3]);
+  }
+}
+
 // Store N columns of one row of O (fp32 in TMEM) / l to global memory.
 template <typename T, int N = 128>
 __device__ __forceinline__ void store_o_row(uint32_t t_row, float inv, uint16_t *dst, bool ok) {
@@ -502,6 +516,11 @@ struct alignas(64) WsParams {
   CUtensorMap tmv;
   PrefillParams p;
   uint32_t row_shift;
+  // Pair kernel work split (1-D grid): items (qt fastest, then kv head, then sequence)
+  // below n_whole run whole; each later item runs as nsplit CTAs over consecutive KV
+  // ranges that write partial rows to part_o, merged by prefill_merge_kernel.
+  int nqt, n_whole, nsplit;
+  float *part_o;  // [split items][nsplit][256 rows][128]; then m and l: [..][256] each
 };
 template <bool TMA>
 constexpr int ws_threads() { return TMA ? 13 * 32 : 11 * 32; }
@@ -523,7 +542,7 @@ enum WsBar { kQFull = 0, kKFull = 1, kKEmpty = 4, kVFull = 7, kVEmpty = 10, kSFu
 struct BoxLookup {
   const int32_t *table;
   const uint64_t *offsets;
-  int bs, kv_hi, nt, bx, grp, j;
+  int bs, kv_hi, nt, bx, grp, j, j0;
   int tile;       // tile this lane's group is gathering
   int blk;        // its block id (-1: past the keys in use)
   uint64_t off;   // its block offset (valid once loaded)
@@ -531,10 +550,11 @@ struct BoxLookup {
     const int key = t * kKvTile + bx * 16;
     return (t < nt && key < kv_hi) ? table[key / bs] : -1;
   }
+  // Tiles j0, j0 + 1, ... below nt_ (the end of the CTA's range).
   __device__ BoxLookup(const int32_t *tb, const uint64_t *of, int bs_, int kv_hi_, int nt_,
-                       int lane)
+                       int lane, int j0_ = 0)
       : table(tb), offsets(of), bs(bs_), kv_hi(kv_hi_), nt(nt_), bx(lane & 7), grp(lane >> 3),
-        j(0), tile(lane >> 3) {
+        j(j0_), j0(j0_), tile(j0_ + (lane >> 3)) {
     blk = blk_of(tile);
     off = blk >= 0 ? offsets[blk] : 0;
   }
@@ -543,7 +563,7 @@ struct BoxLookup {
   // keys in use, or its block offset is misaligned or its 16 rows leave the region.
   // All 32 lanes must call this together.
   __device__ bool next(uint32_t row_stride, uint64_t region_elems, int64_t *e0, bool *bad) {
-    const int g = j & 3;
+    const int g = (j - j0) & 3;
     int64_t zz = 0;
     bool live = false;
     if (grp == g && blk >= 0) {
@@ -558,7 +578,7 @@ struct BoxLookup {
       tile = j + 4;
       blk = blk_of(tile);
     }
-    if (j >= 2 && grp == ((j + 2) & 3)) off = blk >= 0 ? offsets[blk] : 0;  // tile j + 2
+    if (j - j0 >= 2 && grp == ((j - j0 + 2) & 3)) off = blk >= 0 ? offsets[blk] : 0;  // tile j + 2
     ++j;
     *e0 = zz;
     return live;
@@ -961,7 +981,12 @@ __global__ void __launch_bounds__(kPrThreads, 1)
   __shared__ int s_fail;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // Work item of this CTA, and for the split tail its part.
+  const int lin = int(blockIdx.x);
+  const bool split = lin >= P.n_whole;
+  const int item = split ? P.n_whole + (lin - P.n_whole) / P.nsplit : lin;
+  const int part = split ? (lin - P.n_whole) % P.nsplit : 0;
+  const int qt = item % P.nqt, h = (item / P.nqt) % p.hkv, b = item / (P.nqt * p.hkv);
   const int tt = 2 * p.tt;  // tokens per CTA (p.tt per tile)
   const int q0 = p.q_start[b];
   const int qlen = p.q_start[b + 1] - q0;
@@ -975,6 +1000,27 @@ __global__ void __launch_bounds__(kPrThreads, 1)
   const int ti_hi = min((qt + 1) * tt, qlen);
   const int kv_hi = base_pos + ti_hi;
   const int nt = (kv_hi + kKvTile - 1) / kKvTile;
+  // KV tiles [j_lo, j_hi) of this CTA.  Every part of a split item but the last ends at
+  // or below the CTA's first query row, so its rows see no causal mask, and the last
+  // part (which holds the diagonal) gives every row at least one key.
+  int j_lo = 0, j_hi = nt;
+  float *part_o = nullptr, *part_m = nullptr, *part_l = nullptr;
+  if (split) {
+    const int cap = (base_pos + qt * tt) / kKvTile;
+    auto bound = [&](int k) { return k >= P.nsplit ? nt : min(k * nt / P.nsplit, cap); };
+    j_lo = bound(part);
+    j_hi = bound(part + 1);
+    const size_t slot = size_t(item - P.n_whole) * P.nsplit + part;
+    const size_t n_slots = size_t(gridDim.x - P.n_whole);
+    part_o = P.part_o + slot * 256 * kHd;
+    part_m = P.part_o + n_slots * 256 * kHd + slot * 256;
+    part_l = part_m + n_slots * 256;
+    if (j_hi == j_lo) {  // nothing below the first row: the part carries no weight
+      for (int r = tid; r < 256; r += kPrThreads) part_l[r] = 0.f;
+      return;
+    }
+  }
+  const int n_loc = j_hi - j_lo;  // this CTA's tiles; loop counters below run over them
   auto bar = [&](int i) { return sb + kPrOffBar + uint32_t(i) * 8; };
   volatile int *lo_flag = reinterpret_cast<volatile int *>(smem + kPrOffBar + kPrLoFlags * 8);
 
@@ -1027,14 +1073,14 @@ __global__ void __launch_bounds__(kPrThreads, 1)
     const int part = warp == 8 ? 0 : 1;
     if (TMA && lane == 0) ptx::prefetch_tensormap(&P.tmk);
     bool bad = false;
-    BoxLookup lk(table, p.offsets, p.bs, kv_hi, nt, lane);
-    for (int j = 0; j < nt; ++j) {
-      const int st = j % kPrKStages;
+    BoxLookup lk(table, p.offsets, p.bs, kv_hi, j_hi, lane, j_lo);
+    for (int jj = 0; jj < n_loc; ++jj) {
+      const int j = j_lo + jj, st = jj % kPrKStages;
       int64_t e0 = 0;
       bool live = lk.next(row_stride, p.region_elems, &e0, &bad);
-      // both tiles' QK of tile j - kPrKStages must have finished reading this stage
-      if (j >= kPrKStages &&
-          !ws_wait(bar(kPrKEmpty + st), uint32_t((j / kPrKStages - 1) & 1), fail))
+      // both tiles' QK of tile jj - kPrKStages must have finished reading this stage
+      if (jj >= kPrKStages &&
+          !ws_wait(bar(kPrKEmpty + st), uint32_t((jj / kPrKStages - 1) & 1), fail))
         break;
       const uint32_t dst = sb + kPrOffK + st * kTile;
       if constexpr (TMA) {
@@ -1062,14 +1108,14 @@ __global__ void __launch_bounds__(kPrThreads, 1)
     // ---------------- V producer ----------------
     if (TMA && lane == 0) ptx::prefetch_tensormap(&P.tmv);
     bool bad = false;
-    BoxLookup lk(table, p.offsets, p.bs, kv_hi, nt, lane);
-    for (int j = 0; j < nt; ++j) {
-      const int st = j % kPrVStages;
+    BoxLookup lk(table, p.offsets, p.bs, kv_hi, j_hi, lane, j_lo);
+    for (int jj = 0; jj < n_loc; ++jj) {
+      const int j = j_lo + jj, st = jj % kPrVStages;
       int64_t e0 = 0;
       bool live = lk.next(row_stride, p.region_elems, &e0, &bad);
-      // both tiles' P.V of tile j - kPrVStages must have finished reading this stage
-      if (j >= kPrVStages &&
-          !ws_wait(bar(kPrVEmpty + st), uint32_t((j / kPrVStages - 1) & 1), fail))
+      // both tiles' P.V of tile jj - kPrVStages must have finished reading this stage
+      if (jj >= kPrVStages &&
+          !ws_wait(bar(kPrVEmpty + st), uint32_t((jj / kPrVStages - 1) & 1), fail))
         break;
       const uint32_t dst = sb + kPrOffV + st * kTile;
       bool boxes = false;
@@ -1137,7 +1183,7 @@ __global__ void __launch_bounds__(kPrThreads, 1)
             tc::mma_ts(tO, tp + 64 + k * 8, vd, p.idesc_pv, 1u);
           }
         }
-        if (j == nt - 1) tc::commit(bar(kPrOFinal + x));
+        if (j == n_loc - 1) tc::commit(bar(kPrOFinal + x));
       }
       __syncwarp();
     };
@@ -1148,12 +1194,12 @@ __global__ void __launch_bounds__(kPrThreads, 1)
       if (lane == 0) tc::commit(bar(kPrKEmpty));
       __syncwarp();
     }
-    for (int j = 0; ok && j < nt; ++j) {
+    for (int j = 0; ok && j < n_loc; ++j) {  // j: this CTA's tile index (from j_lo)
       const uint32_t ph = uint32_t(j & 1);
       if (!ws_wait(bar(kPrPFull), ph, fail)) break;
       if (!ws_wait(bar(kPrVFull + j % kPrVStages), uint32_t((j / kPrVStages) & 1), fail)) break;
       issue_pv(0, j);
-      const bool more = j + 1 < nt;
+      const bool more = j + 1 < n_loc;
       if (more) {
         if (!ws_wait(bar(kPrKFull + (j + 1) % kPrKStages), uint32_t(((j + 1) / kPrKStages) & 1),
                      fail))
@@ -1186,7 +1232,7 @@ __global__ void __launch_bounds__(kPrThreads, 1)
     const int first_pos = base_pos + qt * tt + x * p.tt;  // position of the tile's first row
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    for (int j = 0; j < nt; ++j) {
+    for (int j = 0; j < n_loc; ++j) {  // j: this CTA's tile index, key tile j_lo + j
       if (!ws_wait(bar(kPrSFull + x), uint32_t(j & 1), fail)) {
         ok = false;
         break;
@@ -1196,8 +1242,9 @@ __global__ void __launch_bounds__(kPrThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) tc::ld32(tS + 32 * c, s + 32 * c);
       tc::wait_ld();
-      const bool need_mask = j * kKvTile + kKvTile - 1 > first_pos;
-      const float mx = masked_max<128>(s, j * kKvTile, qpos, need_mask) * p.scale_log2;
+      const int k0 = (j_lo + j) * kKvTile;
+      const bool need_mask = k0 + kKvTile - 1 > first_pos;
+      const float mx = masked_max<128>(s, k0, qpos, need_mask) * p.scale_log2;
       float alpha;
       bool rescale;
       const float sum = exp_given_max<128>(s, mx, p.scale_log2, j > 0, m_run, alpha, rescale);
@@ -1226,9 +1273,15 @@ __global__ void __launch_bounds__(kPrThreads, 1)
     }
     if (ok && ws_wait(bar(kPrOFinal + x), 0, fail)) {
       tc::fence_after_sync();
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + crow % p.G) * kHd;
-      store_o_row<T, 128>(tO, inv, dst, row_ok);
+      if (split) {  // unnormalised O with the row's running max and sum, for the merge
+        store_o_row_f32(tO, part_o + size_t(crow) * kHd);
+        part_m[crow] = m_run;
+        part_l[crow] = l_run;
+      } else {
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + crow % p.G) * kHd;
+        store_o_row<T, 128>(tO, inv, dst, row_ok);
+      }
     }
   }
 
@@ -1241,7 +1294,68 @@ __global__ void __launch_bounds__(kPrThreads, 1)
   }
 }
 
+// Merge of the split tail: one warp per CTA row of a split item, 4 head-dim columns a
+// lane.  Each part holds its rows' unnormalised O, running max m (log2 units) and sum l;
+// a part with l = 0 saw no key and carries no weight (its O is not read).
+//   out = sum_p 2^(m_p - M) O_p / sum_p 2^(m_p - M) l_p,  M = max over parts with l_p > 0
+template <typename T>
+__global__ void __launch_bounds__(256) prefill_merge_kernel(const __grid_constant__ WsParams P) {
+  const PrefillParams &p = P.p;
+  const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31);
+  const int n_items = int((gridDim.x * 8) / 256);
+  const int r = int(blockIdx.x) * 8 + warp;  // row over all split items
+  const int si = r / 256, crow = r % 256;
+  const int item = P.n_whole + si;
+  const int qt = item % P.nqt, h = (item / P.nqt) % p.hkv, b = item / (P.nqt * p.hkv);
+  const int q0 = p.q_start[b];
+  const int qlen = p.q_start[b + 1] - q0;
+  const int ti = qt * 2 * p.tt + crow / p.G;
+  if (ti >= qlen) return;
+  const size_t n_slots = size_t(n_items) * P.nsplit;
+  const float *om = P.part_o + n_slots * 256 * kHd;
+  const float *ol = om + n_slots * 256;
+  float M = -INFINITY;
+  for (int k = 0; k < P.nsplit; ++k) {
+    const size_t slot = size_t(si) * P.nsplit + k;
+    if (ol[slot * 256 + crow] > 0.f) M = fmaxf(M, om[slot * 256 + crow]);
+  }
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float L = 0.f;
+  for (int k = 0; k < P.nsplit; ++k) {
+    const size_t slot = size_t(si) * P.nsplit + k;
+    const float l = ol[slot * 256 + crow];
+    if (!(l > 0.f)) continue;
+    const float w = exp2f(om[slot * 256 + crow] - M);
+    const float4 o =
+        *reinterpret_cast<const float4 *>(P.part_o + (slot * 256 + crow) * kHd + lane * 4);
+    acc.x += w * o.x;
+    acc.y += w * o.y;
+    acc.z += w * o.z;
+    acc.w += w * o.w;
+    L += w * l;
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  uint2 v;
+  v.x = pack2<T>(acc.x * inv, acc.y * inv);
+  v.y = pack2<T>(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2 *>(p.out + (size_t(q0 + ti) * p.hq + h * p.G + crow % p.G) * kHd +
+                             lane * 4) = v;
+}
+
 }  // namespace
+
+static int prefill_sm_count() {
+  static int counts[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (counts[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    counts[dev] = n;
+  }
+  return counts[dev];
+}
 
 cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
   if (a.head_dim != kHd || a.kv_heads <= 0 || a.num_q_heads % a.kv_heads != 0)
@@ -1307,8 +1421,31 @@ cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
       cudaError_t e =
           cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kPrSmem));
       if (e != cudaSuccess) return e;
-      const dim3 pgrid((a.max_q_len + 2 * p.tt - 1) / (2 * p.tt), a.kv_heads, a.batch);
-      fn<<<pgrid, kPrThreads, kPrSmem, stream>>>(wp);
+      // One CTA per SM: the items past the last whole wave run split over their KV range
+      // into up to 4 parts, so the tail fills the SMs instead of leaving them half idle.
+      const int nqt = (a.max_q_len + 2 * p.tt - 1) / (2 * p.tt);
+      const int items = nqt * a.kv_heads * a.batch;
+      const int sms = prefill_sm_count();
+      const int rem = items % sms;
+      const char *sp = std::getenv("KCMM_PREFILL_SPLIT");
+      int nsplit = 1;
+      if (rem > 0 && !(sp && std::strcmp(sp, "0") == 0)) nsplit = std::min(4, sms / rem);
+      float *part = nullptr;
+      if (nsplit > 1) {
+        const size_t bytes = size_t(rem) * nsplit * 256 * (kHd + 2) * sizeof(float);
+        part = static_cast<float *>(stream_scratch(stream, bytes));
+        if (!part) nsplit = 1;  // no per-stream buffer (e.g. under graph capture)
+      }
+      wp.nqt = nqt;
+      wp.nsplit = nsplit;
+      wp.n_whole = nsplit > 1 ? items - rem : items;
+      wp.part_o = part;
+      const int ctas = wp.n_whole + (items - wp.n_whole) * nsplit;
+      fn<<<ctas, kPrThreads, kPrSmem, stream>>>(wp);
+      e = cudaGetLastError();
+      if (e != cudaSuccess || nsplit == 1) return e;
+      auto mfn = bf16 ? prefill_merge_kernel<__nv_bfloat16> : prefill_merge_kernel<__half>;
+      mfn<<<(items - wp.n_whole) * 256 / 8, 256, 0, stream>>>(wp);
       return cudaGetLastError();
     }
     auto fn = tma ? (bf16 ? prefill_ws_kernel<__nv_bfloat16, true> : prefill_ws_kernel<__half, true>)

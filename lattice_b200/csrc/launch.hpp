@@ -96,6 +96,12 @@ struct PrefillArgs {
 // (kernels/prefill.cu).  head_dim 128; num_q_heads / kv_heads must divide 128.
 cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream);
 
+// Device scratch kept per (device, stream) between calls (kernels/decode.cu), used by the
+// decode split merge and the prefill tail split.  Calls on one stream share it in stream
+// order.  Null while the stream is being captured or once the per-process stream cache is
+// full; the caller then allocates for the call, or skips the split.
+void *stream_scratch(cudaStream_t stream, size_t bytes);
+
 // All-gather over NVLink peer memory (kernels/peer.cu).  dst[r] is rank r's
 // gathered buffer (two halves of world slices of nbytes, P2P-accessible from
 // this device; epoch e fills half e & 1), sig[r] rank r's signal array of

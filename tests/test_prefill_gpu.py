@@ -171,3 +171,33 @@ def test_prefill_peaked_rows(impl, monkeypatch):
         assert wl.pool.kernel_status() == 0
     finally:
         wl.close()
+
+
+SPLIT_CASES = [
+    # ctx lens, chunk lens, hq, hkv: the two-tile kernel's items (query tiles x kv heads x
+    # sequences) against the 148 SMs decide how the tail splits
+    ([3000], [960], 8, 1),               # 30 items, all split in 4 parts
+    ([1640, 1200], [640, 640], 32, 8),   # 160 items: 148 whole, a tail of 12 in 4 parts
+    ([2048], [2048], 8, 1),              # 64 items in 2 parts; full prefill: empty parts
+    ([77, 900, 2100], [77, 900, 800], 16, 2),  # ragged: 174 items, the tail in the longest
+]
+
+
+@pytest.mark.parametrize("split", ["1", "0"])
+@pytest.mark.parametrize("case", SPLIT_CASES, ids=[f"items{i}" for i in range(len(SPLIT_CASES))])
+def test_prefill_tail_split(case, split, monkeypatch):
+    """The items past the last whole wave of the two-tile kernel run as 2-4 CTAs over
+    consecutive KV ranges whose partial rows a merge kernel combines; every part but the
+    last lies below the CTA's first query row (early parts can be empty).  Both the split
+    launch and the unsplit one (KCMM_PREFILL_SPLIT=0) match the oracle."""
+    monkeypatch.setenv("KCMM_PREFILL_SPLIT", split)
+    ctx, chunks, hq, hkv = case
+    wl = make(ctx_lens=ctx, chunk_lens=chunks, num_q_heads=hq, kv_heads=hkv, dtype="bf16",
+              seed=len(ctx) * 7 + hq)
+    try:
+        wl.run()
+        _torch().cuda.synchronize()
+        check(wl)
+        assert wl.pool.kernel_status() == 0
+    finally:
+        wl.close()
