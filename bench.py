@@ -49,6 +49,29 @@ CONFIG = {"workload": "llama3-8b decode attention + fused norm/rope/append (BASE
 LAYERS_FOR_TOKENS = 32
 
 
+_RESULT_FD = [None]  # the process's original stdout once emit_result owns it
+
+
+def claim_stdout() -> None:
+    """Keep stdout for the result line alone: file descriptor 1 is pointed at stderr, so
+    that what libraries print there (NCCL prints its version line when a communicator is
+    created) cannot come before or between result lines, and emit_result writes to the
+    original stdout."""
+    if _RESULT_FD[0] is None:
+        sys.stdout.flush()
+        _RESULT_FD[0] = os.dup(1)
+        os.dup2(2, 1)
+
+
+def emit_result(obj) -> None:
+    line = json.dumps(obj) + "\n"
+    if _RESULT_FD[0] is None:
+        sys.stdout.write(line)
+        sys.stdout.flush()
+    else:
+        os.write(_RESULT_FD[0], line.encode())
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -343,7 +366,7 @@ def run_ours(args):
             "headsplit": hs,
             "secondary": secondary,
         }
-        print(json.dumps(result))
+        emit_result(result)
     if world > 1:
         import torch.distributed as dist
 
@@ -520,7 +543,7 @@ def run_reference(args):
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line))
+    emit_result(line)
     return line
 
 
@@ -543,7 +566,7 @@ def _line(metric, value, unit, config, roofline, extra=None):
            "roofline": roofline}
     out.update(extra or {})
     if not _QUIET[0]:
-        print(json.dumps(out))
+        emit_result(out)
     return out
 
 
@@ -1312,6 +1335,7 @@ def main():
                     help="step = the headline (default); the others print one line for a "
                          "secondary BASELINE config")
     args = ap.parse_args()
+    claim_stdout()
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "append":
