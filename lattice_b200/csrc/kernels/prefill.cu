@@ -1254,7 +1254,17 @@ __global__ void __launch_bounds__(kPrThreads, 1)
       // A warp whose rows need P_lo marks the tile and stores it; the others store
       // zeros there, which is what skipping P_lo gives their rows if another warp's
       // rows make the tile run its P_lo MMAs.
-      if (__any_sync(0xffffffffu, pmax * sum > kLoTau2 * l_run * l_run)) {
+      // The bound is loose on flat rows (max(P) is several times the mean), so a warp
+      // that fails it evaluates sum(P^2) itself before marking the tile.
+      bool mark = __any_sync(0xffffffffu, pmax * sum > kLoTau2 * l_run * l_run);
+      if (mark) {
+        float q2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 128; ++c) q2[c & 3] = fmaf(s[c], s[c], q2[c & 3]);
+        const float s2 = (q2[0] + q2[1]) + (q2[2] + q2[3]);
+        mark = __any_sync(0xffffffffu, s2 > kLoTau2 * l_run * l_run);
+      }
+      if (mark) {
         if (lane == 0) lo_flag[x * 4 + (j & 3)] = j;
         store_p_row128<T>(s, tS, tS + 64);
       } else {
