@@ -786,9 +786,9 @@ static int prefill_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, 
     set_error(h, std::string(op) + ": shape arguments must be positive");
     return -1;
   }
-  if (hd != 128) {
+  if (hd > 256 || hd % 8 != 0) {
     set_error(h, std::string(op) + ": head_dim " + std::to_string(hd) +
-                     " unsupported (the tensor-core prefill kernel is built for 128)");
+                     " unsupported (the tensor-core prefill takes multiples of 8 up to 256)");
     return -1;
   }
   if (hq % hkv != 0 || 128 % (hq / hkv) != 0) {
@@ -830,8 +830,10 @@ static int prefill_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, 
   a.max_blocks_per_seq = int(max_bps);
   a.scale = scale;
   a.diag = p->diag_word();
-  a.tensor_maps = p->tensor_maps(layer, int(hkv), int(hd));
-  a.v_page_map = p->v_page_map(layer, int(hkv), int(hd));
+  if (hd == 128) {  // the TMA page boxes of the two-tile kernel
+    a.tensor_maps = p->tensor_maps(layer, int(hkv), int(hd));
+    a.v_page_map = p->v_page_map(layer, int(hkv), int(hd));
+  }
   return check_launch(h, op, kcmm::dev::paged_prefill(a, S(stream)));
 }
 

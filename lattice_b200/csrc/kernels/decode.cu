@@ -43,6 +43,8 @@ namespace dev {
 namespace {
 
 constexpr int kUnit = 16;            // tokens per pipeline unit
+constexpr int kWarps = 4;            // warps per decode CTA
+constexpr int kStages = 3;           // depth of each warp's unit ring
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // a KV unit that has not landed in 1 s
                                                   // is reported, never waited on forever
 
@@ -92,15 +94,27 @@ struct CascadeParams {
   int max_a;        // prefix slots of a row: at most this many prefix splits
   // Written by shared_prefix_prep_kernel (scratch):
   int32_t *seq_slots;  // [batch]: partial slots of sequence b (prefix + own splits)
-  int32_t *count;      // [1]: CTAs with work
-  int4 *work;          // [2 per CTA] the work entries, prefix work first
+  int32_t *count;      // [1]: work entries
+  int32_t *cursor;     // [1]: next (entry, kv head) item of the persistent CTAs, zeroed by prep
+  int4 *work;          // [2 per entry] the work entries, prefix work first
 };
+
+// A member whose own tokens past the shared prefix take at most this many 16-token
+// units attends them inside its group's last prefix piece (rows of the other members
+// masked) instead of in a work entry of its own: for beams a few tokens past their
+// common prefix, a separate entry would cost a CTA's whole start-up for one unit.
+constexpr int kFoldUnits = 4;
+// Bit of the prep kernel's per-sequence group word: the member's own units are folded.
+constexpr int kFoldFlag = 1 << 30;
 
 // One work entry (two int4): what a CTA of the shared-prefix decode attends.
 //   a = {mode (1 prefix, 2 own tokens), table row b, first unit, end unit}
-//   c = {first member (mode 1), member mask (mode 1), partial slot, tokens}
+//   c = {first member (mode 1), member mask | fold mask << 16 (mode 1), partial slot,
+//        tokens}
 // Mode 1 rows are (member m of the mask, query head); mode 2 rows are sequence
-// b's heads.  `tokens` bounds the keys (the shared units, or the context).
+// b's heads.  `tokens` bounds the keys (the shared units, or the context).  A
+// mode-1 entry also attends the own units of the members in its fold mask, each
+// through the member's own table row with the other members' rows masked.
 
 // One CTA resolves the groups and writes the work list, so the attention CTAs
 // start from one entry, as the plain decode starts from its sequence.  A
@@ -169,28 +183,41 @@ __global__ void shared_prefix_prep_kernel(const DecodeParams p, const CascadePar
     gn[g] = ns;
     if (ns == 0) continue;
     for (int t = 0; t < c.tiles_per_group; ++t) {
-      int mask = 0;
+      int mask = 0, fold = 0;
+      // the last piece is the smallest; members with few own units join it while the
+      // piece stays within 32 units per warp
+      int room = 32 * kWarps - (pu - (ns - 1) * ups);
       for (int m = 0; m < c.members_per_tile; ++m) {
         const int bm = gs[g] + t * c.members_per_tile + m;
-        if (bm < p.batch && sg[bm] == g) mask |= 1 << m;
+        if (bm < p.batch && sg[bm] == g) {
+          mask |= 1 << m;
+          const int own = ceil_div_dev(sl[bm], kUnit) - pu;
+          if (own > 0 && own <= kFoldUnits && own <= room) {
+            room -= own;
+            fold |= 1 << m;
+            sg[bm] = g | kFoldFlag;
+          }
+        }
       }
       if (!mask) continue;
       const int at = atomicAdd(&n_work, ns);
       for (int k = 0; k < ns; ++k) {
         c.work[2 * (at + k)] = make_int4(1, gs[g], k * ups, min(k * ups + ups, pu));
-        c.work[2 * (at + k) + 1] =
-            make_int4(gs[g] + t * c.members_per_tile, mask, k, pu * kUnit);
+        c.work[2 * (at + k) + 1] = make_int4(gs[g] + t * c.members_per_tile,
+                                             mask | (k == ns - 1 ? fold << 16 : 0), k,
+                                             pu * kUnit);
       }
     }
   }
   __syncthreads();  // prefix work first: the long items start first
   for (int b = threadIdx.x; b < p.batch; b += blockDim.x) {
     const int len = sl[b];
-    const int g = sg[b];
+    const bool folded = sg[b] >= 0 && (sg[b] & kFoldFlag);
+    const int g = sg[b] >= 0 ? sg[b] & ~kFoldFlag : -1;
     const int pu = g >= 0 ? gu[g] : 0;
     const int na = g >= 0 ? gn[g] : 0;
     const int n_units = len > 0 ? ceil_div_dev(len, kUnit) : 0;
-    const int nb = n_units > pu ? ceil_div_dev(n_units - pu, p.units_per_split) : 0;
+    const int nb = n_units > pu && !folded ? ceil_div_dev(n_units - pu, p.units_per_split) : 0;
     c.seq_slots[b] = len > 0 ? na + nb : 0;
     if (nb == 0) continue;
     const int at = atomicAdd(&n_work, nb);
@@ -201,7 +228,10 @@ __global__ void shared_prefix_prep_kernel(const DecodeParams p, const CascadePar
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) *c.count = n_work;
+  if (threadIdx.x == 0) {
+    *c.count = n_work;
+    *c.cursor = 0;
+  }
 }
 
 template <typename T, int D, int W, int NS>
@@ -228,9 +258,15 @@ struct Cfg {
 //         first member's block table; a partial into the entry's slot.
 // MODE 2: an own-tokens entry: one sequence's units past its shared prefix; a
 //         partial into the entry's slot, after the prefix ones.
+//
+// rb counts the units that already went through this warp's ring (the persistent
+// shared-prefix CTAs run many entries on barriers initialised once): unit k of this
+// call uses stage (rb + k) % NS at phase parity ((rb + k) / NS) & 1.  MODE 0 passes 0
+// and initialises its barriers here.  Returns false when a wait ran out (the CTA
+// has reported it and must stop).
 template <typename T, int D, int W, int NS, int MODE>
-__device__ __forceinline__ void decode_body(const DecodeParams &p, const int item,
-                                            const int split, const int4 ea = int4{},
+__device__ __forceinline__ bool decode_body(const DecodeParams &p, const int item,
+                                            const int split, int &rb, const int4 ea = int4{},
                                             const int4 ec = int4{}, const int kvh_in = 0) {
   using C = Cfg<T, D, W, NS>;
   using MMA = ptx::Mma<T>;
@@ -252,19 +288,22 @@ __device__ __forceinline__ void decode_body(const DecodeParams &p, const int ite
   int b, seq_len, u_begin, u_end, n_splits_b, G, lo, hi;
   int NR = 0, slot0 = 0, mbase = 0;  // MODE 1/2 only
   unsigned members = 0;              // MODE 1: bit m = member m of the tile is a row source
+  unsigned fold = 0;                 // MODE 1: bit m = member m's own units are in this entry
+  int n_total;                       // units of this CTA (MODE 1: prefix, then folded own)
   if constexpr (MODE == 0) {
     b = item;
     seq_len = p.seq_lens[b];
-    if (seq_len <= 0) return;
+    if (seq_len <= 0) return true;
     seq_len = min(seq_len, p.max_bps * p.bs);
     const int n_units = ceil_div_dev(seq_len, kUnit);
     u_begin = split * p.units_per_split;
-    if (u_begin >= n_units) return;
+    if (u_begin >= n_units) return true;
     u_end = min(u_begin + p.units_per_split, n_units);
     head_range(kvh, ht, p.hq, p.hkv, &lo, &hi);
     G = hi - lo;
-    if (G <= 0) return;
+    if (G <= 0) return true;
     n_splits_b = ceil_div_dev(n_units, p.units_per_split);
+    n_total = u_end - u_begin;
   } else {
     // the work entry of the shared-prefix decode
     b = ea.y;
@@ -274,11 +313,18 @@ __device__ __forceinline__ void decode_body(const DecodeParams &p, const int ite
     seq_len = ec.w;
     head_range(kvh, 0, p.hq, p.hkv, &lo, &hi);
     G = hi - lo;
-    if (G <= 0 || u_begin >= u_end) return;
+    if (G <= 0 || u_begin >= u_end) return true;
+    n_total = u_end - u_begin;
     if constexpr (MODE == 1) {
       mbase = ec.x;
-      members = unsigned(ec.y);
+      members = unsigned(ec.y) & 0xffffu;
+      fold = unsigned(ec.y) >> 16;
       NR = (32 - __clz(int(members))) * G;  // up to the last member in the mask
+      const int pu = seq_len / kUnit, cap = p.max_bps * p.bs;
+      for (unsigned f = fold; f; f &= f - 1) {
+        const int len = min(p.seq_lens[mbase + __ffs(int(f)) - 1], cap);
+        n_total += ceil_div_dev(len, kUnit) - pu;
+      }
     } else {
       NR = G;
     }
@@ -315,8 +361,10 @@ __device__ __forceinline__ void decode_body(const DecodeParams &p, const int ite
   }
   if (threadIdx.x == 0) s_fail = 0;
   uint64_t *my_bars = bars + warp * NS;
-  if (lane == 0) {
-    for (int s = 0; s < NS; ++s) ptx::mbar_init(ptx::smem_u32(my_bars + s), 32);
+  if constexpr (MODE == 0) {
+    if (lane == 0) {
+      for (int s = 0; s < NS; ++s) ptx::mbar_init(ptx::smem_u32(my_bars + s), 32);
+    }
   }
   ptx::fence_proxy_async_smem();
   __syncthreads();
@@ -335,18 +383,42 @@ __device__ __forceinline__ void decode_body(const DecodeParams &p, const int ite
   }
 
   // ---- per-warp unit list and page addresses -----------------------------
-  const int n_w = (u_end - u_begin - warp + W - 1) / W;  // units owned by this warp (<= 32)
-  const int64_t row_stride = int64_t(p.hkv) * D;          // elements between tokens
+  const int n_w = (n_total - warp + W - 1) / W;  // units owned by this warp (<= 32)
+  const int64_t row_stride = int64_t(p.hkv) * D;  // elements between tokens
   int64_t my_elem = 0;
   int my_ok = 0;
+  int my_meta = 0;  // MODE 1: valid tokens | (folded member + 1) << 8 (0: a shared unit)
   if (lane < n_w) {
     int u = u_begin + warp + lane * W;
+    int tb = b;  // table row
+    if constexpr (MODE == 1) {
+      const int i = warp + lane * W;
+      if (i < u_end - u_begin) {
+        my_meta = kUnit;
+      } else {  // the (i - prefix)-th own unit of the folded members, in member order
+        const int pu = seq_len / kUnit, cap = p.max_bps * p.bs;
+        int j = i - (u_end - u_begin);
+        for (unsigned f = fold; f; f &= f - 1) {
+          const int m = __ffs(int(f)) - 1;
+          const int len = min(p.seq_lens[mbase + m], cap);
+          const int own = ceil_div_dev(len, kUnit) - pu;
+          if (j < own) {
+            u = pu + j;
+            tb = mbase + m;
+            my_meta = min(kUnit, len - u * kUnit) | ((m + 1) << 8);
+            break;
+          }
+          j -= own;
+        }
+      }
+    }
     int tok0 = u * kUnit;
     int page = tok0 / p.bs;
-    int blk = p.tables[int64_t(b) * p.bt_stride + page];
+    int blk = p.tables[int64_t(tb) * p.bt_stride + page];
     if constexpr (MODE == 1) {  // the caller's promise: every member holds the same block
       for (int m = 0; m < 16; ++m) {
-        if (((members >> m) & 1u) && p.tables[int64_t(mbase + m) * p.bt_stride + page] != blk)
+        if ((my_meta >> 8) == 0 && ((members >> m) & 1u) &&
+            p.tables[int64_t(mbase + m) * p.bt_stride + page] != blk)
           atomicOr(p.diag, int32_t(kDiagBadLaunch));
       }
     }
@@ -369,12 +441,17 @@ __device__ __forceinline__ void decode_body(const DecodeParams &p, const int ite
   // chunks spread over the 32 lanes (rows past the context are zero-filled);
   // each lane then arrives on the stage's mbarrier once its copies land.
   auto issue = [&](int k) {
-    const int st = k % NS;
+    const int st = (rb + k) % NS;
     const uint32_t bar = ptx::smem_u32(my_bars + st);
     const int64_t elem = __shfl_sync(0xffffffffu, my_elem, k);
     const int ok = __shfl_sync(0xffffffffu, my_ok, k);
-    const int u = u_begin + warp + k * W;
-    const int nvalid = ok ? min(kUnit, seq_len - u * kUnit) : 0;
+    int nvalid;
+    if constexpr (MODE == 1) {
+      nvalid = ok ? (__shfl_sync(0xffffffffu, my_meta, k) & 0xff) : 0;
+    } else {
+      const int u = u_begin + warp + k * W;
+      nvalid = ok ? min(kUnit, seq_len - u * kUnit) : 0;
+    }
     const uint32_t ks_tile = ptx::smem_u32(wst + st * C::STAGE);
     const uint32_t vs_tile = ks_tile + kUnit * C::RS * sizeof(T);
     constexpr int CPR = D / 8;  // 16-byte chunks per row
@@ -401,17 +478,30 @@ __device__ __forceinline__ void decode_body(const DecodeParams &p, const int ite
   for (int k = 0; k < NS && k < n_w; ++k) issue(k);
 
   for (int k = 0; k < n_w; ++k) {
-    const int st = k % NS;
+    const int st = (rb + k) % NS;
     const uint32_t bar = ptx::smem_u32(my_bars + st);
-    const bool landed = ptx::mbar_wait_bounded(bar, uint32_t((k / NS) & 1), kWaitLimitNs);
+    const bool landed =
+        ptx::mbar_wait_bounded(bar, uint32_t(((rb + k) / NS) & 1), kWaitLimitNs);
     if (!__all_sync(0xffffffffu, landed)) {  // warp-uniform exit
       failed = true;
       break;
     }
     __syncwarp();
     const int ok = __shfl_sync(0xffffffffu, my_ok, k);
-    const int u = u_begin + warp + k * W;
-    const int nvalid = min(kUnit, seq_len - u * kUnit);
+    int nvalid;
+    bool live0 = true, live1 = true;  // MODE 1 own unit: only its member's rows attend it
+    if constexpr (MODE == 1) {
+      const int meta = __shfl_sync(0xffffffffu, my_meta, k);
+      nvalid = meta & 0xff;
+      const int mm = (meta >> 8) - 1;
+      if (mm >= 0) {
+        live0 = (lane >> 2) / G == mm;
+        live1 = ((lane >> 2) + 8) / G == mm;
+      }
+    } else {
+      const int u = u_begin + warp + k * W;
+      nvalid = min(kUnit, seq_len - u * kUnit);
+    }
     const T *ks_tile = wst + st * C::STAGE;
     const T *vs_tile = ks_tile + kUnit * C::RS;
     if (ok) {
@@ -436,7 +526,7 @@ __device__ __forceinline__ void decode_body(const DecodeParams &p, const int ite
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           int tok = nt * 8 + 2 * t + (j & 1);
-          float v = tok < nvalid ? s[nt][j] * p.scale_log2 : -INFINITY;
+          float v = tok < nvalid && (j < 2 ? live0 : live1) ? s[nt][j] * p.scale_log2 : -INFINITY;
           s[nt][j] = v;
         }
         mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
@@ -447,16 +537,22 @@ __device__ __forceinline__ void decode_body(const DecodeParams &p, const int ite
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
       const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-      const float a0 = ptx::fast_exp2(m0 - mn0), a1 = ptx::fast_exp2(m1 - mn1);
+      float e0 = mn0, e1 = mn1;  // exponent base
+      if constexpr (MODE == 1) {
+        // a row that has seen only masked keys keeps a zero sum and a max of -inf
+        if (e0 == -INFINITY) e0 = 0.f;
+        if (e1 == -INFINITY) e1 = 0.f;
+      }
+      const float a0 = ptx::fast_exp2(m0 - e0), a1 = ptx::fast_exp2(m1 - e1);
       m0 = mn0;
       m1 = mn1;
       float ps0 = 0.f, ps1 = 0.f;
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        s[nt][0] = ptx::fast_exp2(s[nt][0] - mn0);
-        s[nt][1] = ptx::fast_exp2(s[nt][1] - mn0);
-        s[nt][2] = ptx::fast_exp2(s[nt][2] - mn1);
-        s[nt][3] = ptx::fast_exp2(s[nt][3] - mn1);
+        s[nt][0] = ptx::fast_exp2(s[nt][0] - e0);
+        s[nt][1] = ptx::fast_exp2(s[nt][1] - e0);
+        s[nt][2] = ptx::fast_exp2(s[nt][2] - e1);
+        s[nt][3] = ptx::fast_exp2(s[nt][3] - e1);
         ps0 += s[nt][0] + s[nt][1];
         ps1 += s[nt][2] + s[nt][3];
       }
@@ -493,6 +589,7 @@ __device__ __forceinline__ void decode_body(const DecodeParams &p, const int ite
     __syncwarp();
     if (k + NS < n_w) issue(k + NS);
   }
+  rb += n_w;
 
   if (failed) {
     // Let copies still in flight land before the CTA's shared memory is
@@ -513,7 +610,7 @@ __device__ __forceinline__ void decode_body(const DecodeParams &p, const int ite
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
   __syncthreads();
-  if (s_fail) return;
+  if (s_fail) return false;
   float *cO = reinterpret_cast<float *>(stages);  // [W][16][D]
   float *cm = cO + W * 16 * D;                     // [W][16]
   float *cl = cm + W * 16;                         // [W][16]
@@ -572,34 +669,49 @@ __device__ __forceinline__ void decode_body(const DecodeParams &p, const int ite
       if (d == 0) p.part_lse[row] = M + log2f(L);
     }
   }
+  return true;
 }
 
 template <typename T, int D, int W, int NS>
 __global__ void __launch_bounds__(W * 32, 2) decode_kernel(const DecodeParams p) {
-  decode_body<T, D, W, NS, 0>(p, blockIdx.z, blockIdx.x);
+  int rb = 0;
+  decode_body<T, D, W, NS, 0>(p, blockIdx.z, blockIdx.x, rb);
 }
 
-// Shared-prefix decode: blockIdx.x = entry * Hkv + kv head walks the prep
-// kernel's work list with the kv head fastest, so CTAs start in list order
-// (prefix work first: the long items start together in the first wave).  The
-// grid is sized for the most work the arguments allow; CTAs past the list's
-// count exit after one load.
+// Shared-prefix decode: persistent CTAs (at most 2 per SM) take items
+// entry * Hkv + kv head of the prep kernel's work list through an atomic cursor,
+// with the kv head fastest, so items start in list order (prefix work first: the
+// long items start together in the first wave) and no CTA is launched for work
+// the arguments could have asked for but did not.  Each warp's unit ring and
+// its mbarriers run on across the items.
 template <typename T, int D, int W, int NS>
 __global__ void __launch_bounds__(W * 32, 2)
     decode_shared_prefix_kernel(const DecodeParams p, const CascadeParams cp) {
+  using C = Cfg<T, D, W, NS>;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ int s_item;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(reinterpret_cast<T *>(smem_raw) + C::Q_ELEMS +
+                                                W * NS * C::STAGE);
+  if (lane == 0) {
+    for (int s = 0; s < NS; ++s) ptx::mbar_init(ptx::smem_u32(bars + warp * NS + s), 32);
+  }
   ptx::grid_dependency_wait();  // the work list is the prep kernel's output
-  const int entry = int(blockIdx.x) / p.hkv, kvh = int(blockIdx.x) % p.hkv;
-  const int n = *cp.count;
-  const int4 ea = cp.work[2 * entry], ec = cp.work[2 * entry + 1];
-  if (entry >= n) {
-    ptx::launch_dependents();
-    return;
+  const int n = *cp.count * p.hkv;
+  int rb = 0;
+  for (;;) {
+    __syncthreads();  // the previous item's reads of shared memory are done
+    if (threadIdx.x == 0) s_item = atomicAdd(cp.cursor, 1);
+    __syncthreads();
+    const int item = s_item;
+    if (item >= n) break;
+    const int entry = item / p.hkv, kvh = item % p.hkv;
+    const int4 ea = cp.work[2 * entry], ec = cp.work[2 * entry + 1];
+    const bool ok = ea.x == 1 ? decode_body<T, D, W, NS, 1>(p, 0, 0, rb, ea, ec, kvh)
+                              : decode_body<T, D, W, NS, 2>(p, 0, 0, rb, ea, ec, kvh);
+    if (!ok) break;
   }
-  if (ea.x == 1) {
-    decode_body<T, D, W, NS, 1>(p, 0, 0, ea, ec, kvh);
-  } else {
-    decode_body<T, D, W, NS, 2>(p, 0, 0, ea, ec, kvh);
-  }
+  ptx::launch_dependents();
 }
 
 // Second pass: combine the splits of each (sequence, head) through their
@@ -845,9 +957,6 @@ __global__ void decode_generic_kernel(const DecodeParams p, int D) {
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-
-constexpr int kWarps = 4;
-constexpr int kStages = 3;
 
 using KernelFn = void (*)(const DecodeParams);
 
@@ -1214,8 +1323,8 @@ SharedPrefixPlan make_shared_prefix_plan(const DecodeArgs &a, int n_groups, int 
   const size_t rows = size_t(a.batch) * a.num_q_heads * size_t(pl.max_a + pl.b_splits);
   pl.resolved_off = (rows * size_t(a.head_dim) * 4 + rows * 4 + 15) & ~size_t(15);
   pl.max_work = int64_t(n_groups) * pl.tiles * pl.max_a + int64_t(a.batch) * pl.b_splits;
-  // seq_slots and the count, then the 32-byte work entries (16-byte aligned)
-  pl.scratch_bytes = pl.resolved_off + ((size_t(a.batch) + 1) * 4 + 15) / 16 * 16 +
+  // seq_slots, the count and the cursor, then the 32-byte work entries (16-byte aligned)
+  pl.scratch_bytes = pl.resolved_off + ((size_t(a.batch) + 2) * 4 + 15) / 16 * 16 +
                      size_t(pl.max_work) * 32;
   return pl;
 }
@@ -1279,7 +1388,8 @@ cudaError_t decode_attention_shared_prefix(const DecodeArgs &a, const int32_t *g
   char *res = static_cast<char *>(scratch) + pl.resolved_off;
   cp.seq_slots = reinterpret_cast<int32_t *>(res);
   cp.count = cp.seq_slots + a.batch;
-  cp.work = reinterpret_cast<int4 *>(res + ((size_t(a.batch) + 1) * 4 + 15) / 16 * 16);
+  cp.cursor = cp.count + 1;
+  cp.work = reinterpret_cast<int4 *>(res + ((size_t(a.batch) + 2) * 4 + 15) / 16 * 16);
 
   const size_t prep_smem = (size_t(n_groups) * 4 + 1 + size_t(a.batch) * 2) * 4;
   e = cudaFuncSetAttribute(shared_prefix_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1289,7 +1399,7 @@ cudaError_t decode_attention_shared_prefix(const DecodeArgs &a, const int32_t *g
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(pl.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pl.smem));
   if (e == cudaSuccess) {
-    dim3 grid(unsigned(pl.max_work * a.kv_heads), 1, 1);
+    dim3 grid(unsigned(std::min<int64_t>(pl.max_work * a.kv_heads, int64_t(sm_count()) * 2)));
     e = launch_pdl(pl.fn, grid, dim3(kWarps * 32), pl.smem, stream, p, cp);
   }
   if (e == cudaSuccess) {

@@ -67,6 +67,7 @@ struct PrefillParams {
   const uint16_t *va_v;
   uint64_t region_elems;
   int hq, hkv, G, bs, max_bps, tt;
+  int d;  // head_dim (the single-role kernel; the others are built for 128)
   float scale_log2;
   uint32_t idesc_qk, idesc_pv;
   int32_t *diag;
@@ -137,13 +138,6 @@ __device__ __forceinline__ float exp_given_max(float (&s)[N], float mx, float sc
     sum[c & 3] += s[c];
   }
   return (sum[0] + sum[1]) + (sum[2] + sum[3]);
-}
-
-__device__ __forceinline__ float exp_tile(float (&s)[128], int k0, int qpos, bool need_mask,
-                                          float scale_log2, bool has_prev, float &m_run,
-                                          float &alpha, bool &rescale) {
-  const float mx = masked_max<128>(s, k0, qpos, need_mask) * scale_log2;
-  return exp_given_max<128>(s, mx, scale_log2, has_prev, m_run, alpha, rescale);
 }
 
 template <typename T>
@@ -291,8 +285,39 @@ __device__ __forceinline__ void scale_o_row(uint32_t t_row, float f) {
   tc::wait_st();
 }
 
-template <typename T>
+// Shared memory and TMEM of the single-role kernel for head_dim padded to DP (64, 128,
+// 192 or 256) and KT keys per tile (128, or 64 where DP > 128 so that the tiles fit):
+// Q [DP/64][128 rows][128 B], K and V [2 stages][DP/64][KT rows][128 B], P_hi and P_lo
+// [KT/64][128 rows][128 B], all with the 128-byte swizzle.  TMEM: S in columns
+// [0, KT), O in [128, 128 + DP).
+template <int DP, int KT>
+struct OneRole {
+  static constexpr uint32_t kQ = 128u * DP * 2;   // Q tile bytes
+  static constexpr uint32_t kKV = uint32_t(KT) * DP * 2;  // one K or V stage
+  static constexpr uint32_t kP = 128u * KT * 2;   // one P tile
+  static constexpr uint32_t kKvBlk = uint32_t(KT) * 128;  // a 64-column block of K or V
+  static constexpr uint32_t kOffK = kQ;
+  static constexpr uint32_t kOffV = kOffK + 2 * kKV;
+  static constexpr uint32_t kOffP = kOffV + 2 * kKV;
+  static constexpr uint32_t kOffBar = kOffP + 2 * kP;
+  static constexpr size_t kSmem = kOffBar + 64 + 1024;
+  static constexpr uint32_t kCols = 128 + DP <= 256 ? 256 : 512;
+  static_assert(kSmem <= 232448, "shared memory of one CTA");
+};
+
+// byte offset of 16-byte chunk `chunk` of row `row` in a 128-byte-swizzled tile whose
+// 64-column blocks are `blk` bytes apart
+__device__ __forceinline__ uint32_t swz_blk(int row, int chunk, uint32_t blk) {
+  return uint32_t((chunk >> 3) * blk + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
+}
+
+// The single-role kernel: every thread loads with cp.async, thread 0 issues the MMAs,
+// thread r runs the softmax of row r.  It serves head dims other than 128 (p.d <= DP,
+// a multiple of 8; the columns past p.d are zero in Q and V and are not stored), and
+// head_dim 128 where the block size is not a multiple of 16.
+template <typename T, int DP, int KT>
 __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) {
+  using L = OneRole<DP, KT>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = ptx::smem_u32(smem_raw);
   const uint32_t sb = (raw + 1023u) & ~1023u;  // 1024-aligned base (swizzle atoms)
@@ -309,19 +334,21 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
     if (tid == 0) atomicOr(p.diag, int32_t(kDiagBadLaunch));
     return;
   }
+  const int D = p.d, DC = p.d / 8;  // head_dim, its 16-byte chunks
   const int base_pos = ctx - qlen;
   const int ti_hi = min((qt + 1) * p.tt, qlen);
   const int kv_hi = base_pos + ti_hi;  // keys [0, kv_hi) reach some row of this CTA
-  const int nt = (kv_hi + kKvTile - 1) / kKvTile;
+  const int nt = (kv_hi + KT - 1) / KT;
 
   const int row = tid;
   const int ti = qt * p.tt + row / p.G;
   const bool row_ok = ti < qlen;
   const int qpos = row_ok ? base_pos + ti : kv_hi - 1;
 
-  const uint32_t bar_s = sb + kOffBar, bar_o = sb + kOffBar + 8, slot = sb + kOffBar + 16;
+  const uint32_t bar_s = sb + L::kOffBar, bar_o = sb + L::kOffBar + 8,
+                 slot = sb + L::kOffBar + 16;
   if (warp == 0) {
-    tc::tmem_alloc(slot, kTmemCols);
+    tc::tmem_alloc(slot, L::kCols);
     tc::tmem_relinquish();
     tc::fence_before_sync();
   }
@@ -332,41 +359,40 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
     s_fail = 0;
   }
 
-  // --- Q tile: row r = (token, head) pair, zero rows past the chunk -----------------
+  // --- Q tile: row r = (token, head) pair, zero rows past the chunk and columns past D --
   {
 #pragma unroll 4
-    for (int it = 0; it < 16; ++it) {
-      const int idx = it * 128 + tid, r = idx >> 4, c = idx & 15;
+    for (int it = 0; it < DP / 8; ++it) {
+      const int idx = it * 128 + tid, r = idx / (DP / 8), c = idx % (DP / 8);
       const int t_r = qt * p.tt + r / p.G, h_r = h * p.G + r % p.G;
-      const bool ok = t_r < qlen;
-      const uint16_t *src =
-          ok ? p.q + (size_t(q0 + t_r) * p.hq + h_r) * kHd + c * 8 : p.q;
-      ptx::cp_async16(sb + kOffQ + swz(r, c), src, ok ? 16u : 0u);
+      const bool ok = t_r < qlen && c < DC;
+      const uint16_t *src = ok ? p.q + (size_t(q0 + t_r) * p.hq + h_r) * D + c * 8 : p.q;
+      ptx::cp_async16(sb + swz_blk(r, c, kHalf), src, ok ? 16u : 0u);
     }
     ptx::cp_async_commit();
   }
 
-  const size_t tok_stride = size_t(p.hkv) * kHd;
+  const size_t tok_stride = size_t(p.hkv) * D;
   const int32_t *table = p.tables + size_t(b) * p.max_bps;
   bool bad = false;
   auto load_kv = [&](int j, int st) {
-    const uint32_t kb = sb + kOffK + st * kTile, vb = sb + kOffV + st * kTile;
+    const uint32_t kb = sb + L::kOffK + st * L::kKV, vb = sb + L::kOffV + st * L::kKV;
 #pragma unroll 4
-    for (int it = 0; it < 16; ++it) {
-      const int idx = it * 128 + tid, n = idx >> 4, c = idx & 15;
-      const int kv = j * kKvTile + n;
+    for (int it = 0; it < KT * DP / 1024; ++it) {
+      const int idx = it * 128 + tid, n = idx / (DP / 8), c = idx % (DP / 8);
+      const int kv = j * KT + n;
       int64_t e = -1;
-      if (kv < kv_hi) {
+      if (kv < kv_hi && c < DC) {
         const int blk = table[kv / p.bs];
         const uint64_t off = p.offsets[blk];
-        const uint64_t elem = off + uint64_t(kv % p.bs) * tok_stride + uint64_t(h) * kHd + c * 8;
+        const uint64_t elem = off + uint64_t(kv % p.bs) * tok_stride + uint64_t(h) * D + c * 8;
         if ((off & 7) == 0 && elem + 8 <= p.region_elems) {
           e = int64_t(elem);
         } else {
           bad = true;
         }
       }
-      const uint32_t so = swz(n, c);
+      const uint32_t so = swz_blk(n, c, L::kKvBlk);
       ptx::cp_async16(kb + so, e >= 0 ? p.va_k + e : p.va_k, e >= 0 ? 16u : 0u);
       ptx::cp_async16(vb + so, e >= 0 ? p.va_v + e : p.va_v, e >= 0 ? 16u : 0u);
     }
@@ -376,7 +402,7 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
   load_kv(0, 0);
   __syncthreads();
   tc::fence_after_sync();
-  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + kOffBar + 16);
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + L::kOffBar + 16);
   const uint32_t lane_base = uint32_t(warp * 32) << 16;
   const uint32_t tS = tmem, tO = tmem + 128;
 
@@ -402,32 +428,51 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
     }
     if (tid == 0) {
       tc::fence_after_sync();
-      const uint32_t qa = sb + kOffQ, ka = sb + kOffK + st * kTile;
+      const uint32_t qa = sb, ka = sb + L::kOffK + st * L::kKV;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const uint32_t o = uint32_t((k >> 2) * kHalf + (k & 3) * 32);
-        tc::mma_ss(tS, tc::sw128_desc(qa + o, 16, 1024), tc::sw128_desc(ka + o, 16, 1024),
-                   p.idesc_qk, k > 0);
+      for (int k = 0; k < DP / 16; ++k) {
+        const uint32_t in_row = uint32_t(k & 3) * 32;
+        tc::mma_ss(tS, tc::sw128_desc(qa + (k >> 2) * kHalf + in_row, 16, 1024),
+                   tc::sw128_desc(ka + (k >> 2) * L::kKvBlk + in_row, 16, 1024), p.idesc_qk,
+                   k > 0);
       }
       tc::commit(bar_s);
     }
     if (!ptx::mbar_wait_bounded(bar_s, uint32_t(j & 1), kLimitNs)) s_fail = 1;
     tc::fence_after_sync();
 
-    float s[128];
+    float s[KT];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) tc::ld32(tS + lane_base + c * 32, s + c * 32);
+    for (int c = 0; c < KT / 32; ++c) tc::ld32(tS + lane_base + c * 32, s + c * 32);
     tc::wait_ld();
 
-    const uint32_t pa = sb + kOffP, pl = pa + kTile;
+    const uint32_t pa = sb + L::kOffP, pl = pa + L::kP;
     float alpha;
     bool rescale;
-    const float sum = exp_tile(s, j * kKvTile, qpos, j * kKvTile + kKvTile - 1 > base_pos + qt * p.tt,
-                               p.scale_log2, j > 0, m_run, alpha, rescale);
-    store_p<T>(s, pa, pl, row);
+    const float mx = masked_max<KT>(s, j * KT, qpos, j * KT + KT - 1 > base_pos + qt * p.tt) *
+                     p.scale_log2;
+    const float sum = exp_given_max<KT>(s, mx, p.scale_log2, j > 0, m_run, alpha, rescale);
+#pragma unroll
+    for (int c = 0; c < KT / 8; ++c) {  // P row -> P_hi, P_lo (keys along the row)
+      uint32_t w[4], r[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float a = s[c * 8 + 2 * e], bb = s[c * 8 + 2 * e + 1];
+        w[e] = pack2<T>(a, bb);
+        const float2 hv = unpack2<T>(w[e]);
+        r[e] = pack2<T>(a - hv.x, bb - hv.y);
+      }
+      const uint32_t so = swz_blk(row, c, kHalf);
+      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(pa + so), "r"(w[0]),
+                   "r"(w[1]), "r"(w[2]), "r"(w[3])
+                   : "memory");
+      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(pl + so), "r"(r[0]),
+                   "r"(r[1]), "r"(r[2]), "r"(r[3])
+                   : "memory");
+    }
     l_run = l_run * alpha + sum;
 
-    if (__any_sync(0xffffffffu, rescale)) scale_o_row(tO + lane_base, rescale ? alpha : 1.f);
+    if (__any_sync(0xffffffffu, rescale)) scale_o_row<DP>(tO + lane_base, rescale ? alpha : 1.f);
     ptx::fence_proxy_async_smem();
     tc::fence_before_sync();
     __syncthreads();
@@ -437,12 +482,12 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
     }
     if (tid == 0) {
       tc::fence_after_sync();
-      const uint32_t va = sb + kOffV + st * kTile;
+      const uint32_t va = sb + L::kOffV + st * L::kKV;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < KT / 16; ++k) {
         const uint32_t ao = uint32_t((k >> 2) * kHalf + (k & 3) * 32);
-        // V: rows = keys (K), 64-element halves of head_dim (N) kHalf apart
-        const uint64_t vd = tc::sw128_desc(va + uint32_t(k) * 2048, kHalf, 1024);
+        // V: rows = keys (K), 64-element blocks of head_dim (N) kKvBlk apart
+        const uint64_t vd = tc::sw128_desc(va + uint32_t(k) * 2048, L::kKvBlk, 1024);
         tc::mma_ss(tO, tc::sw128_desc(pa + ao, 16, 1024), vd, p.idesc_pv,
                    (j > 0 || k > 0) ? 1u : 0u);
         tc::mma_ss(tO, tc::sw128_desc(pl + ao, 16, 1024), vd, p.idesc_pv, 1u);
@@ -459,8 +504,28 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
   failed = failed || s_fail;
   if (!failed) {
     const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-    uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + row % p.G) * kHd;
-    store_o_row<T>(tO + lane_base, inv, dst, row_ok);
+    uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + row % p.G) * D;
+    if (D == DP) {
+      store_o_row<T, DP>(tO + lane_base, inv, dst, row_ok);
+    } else {  // 8 columns per store, the first D of them
+#pragma unroll
+      for (int c = 0; c < DP / 32; ++c) {
+        float o[32];
+        tc::ld32(tO + lane_base + c * 32, o);
+        tc::wait_ld();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (row_ok && c * 32 + q * 8 < D) {
+            uint4 v;
+            v.x = pack2<T>(o[q * 8 + 0] * inv, o[q * 8 + 1] * inv);
+            v.y = pack2<T>(o[q * 8 + 2] * inv, o[q * 8 + 3] * inv);
+            v.z = pack2<T>(o[q * 8 + 4] * inv, o[q * 8 + 5] * inv);
+            v.w = pack2<T>(o[q * 8 + 6] * inv, o[q * 8 + 7] * inv);
+            *reinterpret_cast<uint4 *>(dst + c * 32 + q * 8) = v;
+          }
+        }
+      }
+    }
   } else {
     ptx::cp_async_wait<0>();
     if (tid == 0) atomicOr(p.diag, int32_t(kDiagWaitTimeout));
@@ -470,7 +535,7 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
   __syncthreads();
   if (warp == 0) {
     tc::fence_after_sync();
-    tc::tmem_dealloc(tmem, kTmemCols);
+    tc::tmem_dealloc(tmem, L::kCols);
   }
 }
 
@@ -1367,8 +1432,36 @@ static int prefill_sm_count() {
   return counts[dev];
 }
 
+namespace {
+
+using OneRoleFn = void (*)(const PrefillParams);
+
+// The single-role kernel for head_dim d: padded to the next multiple of 64, with
+// 64-key tiles above 128 so that Q, two K/V stages and P fit in shared memory.
+template <typename T>
+bool pick_one_role(int d, OneRoleFn *fn, size_t *smem) {
+  if (d <= 0 || d > 256 || d % 8 != 0) return false;
+  if (d <= 64) {
+    *fn = prefill_kernel<T, 64, 128>;
+    *smem = OneRole<64, 128>::kSmem;
+  } else if (d <= 128) {
+    *fn = prefill_kernel<T, 128, 128>;
+    *smem = OneRole<128, 128>::kSmem;
+  } else if (d <= 192) {
+    *fn = prefill_kernel<T, 192, 64>;
+    *smem = OneRole<192, 64>::kSmem;
+  } else {
+    *fn = prefill_kernel<T, 256, 64>;
+    *smem = OneRole<256, 64>::kSmem;
+  }
+  return true;
+}
+
+}  // namespace
+
 cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
-  if (a.head_dim != kHd || a.kv_heads <= 0 || a.num_q_heads % a.kv_heads != 0)
+  if (a.head_dim <= 0 || a.head_dim > 256 || a.head_dim % 8 != 0 || a.kv_heads <= 0 ||
+      a.num_q_heads % a.kv_heads != 0)
     return cudaErrorInvalidValue;
   const int G = a.num_q_heads / a.kv_heads;
   if (G > kRows || kRows % G != 0) return cudaErrorInvalidValue;
@@ -1396,7 +1489,22 @@ cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
   p.idesc_qk = tc::idesc_f16(bf16, 128, 128, false, false);
   p.idesc_pv = tc::idesc_f16(bf16, 128, 128, false, true);
   p.diag = a.diag;
+  p.d = a.head_dim;
   dim3 grid((a.max_q_len + p.tt - 1) / p.tt, a.kv_heads, a.batch);
+  if (a.head_dim != kHd) {  // other head dims: the single-role kernel, S = 128 x KT, O = 128 x DP
+    OneRoleFn fn;
+    size_t smem;
+    const bool ok = bf16 ? pick_one_role<__nv_bfloat16>(a.head_dim, &fn, &smem)
+                         : pick_one_role<__half>(a.head_dim, &fn, &smem);
+    if (!ok) return cudaErrorInvalidValue;
+    const int dp = (a.head_dim + 63) / 64 * 64, kt = dp > 128 ? 64 : 128;
+    p.idesc_qk = tc::idesc_f16(bf16, 128, kt, false, false);
+    p.idesc_pv = tc::idesc_f16(bf16, 128, dp, false, true);
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    fn<<<grid, 128, smem, stream>>>(p);
+    return cudaGetLastError();
+  }
   // The warp-specialised kernel gathers 16-token page boxes: block_size % 16 == 0.
   // Otherwise (or with KCMM_PREFILL_IMPL=cpasync) the single-role kernel runs.
   const char *impl = std::getenv("KCMM_PREFILL_IMPL");
@@ -1466,10 +1574,11 @@ cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
     fn<<<grid, tma ? ws_threads<true>() : ws_threads<false>(), kWsSmem, stream>>>(wp);
     return cudaGetLastError();
   }
-  auto fn = bf16 ? prefill_kernel<__nv_bfloat16> : prefill_kernel<__half>;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem));
+  auto fn = bf16 ? prefill_kernel<__nv_bfloat16, 128, 128> : prefill_kernel<__half, 128, 128>;
+  constexpr size_t smem = OneRole<128, 128>::kSmem;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  fn<<<grid, 128, kSmem, stream>>>(p);
+  fn<<<grid, 128, smem, stream>>>(p);
   return cudaGetLastError();
 }
 

@@ -94,6 +94,34 @@ def test_prefill_kernel_paths(impl, bs, monkeypatch):
         wl.close()
 
 
+HEAD_DIMS = [
+    # head_dim, dtype, ctx lens, chunk lens, hq, hkv, block size
+    (64, "bf16", [300, 1000, 45], [100, 256, 45], 8, 1, 16),
+    (64, "f16", [129, 513], [1, 200], 32, 8, 16),
+    (80, "bf16", [400, 333], [130, 333], 16, 2, 16),
+    (96, "bf16", [600, 90], [77, 90], 32, 2, 8),
+    (192, "bf16", [300, 517], [300, 200], 12, 3, 16),
+    (256, "bf16", [700, 260, 31], [300, 260, 31], 16, 2, 16),
+    (256, "f16", [129, 513], [128, 200], 4, 4, 32),
+]
+
+
+@pytest.mark.parametrize("case", HEAD_DIMS, ids=[f"d{c[0]}_{c[1]}" for c in HEAD_DIMS])
+def test_prefill_other_head_dims(case):
+    """Head dims other than 128 (vLLM's 64, 80, 96, 192 and 256) run the single-role
+    tcgen05 kernel with head_dim padded to a multiple of 64 and 64-key tiles above 128."""
+    d, dtype, ctx, chunks, hq, hkv, bs = case
+    wl = make(ctx_lens=ctx, chunk_lens=chunks, num_q_heads=hq, kv_heads=hkv, head_dim=d,
+              dtype=dtype, block_size=bs, seed=d + len(ctx))
+    try:
+        wl.run()
+        _torch().cuda.synchronize()
+        check(wl)
+        assert wl.pool.kernel_status() == 0
+    finally:
+        wl.close()
+
+
 def test_prefill_last_row_equals_decode():
     """The last row of a chunk is a decode step over the whole context: both kernels agree."""
     torch = _torch()
@@ -145,8 +173,10 @@ def test_prefill_rejects_unsupported_shapes():
                     context_lens_ptr=wl.d_ctx.data_ptr(),
                     block_offsets_f16_ptr=kv.d_offsets.data_ptr(), batch=1, max_query_len=8,
                     block_size=16, max_blocks_per_seq=kv.max_blocks_per_seq, scale=0.1)
-        with pytest.raises(KcmmError, match="head_dim 64 unsupported"):
-            wl.pool.paged_prefill(0, num_q_heads=8, kv_heads=1, head_dim=64, **base)
+        with pytest.raises(KcmmError, match="head_dim 100 unsupported"):
+            wl.pool.paged_prefill(0, num_q_heads=8, kv_heads=1, head_dim=100, **base)
+        with pytest.raises(KcmmError, match="head_dim 264 unsupported"):
+            wl.pool.paged_prefill(0, num_q_heads=8, kv_heads=1, head_dim=264, **base)
         with pytest.raises(KcmmError, match="dividing 128"):
             wl.pool.paged_prefill(0, num_q_heads=6, kv_heads=2, head_dim=128, **base)
     finally:

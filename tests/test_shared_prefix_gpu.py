@@ -141,6 +141,16 @@ def test_more_sequences_than_prep_threads():
     _run_case([3] * 500, [2] * 500, [32] * 500, lens, 3, hq=8, hkv=2, seed=7)
 
 
+def test_own_tokens_folded_into_the_prefix_piece_within_its_room():
+    """Members a few units past their group's prefix attend those units inside the
+    group's last prefix piece while it has room (32 units per warp); the others get
+    entries of their own.  40 groups of 4 fill a wave with one 125-unit piece each,
+    leaving room for 3 units: per group the members' own units are 1 and 2 (folded),
+    then 1 (no room left) and 5 (more than a folded member may bring)."""
+    lens = [2000 + 16, 2000 + 32, 2000 + 1, 2000 + 69] * 40
+    _run_case([4] * 40, [125] * 40, [2000] * 40, lens, 4, hq=16, hkv=8, seed=8)
+
+
 def test_malformed_groups_keep_the_result():
     torch = _torch()
     wl = _build([4, 4], [20, 20], [400, 380, 330, 390, 350, 341, 399, 333], seed=4)
