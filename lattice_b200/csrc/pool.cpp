@@ -159,6 +159,21 @@ size_t checked_block_bytes(const PoolConfig &c) {
 }
 }  // namespace
 
+// Bytes of virtual address space per K or V region.  The reference reserves
+// align_up(max_blocks_total * block_bytes, 2 MiB) (ref src/kcmm/pool.rs:216-218), but
+// its capacity rule (ref src/kcmm/pool.rs:323-340) admits whole superblocks of
+// floor(2 MiB / block_bytes) blocks up to ceil(max_blocks_total / blocks_per_superblock)
+// of them.  Where block_bytes does not divide 2 MiB (head_dim 192 with one kv head:
+// 6144-byte blocks, 341 per superblock) the last admitted superblock lies past that
+// reservation and mapping it fails.  The region here holds every admitted superblock;
+// block ids, offsets and the capacity error are unchanged.
+static size_t region_bytes_for(size_t max_blocks_total, size_t block_bytes) {
+  const size_t flat = align_up(max_blocks_total * block_bytes, kSuperblockBytes);
+  if (block_bytes == 0 || block_bytes > kSuperblockBytes) return flat;
+  const size_t bps = kSuperblockBytes / block_bytes;
+  return std::max(flat, (max_blocks_total + bps - 1) / bps * kSuperblockBytes);
+}
+
 Pool::Pool(const PoolConfig &cfg, std::unique_ptr<Vmm> vmm)
     : cfg_(cfg),
       block_size(cfg.block_size),
@@ -168,7 +183,7 @@ Pool::Pool(const PoolConfig &cfg, std::unique_ptr<Vmm> vmm)
       max_blocks_per_seq((cfg.max_seq_len + cfg.block_size - 1) / cfg.block_size),
       max_blocks_total(cfg.max_batch * ((cfg.max_seq_len + cfg.block_size - 1) / cfg.block_size)),
       num_layers(cfg.num_layers),
-      region_bytes(align_up(max_blocks_total * block_bytes, kSuperblockBytes)),
+      region_bytes(region_bytes_for(max_blocks_total, block_bytes)),
       vmm_(std::move(vmm)),
       alloc_(block_bytes),
       policy_(make_policy(cfg.eviction_policy, cfg.max_blocks, cfg.sink_blocks,

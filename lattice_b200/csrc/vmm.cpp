@@ -154,10 +154,14 @@ class HostVmm final : public Vmm {
     regions_.push_back({uint64_t(p), bytes});
     return uint64_t(p);
   }
-  void create_and_map(uint64_t, size_t) override {
+  void create_and_map(uint64_t va, size_t bytes) override {
     if (fail_after_ >= 0 && created_ >= fail_after_) {
       throw Error("cuMemCreate failed: CUresult 2 (injected by KCMM_HOST_VMM_FAIL_AFTER)");
     }
+    // as cuMemMap does, refuse a range outside every reservation
+    bool inside = false;
+    for (const auto &r : regions_) inside = inside || (va >= r.first && va + bytes <= r.first + r.second);
+    if (!inside) throw Error("cuMemMap failed: CUresult 1 (range outside the reserved region)");
     ++created_;
   }
   void release_all() noexcept override {

@@ -38,6 +38,23 @@ def test_capacity_kat(host_pool_factory, golden):
     assert pool.blocks_in_use() == 0
 
 
+def test_last_admitted_superblock_maps_when_blocks_do_not_divide_it(host_pool_factory):
+    """6144-byte blocks (1 kv head x 16 tokens x head_dim 192) leave 341 per 2 MiB
+    superblock.  The capacity rule (ref src/kcmm/pool.rs:323-340) admits
+    ceil(2048 / 341) = 7 superblocks for 2048 blocks, one more than
+    align_up(2048 x 6144, 2 MiB) of address space holds: every admitted block must
+    still map, and the next allocation fail with the capacity error."""
+    pool = host_pool_factory(num_layers=1, kv_heads=1, head_dim=192, max_batch=1,
+                             max_seq_len=2048 * 16)
+    st = pool.stats()
+    assert (st["block_bytes"], st["blocks_per_superblock"]) == (6144, 341)
+    got = pool.alloc_blocks(7 * 341)
+    assert len(set(got)) == 7 * 341
+    with pytest.raises(KcmmError, match="capacity exhausted"):
+        pool.alloc_blocks(1)
+    pool.free_blocks(got)
+
+
 def test_superblock_sizing_kat(golden):
     for case in golden["kats"]["superblock_sizing"]["cases"]:
         a = PhysicalBlockAllocator(case["block_bytes"])
