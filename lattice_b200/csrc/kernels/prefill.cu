@@ -288,8 +288,9 @@ __device__ __forceinline__ void scale_o_row(uint32_t t_row, float f) {
 // Shared memory and TMEM of the single-role kernel for head_dim padded to DP (64, 128,
 // 192 or 256) and KT keys per tile (128, or 64 where DP > 128 so that the tiles fit):
 // Q [DP/64][128 rows][128 B], K and V [2 stages][DP/64][KT rows][128 B], P_hi and P_lo
-// [KT/64][128 rows][128 B], all with the 128-byte swizzle.  TMEM: S in columns
-// [0, KT), O in [128, 128 + DP).
+// [KT/64][128 rows][128 B], all with the 128-byte swizzle, then a ring of key rows
+// [3 tiles][KT].  TMEM (512 columns): S of tiles j even / odd in columns [0, KT) /
+// [KT, 2 KT), O in [256, 256 + DP).
 template <int DP, int KT>
 struct OneRole {
   static constexpr uint32_t kQ = 128u * DP * 2;   // Q tile bytes
@@ -299,11 +300,14 @@ struct OneRole {
   static constexpr uint32_t kOffK = kQ;
   static constexpr uint32_t kOffV = kOffK + 2 * kKV;
   static constexpr uint32_t kOffP = kOffV + 2 * kKV;
-  static constexpr uint32_t kOffBar = kOffP + 2 * kP;
+  static constexpr uint32_t kOffRow = kOffP + 2 * kP;        // [3 tiles][KT] key rows
+  static constexpr uint32_t kOffBar = kOffRow + 3 * KT * 4;  // 2 mbarriers, TMEM slot, fail
   static constexpr size_t kSmem = kOffBar + 64 + 1024;
-  static constexpr uint32_t kCols = 128 + DP <= 256 ? 256 : 512;
+  static constexpr uint32_t kCols = 512;
   static_assert(kSmem <= 232448, "shared memory of one CTA");
 };
+
+constexpr uint32_t kNoRow = 0xFFFFFFFFu;  // a key past the range or with a bad address
 
 // byte offset of 16-byte chunk `chunk` of row `row` in a 128-byte-swizzled tile whose
 // 64-column blocks are `blk` bytes apart
@@ -315,6 +319,20 @@ __device__ __forceinline__ uint32_t swz_blk(int row, int chunk, uint32_t blk) {
 // thread r runs the softmax of row r.  It serves head dims other than 128 (p.d <= DP,
 // a multiple of 8; the columns past p.d are zero in Q and V and are not stored), and
 // head_dim 128 where the block size is not a multiple of 16.
+// Pipeline, per key tile j (K and V stages j & 1, S buffer j & 1):
+//   wait S(j) -> read S(j) -> K(j+1) landed: issue S(j+1) -> copy K(j+2) into the
+//   stage S(j) has freed -> softmax(j) in registers -> wait P.V(j-1) -> rescale O,
+//   store P(j) -> copy V(j+1) into the stage P.V(j-1) has freed -> V(j) landed:
+//   issue P.V(j).
+// So the tensor pipe computes S(j+1) and P.V(j-1) while the threads run softmax(j),
+// and every copy is issued one tile ahead.  Each thread commits one cp.async group per
+// K tile and one per V tile, in the order K(j+2), V(j+1) within tile j (after K(0),
+// K(1), V(0) up front), empty where the tile does not exist, so "K(j+1) landed" is
+// wait_group 1 and "V(j) landed" is wait_group 2.  The copies read each key's row
+// address from a shared ring of 3 tiles (element offset / 8, or kNoRow): thread n
+// resolves key n of tile j+3 during tile j (block table, then offsets table, the two
+// loads issued around the softmax) into the slot of tile j, whose last copy (V(j)) was
+// issued in tile j-1, so no copy waits on a table lookup.
 template <typename T, int DP, int KT>
 __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) {
   using L = OneRole<DP, KT>;
@@ -322,7 +340,8 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
   const uint32_t raw = ptx::smem_u32(smem_raw);
   const uint32_t sb = (raw + 1023u) & ~1023u;  // 1024-aligned base (swizzle atoms)
   unsigned char *smem = smem_raw + (sb - raw);
-  __shared__ int s_fail;
+  volatile int &s_fail = *reinterpret_cast<volatile int *>(smem + L::kOffBar + 20);
+  uint32_t *rows = reinterpret_cast<uint32_t *>(smem + L::kOffRow);  // [3][KT]
 
   const int tid = threadIdx.x, warp = tid >> 5;
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -375,83 +394,118 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
   const size_t tok_stride = size_t(p.hkv) * D;
   const int32_t *table = p.tables + size_t(b) * p.max_bps;
   bool bad = false;
-  auto load_kv = [&](int j, int st) {
-    const uint32_t kb = sb + L::kOffK + st * L::kKV, vb = sb + L::kOffV + st * L::kKV;
-#pragma unroll 4
-    for (int it = 0; it < KT * DP / 1024; ++it) {
-      const int idx = it * 128 + tid, n = idx / (DP / 8), c = idx % (DP / 8);
-      const int kv = j * KT + n;
-      int64_t e = -1;
-      if (kv < kv_hi && c < DC) {
-        const int blk = table[kv / p.bs];
-        const uint64_t off = p.offsets[blk];
-        const uint64_t elem = off + uint64_t(kv % p.bs) * tok_stride + uint64_t(h) * D + c * 8;
-        if ((off & 7) == 0 && elem + 8 <= p.region_elems) {
-          e = int64_t(elem);
-        } else {
-          bad = true;
-        }
+  // Key n of tile t: its block id (first load), then its row (second load) into the
+  // ring slot t % 3.  Threads n >= KT take no key.
+  auto key_block = [&](int t) -> int {
+    const int kv = t * KT + tid;
+    return tid < KT && t < nt && kv < kv_hi ? table[kv / p.bs] : -1;
+  };
+  auto key_row = [&](int t, int blk) {
+    if (tid >= KT) return;
+    uint32_t r = kNoRow;
+    if (blk >= 0) {
+      const int kv = t * KT + tid;
+      const uint64_t off = p.offsets[blk];
+      const uint64_t elem = off + uint64_t(kv % p.bs) * tok_stride + uint64_t(h) * D;
+      if ((off & 7) == 0 && elem + uint64_t(D) <= p.region_elems && (elem >> 3) < kNoRow) {
+        r = uint32_t(elem >> 3);
+      } else {
+        bad = true;
       }
-      const uint32_t so = swz_blk(n, c, L::kKvBlk);
-      ptx::cp_async16(kb + so, e >= 0 ? p.va_k + e : p.va_k, e >= 0 ? 16u : 0u);
-      ptx::cp_async16(vb + so, e >= 0 ? p.va_v + e : p.va_v, e >= 0 ? 16u : 0u);
+    }
+    rows[(t % 3) * KT + tid] = r;
+  };
+  // One K or V tile of keys [j * KT, j * KT + KT) into stage st from the ring, then a
+  // commit (an empty group for a tile past the last).
+  auto load_tile = [&](int j, int st, bool is_v) {
+    if (j < nt) {
+      const uint32_t dst = sb + (is_v ? L::kOffV : L::kOffK) + st * L::kKV;
+      const uint16_t *base = is_v ? p.va_v : p.va_k;
+      const uint32_t *rj = rows + (j % 3) * KT;
+#pragma unroll 4
+      for (int it = 0; it < KT * DP / 1024; ++it) {
+        const int idx = it * 128 + tid, n = idx / (DP / 8), c = idx % (DP / 8);
+        const uint32_t r = rj[n];
+        const bool ok = r != kNoRow && c < DC;
+        ptx::cp_async16(dst + swz_blk(n, c, L::kKvBlk),
+                        ok ? base + (uint64_t(r) << 3) + c * 8 : base, ok ? 16u : 0u);
+      }
     }
     ptx::cp_async_commit();
   };
 
-  load_kv(0, 0);
+  {  // rows of tiles 0, 1 and 2
+    const int b0 = key_block(0), b1 = key_block(1), b2 = key_block(2);
+    key_row(0, b0);
+    key_row(1, b1);
+    key_row(2, b2);
+  }
+  __syncthreads();
+  load_tile(0, 0, false);
+  load_tile(1, 1, false);
+  load_tile(0, 0, true);
+  ptx::cp_async_wait<2>();  // Q and K(0)
+  ptx::fence_proxy_async_smem();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + L::kOffBar + 16);
   const uint32_t lane_base = uint32_t(warp * 32) << 16;
-  const uint32_t tS = tmem, tO = tmem + 128;
+  const uint32_t tO = tmem + 256;
+  // S(j) = Q K(j)^T into S buffer j & 1 (thread 0)
+  auto issue_s = [&](int j) {
+    const uint32_t ka = sb + L::kOffK + (j & 1) * L::kKV, tS = tmem + (j & 1) * KT;
+#pragma unroll
+    for (int k = 0; k < DP / 16; ++k) {
+      const uint32_t in_row = uint32_t(k & 3) * 32;
+      tc::mma_ss(tS, tc::sw128_desc(sb + (k >> 2) * kHalf + in_row, 16, 1024),
+                 tc::sw128_desc(ka + (k >> 2) * L::kKvBlk + in_row, 16, 1024), p.idesc_qk,
+                 k > 0);
+    }
+    tc::commit(bar_s);
+  };
+  if (tid == 0) {
+    tc::fence_after_sync();
+    issue_s(0);
+  }
 
   float m_run = -INFINITY, l_run = 0.f;
   bool failed = false;
+  const uint32_t pa = sb + L::kOffP, pl = pa + L::kP;
   for (int j = 0; j < nt; ++j) {
-    const int st = j & 1;
-    if (j > 0) {  // P.V of tile j-1 done: its V stage, P and O are free
-      if (!ptx::mbar_wait_bounded(bar_o, uint32_t((j - 1) & 1), kLimitNs)) s_fail = 1;
-      tc::fence_after_sync();
-    }
-    if (j + 1 < nt) {
-      load_kv(j + 1, st ^ 1);
-      ptx::cp_async_wait<1>();
-    } else {
-      ptx::cp_async_wait<0>();
-    }
+    if (!ptx::mbar_wait_bounded(bar_s, uint32_t(j & 1), kLimitNs)) s_fail = 1;
+    tc::fence_after_sync();
+    float s[KT];
+#pragma unroll
+    for (int c = 0; c < KT / 32; ++c) tc::ld32(tmem + (j & 1) * KT + lane_base + c * 32, s + c * 32);
+    tc::wait_ld();
+    // S(j) is read by every thread and K(j + 1) has landed: S(j + 1) may start
+    ptx::cp_async_wait<1>();
     ptx::fence_proxy_async_smem();
+    tc::fence_before_sync();
     __syncthreads();
     if (s_fail) {
       failed = true;
       break;
     }
-    if (tid == 0) {
+    if (tid == 0 && j + 1 < nt) {
       tc::fence_after_sync();
-      const uint32_t qa = sb, ka = sb + L::kOffK + st * L::kKV;
-#pragma unroll
-      for (int k = 0; k < DP / 16; ++k) {
-        const uint32_t in_row = uint32_t(k & 3) * 32;
-        tc::mma_ss(tS, tc::sw128_desc(qa + (k >> 2) * kHalf + in_row, 16, 1024),
-                   tc::sw128_desc(ka + (k >> 2) * L::kKvBlk + in_row, 16, 1024), p.idesc_qk,
-                   k > 0);
-      }
-      tc::commit(bar_s);
+      issue_s(j + 1);
     }
-    if (!ptx::mbar_wait_bounded(bar_s, uint32_t(j & 1), kLimitNs)) s_fail = 1;
-    tc::fence_after_sync();
+    load_tile(j + 2, j & 1, false);  // the K stage S(j) has finished with
+    const int blk3 = key_block(j + 3);  // in flight during the softmax
 
-    float s[KT];
-#pragma unroll
-    for (int c = 0; c < KT / 32; ++c) tc::ld32(tS + lane_base + c * 32, s + c * 32);
-    tc::wait_ld();
-
-    const uint32_t pa = sb + L::kOffP, pl = pa + L::kP;
     float alpha;
     bool rescale;
     const float mx = masked_max<KT>(s, j * KT, qpos, j * KT + KT - 1 > base_pos + qt * p.tt) *
                      p.scale_log2;
     const float sum = exp_given_max<KT>(s, mx, p.scale_log2, j > 0, m_run, alpha, rescale);
+    l_run = l_run * alpha + sum;
+
+    if (j > 0) {  // P.V(j - 1) done: P, O and V stage (j + 1) & 1 are free
+      if (!ptx::mbar_wait_bounded(bar_o, uint32_t((j - 1) & 1), kLimitNs)) s_fail = 1;
+      tc::fence_after_sync();
+    }
+    if (__any_sync(0xffffffffu, rescale)) scale_o_row<DP>(tO + lane_base, rescale ? alpha : 1.f);
 #pragma unroll
     for (int c = 0; c < KT / 8; ++c) {  // P row -> P_hi, P_lo (keys along the row)
       uint32_t w[4], r[4];
@@ -470,9 +524,9 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
                    "r"(r[1]), "r"(r[2]), "r"(r[3])
                    : "memory");
     }
-    l_run = l_run * alpha + sum;
-
-    if (__any_sync(0xffffffffu, rescale)) scale_o_row<DP>(tO + lane_base, rescale ? alpha : 1.f);
+    load_tile(j + 1, (j + 1) & 1, true);  // the V stage P.V(j - 1) has finished with
+    key_row(j + 3, blk3);  // slot (j + 3) % 3: tile j's, whose copies are all issued
+    ptx::cp_async_wait<2>();  // V(j)
     ptx::fence_proxy_async_smem();
     tc::fence_before_sync();
     __syncthreads();
@@ -482,7 +536,7 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
     }
     if (tid == 0) {
       tc::fence_after_sync();
-      const uint32_t va = sb + L::kOffV + st * L::kKV;
+      const uint32_t va = sb + L::kOffV + (j & 1) * L::kKV;
 #pragma unroll
       for (int k = 0; k < KT / 16; ++k) {
         const uint32_t ao = uint32_t((k >> 2) * kHalf + (k & 3) * 32);
