@@ -925,15 +925,17 @@ def run_prefill_leg(args):
     """Chunked prefill (per GPU: 8 q heads on 1 kv head, D 128, bf16):
     8 sequences of 32,768 tokens prefilled in 16 chunks of 2048 tokens, one launch per
     chunk for all 8 sequences (one layer).  Tensor-bound: causal FLOPs / time against
-    the measured bf16 dense peak."""
+    the measured bf16 dense peak.  `--head-dim` runs the same shape at another head_dim
+    (128: the two-tile kernel; others: the single-role kernel)."""
     import torch
 
     from lattice_b200.workloads import PrefillWorkload
 
     torch.cuda.set_device(0)
     seqs, ctx, chunk, hq, hkv = 8, 32768, 2048, 8, 1
+    hd = getattr(args, "head_dim", 128)
     wl = PrefillWorkload(ctx_lens=[ctx] * seqs, chunk_lens=[chunk] * seqs, num_q_heads=hq,
-                         kv_heads=hkv, seed=5, fill="device").build()
+                         kv_heads=hkv, head_dim=hd, seed=5, fill="device").build()
     ctx_by_chunk = [torch.full((seqs,), (c + 1) * chunk, dtype=torch.int32, device="cuda")
                     for c in range(ctx // chunk)]
     sp = torch.cuda.current_stream().cuda_stream
@@ -944,7 +946,7 @@ def run_prefill_leg(args):
 
     def flops(c):
         base = c * chunk
-        return 4 * 128 * hq * seqs * (chunk * base + chunk * (chunk + 1) // 2)
+        return 4 * hd * hq * seqs * (chunk * base + chunk * (chunk + 1) // 2)
 
     for _ in range(max(args.warmup, 3)):
         chunk_call(ctx // chunk - 1)
@@ -979,10 +981,11 @@ def run_prefill_leg(args):
     return _line(
         "chunked prefill TFLOP/s (causal, 32k context in 2048-token chunks)", tf, "TFLOP/s",
         {"workload": "BASELINE config 5 per GPU: 8 seqs x 32768 tokens, 2048-token chunks, "
-                     "8 q heads / 1 kv head, D 128, bf16, one layer", "launches": nchunks},
+                     f"8 q heads / 1 kv head, D {hd}, bf16, one layer", "launches": nchunks},
         {"bound": "tensor", "achieved": round(last_tf, 1), "peak": peak, "unit": "TFLOP/s",
          "frac": round(last_tf / peak, 4), "traffic": None, "peak_kind": kind,
-         "kernel": "prefill_kernel, last chunk (2048 queries x 32768 keys x 8 seqs)",
+         "kernel": ("prefill_pair_kernel" if hd == 128 else "prefill_kernel (single-role)")
+                   + ", last chunk (2048 queries x 32768 keys x 8 seqs)",
          "algorithmic_flops_per_launch": flops(nchunks - 1)},
         {"ms_per_layer": round(ms, 3), "total_flops": total,
          "frac_of_peak_all_chunks": round(tf / peak, 4),
@@ -1334,6 +1337,8 @@ def main():
                     help="profiling case for ncu: 12k-block pool, no CPU baseline / e2e legs")
     ap.add_argument("--no-secondary", dest="no_secondary", action="store_true",
                     help="skip the secondary configurations after the headline (one GPU)")
+    ap.add_argument("--head-dim", dest="head_dim", type=int, default=128,
+                    help="head_dim of the prefill leg (BASELINE config 5 uses 128)")
     ap.add_argument("--workload",
                     choices=["step", "append", "cow", "swap", "prefill", "headsplit",
                              "tables"],
