@@ -289,8 +289,9 @@ __device__ __forceinline__ void scale_o_row(uint32_t t_row, float f) {
 // 192 or 256) and KT keys per tile (128, or 64 where DP > 128 so that the tiles fit):
 // Q [DP/64][128 rows][128 B], K and V [2 stages][DP/64][KT rows][128 B], P_hi and P_lo
 // [KT/64][128 rows][128 B], all with the 128-byte swizzle, then a ring of key rows
-// [3 tiles][KT].  TMEM (512 columns): S of tiles j even / odd in columns [0, KT) /
-// [KT, 2 KT), O in [256, 256 + DP).
+// [3 tiles][KT] and the two halves' row values [2][128] (tile max, final sum).  TMEM
+// (512 columns): S of tiles j even / odd in columns [0, KT) / [KT, 2 KT), O in
+// [256, 256 + DP).
 template <int DP, int KT>
 struct OneRole {
   static constexpr uint32_t kQ = 128u * DP * 2;   // Q tile bytes
@@ -301,13 +302,17 @@ struct OneRole {
   static constexpr uint32_t kOffV = kOffK + 2 * kKV;
   static constexpr uint32_t kOffP = kOffV + 2 * kKV;
   static constexpr uint32_t kOffRow = kOffP + 2 * kP;        // [3 tiles][KT] key rows
-  static constexpr uint32_t kOffBar = kOffRow + 3 * KT * 4;  // 2 mbarriers, TMEM slot, fail
+  static constexpr uint32_t kOffX = kOffRow + 3 * KT * 4;    // [2 halves][128 rows] f32
+  static constexpr uint32_t kOffBar = kOffX + 2 * 128 * 4;   // 2 mbarriers, TMEM slot, fail
   static constexpr size_t kSmem = kOffBar + 64 + 1024;
   static constexpr uint32_t kCols = 512;
   static_assert(kSmem <= 232448, "shared memory of one CTA");
 };
 
 constexpr uint32_t kNoRow = 0xFFFFFFFFu;  // a key past the range or with a bad address
+constexpr int kOneRoleThreads = 256;      // two threads per query row
+// keys per tile of the single-role kernel for head_dim padded to dp
+constexpr int one_role_kt(int dp) { return dp <= 64 ? 128 : 64; }
 
 // byte offset of 16-byte chunk `chunk` of row `row` in a 128-byte-swizzled tile whose
 // 64-column blocks are `blk` bytes apart
@@ -316,7 +321,11 @@ __device__ __forceinline__ uint32_t swz_blk(int row, int chunk, uint32_t blk) {
 }
 
 // The single-role kernel: every thread loads with cp.async, thread 0 issues the MMAs,
-// thread r runs the softmax of row r.  It serves head dims other than 128 (p.d <= DP,
+// threads r and r + 128 (warps w and w + 4 reach the same TMEM lanes) run the softmax
+// of row r over the first and second half of each key tile and own the first and
+// second half of O's columns; they combine the tile's row max through shared memory at
+// the barrier that follows the S read, and their row sums at the end.  It serves head
+// dims other than 128 (p.d <= DP,
 // a multiple of 8; the columns past p.d are zero in Q and V and are not stored), and
 // head_dim 128 where the block size is not a multiple of 16.
 // Pipeline, per key tile j (K and V stages j & 1, S buffer j & 1):
@@ -334,7 +343,7 @@ __device__ __forceinline__ uint32_t swz_blk(int row, int chunk, uint32_t blk) {
 // loads issued around the softmax) into the slot of tile j, whose last copy (V(j)) was
 // issued in tile j-1, so no copy waits on a table lookup.
 template <typename T, int DP, int KT>
-__global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) {
+__global__ void __launch_bounds__(kOneRoleThreads, 1) prefill_kernel(const PrefillParams p) {
   using L = OneRole<DP, KT>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = ptx::smem_u32(smem_raw);
@@ -342,8 +351,10 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
   unsigned char *smem = smem_raw + (sb - raw);
   volatile int &s_fail = *reinterpret_cast<volatile int *>(smem + L::kOffBar + 20);
   uint32_t *rows = reinterpret_cast<uint32_t *>(smem + L::kOffRow);  // [3][KT]
+  float *xch = reinterpret_cast<float *>(smem + L::kOffX);            // [2][128]
+  constexpr int NT = kOneRoleThreads, KH = KT / 2, OH = DP / 2;
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, half = tid >> 7;
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int q0 = p.q_start[b];
   const int qlen = p.q_start[b + 1] - q0;
@@ -359,7 +370,7 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
   const int kv_hi = base_pos + ti_hi;  // keys [0, kv_hi) reach some row of this CTA
   const int nt = (kv_hi + KT - 1) / KT;
 
-  const int row = tid;
+  const int row = tid & 127;
   const int ti = qt * p.tt + row / p.G;
   const bool row_ok = ti < qlen;
   const int qpos = row_ok ? base_pos + ti : kv_hi - 1;
@@ -381,8 +392,8 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
   // --- Q tile: row r = (token, head) pair, zero rows past the chunk and columns past D --
   {
 #pragma unroll 4
-    for (int it = 0; it < DP / 8; ++it) {
-      const int idx = it * 128 + tid, r = idx / (DP / 8), c = idx % (DP / 8);
+    for (int it = 0; it < 128 * DP / 8 / NT; ++it) {
+      const int idx = it * NT + tid, r = idx / (DP / 8), c = idx % (DP / 8);
       const int t_r = qt * p.tt + r / p.G, h_r = h * p.G + r % p.G;
       const bool ok = t_r < qlen && c < DC;
       const uint16_t *src = ok ? p.q + (size_t(q0 + t_r) * p.hq + h_r) * D + c * 8 : p.q;
@@ -423,8 +434,8 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
       const uint16_t *base = is_v ? p.va_v : p.va_k;
       const uint32_t *rj = rows + (j % 3) * KT;
 #pragma unroll 4
-      for (int it = 0; it < KT * DP / 1024; ++it) {
-        const int idx = it * 128 + tid, n = idx / (DP / 8), c = idx % (DP / 8);
+      for (int it = 0; it < KT * DP / 8 / NT; ++it) {
+        const int idx = it * NT + tid, n = idx / (DP / 8), c = idx % (DP / 8);
         const uint32_t r = rj[n];
         const bool ok = r != kNoRow && c < DC;
         ptx::cp_async16(dst + swz_blk(n, c, L::kKvBlk),
@@ -474,10 +485,15 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
   for (int j = 0; j < nt; ++j) {
     if (!ptx::mbar_wait_bounded(bar_s, uint32_t(j & 1), kLimitNs)) s_fail = 1;
     tc::fence_after_sync();
-    float s[KT];
+    float s[KH];
 #pragma unroll
-    for (int c = 0; c < KT / 32; ++c) tc::ld32(tmem + (j & 1) * KT + lane_base + c * 32, s + c * 32);
+    for (int c = 0; c < KH / 32; ++c)
+      tc::ld32(tmem + (j & 1) * KT + half * KH + lane_base + c * 32, s + c * 32);
     tc::wait_ld();
+    const float mx_half = masked_max<KH>(s, j * KT + half * KH, qpos,
+                                         j * KT + KT - 1 > base_pos + qt * p.tt) *
+                          p.scale_log2;
+    xch[half * 128 + row] = mx_half;  // read by the other half after the barrier
     // S(j) is read by every thread and K(j + 1) has landed: S(j + 1) may start
     ptx::cp_async_wait<1>();
     ptx::fence_proxy_async_smem();
@@ -496,18 +512,18 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
 
     float alpha;
     bool rescale;
-    const float mx = masked_max<KT>(s, j * KT, qpos, j * KT + KT - 1 > base_pos + qt * p.tt) *
-                     p.scale_log2;
-    const float sum = exp_given_max<KT>(s, mx, p.scale_log2, j > 0, m_run, alpha, rescale);
-    l_run = l_run * alpha + sum;
+    const float mx = fmaxf(mx_half, xch[(half ^ 1) * 128 + row]);  // the row's tile max
+    const float sum = exp_given_max<KH>(s, mx, p.scale_log2, j > 0, m_run, alpha, rescale);
+    l_run = l_run * alpha + sum;  // this half's share of the row sum
 
     if (j > 0) {  // P.V(j - 1) done: P, O and V stage (j + 1) & 1 are free
       if (!ptx::mbar_wait_bounded(bar_o, uint32_t((j - 1) & 1), kLimitNs)) s_fail = 1;
       tc::fence_after_sync();
     }
-    if (__any_sync(0xffffffffu, rescale)) scale_o_row<DP>(tO + lane_base, rescale ? alpha : 1.f);
+    if (__any_sync(0xffffffffu, rescale))
+      scale_o_row<OH>(tO + half * OH + lane_base, rescale ? alpha : 1.f);
 #pragma unroll
-    for (int c = 0; c < KT / 8; ++c) {  // P row -> P_hi, P_lo (keys along the row)
+    for (int c = 0; c < KH / 8; ++c) {  // P half row -> P_hi, P_lo (keys along the row)
       uint32_t w[4], r[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -516,7 +532,7 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
         const float2 hv = unpack2<T>(w[e]);
         r[e] = pack2<T>(a - hv.x, bb - hv.y);
       }
-      const uint32_t so = swz_blk(row, c, kHalf);
+      const uint32_t so = swz_blk(row, half * (KH / 8) + c, kHalf);
       asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(pa + so), "r"(w[0]),
                    "r"(w[1]), "r"(w[2]), "r"(w[3])
                    : "memory");
@@ -554,22 +570,22 @@ __global__ void __launch_bounds__(128, 1) prefill_kernel(const PrefillParams p) 
     if (!ptx::mbar_wait_bounded(bar_o, uint32_t((nt - 1) & 1), kLimitNs)) s_fail = 1;
     tc::fence_after_sync();
   }
+  xch[half * 128 + row] = l_run;
   __syncthreads();
   failed = failed || s_fail;
   if (!failed) {
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-    uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + row % p.G) * D;
-    if (D == DP) {
-      store_o_row<T, DP>(tO + lane_base, inv, dst, row_ok);
-    } else {  // 8 columns per store, the first D of them
+    const float l = l_run + xch[(half ^ 1) * 128 + row];
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + row % p.G) * D + half * OH;
+    {  // this half's columns of O, 8 per store, those below D
 #pragma unroll
-      for (int c = 0; c < DP / 32; ++c) {
+      for (int c = 0; c < OH / 32; ++c) {
         float o[32];
-        tc::ld32(tO + lane_base + c * 32, o);
+        tc::ld32(tO + half * OH + lane_base + c * 32, o);
         tc::wait_ld();
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          if (row_ok && c * 32 + q * 8 < D) {
+          if (row_ok && half * OH + c * 32 + q * 8 < D) {
             uint4 v;
             v.x = pack2<T>(o[q * 8 + 0] * inv, o[q * 8 + 1] * inv);
             v.y = pack2<T>(o[q * 8 + 2] * inv, o[q * 8 + 3] * inv);
@@ -1496,17 +1512,17 @@ template <typename T>
 bool pick_one_role(int d, OneRoleFn *fn, size_t *smem) {
   if (d <= 0 || d > 256 || d % 8 != 0) return false;
   if (d <= 64) {
-    *fn = prefill_kernel<T, 64, 128>;
-    *smem = OneRole<64, 128>::kSmem;
+    *fn = prefill_kernel<T, 64, one_role_kt(64)>;
+    *smem = OneRole<64, one_role_kt(64)>::kSmem;
   } else if (d <= 128) {
-    *fn = prefill_kernel<T, 128, 128>;
-    *smem = OneRole<128, 128>::kSmem;
+    *fn = prefill_kernel<T, 128, one_role_kt(128)>;
+    *smem = OneRole<128, one_role_kt(128)>::kSmem;
   } else if (d <= 192) {
-    *fn = prefill_kernel<T, 192, 64>;
-    *smem = OneRole<192, 64>::kSmem;
+    *fn = prefill_kernel<T, 192, one_role_kt(192)>;
+    *smem = OneRole<192, one_role_kt(192)>::kSmem;
   } else {
-    *fn = prefill_kernel<T, 256, 64>;
-    *smem = OneRole<256, 64>::kSmem;
+    *fn = prefill_kernel<T, 256, one_role_kt(256)>;
+    *smem = OneRole<256, one_role_kt(256)>::kSmem;
   }
   return true;
 }
@@ -1545,20 +1561,23 @@ cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
   p.diag = a.diag;
   p.d = a.head_dim;
   dim3 grid((a.max_q_len + p.tt - 1) / p.tt, a.kv_heads, a.batch);
-  if (a.head_dim != kHd) {  // other head dims: the single-role kernel, S = 128 x KT, O = 128 x DP
+  // the single-role kernel: S = 128 x KT, O = 128 x DP
+  auto one_role = [&]() -> cudaError_t {
     OneRoleFn fn;
     size_t smem;
     const bool ok = bf16 ? pick_one_role<__nv_bfloat16>(a.head_dim, &fn, &smem)
                          : pick_one_role<__half>(a.head_dim, &fn, &smem);
     if (!ok) return cudaErrorInvalidValue;
-    const int dp = (a.head_dim + 63) / 64 * 64, kt = dp > 128 ? 64 : 128;
-    p.idesc_qk = tc::idesc_f16(bf16, 128, kt, false, false);
-    p.idesc_pv = tc::idesc_f16(bf16, 128, dp, false, true);
+    const int dp = (a.head_dim + 63) / 64 * 64, kt = one_role_kt(dp);
+    PrefillParams q = p;
+    q.idesc_qk = tc::idesc_f16(bf16, 128, kt, false, false);
+    q.idesc_pv = tc::idesc_f16(bf16, 128, dp, false, true);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
-    fn<<<grid, 128, smem, stream>>>(p);
+    fn<<<grid, kOneRoleThreads, smem, stream>>>(q);
     return cudaGetLastError();
-  }
+  };
+  if (a.head_dim != kHd) return one_role();
   // The warp-specialised kernel gathers 16-token page boxes: block_size % 16 == 0.
   // Otherwise (or with KCMM_PREFILL_IMPL=cpasync) the single-role kernel runs.
   const char *impl = std::getenv("KCMM_PREFILL_IMPL");
@@ -1628,12 +1647,7 @@ cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
     fn<<<grid, tma ? ws_threads<true>() : ws_threads<false>(), kWsSmem, stream>>>(wp);
     return cudaGetLastError();
   }
-  auto fn = bf16 ? prefill_kernel<__nv_bfloat16, 128, 128> : prefill_kernel<__half, 128, 128>;
-  constexpr size_t smem = OneRole<128, 128>::kSmem;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-  if (e != cudaSuccess) return e;
-  fn<<<grid, 128, smem, stream>>>(p);
-  return cudaGetLastError();
+  return one_role();
 }
 
 }  // namespace dev
