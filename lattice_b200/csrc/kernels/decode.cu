@@ -264,7 +264,8 @@ struct Cfg {
 // call uses stage (rb + k) % NS at phase parity ((rb + k) / NS) & 1.  MODE 0 passes 0
 // and initialises its barriers here.  Returns false when a wait ran out (the CTA
 // has reported it and must stop).
-template <typename T, int D, int W, int NS, int MODE>
+// TWO (MODE 0 only): 8-token pages, a unit's rows 8-15 read from the next page.
+template <typename T, int D, int W, int NS, int MODE, bool TWO = false>
 __device__ __forceinline__ bool decode_body(const DecodeParams &p, const int item,
                                             const int split, int &rb, const int4 ea = int4{},
                                             const int4 ec = int4{}, const int kvh_in = 0) {
@@ -386,6 +387,10 @@ __device__ __forceinline__ bool decode_body(const DecodeParams &p, const int ite
   const int n_w = (n_total - warp + W - 1) / W;  // units owned by this warp (<= 32)
   const int64_t row_stride = int64_t(p.hkv) * D;  // elements between tokens
   int64_t my_elem = 0;
+  // 8-token pages: a unit's rows 8-15 lie in the next page, based here
+  constexpr bool two_pages = TWO;
+  static_assert(!TWO || MODE == 0, "two-page units are a plain-decode layout");
+  int64_t my_elem2 = 0;
   int my_ok = 0;
   int my_meta = 0;  // MODE 1: valid tokens | (folded member + 1) << 8 (0: a shared unit)
   if (lane < n_w) {
@@ -422,13 +427,20 @@ __device__ __forceinline__ bool decode_body(const DecodeParams &p, const int ite
           atomicOr(p.diag, int32_t(kDiagBadLaunch));
       }
     }
-    if (blk >= 0) {
-      uint64_t off = p.offsets[blk];
-      int64_t e = int64_t(off) + int64_t(tok0 % p.bs) * row_stride + int64_t(kvh) * D;
-      bool aligned = (off & 7) == 0;
-      bool inside = uint64_t(e + (kUnit - 1) * row_stride + D) <= p.region_elems;
+    // second page of the unit (8-token pages), read only when the unit reaches it
+    const int blk2 = two_pages && tok0 + 8 < seq_len
+                         ? p.tables[int64_t(tb) * p.bt_stride + page + 1] : blk;
+    const int rows_a = two_pages ? 8 : kUnit;  // rows of the unit in the first page
+    if (blk >= 0 && blk2 >= 0) {
+      const uint64_t off = p.offsets[blk], off2 = p.offsets[blk2];
+      const int64_t e = int64_t(off) + int64_t(tok0 % p.bs) * row_stride + int64_t(kvh) * D;
+      const int64_t e2 = int64_t(off2) + int64_t(kvh) * D;
+      const bool aligned = ((off | off2) & 7) == 0;
+      const bool inside = uint64_t(e + (rows_a - 1) * row_stride + D) <= p.region_elems &&
+                          (!two_pages || uint64_t(e2 + 7 * row_stride + D) <= p.region_elems);
       my_ok = aligned && inside;
       my_elem = e;
+      my_elem2 = two_pages ? e2 : e;
     }
     if (!my_ok) atomicOr(p.diag, int32_t(kDiagBadOffset));
   }
@@ -444,6 +456,7 @@ __device__ __forceinline__ bool decode_body(const DecodeParams &p, const int ite
     const int st = (rb + k) % NS;
     const uint32_t bar = ptx::smem_u32(my_bars + st);
     const int64_t elem = __shfl_sync(0xffffffffu, my_elem, k);
+    const int64_t elem2 = two_pages ? __shfl_sync(0xffffffffu, my_elem2, k) : elem;
     const int ok = __shfl_sync(0xffffffffu, my_ok, k);
     int nvalid;
     if constexpr (MODE == 1) {
@@ -458,7 +471,8 @@ __device__ __forceinline__ bool decode_body(const DecodeParams &p, const int ite
 #pragma unroll
     for (int j = lane; j < kUnit * CPR; j += 32) {
       const int r = j / CPR, c = j % CPR;
-      const int64_t off = elem + int64_t(r) * row_stride + c * 8;
+      const int64_t off = (two_pages && r >= 8 ? elem2 + int64_t(r - 8) * row_stride
+                                               : elem + int64_t(r) * row_stride) + c * 8;
       const uint32_t n = r < nvalid ? 16u : 0u;
       const uint32_t so = uint32_t((r * C::RS + c * 8) * sizeof(T));
       ptx::cp_async16(ks_tile + so, vak + (n ? off : 0), n);
@@ -672,10 +686,10 @@ __device__ __forceinline__ bool decode_body(const DecodeParams &p, const int ite
   return true;
 }
 
-template <typename T, int D, int W, int NS>
+template <typename T, int D, int W, int NS, bool TWO = false>
 __global__ void __launch_bounds__(W * 32, 2) decode_kernel(const DecodeParams p) {
   int rb = 0;
-  decode_body<T, D, W, NS, 0>(p, blockIdx.z, blockIdx.x, rb);
+  decode_body<T, D, W, NS, 0, TWO>(p, blockIdx.z, blockIdx.x, rb);
 }
 
 // Shared-prefix decode: persistent CTAs (at most 2 per SM) take items
@@ -961,16 +975,18 @@ __global__ void decode_generic_kernel(const DecodeParams p, int D) {
 using KernelFn = void (*)(const DecodeParams);
 
 template <typename T, int D>
-KernelFn fast_kernel() {
-  return decode_kernel<T, D, kWarps, kStages>;
+KernelFn fast_kernel(bool two_pages) {
+  return two_pages ? decode_kernel<T, D, kWarps, kStages, true>
+                   : decode_kernel<T, D, kWarps, kStages, false>;
 }
 
+// two_pages: 8-token pages (each 16-token unit spans two of them)
 template <typename T>
-bool pick_fast(int D, KernelFn *fn, size_t *smem) {
+bool pick_fast(int D, KernelFn *fn, size_t *smem, bool two_pages = false) {
   switch (D) {
 #define KCMM_CASE(DD)                                 \
   case DD:                                            \
-    *fn = fast_kernel<T, DD>();                       \
+    *fn = fast_kernel<T, DD>(two_pages);              \
     *smem = Cfg<T, DD, kWarps, kStages>::SMEM;        \
     return true;
     KCMM_CASE(32)
@@ -1020,10 +1036,12 @@ struct Plan {
 Plan make_plan(const DecodeArgs &a) {
   Plan pl;
   const int D = a.head_dim;
-  bool shape_ok = D % 16 == 0 && a.block_size % kUnit == 0;
+  // 16-token units within a page, or across two 8-token pages
+  bool shape_ok = D % 16 == 0 && (a.block_size % kUnit == 0 || a.block_size == 8);
   if (shape_ok) {
-    pl.fast = a.dtype == Dtype::BF16 ? pick_fast<__nv_bfloat16>(D, &pl.fn, &pl.smem)
-                                     : pick_fast<__half>(D, &pl.fn, &pl.smem);
+    const bool two = a.block_size == 8;
+    pl.fast = a.dtype == Dtype::BF16 ? pick_fast<__nv_bfloat16>(D, &pl.fn, &pl.smem, two)
+                                     : pick_fast<__half>(D, &pl.fn, &pl.smem, two);
   }
   if (!pl.fast) return pl;
   const int g_max = (a.num_q_heads + a.kv_heads - 1) / a.kv_heads;

@@ -63,7 +63,10 @@ SHAPES = [
     (3, 8, 2, 96, 16),
     (2, 8, 2, 256, 16),
     (2, 6, 3, 72, 16),      # head_dim not a multiple of 16: generic kernel
-    (2, 8, 2, 64, 8),       # block_size 8: generic kernel
+    (2, 8, 2, 64, 8),       # block_size 8: units span two pages
+    (6, 32, 8, 128, 8),     # Llama-3-8B heads on 8-token pages
+    (3, 8, 1, 256, 8),
+    (2, 8, 2, 64, 4),       # block_size 4: generic kernel
     (3, 10, 4, 64, 16),     # query heads not a multiple of kv heads
 ]
 
