@@ -674,16 +674,25 @@ enum WsBar { kQFull = 0, kKFull = 1, kKEmpty = 4, kVFull = 7, kVEmpty = 10, kSFu
 // tiles g, g+4, g+8, ...  After its tile j is issued the group loads the block ids of
 // tile j+4, and two tiles later their offsets, so each dependent global load has two
 // tiles of time to return.
+// With 8-token pages a box spans two pages: each lane also follows the block holding
+// the box's rows 8-15 (blk2 / off2) and hands out its base as e1; otherwise e1 is the
+// row 8 of the same page.  TWO = false (the TMA kernels, 16-token pages only) compiles
+// the second page out.
+template <bool TWO>
 struct BoxLookup {
   const int32_t *table;
   const uint64_t *offsets;
   int bs, kv_hi, nt, bx, grp, j, j0;
-  int tile;       // tile this lane's group is gathering
-  int blk;        // its block id (-1: past the keys in use)
-  uint64_t off;   // its block offset (valid once loaded)
+  int tile;        // tile this lane's group is gathering
+  int blk, blk2;   // its block ids (-1: past the keys in use); blk2 for 8-token pages
+  uint64_t off, off2;  // their block offsets (valid once loaded)
   __device__ int blk_of(int t) const {
     const int key = t * kKvTile + bx * 16;
     return (t < nt && key < kv_hi) ? table[key / bs] : -1;
+  }
+  __device__ int blk2_of(int t) const {
+    const int key = t * kKvTile + bx * 16 + 8;
+    return (TWO && bs == 8 && t < nt && key < kv_hi) ? table[key / bs] : -1;
   }
   // Tiles j0, j0 + 1, ... below nt_ (the end of the CTA's range).
   __device__ BoxLookup(const int32_t *tb, const uint64_t *of, int bs_, int kv_hi_, int nt_,
@@ -691,31 +700,51 @@ struct BoxLookup {
       : table(tb), offsets(of), bs(bs_), kv_hi(kv_hi_), nt(nt_), bx(lane & 7), grp(lane >> 3),
         j(j0_), j0(j0_), tile(j0_ + (lane >> 3)) {
     blk = blk_of(tile);
+    blk2 = TWO ? blk2_of(tile) : -1;
     off = blk >= 0 ? offsets[blk] : 0;
+    off2 = TWO && blk2 >= 0 ? offsets[blk2] : 0;
   }
   // Element offset (2-byte units) of the first token row of this lane's box (lane & 7)
   // in the next tile, from the group that holds it; false when the box lies past the
   // keys in use, or its block offset is misaligned or its 16 rows leave the region.
   // All 32 lanes must call this together.
-  __device__ bool next(uint32_t row_stride, uint64_t region_elems, int64_t *e0, bool *bad) {
+  __device__ bool next(uint32_t row_stride, uint64_t region_elems, int64_t *e0, int64_t *e1,
+                       bool *bad) {
     const int g = (j - j0) & 3;
-    int64_t zz = 0;
+    int64_t zz = 0, zz2 = 0;
     bool live = false;
     if (grp == g && blk >= 0) {
       zz = int64_t(off + uint64_t((j * kKvTile + bx * 16) % bs) * row_stride);
-      live = (off & 7) == 0 && uint64_t(zz) + 16ull * row_stride <= region_elems;
+      if (TWO && bs == 8) {  // rows 0-7 in this page, rows 8-15 (if in use) in blk2's
+        zz2 = int64_t(off2);
+        live = (off & 7) == 0 && uint64_t(zz) + 8ull * row_stride <= region_elems &&
+               (blk2 < 0 || ((off2 & 7) == 0 && off2 + 8ull * row_stride <= region_elems));
+      } else {
+        zz2 = zz + 8 * int64_t(row_stride);
+        live = (off & 7) == 0 && uint64_t(zz) + 16ull * row_stride <= region_elems;
+      }
       if (!live) *bad = true;
     }
     const int src = (g << 3) | bx;
     zz = __shfl_sync(0xffffffffu, zz, src);
+    if constexpr (TWO) {
+      zz2 = __shfl_sync(0xffffffffu, zz2, src);
+    } else {
+      zz2 = zz + 8 * int64_t(row_stride);
+    }
     live = __shfl_sync(0xffffffffu, int(live), src) != 0;
     if (grp == g) {  // start gathering tile j + 4
       tile = j + 4;
       blk = blk_of(tile);
+      if constexpr (TWO) blk2 = blk2_of(tile);
     }
-    if (j - j0 >= 2 && grp == ((j - j0 + 2) & 3)) off = blk >= 0 ? offsets[blk] : 0;  // tile j + 2
+    if (j - j0 >= 2 && grp == ((j - j0 + 2) & 3)) {  // tile j + 2
+      off = blk >= 0 ? offsets[blk] : 0;
+      if constexpr (TWO) off2 = blk2 >= 0 ? offsets[blk2] : 0;
+    }
     ++j;
     *e0 = zz;
+    *e1 = zz2;
     return live;
   }
 };
@@ -738,22 +767,26 @@ __device__ __forceinline__ bool ws_wait(uint32_t bar, uint32_t parity, volatile 
 
 // One warp copies a 128-key tile of one kv head into the swizzled [2 halves][128
 // rows][128 B] layout with 16-byte cp.async: each half-warp moves one 256-byte token
-// row per step.  Box b (keys 16b .. 16b+15) starts at element e0 of lane b; keys past
+// row per step.  Box b (keys 16b .. 16b+15) has its rows 0-7 from element e0 and rows
+// 8-15 from element e1 of lane b (TWO; otherwise all 16 rows from e0); keys past
 // kv_hi and boxes that are not live are zero-filled.
-template <bool BOXV = false, int B0 = 0, int NB = 8>
-__device__ __forceinline__ void gather_tile(const uint16_t *va, uint32_t dst, int64_t e0, bool live,
-                                            int j, int kv_hi, uint32_t row_stride, int h,
-                                            int lane) {
+template <bool BOXV = false, int B0 = 0, int NB = 8, bool TWO = false>
+__device__ __forceinline__ void gather_tile(const uint16_t *va, uint32_t dst, int64_t e0,
+                                            int64_t e1, bool live, int j, int kv_hi,
+                                            uint32_t row_stride, int h, int lane) {
   const int hw = lane >> 4, c = lane & 15;
 #pragma unroll
   for (int b = B0; b < B0 + NB; ++b) {
     const int64_t eb = __shfl_sync(0xffffffffu, e0, b);
+    const int64_t eb1 = TWO ? __shfl_sync(0xffffffffu, e1, b) : 0;
     const bool lb = __shfl_sync(0xffffffffu, int(live), b) != 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int r = 2 * i + hw, row = b * 16 + r;
       const bool ok = lb && j * kKvTile + row < kv_hi;
-      const uint16_t *src = va + eb + int64_t(r) * row_stride + h * kHd + c * 8;
+      const int64_t er = !TWO || i < 4 ? eb + int64_t(r) * row_stride
+                                       : eb1 + int64_t(r - 8) * row_stride;
+      const uint16_t *src = va + er + h * kHd + c * 8;
       ptx::cp_async16(dst + (BOXV ? swz_v(row, c) : swz(row, c)), ok ? src : va, ok ? 16u : 0u);
     }
   }
@@ -839,11 +872,11 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
     const int part = warp == 8 ? 0 : 1;
     if (TMA && lane == 0) ptx::prefetch_tensormap(&P.tmk);
     bool bad = false;
-    BoxLookup lk(table, p.offsets, p.bs, kv_hi, nt, lane);
+    BoxLookup<!TMA> lk(table, p.offsets, p.bs, kv_hi, nt, lane);
     for (int j = 0; j < nt; ++j) {
       const int st = j % kKStages;
-      int64_t e0 = 0;
-      bool live = lk.next(row_stride, p.region_elems, &e0, &bad);
+      int64_t e0 = 0, e1 = 0;
+      bool live = lk.next(row_stride, p.region_elems, &e0, &e1, &bad);
       // QK of tile j - kKStages must have finished reading this stage
       if (j >= kKStages &&
           !ws_wait(bar(kKEmpty + st), uint32_t((j / kKStages - 1) & 1), fail))
@@ -864,7 +897,7 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
                            int(e0 >> P.row_shift), bar(kKFull + st));
         }
       } else {
-        gather_tile(p.va_k, dst, e0, live, j, kv_hi, row_stride, h, lane);
+        gather_tile<false, 0, 8, !TMA>(p.va_k, dst, e0, e1, live, j, kv_hi, row_stride, h, lane);
         ptx::cp_async_mbar_arrive(bar(kKFull + st));
       }
     }
@@ -875,11 +908,11 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
     const int part = warp == 10 ? 0 : 1;
     if (TMA && lane == 0) ptx::prefetch_tensormap(&P.tmv);
     bool bad = false;
-    BoxLookup lk(table, p.offsets, p.bs, kv_hi, nt, lane);
+    BoxLookup<!TMA> lk(table, p.offsets, p.bs, kv_hi, nt, lane);
     for (int j = 0; j < nt; ++j) {
       const int st = j % kVStages;
-      int64_t e0 = 0;
-      bool live = lk.next(row_stride, p.region_elems, &e0, &bad);
+      int64_t e0 = 0, e1 = 0;
+      bool live = lk.next(row_stride, p.region_elems, &e0, &e1, &bad);
       // P.V of tile j - kVStages must have finished reading this stage
       if (j >= kVStages &&
           !ws_wait(bar(kVEmpty + st), uint32_t((j / kVStages - 1) & 1), fail))
@@ -903,14 +936,14 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
           }
         } else {
           if (part == 0) {
-            gather_tile<true, 0, 4>(p.va_v, dst, e0, live, j, kv_hi, row_stride, h, lane);
+            gather_tile<true, 0, 4, !TMA>(p.va_v, dst, e0, e1, live, j, kv_hi, row_stride, h, lane);
           } else {
-            gather_tile<true, 4, 4>(p.va_v, dst, e0, live, j, kv_hi, row_stride, h, lane);
+            gather_tile<true, 4, 4, !TMA>(p.va_v, dst, e0, e1, live, j, kv_hi, row_stride, h, lane);
           }
           ptx::cp_async_mbar_arrive(bar(kVFull + st));
         }
       } else {
-        gather_tile<true>(p.va_v, dst, e0, live, j, kv_hi, row_stride, h, lane);
+        gather_tile<true, 0, 8, !TMA>(p.va_v, dst, e0, e1, live, j, kv_hi, row_stride, h, lane);
         ptx::cp_async_mbar_arrive(bar(kVFull + st));
       }
     }
@@ -1208,11 +1241,11 @@ __global__ void __launch_bounds__(kPrThreads, 1)
     const int part = warp == 8 ? 0 : 1;
     if (TMA && lane == 0) ptx::prefetch_tensormap(&P.tmk);
     bool bad = false;
-    BoxLookup lk(table, p.offsets, p.bs, kv_hi, j_hi, lane, j_lo);
+    BoxLookup<!TMA> lk(table, p.offsets, p.bs, kv_hi, j_hi, lane, j_lo);
     for (int jj = 0; jj < n_loc; ++jj) {
       const int j = j_lo + jj, st = jj % kPrKStages;
-      int64_t e0 = 0;
-      bool live = lk.next(row_stride, p.region_elems, &e0, &bad);
+      int64_t e0 = 0, e1 = 0;
+      bool live = lk.next(row_stride, p.region_elems, &e0, &e1, &bad);
       // both tiles' QK of tile jj - kPrKStages must have finished reading this stage
       if (jj >= kPrKStages &&
           !ws_wait(bar(kPrKEmpty + st), uint32_t((jj / kPrKStages - 1) & 1), fail))
@@ -1233,7 +1266,7 @@ __global__ void __launch_bounds__(kPrThreads, 1)
                            int(e0 >> P.row_shift), bar(kPrKFull + st));
         }
       } else {
-        gather_tile(p.va_k, dst, e0, live, j, kv_hi, row_stride, h, lane);
+        gather_tile<false, 0, 8, !TMA>(p.va_k, dst, e0, e1, live, j, kv_hi, row_stride, h, lane);
         ptx::cp_async_mbar_arrive(bar(kPrKFull + st));
       }
     }
@@ -1243,11 +1276,11 @@ __global__ void __launch_bounds__(kPrThreads, 1)
     // ---------------- V producer ----------------
     if (TMA && lane == 0) ptx::prefetch_tensormap(&P.tmv);
     bool bad = false;
-    BoxLookup lk(table, p.offsets, p.bs, kv_hi, j_hi, lane, j_lo);
+    BoxLookup<!TMA> lk(table, p.offsets, p.bs, kv_hi, j_hi, lane, j_lo);
     for (int jj = 0; jj < n_loc; ++jj) {
       const int j = j_lo + jj, st = jj % kPrVStages;
-      int64_t e0 = 0;
-      bool live = lk.next(row_stride, p.region_elems, &e0, &bad);
+      int64_t e0 = 0, e1 = 0;
+      bool live = lk.next(row_stride, p.region_elems, &e0, &e1, &bad);
       // both tiles' P.V of tile jj - kPrVStages must have finished reading this stage
       if (jj >= kPrVStages &&
           !ws_wait(bar(kPrVEmpty + st), uint32_t((jj / kPrVStages - 1) & 1), fail))
@@ -1272,7 +1305,7 @@ __global__ void __launch_bounds__(kPrThreads, 1)
                            bar(kPrVFull + st));
         }
       } else {
-        gather_tile<true>(p.va_v, dst, e0, live, j, kv_hi, row_stride, h, lane);
+        gather_tile<true, 0, 8, !TMA>(p.va_v, dst, e0, e1, live, j, kv_hi, row_stride, h, lane);
         ptx::cp_async_mbar_arrive(bar(kPrVFull + st));
       }
     }
@@ -1578,17 +1611,19 @@ cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
     return cudaGetLastError();
   };
   if (a.head_dim != kHd) return one_role();
-  // The warp-specialised kernel gathers 16-token page boxes: block_size % 16 == 0.
-  // Otherwise (or with KCMM_PREFILL_IMPL=cpasync) the single-role kernel runs.
+  // The warp-specialised kernels gather 16-token boxes: block_size a multiple of 16, or 8
+  // (a box over two pages).  Otherwise (or with KCMM_PREFILL_IMPL=cpasync) the
+  // single-role kernel runs.
   const char *impl = std::getenv("KCMM_PREFILL_IMPL");
   const bool single = impl && std::strcmp(impl, "cpasync") == 0;
   const bool gather = impl && std::strcmp(impl, "gather") == 0;
-  if (a.block_size % 16 == 0 && !single) {
-    // TMA boxes address whole token rows of the {D, Hkv, tokens} view: Hkv * D must be
-    // a power of two dividing the 2 MiB superblock (1 Mi elements).
+  if ((a.block_size % 16 == 0 || a.block_size == 8) && !single) {
+    // TMA boxes address 16 whole token rows of the {D, Hkv, tokens} view: pages of a
+    // multiple of 16 tokens, and Hkv * D a power of two dividing the 2 MiB superblock
+    // (1 Mi elements).  8-token pages take the copy-gather producers (two pages a box).
     const uint32_t rs = uint32_t(a.kv_heads) * kHd;
-    const bool tma = !gather && a.tensor_maps && a.v_page_map && (rs & (rs - 1)) == 0 &&
-                     (1u << 20) % rs == 0;
+    const bool tma = !gather && a.block_size % 16 == 0 && a.tensor_maps && a.v_page_map &&
+                     (rs & (rs - 1)) == 0 && (1u << 20) % rs == 0;
     WsParams wp;
     std::memset(static_cast<void *>(&wp), 0, sizeof(wp));
     wp.p = p;

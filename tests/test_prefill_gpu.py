@@ -75,12 +75,14 @@ def test_prefill_matches_oracle(case, dtype):
 
 
 @pytest.mark.parametrize("impl,bs", [("cpasync", 16), ("pair", 32), ("pair", 8), ("ws", 16),
-                                     ("ws", 32), ("gather", 16)])
+                                     ("ws", 32), ("ws", 8), ("gather", 16), ("cpasync", 8),
+                                     ("pair", 4)])
 def test_prefill_kernel_paths(impl, bs, monkeypatch):
     """Every kernel path agrees with the oracle: the two-tile kernel (the default) with
-    32-token pages (two boxes per page); the single-role kernel (forced, and chosen for
-    8-token pages); the one-tile warp-specialised kernel (forced); the copy-gather
-    variant (forced) for layouts without tensor maps."""
+    32-token pages (two boxes per page) and with 8-token pages (copy-gather producers, a
+    box over two pages); the single-role kernel (forced, and chosen for 4-token pages);
+    the one-tile warp-specialised kernel (forced, also on 8-token pages); the
+    copy-gather variant (forced) for layouts without tensor maps."""
     if impl != "pair":
         monkeypatch.setenv("KCMM_PREFILL_IMPL", impl)
     wl = make(ctx_lens=[700, 260], chunk_lens=[300, 260], num_q_heads=16, kv_heads=2,
