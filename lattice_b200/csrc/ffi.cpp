@@ -604,12 +604,15 @@ static int decode_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, u
     return 0;
   }
   if (groups) {
-    if (check_launch(h, op,
-                     kcmm::dev::decode_attention_shared_prefix(
-                         a, reinterpret_cast<const int32_t *>(groups->group_starts),
-                         reinterpret_cast<const int32_t *>(groups->prefix_lens),
-                         int(groups->n_groups), int(groups->max_group_size), S(stream))))
-      return -1;
+    cudaError_t e = kcmm::dev::decode_attention_shared_prefix(
+        a, reinterpret_cast<const int32_t *>(groups->group_starts),
+        reinterpret_cast<const int32_t *>(groups->prefix_lens), int(groups->n_groups),
+        int(groups->max_group_size), S(stream));
+    // Shapes the shared-prefix kernels are not built for (head_dim outside 64 / 128 /
+    // 256, pages not a multiple of 16 tokens, more than 16 query heads per kv head) get
+    // the plain decode: the same result, each sequence reading its own pages.
+    if (e == cudaErrorNotSupported) e = kcmm::dev::decode_attention(a, S(stream));
+    if (check_launch(h, op, e)) return -1;
     return 0;
   }
   if (check_launch(h, op, kcmm::dev::decode_attention(a, S(stream)))) return -1;

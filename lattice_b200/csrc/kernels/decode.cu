@@ -1354,8 +1354,10 @@ cudaError_t decode_attention_shared_prefix(const DecodeArgs &a, const int32_t *g
                                            int max_group, cudaStream_t stream) {
   const SharedPrefixPlan pl = make_shared_prefix_plan(a, n_groups, max_group);
   if (!pl.fn) return cudaErrorNotSupported;
+  // batches the prep kernel cannot resolve in one CTA's shared memory: not supported
+  // (the caller falls back to the plain decode)
   if (a.batch > kSharedPrefixMaxBatch || pl.max_work * a.kv_heads > 0x7fffffff)
-    return cudaErrorInvalidValue;
+    return cudaErrorNotSupported;
   DecodeParams p = {};
   p.q = a.q;
   p.out = a.out;

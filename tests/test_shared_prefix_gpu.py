@@ -151,6 +151,31 @@ def test_own_tokens_folded_into_the_prefix_piece_within_its_room():
     _run_case([4] * 40, [125] * 40, [2000] * 40, lens, 4, hq=16, hkv=8, seed=8)
 
 
+@pytest.mark.parametrize("bs,d", [(8, 128), (16, 96)])
+def test_shapes_outside_the_shared_kernels_get_the_plain_decode(bs, d):
+    """8-token pages and head_dim 96 have no shared-prefix kernel: the call still gives
+    the oracle's result (through the plain decode) instead of failing."""
+    torch = _torch()
+    from lattice_b200.workloads import DecodeWorkload
+
+    lens = [300, 290, 310, 305]
+    wl = DecodeWorkload(batch=4, num_q_heads=8, kv_heads=2, head_dim=d, block_size=bs,
+                        pool_blocks=sum(-(-L // bs) for L in lens) + 64, seq_lens_override=lens,
+                        max_len=max(lens) + 16, seed=9, fill="host").build()
+    try:
+        k = 256 // bs
+        for m in range(1, 4):
+            wl.tables[m, :k] = wl.tables[0, :k]
+        wl.d_tables = torch.from_numpy(wl.tables).cuda()
+        ref = _oracle(wl)
+        out = torch.zeros_like(wl.q)
+        _call(wl, [0, 4], [256], 4, out)
+        _check(wl, out, ref)
+        assert wl.pool.kernel_status() == 0
+    finally:
+        wl.close()
+
+
 def test_malformed_groups_keep_the_result():
     torch = _torch()
     wl = _build([4, 4], [20, 20], [400, 380, 330, 390, 350, 341, 399, 333], seed=4)
