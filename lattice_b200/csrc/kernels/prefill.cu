@@ -47,13 +47,7 @@ constexpr int kKvTile = 128;  // keys per tile (MMA N of S, K of P.V)
 constexpr int kHd = 128;      // head_dim
 constexpr uint32_t kTile = 128 * 128 * 2;  // one 128 x 128 16-bit tile: 32 KB
 constexpr uint32_t kHalf = 128 * 128;      // one 64-column half (128 rows x 128 B)
-constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffK = kOffQ + kTile;        // 2 stages
-constexpr uint32_t kOffV = kOffK + 2 * kTile;    // 2 stages
-constexpr uint32_t kOffP = kOffV + 2 * kTile;    // P_hi, then P_lo
-constexpr uint32_t kOffBar = kOffP + 2 * kTile;  // 2 mbarriers + TMEM slot
-constexpr size_t kSmem = kOffBar + 64 + 1024;    // + alignment slack
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kOffQ = 0;                    // the Q tile opens every kernel's layout
 constexpr uint64_t kLimitNs = 1000000000ull;     // an MMA that has not finished in 1 s
 
 struct PrefillParams {
@@ -1154,7 +1148,10 @@ __global__ void __launch_bounds__(kPrThreads, 1)
   const bool split = lin >= P.n_whole;
   const int item = split ? P.n_whole + (lin - P.n_whole) / P.nsplit : lin;
   const int part = split ? (lin - P.n_whole) % P.nsplit : 0;
-  const int qt = item % P.nqt, h = (item / P.nqt) % p.hkv, b = item / (P.nqt * p.hkv);
+  // Query tiles run last-first: under the causal mask the last tile of a chunk attends
+  // the most keys, so the longest items start first and the short ones fill the tail.
+  const int qt = P.nqt - 1 - item % P.nqt, h = (item / P.nqt) % p.hkv,
+            b = item / (P.nqt * p.hkv);
   const int tt = 2 * p.tt;  // tokens per CTA (p.tt per tile)
   const int q0 = p.q_start[b];
   const int qlen = p.q_start[b + 1] - q0;
@@ -1484,7 +1481,8 @@ __global__ void __launch_bounds__(256) prefill_merge_kernel(const __grid_constan
   const int r = int(blockIdx.x) * 8 + warp;  // row over all split items
   const int si = r / 256, crow = r % 256;
   const int item = P.n_whole + si;
-  const int qt = item % P.nqt, h = (item / P.nqt) % p.hkv, b = item / (P.nqt * p.hkv);
+  const int qt = P.nqt - 1 - item % P.nqt, h = (item / P.nqt) % p.hkv,
+            b = item / (P.nqt * p.hkv);  // the pair kernel's item order
   const int q0 = p.q_start[b];
   const int qlen = p.q_start[b + 1] - q0;
   const int ti = qt * 2 * p.tt + crow / p.G;
