@@ -349,7 +349,8 @@ __global__ void __launch_bounds__(kOneRoleThreads, 1) prefill_kernel(const Prefi
   constexpr int NT = kOneRoleThreads, KH = KT / 2, OH = DP / 2;
 
   const int tid = threadIdx.x, warp = tid >> 5, half = tid >> 7;
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // query tiles last-first: the longest causal items start first
+  const int qt = int(gridDim.x) - 1 - int(blockIdx.x), h = blockIdx.y, b = blockIdx.z;
   const int q0 = p.q_start[b];
   const int qlen = p.q_start[b + 1] - q0;
   const int ctx = p.ctx_lens[b];
