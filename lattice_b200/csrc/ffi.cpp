@@ -794,8 +794,8 @@ static int prefill_impl(kcmm_pool_t *h, kcmm::dev::Dtype dtype, uint32_t layer, 
                      " unsupported (the tensor-core prefill takes multiples of 8 up to 256)");
     return -1;
   }
-  if (hq % hkv != 0 || 128 % (hq / hkv) != 0) {
-    set_error(h, std::string(op) + ": num_q_heads / kv_heads must be an integer dividing 128");
+  if (hq % hkv != 0 || hq / hkv > 128) {
+    set_error(h, std::string(op) + ": num_q_heads / kv_heads must be an integer of at most 128");
     return -1;
   }
   if (hq > 0xFFFF || hkv > 0xFFFF || bs > 0xFFFF || max_bps > 0xFFFF || batch > 0xFFFF) {

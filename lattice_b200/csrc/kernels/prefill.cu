@@ -60,7 +60,8 @@ struct PrefillParams {
   const uint16_t *va_k;
   const uint16_t *va_v;
   uint64_t region_elems;
-  int hq, hkv, G, bs, max_bps, tt;
+  int hq, hkv, G, bs, max_bps, tt;  // G: query heads per kv head padded to a power of two
+  int gr;                            // the real query heads per kv head (rows j >= gr idle)
   int d;  // head_dim (the single-role kernel; the others are built for 128)
   float scale_log2;
   uint32_t idesc_qk, idesc_pv;
@@ -367,7 +368,7 @@ __global__ void __launch_bounds__(kOneRoleThreads, 1) prefill_kernel(const Prefi
 
   const int row = tid & 127;
   const int ti = qt * p.tt + row / p.G;
-  const bool row_ok = ti < qlen;
+  const bool row_ok = ti < qlen && row % p.G < p.gr;
   const int qpos = row_ok ? base_pos + ti : kv_hi - 1;
 
   const uint32_t bar_s = sb + L::kOffBar, bar_o = sb + L::kOffBar + 8,
@@ -389,8 +390,8 @@ __global__ void __launch_bounds__(kOneRoleThreads, 1) prefill_kernel(const Prefi
 #pragma unroll 4
     for (int it = 0; it < 128 * DP / 8 / NT; ++it) {
       const int idx = it * NT + tid, r = idx / (DP / 8), c = idx % (DP / 8);
-      const int t_r = qt * p.tt + r / p.G, h_r = h * p.G + r % p.G;
-      const bool ok = t_r < qlen && c < DC;
+      const int t_r = qt * p.tt + r / p.G, h_r = h * p.gr + r % p.G;
+      const bool ok = t_r < qlen && r % p.G < p.gr && c < DC;
       const uint16_t *src = ok ? p.q + (size_t(q0 + t_r) * p.hq + h_r) * D + c * 8 : p.q;
       ptx::cp_async16(sb + swz_blk(r, c, kHalf), src, ok ? 16u : 0u);
     }
@@ -571,7 +572,7 @@ __global__ void __launch_bounds__(kOneRoleThreads, 1) prefill_kernel(const Prefi
   if (!failed) {
     const float l = l_run + xch[(half ^ 1) * 128 + row];
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + row % p.G) * D + half * OH;
+    uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.gr + row % p.G) * D + half * OH;
     {  // this half's columns of O, 8 per store, those below D
 #pragma unroll
       for (int c = 0; c < OH / 32; ++c) {
@@ -857,8 +858,8 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
     if (warp == 8) {
       for (int it = 0; it < 64; ++it) {
         const int idx = it * 32 + lane, r = idx >> 4, c = idx & 15;
-        const int t_r = qt * p.tt + r / p.G, h_r = h * p.G + r % p.G;
-        const bool ok = t_r < qlen;
+        const int t_r = qt * p.tt + r / p.G, h_r = h * p.gr + r % p.G;
+        const bool ok = t_r < qlen && r % p.G < p.gr;
         const uint16_t *src = ok ? p.q + (size_t(q0 + t_r) * p.hq + h_r) * kHd + c * 8 : p.q;
         ptx::cp_async16(sb + kOffQ + swz(r, c), src, ok ? 16u : 0u);
       }
@@ -1067,8 +1068,8 @@ __global__ void __launch_bounds__(ws_threads<TMA>(), 1)
     if (ok && ws_wait(bar(kOFinal), 0, fail)) {
       tc::fence_after_sync();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + row % p.G) * kHd + hf * 64;
-      store_o_row<T, 64>(tO, inv, dst, row_ok);
+      uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.gr + row % p.G) * kHd + hf * 64;
+      store_o_row<T, 64>(tO, inv, dst, row_ok && row % p.G < p.gr);  // idle rows: no store
     }
   }
 
@@ -1228,8 +1229,8 @@ __global__ void __launch_bounds__(kPrThreads, 1)
     if (warp == 8) {
       for (int it = 0; it < 128; ++it) {
         const int idx = it * 32 + lane, r = idx >> 4, c = idx & 15;  // r: CTA row 0..255
-        const int t_r = qt * tt + r / p.G, h_r = h * p.G + r % p.G;
-        const bool ok = t_r < qlen;
+        const int t_r = qt * tt + r / p.G, h_r = h * p.gr + r % p.G;
+        const bool ok = t_r < qlen && r % p.G < p.gr;
         const uint16_t *src = ok ? p.q + (size_t(q0 + t_r) * p.hq + h_r) * kHd + c * 8 : p.q;
         ptx::cp_async16(sb + kPrOffQ + uint32_t(r >> 7) * kTile + swz(r & 127, c), src,
                         ok ? 16u : 0u);
@@ -1455,8 +1456,8 @@ __global__ void __launch_bounds__(kPrThreads, 1)
         part_l[crow] = l_run;
       } else {
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.G + crow % p.G) * kHd;
-        store_o_row<T, 128>(tO, inv, dst, row_ok);
+        uint16_t *dst = p.out + (size_t(q0 + ti) * p.hq + h * p.gr + crow % p.G) * kHd;
+        store_o_row<T, 128>(tO, inv, dst, row_ok && crow % p.G < p.gr);  // idle rows: no store
       }
     }
   }
@@ -1487,7 +1488,7 @@ __global__ void __launch_bounds__(256) prefill_merge_kernel(const __grid_constan
   const int q0 = p.q_start[b];
   const int qlen = p.q_start[b + 1] - q0;
   const int ti = qt * 2 * p.tt + crow / p.G;
-  if (ti >= qlen) return;
+  if (ti >= qlen || crow % p.G >= p.gr) return;
   const size_t n_slots = size_t(n_items) * P.nsplit;
   const float *om = P.part_o + n_slots * 256 * kHd;
   const float *ol = om + n_slots * 256;
@@ -1515,7 +1516,7 @@ __global__ void __launch_bounds__(256) prefill_merge_kernel(const __grid_constan
   uint2 v;
   v.x = pack2<T>(acc.x * inv, acc.y * inv);
   v.y = pack2<T>(acc.z * inv, acc.w * inv);
-  *reinterpret_cast<uint2 *>(p.out + (size_t(q0 + ti) * p.hq + h * p.G + crow % p.G) * kHd +
+  *reinterpret_cast<uint2 *>(p.out + (size_t(q0 + ti) * p.hq + h * p.gr + crow % p.G) * kHd +
                              lane * 4) = v;
 }
 
@@ -1566,7 +1567,12 @@ cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
       a.num_q_heads % a.kv_heads != 0)
     return cudaErrorInvalidValue;
   const int G = a.num_q_heads / a.kv_heads;
-  if (G > kRows || kRows % G != 0) return cudaErrorInvalidValue;
+  if (G < 1 || G > kRows) return cudaErrorInvalidValue;
+  // A CTA's rows are (token, head) pairs, token = row / Gp: a group that does not divide
+  // the 128 rows is padded to the next power of two, its extra rows idle (zero queries,
+  // never stored), e.g. 7 query heads per kv head run as 8.
+  int Gp = 1;
+  while (Gp < G) Gp *= 2;
   if ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.out)) & 15)
     return cudaErrorInvalidValue;
   if (a.batch <= 0 || a.max_q_len <= 0) return cudaSuccess;
@@ -1582,10 +1588,11 @@ cudaError_t paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
   p.region_elems = a.region_elems;
   p.hq = a.num_q_heads;
   p.hkv = a.kv_heads;
-  p.G = G;
+  p.G = Gp;
+  p.gr = G;
   p.bs = a.block_size;
   p.max_bps = a.max_blocks_per_seq;
-  p.tt = kRows / G;
+  p.tt = kRows / Gp;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   const bool bf16 = a.dtype == Dtype::BF16;
   p.idesc_qk = tc::idesc_f16(bf16, 128, 128, false, false);

@@ -161,8 +161,8 @@ def test_kernel_entry_points_refuse_host_pool(host_pool_factory):
 @pytest.mark.parametrize("kw,msg", [
     (dict(head_dim=100), "head_dim 100 unsupported"),
     (dict(head_dim=264), "head_dim 264 unsupported"),
-    (dict(num_q_heads=6, kv_heads=4), "dividing 128"),
-    (dict(num_q_heads=384, kv_heads=1), "dividing 128"),
+    (dict(num_q_heads=6, kv_heads=4), "at most 128"),
+    (dict(num_q_heads=384, kv_heads=1), "at most 128"),
     (dict(batch=0), "must be positive"),
     (dict(query_ptr=24), "16-byte aligned"),
     (dict(block_tables_ptr=0), "null pointer"),

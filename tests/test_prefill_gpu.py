@@ -124,6 +124,30 @@ def test_prefill_other_head_dims(case):
         wl.close()
 
 
+@pytest.mark.parametrize("hq,hkv,d,bs,impl", [
+    (21, 3, 128, 16, None),      # 7 query heads per kv head (Qwen2.5-7B's 28 / 4): rows of 8
+    (10, 2, 128, 8, None),       # 5 per kv head on 8-token pages (copy-gather producers)
+    (6, 2, 128, 16, "ws"),       # 3 per kv head on the one-tile kernel
+    (12, 4, 64, 16, None),       # 3 per kv head, head_dim 64 (single-role kernel)
+    (14, 2, 128, 16, "cpasync"), # 7 per kv head on the single-role kernel
+])
+def test_prefill_group_not_dividing_128(hq, hkv, d, bs, impl, monkeypatch):
+    """Query heads per kv head that do not divide a CTA's 128 rows run padded to the next
+    power of two; the idle rows are neither read nor stored, so every real head's rows
+    must match the oracle (a store from an idle row would land on a real head's row)."""
+    if impl:
+        monkeypatch.setenv("KCMM_PREFILL_IMPL", impl)
+    wl = make(ctx_lens=[300, 517, 64], chunk_lens=[300, 200, 1], num_q_heads=hq, kv_heads=hkv,
+              head_dim=d, block_size=bs, seed=hq * 7 + d)
+    try:
+        wl.run()
+        _torch().cuda.synchronize()
+        check(wl)
+        assert wl.pool.kernel_status() == 0
+    finally:
+        wl.close()
+
+
 def test_prefill_last_row_equals_decode():
     """The last row of a chunk is a decode step over the whole context: both kernels agree."""
     torch = _torch()
@@ -179,8 +203,8 @@ def test_prefill_rejects_unsupported_shapes():
             wl.pool.paged_prefill(0, num_q_heads=8, kv_heads=1, head_dim=100, **base)
         with pytest.raises(KcmmError, match="head_dim 264 unsupported"):
             wl.pool.paged_prefill(0, num_q_heads=8, kv_heads=1, head_dim=264, **base)
-        with pytest.raises(KcmmError, match="dividing 128"):
-            wl.pool.paged_prefill(0, num_q_heads=6, kv_heads=2, head_dim=128, **base)
+        with pytest.raises(KcmmError, match="at most 128"):
+            wl.pool.paged_prefill(0, num_q_heads=6, kv_heads=4, head_dim=128, **base)
     finally:
         wl.close()
 
