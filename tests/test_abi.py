@@ -181,16 +181,22 @@ def test_prefill_argument_checks(host_pool_factory, kw, msg):
         pool.paged_prefill(0, **args)
 
 
-def test_prefill_refuses_host_pool(host_pool_factory):
+@pytest.mark.parametrize("hq,hd,bs", [(8, 128, 16), (14, 128, 16), (6, 64, 8), (10, 256, 16),
+                                      (256, 96, 32)])
+def test_prefill_refuses_host_pool(host_pool_factory, hq, hd, bs):
+    """Shapes the prefill accepts (query-head groups of 4, 7, 3, 5 and 128, head dims 64
+    to 256, 8- to 32-token pages) pass the argument checks and stop only at the missing
+    device memory of a host pool."""
     from lattice_b200 import KcmmError
 
-    pool = host_pool_factory(kv_heads=2, head_dim=128, max_batch=1, max_seq_len=32)
+    pool = host_pool_factory(kv_heads=2, head_dim=hd, max_batch=1, max_seq_len=32,
+                             block_size=bs)
     with pytest.raises(KcmmError, match="no device memory"):
         pool.paged_prefill(0, query_ptr=16, out_ptr=16, block_tables_ptr=16,
                            query_start_loc_ptr=16, context_lens_ptr=16,
-                           block_offsets_f16_ptr=16, batch=1, max_query_len=4, num_q_heads=8,
-                           kv_heads=2, head_dim=128, block_size=16, max_blocks_per_seq=2,
-                           scale=0.1)
+                           block_offsets_f16_ptr=16, batch=1, max_query_len=4,
+                           num_q_heads=hq, kv_heads=2, head_dim=hd, block_size=bs,
+                           max_blocks_per_seq=2, scale=0.1)
 
 
 def test_step_tables_need_a_device_pool(kcmm_lib, host_pool_factory):
